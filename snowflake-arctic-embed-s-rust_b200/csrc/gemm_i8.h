@@ -1,0 +1,37 @@
+// Host interface of the tcgen05 int8 GEMM (gemm_i8.cu).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace ae {
+
+enum GemmEpilogue : int {
+  EPI_F32 = 0,
+  EPI_LN_QUANT = 1,
+  EPI_GELU_QUANT = 2,
+  EPI_LN_FINAL = 3,
+};
+
+struct GemmArgs {
+  int M, N, K;
+  const float* a_scale;     // [M]
+  const float* w_scale;     // [N]
+  const float* bias;        // [N]
+  const float* res;         // [M, ldr] residual or nullptr
+  int ldr;
+  const float* gamma;       // [384] LayerNorm weight (LN epilogues)
+  const float* beta;        // [384] LayerNorm bias
+  const float* inv_smooth;  // [N] SmoothQuant inverse scale of the next GEMM's input (quant epilogues)
+  float* out_f32;           // [M, ldo] fp32 output (F32 / LN epilogues)
+  int ldo;
+  int8_t* out_q;            // [M, N] int8 output (quant epilogues)
+  float* out_scale;         // [M] row scale of out_q
+  int32_t* acc_dbg;         // [M, N] raw int32 accumulators, or nullptr
+  int* err;                 // device error word
+};
+
+int make_tmap_i8(CUtensorMap* map, const void* base, int rows, int K);
+int gemm_i8_launch(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, cudaStream_t st);
+
+}  // namespace ae

@@ -1,0 +1,62 @@
+// Per-row arithmetic in the exact operation order of the reference CPU path (x86_64 AVX2 kernels),
+// so that a GPU thread that owns one row rounds exactly as the reference does. The library is
+// compiled with --fmad=false: every fused multiply-add below is an explicit fmaf, every other
+// product/sum rounds separately, as in the reference.
+#pragma once
+#include <cstdint>
+
+namespace ae {
+
+constexpr int kHidden = 384;
+constexpr int kInter = 1536;
+constexpr int kHeads = 12;
+constexpr int kHeadDim = 32;
+constexpr int kLayers = 12;
+constexpr int kVocab = 30522;
+constexpr int kMaxPos = 512;
+constexpr float kLnEps = 1e-12f;
+
+// hsum256_ps(sum0 + sum1) of src/simd_math.rs:3075-3084 applied to 16 partial lanes p[0..16)
+// (p[l] accumulates elements with index % 16 == l, as the two AVX2 accumulators do).
+__device__ __forceinline__ float tree16(const float (&p)[16]) {
+  float v[8];
+#pragma unroll
+  for (int l = 0; l < 8; ++l) v[l] = p[l] + p[8 + l];
+  return ((v[0] + v[4]) + (v[1] + v[5])) + ((v[2] + v[6]) + (v[3] + v[7]));
+}
+
+// hsum256_ps of one 8-lane vector.
+__device__ __forceinline__ float tree8(const float (&v)[8]) {
+  return ((v[0] + v[4]) + (v[1] + v[5])) + ((v[2] + v[6]) + (v[3] + v[7]));
+}
+
+// Clamp-and-round of the AVX2 quantizers: min(max(v, -127), 127) then cvtps_epi32 (half-even).
+__device__ __forceinline__ int quant_i8(float v) {
+  v = fminf(fmaxf(v, -127.0f), 127.0f);
+  return __float2int_rn(v);
+}
+
+// avx2_exp_f32, src/simd_math.rs:113-143 (Cody-Waite range reduction + degree-5 polynomial).
+__device__ __forceinline__ float cw_exp(float x) {
+  float y = fmaxf(fminf(x, 88.0f), -87.3f);
+  float n = rintf(y * 1.44269504088896341f);  // LOG2_E rounded to f32
+  float r = fmaf(-n, 1.428606765330187e-6f, fmaf(-n, 0.693145751953125f, y));
+  float p = fmaf(r, 0.008333334f, 0.041666668f);
+  p = fmaf(r, p, 0.16666667f);
+  p = fmaf(r, p, 0.5f);
+  p = fmaf(r, p, 1.0f);
+  p = fmaf(r, p, 1.0f);
+  int ni = __float2int_rn(n) + 127;
+  return p * __int_as_float(ni << 23);
+}
+
+// Scalar `f32::exp` used by the reference for softmax tail elements. Evaluated in double and
+// rounded once, which is the correctly rounded result except in rare double-rounding cases.
+__device__ __forceinline__ float scalar_expf(float x) { return static_cast<float>(exp(static_cast<double>(x))); }
+
+// GELU with the exact error function (0.5 x (1 + erf(x / sqrt 2))).
+__device__ __forceinline__ float gelu_erf(float x) {
+  return (0.5f * x) * (1.0f + erff(x * 0.70710678118654752f));
+}
+
+}  // namespace ae
