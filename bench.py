@@ -1,0 +1,426 @@
+#!/usr/bin/env python
+"""Benchmark of the arctic-embed-s int8 forward pass on B200.
+
+Headline (BASELINE.json metric): embeddings/sec at 128 tokens, config 3 — batches of 512
+sequences x 128 tokens per GPU, one batch per step, sharded over N GPUs (one process per GPU under
+torchrun, no collective on the data path: weak scaling). Synthetic seeded model and token ids.
+
+  value     device-resident throughput: token ids already in HBM, ae_forward_ragged_device per step,
+            CUDA events per step on the launch stream, L2 flushed between steps (outside the events),
+            total = max over ranks
+  e2e       the same metric through the public host API (ae_forward_ragged): every step copies the
+            ids from host memory to the GPU and the embeddings back, host wall clock, max over ranks
+  latency   p50 / p99 of ae_forward_cls (batch 1, CUDA-graph replay, host buffers) at 32 and 512 tokens
+  roofline  the dominant kernel of a step, timed alone with CUDA events at the step's shapes
+  cpu_baseline  the CPU oracle (C++ restatement of the reference's x86 path) on a bounded sample,
+            all host threads
+
+`--impl reference` times the reference's CPU path (the oracle; the Rust crate cannot be built
+here) on the same metric and prints its own JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "snowflake-arctic-embed-s-rust_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "embeddings/sec @128 tok"
+SEQ_LEN = 128
+BATCH_SEQS = 512
+H = 384
+L2_BYTES = 126 * 1024 * 1024
+
+
+def int8_ops_per_seq(L: int) -> float:
+    """Algorithmic int8 ops of one sequence: 2 x (19,759,104 L + 1,474,560) MACs."""
+    return 2.0 * (19759104.0 * L + 1474560.0)
+
+
+def attn_flops_per_seq(L: int) -> float:
+    """Algorithmic fp32 attention flop of one sequence: 2 x (8,448 L^2 + 768 L) MACs."""
+    return 2.0 * (8448.0 * L * L + 768.0 * L)
+
+
+def make_batches(n_batches: int, seed: int, seqs: int = BATCH_SEQS, L: int = SEQ_LEN):
+    from arctic_embed_s_int8 import synth
+
+    r = np.random.Generator(np.random.PCG64(seed))
+    out = []
+    for _ in range(n_batches):
+        ids = np.concatenate([synth.token_ids(L, r) for _ in range(seqs)]).astype(np.uint16)
+        cu = (np.arange(seqs + 1, dtype=np.uint32) * L).astype(np.uint32)
+        out.append((ids, cu))
+    return out
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_baseline(seconds: float = 10.0, L: int = SEQ_LEN, threads: int | None = None):
+    """Oracle embed_batch (all host threads) on a bounded sample of 128-token sequences."""
+    from arctic_embed_s_int8 import synth
+    from oracle import oracle as orc
+
+    orc.build()
+    threads = threads or os.cpu_count() or 1
+    m = orc.OracleModel(synth.pack_path(0))
+    r = np.random.Generator(np.random.PCG64(99))
+    probe = [synth.token_ids(L, r) for _ in range(threads)]
+    t0 = time.perf_counter()
+    m.embed_batch(probe, threads)
+    per_round = max(time.perf_counter() - t0, 1e-3)
+    n = int(max(threads, min(8192, threads * seconds / per_round)))
+    seqs = [synth.token_ids(L, r) for _ in range(n)]
+    t0 = time.perf_counter()
+    m.embed_batch(seqs, threads)
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": "embeddings/s", "cores": threads,
+            "kind": "port", "sample": f"{n} sequences x {L} tokens, embed_batch over {threads} threads, {dt:.1f} s",
+            "cpu": _cpu_name()}
+
+
+def _cpu_name():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU path (oracle port) on this host's cores, rank 0 only."""
+    if rank != 0:
+        return 0
+    from arctic_embed_s_int8 import synth
+    from oracle import oracle as orc
+
+    orc.build()
+    threads = os.cpu_count() or 1
+    m = orc.OracleModel(synth.pack_path(0))
+    r = np.random.Generator(np.random.PCG64(7))
+    per_step = max(threads, args.ref_seqs_per_step)
+    for _ in range(args.warmup):
+        m.embed_batch([synth.token_ids(SEQ_LEN, r) for _ in range(threads)], threads)
+    times = []
+    for _ in range(args.steps):
+        seqs = [synth.token_ids(SEQ_LEN, r) for _ in range(per_step)]
+        t0 = time.perf_counter()
+        m.embed_batch(seqs, threads)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = per_step * args.steps / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "embeddings/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8 GEMM / fp32",
+        "data": "synthetic (seeded .ae8 pack and token ids)",
+        "config": {"workload": "config 3: 128-token sequences (a bounded sample per step on the CPU)",
+                   "seq_len": SEQ_LEN, "seqs_per_step": per_step},
+        "cpu_baseline": {"value": value, "unit": "embeddings/s", "cores": threads, "kind": "port",
+                         "sample": f"{per_step} sequences x {SEQ_LEN} tokens per step, embed_batch, {threads} threads",
+                         "cpu": _cpu_name()},
+        "e2e": {"value": value, "unit": "embeddings/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def kernel_breakdown(eng, T: int, n: int, L: int, reps: int = 5):
+    """Times each kernel of a step alone (CUDA events on the engine's stream) at the step's shapes."""
+    import torch
+
+    st = torch.cuda.current_stream()
+    dev = "cuda"
+    g = torch.Generator(device="cpu").manual_seed(0)
+    a384 = torch.randint(-127, 128, (T, 384), dtype=torch.int8, generator=g).to(dev)
+    a1536 = torch.randint(-127, 128, (T, 1536), dtype=torch.int8, generator=g).to(dev)
+    sc = torch.rand(T, generator=g).to(dev) * 9e-3 + 1e-3
+
+    def w(N, K):
+        return (torch.randint(-127, 128, (N, K), dtype=torch.int8, generator=g).to(dev),
+                (torch.rand(N, generator=g) * 9e-3 + 1e-3).to(dev), (torch.randn(N, generator=g) * 0.02).to(dev))
+
+    wq, wo, wi, wd = w(1152, 384), w(384, 384), w(1536, 384), w(384, 1536)
+    gam = torch.ones(384, device=dev)
+    bet = torch.zeros(384, device=dev)
+    inv384 = torch.ones(384, device=dev)
+    inv1536 = torch.ones(1536, device=dev)
+    out1152 = torch.empty(T, 1152, device=dev)
+    res = torch.randn(T, 384, device=dev)
+    q384 = torch.empty(T, 384, dtype=torch.int8, device=dev)
+    s_out = torch.empty(T, device=dev)
+    q1536 = torch.empty(T, 1536, dtype=torch.int8, device=dev)
+    qkv = torch.randn(T, 1152, device=dev)
+    cu = torch.arange(0, n + 1, dtype=torch.int32, device=dev) * L
+    ctx = torch.empty(T, 384, device=dev)
+    kernels = {
+        "gemm_qkv": lambda: eng.gemm_i8(0, a384, sc, *wq, out=out1152),
+        "gemm_attn_out_ln": lambda: eng.gemm_i8(1, a384, sc, *wo, res=res, gamma=gam, beta=bet, inv_smooth=inv384,
+                                                out=res, out_q=q384, out_scale=s_out),
+        "gemm_ffn_up_gelu": lambda: eng.gemm_i8(2, a384, sc, *wi, inv_smooth=inv1536, out_q=q1536, out_scale=s_out),
+        "gemm_ffn_down_ln": lambda: eng.gemm_i8(1, a1536, sc, *wd, res=res, gamma=gam, beta=bet, inv_smooth=inv384,
+                                                out=res, out_q=q384, out_scale=s_out),
+        "attention": lambda: eng.attention_f32(qkv, cu, n, L, ctx),
+    }
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
+    res_ms = {}
+    for name, fn in kernels.items():
+        fn()
+        ts = []
+        for _ in range(reps):
+            flush.fill_(1.0)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            fn()
+            e1.record(st)
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        res_ms[name] = float(np.median(ts))
+    eng.sync()
+    # algorithmic work per launch
+    gemm_shapes = {"gemm_qkv": (384, 1152), "gemm_attn_out_ln": (384, 384), "gemm_ffn_up_gelu": (384, 1536),
+                   "gemm_ffn_down_ln": (1536, 384)}
+    info = {}
+    for k, ms in res_ms.items():
+        if k in gemm_shapes:
+            K, N = gemm_shapes[k]
+            ops = 2.0 * T * K * N
+            info[k] = {"ms": ms, "tops": ops / ms / 1e9, "ops": ops}
+        else:
+            fl = n * 2.0 * 2.0 * 12 * L * L * 32
+            info[k] = {"ms": ms, "tflops": fl / ms / 1e9, "flop": fl}
+    return info
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--latency-runs", type=int, default=1000)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ref-seqs-per-step", type=int, default=64)
+    ap.add_argument("--no-extras", action="store_true", help="skip latency, kernel breakdown and CPU baseline")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    args.warmup = max(args.warmup, 3)
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    from arctic_embed_s_int8 import Engine, synth
+
+    pack = synth.pack_path(0)
+    eng = Engine(local).load_file(pack)
+    stream = torch.cuda.Stream()
+    eng.set_stream(stream)
+    n_batches = args.warmup + args.steps
+    batches = make_batches(n_batches, seed=1000 + rank)
+    T = BATCH_SEQS * SEQ_LEN
+    eng.reserve(T, BATCH_SEQS)
+    d_in = [(torch.from_numpy(ids.view(np.int16)).cuda(), torch.from_numpy(cu.view(np.int32)).cuda()) for ids, cu in batches]
+    d_out = torch.empty(BATCH_SEQS, H, dtype=torch.float32, device="cuda")
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
+
+    # ---- value: device-resident inputs
+    launches0 = eng.kernel_launches()
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            eng.forward_device(d_in[i][0], d_in[i][1], BATCH_SEQS, T, SEQ_LEN, d_out)
+        eng.sync()
+        barrier()
+        launches0 = eng.kernel_launches()
+        evs = []
+        with ClockSampler(local) as clk:
+            for i in range(args.steps):
+                flush.fill_(float(i))
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                b = d_in[args.warmup + i]
+                eng.forward_device(b[0], b[1], BATCH_SEQS, T, SEQ_LEN, d_out)
+                e1.record(stream)
+                evs.append((e0, e1))
+            stream.synchronize()
+            eng.sync()
+            barrier()
+        launches = eng.kernel_launches() - launches0
+    step_ms = [a.elapsed_time(b) for a, b in evs]
+    total_s = max_over_ranks(sum(step_ms) / 1e3)
+    value = world * BATCH_SEQS * args.steps / total_s
+
+    # ---- e2e: host buffers through the public API
+    h_batches = batches
+    for i in range(args.warmup):
+        eng.forward_packed(*h_batches[i])
+    barrier()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        out = eng.forward_packed(*h_batches[args.warmup + i])
+    t_e2e = time.perf_counter() - t0
+    barrier()
+    t_e2e = max_over_ranks(t_e2e)
+    e2e = world * BATCH_SEQS * args.steps / t_e2e
+    h2d = int(batches[0][0].nbytes + batches[0][1].nbytes)
+    d2h = int(out.nbytes)
+
+    result = {
+        "metric": METRIC, "value": value, "unit": "embeddings/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * total_s / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8 GEMM (int32 acc) / fp32 elementwise+attention",
+        "data": "synthetic (seeded .ae8 pack, random-init arctic-embed-s weights; token ids [CLS]+U[1000,30521]+[SEP])",
+        "config": {"workload": "config 3: batches of 512 sequences x 128 tokens per GPU, one batch per step",
+                   "global_batch": world * BATCH_SEQS, "seq_len": SEQ_LEN, "tokens_per_step_per_gpu": T,
+                   "parallelism": f"data-parallel shards x{world}, no collective",
+                   "l2": "flushed (256 MB write) between timed steps, outside the step events"},
+        "e2e": {"value": e2e, "unit": "embeddings/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "api": "ae_forward_ragged (host ids in, host embeddings out; wall clock)"},
+        "gpu_launches": int(launches),
+        "clocks": clk.summary(),
+    }
+
+    if not args.no_extras and rank == 0:
+        # latency (config 2 subset): p50/p99 of forward_cls, host buffers, CUDA-graph replay
+        lat = {}
+        r = np.random.Generator(np.random.PCG64(42))
+        for L, runs in ((32, args.latency_runs), (512, max(50, args.latency_runs // 3))):
+            ids = synth.token_ids(L, r)
+            for _ in range(20):
+                eng.forward_cls(ids)
+            ts = []
+            for _ in range(runs):
+                t0 = time.perf_counter()
+                eng.forward_cls(ids)
+                ts.append((time.perf_counter() - t0) * 1e3)
+            lat[f"p50_ms@{L}"] = float(np.percentile(ts, 50))
+            lat[f"p99_ms@{L}"] = float(np.percentile(ts, 99))
+            lat[f"runs@{L}"] = runs
+        result["latency"] = lat
+        # kernel breakdown and roofline of the dominant kernel
+        kb = kernel_breakdown(eng, T, BATCH_SEQS, SEQ_LEN)
+        per_step = {k: v["ms"] * 11 for k, v in kb.items()}
+        dom = max(per_step, key=per_step.get)
+        peaks = {}
+        try:
+            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+                peaks = json.load(f)
+        except OSError:
+            pass
+        bf16 = peaks.get("bf16_tflops", 1590.0)
+        hbm = peaks.get("hbm_gbs", 6650.0)
+        src = "of measured" if peaks else "of fallback"
+        if dom.startswith("gemm"):
+            ach = kb[dom]["tops"]
+            peak = 2.0 * bf16
+            result["roofline"] = {"kernel": dom, "bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS (int8)",
+                                  "frac": ach / peak, "traffic": None,
+                                  "peak_basis": f"int8 dense = 2 x bf16 dense {src} ({bf16} TFLOP/s)"}
+        else:
+            ach = kb[dom]["tflops"]
+            result["roofline"] = {"kernel": dom, "bound": "tensor", "achieved": ach, "peak": bf16, "unit": "TFLOP/s",
+                                  "frac": ach / bf16, "traffic": None,
+                                  "peak_basis": f"bf16 dense {src}; kernel runs fp32 on the CUDA cores"}
+        result["kernels_ms_per_launch"] = {k: round(v["ms"], 4) for k, v in kb.items()}
+        result["kernels_share_of_step"] = {k: round(v / (1e3 * total_s / args.steps), 3) for k, v in per_step.items()}
+        result["int8_tops_whole_step"] = BATCH_SEQS * int8_ops_per_seq(SEQ_LEN) / (total_s / args.steps) / 1e12
+        try:
+            result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+        except Exception as e:  # reported, not fatal
+            result["cpu_baseline"] = {"error": str(e)}
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    eng.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

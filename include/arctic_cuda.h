@@ -1,0 +1,156 @@
+/* arctic_cuda.h — C ABI of the B200 (sm_100a) backend for the arctic-embed-s int8 W8A8 encoder.
+ *
+ * This is the boundary a host crate binds through FFI in place of the reference crate's CPU
+ * kernels (mdlockyer/snowflake-arctic-embed-s-rust). Plain pointers and sizes only. Every function
+ * returns 0 on success or a negative AE_ERR_* code; ae_last_error() gives the message of the last
+ * failure on a context. No exception, abort or panic crosses this boundary.
+ *
+ * Threading: one ae_ctx drives one GPU. A context is NOT thread-safe (it owns its workspace,
+ * like the reference's `&mut Workspace`); different contexts may be driven from different host
+ * threads at the same time. ae_embed_batch_multi drives several contexts itself.
+ *
+ * Units: a "sequence" is a list of token ids ([CLS] ... [SEP] as produced by the WordPiece
+ * tokenizer); sequences longer than 512 are truncated to their first 512 ids, as the reference
+ * does (src/model.rs:191, src/tokenizer.rs:98-101). Outputs are L2-normalised 384-d [CLS]
+ * embeddings, row-major float32.
+ */
+#ifndef ARCTIC_CUDA_H
+#define ARCTIC_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AE_HIDDEN 384
+#define AE_MAX_POSITIONS 512
+
+enum {
+  AE_OK = 0,
+  AE_ERR_INVALID_ARG = -1,  /* null pointer, bad size, empty sequence */
+  AE_ERR_CUDA = -2,         /* CUDA runtime error (message has the CUDA error string) */
+  AE_ERR_NO_MODEL = -3,     /* forward called before ae_model_load */
+  AE_ERR_BAD_PACK = -4,     /* malformed .ae8 pack or model descriptor */
+  AE_ERR_TOKEN_RANGE = -5,  /* token id >= 30522 (the reference panics on a slice index) */
+  AE_ERR_DEVICE = -6,       /* a kernel reported an error (bounded wait ran out, bad shape) */
+  AE_ERR_CAPACITY = -7,     /* request larger than the reserved workspace */
+};
+
+typedef struct ae_ctx ae_ctx;
+
+/* One int8 linear layer: QuantizedLinearRaw (src/quantize.rs:22-30) /
+ * PackedLinearInt8::from_raw_row_major (src/gemm.rs:186-246). Host pointers; copied to the GPU by
+ * ae_model_load. n_out == 0 means "pruned": only inv_smooth is kept (src/gemm.rs:195-205). */
+typedef struct {
+  uint64_t n_out;
+  uint64_t k_in;
+  const int8_t* w_q;        /* [n_out * k_in] row-major (out_features x in_features) */
+  const float* w_scale;     /* [n_out] */
+  const float* bias;        /* [n_out] */
+  const float* inv_smooth;  /* [k_in] */
+} ae_linear_desc;
+
+/* QuantizedLayerRaw (src/quantize.rs:46-58). */
+typedef struct {
+  ae_linear_desc qkv;
+  int32_t has_split;        /* 1 on layer 11: q_only / kv_only are valid */
+  ae_linear_desc q_only;
+  ae_linear_desc kv_only;
+  ae_linear_desc attn_out;
+  const float* ln1_weight;
+  const float* ln1_bias;
+  ae_linear_desc ffn_inter;
+  ae_linear_desc ffn_out;
+  const float* ln2_weight;
+  const float* ln2_bias;
+} ae_layer_desc;
+
+/* QuantizedModelRaw (src/quantize.rs:60-72): what QuantizedModelRaw::load_ae8 produces. */
+typedef struct {
+  const int8_t* word_emb_q;   const float* word_emb_scale;  /* [30522*384], [30522] */
+  const int8_t* pos_emb_q;    const float* pos_emb_scale;   /* [512*384],   [512]   */
+  const int8_t* type_emb_q;   const float* type_emb_scale;  /* [2*384],     [2]     */
+  const float* emb_ln_weight; const float* emb_ln_bias;     /* [384] */
+  ae_layer_desc layers[12];
+} ae_model_desc;
+
+/* Context on CUDA device `device` (its own stream and device error word).
+ * Replaces: nothing in the reference (the CPU crate has no device); pairs with Workspace::new
+ * (src/model.rs:146-173) for the memory it owns. */
+int ae_ctx_create(int device, ae_ctx** out);
+int ae_ctx_destroy(ae_ctx* ctx);
+/* Message of the last failure on ctx (or of the last ae_ctx_create failure when ctx is NULL). */
+const char* ae_last_error(const ae_ctx* ctx);
+/* Stream the context launches on (a cudaStream_t); NULL selects the context's own stream. */
+int ae_ctx_set_stream(ae_ctx* ctx, void* cuda_stream);
+int ae_ctx_device(const ae_ctx* ctx);
+
+/* Uploads the model. Replaces PackedModel::from_raw (src/model.rs:49-84), which repacks the
+ * weights for a CPU SIMD backend; here the row-major int8 weights are already the K-major
+ * tcgen05 operand layout and are copied as they are. Validates every size. */
+int ae_model_load(ae_ctx* ctx, const ae_model_desc* desc);
+/* Convenience: QuantizedModelRaw::load_ae8 (src/quantize.rs:76-137) + ae_model_load. */
+int ae_model_load_file(ae_ctx* ctx, const char* path);
+
+/* Reserves the device workspace for batches of up to max_tokens packed rows and max_seqs
+ * sequences (Workspace::new, src/model.rs:146-173, sized for a token budget instead of 512).
+ * Called implicitly (growing) by the forward functions. */
+int ae_reserve(ae_ctx* ctx, uint32_t max_tokens, uint32_t max_seqs);
+
+/* PackedModel::forward_cls (src/model.rs:185-513) / ArcticEmbedS::embed_tokens (src/lib.rs:96-102):
+ * one sequence -> out[384]. Host buffers. Latency mode: replays a CUDA graph per length. */
+int ae_forward_cls(ae_ctx* ctx, const uint16_t* ids, uint32_t len, float* out384);
+
+/* PackedModel::forward_ragged_cls (src/model.rs:521-914) without its 64-sequence / 512-row limits:
+ * n_seqs sequences packed back to back in ids, sequence i = ids[cu_seqlens[i] .. cu_seqlens[i+1]),
+ * each truncated to 512 ids on its own. out: [n_seqs * 384]. Host buffers (copied in/out inside). */
+int ae_forward_ragged(ae_ctx* ctx, const uint16_t* ids, const uint32_t* cu_seqlens, uint32_t n_seqs, float* out);
+
+/* Same as ae_forward_ragged with every buffer already in device memory of ctx's GPU and every
+ * sequence already 1..512 ids long (a kernel checks and reports AE_ERR_DEVICE otherwise);
+ * max_len bounds the longest sequence. Asynchronous on the context's stream; no host sync. */
+int ae_forward_ragged_device(ae_ctx* ctx, const uint16_t* d_ids, const uint32_t* d_cu_seqlens, uint32_t n_seqs,
+                             uint32_t total_tokens, uint32_t max_len, float* d_out);
+
+/* ArcticEmbedS::embed_batch (src/lib.rs:138-260) over pre-tokenised sequences, sharded across
+ * n_ctx contexts (GPUs) by token-weighted greedy assignment, one host thread per context; results
+ * in input order. `max_batch_tokens` (0 = 65536) bounds the rows of one device batch. */
+int ae_embed_batch_multi(ae_ctx* const* ctxs, int n_ctx, const uint16_t* ids, const uint32_t* cu_seqlens,
+                         uint32_t n_seqs, uint32_t max_batch_tokens, float* out);
+
+/* The sharding plan ae_embed_batch_multi uses (host only, no GPU needed): shard_of[i] in
+ * [0, n_shards) for every sequence, token-weighted greedy (longest first) over the cost
+ * 19,759,104 L + 8,448 L^2 MACs of an L-token sequence. Replaces the work-stealing counter of
+ * embed_batch (src/lib.rs:163-167), which balances threads dynamically on one CPU. */
+int ae_plan_shards(const uint32_t* cu_seqlens, uint32_t n_seqs, int n_shards, int32_t* shard_of);
+
+/* gemm_int8_fused (src/gemm.rs:630-671) on device buffers, for tests and the kernel microbench:
+ *   epi 0: out = fma(float(A W^T), a_scale * w_scale, bias (+ res))              [M, N] f32
+ *   epi 1: epi 0 with res, then LayerNorm(gamma, beta) -> out (the new residual) and the
+ *          SmoothQuant row quantization with inv_smooth -> out_q [M, 384], out_scale [M]  (N = 384)
+ *   epi 2: GELU(epi 0) * inv_smooth, row-quantized -> out_q [M, 1536], out_scale [M]    (N = 1536)
+ *   epi 3: epi 0 with res, then layernorm_inplace_row + l2_normalize_inplace -> out     (N = 384)
+ * A [M, K] int8, W [N, K] int8 row-major; K a multiple of 128. acc (nullable) receives the raw
+ * int32 accumulators [M, N]. */
+int ae_gemm_i8(ae_ctx* ctx, int epi, uint32_t M, uint32_t N, uint32_t K, const int8_t* d_a, const float* d_a_scale,
+               const int8_t* d_w, const float* d_w_scale, const float* d_bias, const float* d_res,
+               const float* d_gamma, const float* d_beta, const float* d_inv_smooth, float* d_out, int8_t* d_out_q,
+               float* d_out_scale, int32_t* d_acc);
+
+/* The attention of one layer (src/model.rs:294-321 per segment) on device buffers:
+ * qkv [total, 1152] f32 (Q | K | V, head h at columns 32h..32h+31 of each third) -> ctx [total, 384]. */
+int ae_attention_f32(ae_ctx* ctx, const float* d_qkv, const uint32_t* d_cu_seqlens, uint32_t n_seqs,
+                     uint32_t max_len, float* d_ctx);
+
+/* Number of this library's kernels the context has launched so far (graph replays included). */
+uint64_t ae_kernel_launches(const ae_ctx* ctx);
+
+/* Waits for the context's stream; reports a device-side error (AE_ERR_DEVICE) if one was raised. */
+int ae_sync(ae_ctx* ctx);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ARCTIC_CUDA_H */

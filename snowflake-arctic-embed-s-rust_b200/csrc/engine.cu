@@ -1,0 +1,955 @@
+// Host engine behind the C ABI (include/arctic_cuda.h): one context per GPU owns the uploaded
+// model, a device workspace sized for a token budget, pinned staging buffers, a stream and a device
+// error word, and enqueues the forward pass of a packed batch:
+//
+//   row metadata -> embedding+LN+quant -> 11 x [QKV GEMM -> attention -> ctx quant ->
+//   attn-out GEMM (+res, LN1, quant) -> FFN-up GEMM (GELU, quant) -> FFN-down GEMM (+res, LN2, quant)]
+//   -> layer 11: KV GEMM over all rows, gather [CLS] rows, Q GEMM, [CLS] attention, ctx quant,
+//      attn-out (+LN1), FFN-up, FFN-down (+LN2, L2 norm) -> [n, 384]
+//
+// which is PackedModel::forward_ragged_cls (src/model.rs:521-914) without its 64-sequence and
+// 512-row limits; a single sequence (forward_cls, src/model.rs:185-513) is the n = 1 case and is
+// replayed from a CUDA graph per length.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <fstream>
+#include <map>
+#include <mutex>
+#include <numeric>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/arctic_cuda.h"
+#include "gemm_i8.h"
+#include "kernels.h"
+#include "ptx.cuh"
+#include "rowmath.cuh"
+
+using namespace ae;
+
+namespace {
+
+struct DevLinear {
+  int n = 0, k = 0;
+  int8_t* w = nullptr;
+  float* ws = nullptr;
+  float* bias = nullptr;
+  float* inv_s = nullptr;
+  CUtensorMap tmap;
+};
+
+struct DevLayer {
+  DevLinear qkv, q_only, kv_only, ao, fi, fo;
+  float *ln1w = nullptr, *ln1b = nullptr, *ln2w = nullptr, *ln2b = nullptr;
+};
+
+struct DevModel {
+  void* arena = nullptr;
+  size_t arena_bytes = 0;
+  int8_t* word_q = nullptr;
+  float* word_s = nullptr;
+  int8_t* pos_q = nullptr;
+  float* pos_s = nullptr;
+  float* type0 = nullptr;
+  float *emb_lnw = nullptr, *emb_lnb = nullptr;
+  DevLayer layers[kLayers];
+};
+
+struct Workspace {
+  uint32_t cap_tokens = 0, cap_seqs = 0;
+  void* arena = nullptr;
+  uint16_t* ids = nullptr;
+  uint32_t* cu = nullptr;
+  uint16_t* pos = nullptr;
+  int32_t* cls_row = nullptr;
+  float* hidden = nullptr;
+  int8_t* act_q = nullptr;
+  float* act_s = nullptr;
+  float* qkv = nullptr;
+  float* ctx = nullptr;
+  int8_t* inter_q = nullptr;
+  float* inter_s = nullptr;
+  int8_t* cq = nullptr;
+  float* cs = nullptr;
+  float* ch = nullptr;
+  float* q_cls = nullptr;
+  float* cctx = nullptr;
+  int8_t* cinter_q = nullptr;
+  float* cinter_s = nullptr;
+  float* out = nullptr;
+  CUtensorMap tm_act_q, tm_inter_q, tm_cq, tm_cinter_q;
+  // pinned host staging
+  uint16_t* h_ids = nullptr;
+  uint32_t* h_cu = nullptr;
+  float* h_out = nullptr;
+};
+
+struct Graph {
+  cudaGraph_t g = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  uint64_t kernels = 0;
+};
+
+}  // namespace
+
+struct ae_ctx {
+  int device = 0;
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t stream = nullptr;
+  int* d_err = nullptr;
+  bool has_model = false;
+  DevModel model;
+  Workspace ws;
+  std::map<uint32_t, Graph> graphs;  // forward_cls graph per sequence length
+  std::string err;
+  int gelu_erf = 0;       // ARCTIC_GELU=erf selects the exact-erf GELU (outside the parity tolerance)
+  uint64_t launches = 0;  // kernels enqueued (or replayed from a graph) on this context
+  uint64_t graph_kernels = 0;
+};
+
+namespace {
+
+thread_local std::string g_create_err;
+
+int fail(ae_ctx* c, int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  if (c) c->err = buf;
+  else g_create_err = buf;
+  return code;
+}
+
+#define CUDA_TRY(c, expr)                                                                         \
+  do {                                                                                            \
+    cudaError_t e_ = (expr);                                                                      \
+    if (e_ != cudaSuccess) return fail((c), AE_ERR_CUDA, "%s: %s", #expr, cudaGetErrorString(e_)); \
+  } while (0)
+
+#define AE_TRY(expr)        \
+  do {                      \
+    int r_ = (expr);        \
+    if (r_ != 0) return r_; \
+  } while (0)
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// ------------------------------------------------------------------------------------------ model
+struct Carve {
+  uint8_t* base;
+  size_t off = 0;
+  template <class T>
+  T* take(size_t n) {
+    off = align_up(off, 256);
+    T* p = reinterpret_cast<T*>(base + off);
+    off += n * sizeof(T);
+    return p;
+  }
+};
+
+size_t linear_bytes(const ae_linear_desc& d) {
+  return align_up(d.n_out * d.k_in, 256) + 3 * align_up(d.n_out * 4, 256) + align_up(d.k_in * 4, 256) + 1024;
+}
+
+bool check_linear(const ae_linear_desc& d, uint64_t n, uint64_t k, bool allow_pruned) {
+  if (allow_pruned && d.n_out == 0) return d.k_in == k && d.inv_smooth;
+  return d.n_out == n && d.k_in == k && d.w_q && d.w_scale && d.bias && d.inv_smooth;
+}
+
+int upload_linear(ae_ctx* c, Carve& cv, const ae_linear_desc& d, DevLinear& o) {
+  o.n = int(d.n_out);
+  o.k = int(d.k_in);
+  o.inv_s = cv.take<float>(d.k_in);
+  CUDA_TRY(c, cudaMemcpy(o.inv_s, d.inv_smooth, d.k_in * 4, cudaMemcpyHostToDevice));
+  if (d.n_out == 0) return 0;
+  o.w = cv.take<int8_t>(d.n_out * d.k_in);
+  o.ws = cv.take<float>(d.n_out);
+  o.bias = cv.take<float>(d.n_out);
+  CUDA_TRY(c, cudaMemcpy(o.w, d.w_q, d.n_out * d.k_in, cudaMemcpyHostToDevice));
+  CUDA_TRY(c, cudaMemcpy(o.ws, d.w_scale, d.n_out * 4, cudaMemcpyHostToDevice));
+  CUDA_TRY(c, cudaMemcpy(o.bias, d.bias, d.n_out * 4, cudaMemcpyHostToDevice));
+  if (make_tmap_i8(&o.tmap, o.w, o.n, o.k) != 0) return fail(c, AE_ERR_CUDA, "cuTensorMapEncodeTiled failed for weights");
+  return 0;
+}
+
+template <class T>
+int upload(ae_ctx* c, T* dst, const T* src, size_t n) {
+  CUDA_TRY(c, cudaMemcpy(dst, src, n * sizeof(T), cudaMemcpyHostToDevice));
+  return 0;
+}
+
+void free_model(ae_ctx* c) {
+  if (c->model.arena) cudaFree(c->model.arena);
+  c->model = DevModel();
+  c->has_model = false;
+}
+
+// ------------------------------------------------------------------------------------------ workspace
+void free_ws(ae_ctx* c) {
+  Workspace& w = c->ws;
+  if (w.arena) cudaFree(w.arena);
+  if (w.h_ids) cudaFreeHost(w.h_ids);
+  if (w.h_cu) cudaFreeHost(w.h_cu);
+  if (w.h_out) cudaFreeHost(w.h_out);
+  w = Workspace();
+}
+
+void drop_graphs(ae_ctx* c) {
+  for (auto& kv : c->graphs) {
+    if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    if (kv.second.g) cudaGraphDestroy(kv.second.g);
+  }
+  c->graphs.clear();
+}
+
+int reserve(ae_ctx* c, uint32_t tokens, uint32_t seqs) {
+  Workspace& w = c->ws;
+  if (tokens <= w.cap_tokens && seqs <= w.cap_seqs && w.arena) return 0;
+  tokens = std::max(tokens, w.cap_tokens);
+  seqs = std::max(seqs, w.cap_seqs);
+  tokens = std::max<uint32_t>(align_up(tokens, 128), 128);
+  seqs = std::max<uint32_t>(align_up(seqs, 128), 128);
+  drop_graphs(c);
+  free_ws(c);
+  const size_t T = tokens, B = seqs;
+  size_t bytes = 0;
+  auto add = [&](size_t n) { bytes = align_up(bytes, 256) + n; };
+  add(T * 2);                 // ids
+  add((B + 1) * 4);           // cu
+  add(T * 2);                 // pos
+  add(B * 4);                 // cls_row
+  add(T * kHidden * 4);       // hidden
+  add(T * kHidden);           // act_q
+  add(T * 4);                 // act_s
+  add(T * 3 * kHidden * 4);   // qkv
+  add(T * kHidden * 4);       // ctx
+  add(T * kInter);            // inter_q
+  add(T * 4);                 // inter_s
+  add(B * kHidden);           // cq
+  add(B * 4);                 // cs
+  add(B * kHidden * 4);       // ch
+  add(B * kHidden * 4);       // q_cls
+  add(B * kHidden * 4);       // cctx
+  add(B * kInter);            // cinter_q
+  add(B * 4);                 // cinter_s
+  add(B * kHidden * 4);       // out
+  bytes += 4096;
+  void* arena = nullptr;
+  CUDA_TRY(c, cudaMalloc(&arena, bytes));
+  CUDA_TRY(c, cudaMemset(arena, 0, bytes));
+  w.arena = arena;
+  Carve cv{static_cast<uint8_t*>(arena)};
+  w.ids = cv.take<uint16_t>(T);
+  w.cu = cv.take<uint32_t>(B + 1);
+  w.pos = cv.take<uint16_t>(T);
+  w.cls_row = cv.take<int32_t>(B);
+  w.hidden = cv.take<float>(T * kHidden);
+  w.act_q = cv.take<int8_t>(T * kHidden);
+  w.act_s = cv.take<float>(T);
+  w.qkv = cv.take<float>(T * 3 * kHidden);
+  w.ctx = cv.take<float>(T * kHidden);
+  w.inter_q = cv.take<int8_t>(T * kInter);
+  w.inter_s = cv.take<float>(T);
+  w.cq = cv.take<int8_t>(B * kHidden);
+  w.cs = cv.take<float>(B);
+  w.ch = cv.take<float>(B * kHidden);
+  w.q_cls = cv.take<float>(B * kHidden);
+  w.cctx = cv.take<float>(B * kHidden);
+  w.cinter_q = cv.take<int8_t>(B * kInter);
+  w.cinter_s = cv.take<float>(B);
+  w.out = cv.take<float>(B * kHidden);
+  w.cap_tokens = tokens;
+  w.cap_seqs = seqs;
+  if (make_tmap_i8(&w.tm_act_q, w.act_q, int(T), kHidden) || make_tmap_i8(&w.tm_inter_q, w.inter_q, int(T), kInter) ||
+      make_tmap_i8(&w.tm_cq, w.cq, int(B), kHidden) || make_tmap_i8(&w.tm_cinter_q, w.cinter_q, int(B), kInter))
+    return fail(c, AE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the workspace");
+  CUDA_TRY(c, cudaMallocHost(&w.h_ids, T * 2));
+  CUDA_TRY(c, cudaMallocHost(&w.h_cu, (B + 1) * 4));
+  CUDA_TRY(c, cudaMallocHost(&w.h_out, B * kHidden * 4));
+  return 0;
+}
+
+// ------------------------------------------------------------------------------------------ forward
+int gemm(ae_ctx* c, int epi, const CUtensorMap& ta, const DevLinear& L, int M, const float* a_scale, const float* res,
+         int ldr, const float* gamma, const float* beta, const float* inv_next, float* out, int ldo, int8_t* out_q,
+         float* out_s) {
+  GemmArgs g{};
+  g.M = M;
+  g.N = L.n;
+  g.K = L.k;
+  g.a_scale = a_scale;
+  g.w_scale = L.ws;
+  g.bias = L.bias;
+  g.res = res;
+  g.ldr = ldr;
+  g.gamma = gamma;
+  g.beta = beta;
+  g.inv_smooth = inv_next;
+  g.out_f32 = out;
+  g.ldo = ldo;
+  g.out_q = out_q;
+  g.out_scale = out_s;
+  g.acc_dbg = nullptr;
+  g.err = c->d_err;
+  g.gelu_erf = c->gelu_erf;
+  int r = gemm_i8_launch(epi, ta, L.tmap, g, c->stream);
+  ++c->launches;
+  if (r) return fail(c, AE_ERR_CUDA, "GEMM launch failed (epilogue %d, M=%d N=%d K=%d): code %d", epi, M, L.n, L.k, r);
+  return 0;
+}
+
+int attention(ae_ctx* c, const float* q, int qs, const float* k, const float* v, int kvs, float* out,
+              const uint32_t* cu, int n, int max_len, int cls) {
+  AttnArgs a{};
+  a.q = q;
+  a.q_stride = qs;
+  a.k = k;
+  a.v = v;
+  a.kv_stride = kvs;
+  a.out = out;
+  a.out_stride = kHidden;
+  a.cu = cu;
+  a.max_len = max_len;
+  a.cls_mode = cls;
+  a.err = c->d_err;
+  ++c->launches;
+  if (launch_attention_exact(a, n, c->stream)) return fail(c, AE_ERR_CUDA, "attention launch failed");
+  return 0;
+}
+
+// Enqueues the whole forward pass of a packed batch on the context's stream.
+int enqueue_forward(ae_ctx* c, const uint16_t* d_ids, const uint32_t* d_cu, int T, int n, int max_len, float* d_out) {
+  Workspace& W = c->ws;
+  const DevModel& M = c->model;
+  cudaStream_t st = c->stream;
+  const uint64_t launches0 = c->launches;
+  c->launches += 2;  // row metadata + embedding
+  if (launch_row_meta(d_cu, n, W.pos, W.cls_row, c->d_err, st)) return fail(c, AE_ERR_CUDA, "row metadata launch failed");
+  EmbedArgs e{};
+  e.T = T;
+  e.ids = d_ids;
+  e.pos = W.pos;
+  e.word_q = M.word_q;
+  e.word_s = M.word_s;
+  e.pos_q = M.pos_q;
+  e.pos_s = M.pos_s;
+  e.type0 = M.type0;
+  e.gamma = M.emb_lnw;
+  e.beta = M.emb_lnb;
+  e.inv_smooth = M.layers[0].qkv.inv_s;
+  e.hidden = W.hidden;
+  e.act_q = W.act_q;
+  e.act_s = W.act_s;
+  e.err = c->d_err;
+  if (launch_embed(e, st)) return fail(c, AE_ERR_CUDA, "embedding launch failed");
+
+  for (int l = 0; l + 1 < kLayers; ++l) {
+    const DevLayer& Ly = M.layers[l];
+    AE_TRY(gemm(c, EPI_F32, W.tm_act_q, Ly.qkv, T, W.act_s, nullptr, 0, nullptr, nullptr, nullptr, W.qkv, 3 * kHidden,
+                nullptr, nullptr));
+    AE_TRY(attention(c, W.qkv, 3 * kHidden, W.qkv + kHidden, W.qkv + 2 * kHidden, 3 * kHidden, W.ctx, d_cu, n, max_len,
+                     0));
+    ++c->launches;
+    if (launch_smooth_quant(W.ctx, Ly.ao.inv_s, W.act_q, W.act_s, T, st))
+      return fail(c, AE_ERR_CUDA, "context quantization launch failed");
+    AE_TRY(gemm(c, EPI_LN_QUANT, W.tm_act_q, Ly.ao, T, W.act_s, W.hidden, kHidden, Ly.ln1w, Ly.ln1b, Ly.fi.inv_s,
+                W.hidden, kHidden, W.act_q, W.act_s));
+    AE_TRY(gemm(c, EPI_GELU_QUANT, W.tm_act_q, Ly.fi, T, W.act_s, nullptr, 0, nullptr, nullptr, Ly.fo.inv_s, nullptr, 0,
+                W.inter_q, W.inter_s));
+    AE_TRY(gemm(c, EPI_LN_QUANT, W.tm_inter_q, Ly.fo, T, W.inter_s, W.hidden, kHidden, Ly.ln2w, Ly.ln2b,
+                M.layers[l + 1].qkv.inv_s, W.hidden, kHidden, W.act_q, W.act_s));
+  }
+  const DevLayer& Z = M.layers[kLayers - 1];
+  AE_TRY(gemm(c, EPI_F32, W.tm_act_q, Z.kv_only, T, W.act_s, nullptr, 0, nullptr, nullptr, nullptr, W.qkv, 2 * kHidden,
+              nullptr, nullptr));
+  c->launches += 2;  // gather + [CLS] context quantization
+  if (launch_gather_cls(W.cls_row, n, W.act_q, W.act_s, W.hidden, W.cq, W.cs, W.ch, st))
+    return fail(c, AE_ERR_CUDA, "gather launch failed");
+  AE_TRY(gemm(c, EPI_F32, W.tm_cq, Z.q_only, n, W.cs, nullptr, 0, nullptr, nullptr, nullptr, W.q_cls, kHidden, nullptr,
+              nullptr));
+  AE_TRY(attention(c, W.q_cls, kHidden, W.qkv, W.qkv + kHidden, 2 * kHidden, W.cctx, d_cu, n, max_len, 1));
+  if (launch_smooth_quant(W.cctx, Z.ao.inv_s, W.cq, W.cs, n, st))
+    return fail(c, AE_ERR_CUDA, "context quantization launch failed");
+  AE_TRY(gemm(c, EPI_LN_QUANT, W.tm_cq, Z.ao, n, W.cs, W.ch, kHidden, Z.ln1w, Z.ln1b, Z.fi.inv_s, W.ch, kHidden, W.cq,
+              W.cs));
+  AE_TRY(gemm(c, EPI_GELU_QUANT, W.tm_cq, Z.fi, n, W.cs, nullptr, 0, nullptr, nullptr, Z.fo.inv_s, nullptr, 0, W.cinter_q,
+              W.cinter_s));
+  AE_TRY(gemm(c, EPI_LN_FINAL, W.tm_cinter_q, Z.fo, n, W.cinter_s, W.ch, kHidden, Z.ln2w, Z.ln2b, nullptr, d_out,
+              kHidden, nullptr, nullptr));
+  c->graph_kernels = c->launches - launches0;
+  return 0;
+}
+
+int check_dev_err(ae_ctx* c) {
+  int h = 0;
+  CUDA_TRY(c, cudaMemcpy(&h, c->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (h != 0) {
+    int z = 0;
+    cudaMemcpy(c->d_err, &z, sizeof(int), cudaMemcpyHostToDevice);
+    static const char* names[] = {"ok", "producer wait timed out", "MMA wait timed out", "epilogue wait timed out",
+                                  "sequence length outside 1..512", "token id out of range"};
+    return fail(c, AE_ERR_DEVICE, "device error %d (%s)", h, (h >= 0 && h <= 5) ? names[h] : "?");
+  }
+  return 0;
+}
+
+// Packs host sequences (truncating each to 512) into the pinned staging buffers.
+int pack_host(ae_ctx* c, const uint16_t* ids, const uint32_t* cu, uint32_t n, int* T_out, int* maxlen_out) {
+  uint64_t T = 0;
+  int max_len = 0;
+  for (uint32_t i = 0; i < n; ++i) {
+    if (cu[i + 1] < cu[i]) return fail(c, AE_ERR_INVALID_ARG, "cu_seqlens must be non-decreasing");
+    const uint32_t len = std::min<uint32_t>(cu[i + 1] - cu[i], kMaxPos);
+    if (len == 0) return fail(c, AE_ERR_INVALID_ARG, "sequence %u is empty (input_ids must not be empty)", i);
+    T += len;
+    max_len = std::max<int>(max_len, int(len));
+  }
+  if (T > 0x7fffffffu) return fail(c, AE_ERR_CAPACITY, "batch too large");
+  AE_TRY(reserve(c, uint32_t(T), n));
+  Workspace& W = c->ws;
+  uint32_t off = 0;
+  W.h_cu[0] = 0;
+  for (uint32_t i = 0; i < n; ++i) {
+    const uint32_t len = std::min<uint32_t>(cu[i + 1] - cu[i], kMaxPos);
+    const uint16_t* src = ids + cu[i];
+    for (uint32_t j = 0; j < len; ++j) {
+      if (src[j] >= kVocab) return fail(c, AE_ERR_TOKEN_RANGE, "token id %u at sequence %u is >= 30522", src[j], i);
+    }
+    std::memcpy(W.h_ids + off, src, len * 2);
+    off += len;
+    W.h_cu[i + 1] = off;
+  }
+  *T_out = int(T);
+  *maxlen_out = max_len;
+  return 0;
+}
+
+int forward_ragged_host(ae_ctx* c, const uint16_t* ids, const uint32_t* cu, uint32_t n, float* out) {
+  if (!c->has_model) return fail(c, AE_ERR_NO_MODEL, "no model loaded");
+  if (n == 0) return 0;
+  if (!ids || !cu || !out) return fail(c, AE_ERR_INVALID_ARG, "null pointer");
+  int T = 0, max_len = 0;
+  AE_TRY(pack_host(c, ids, cu, n, &T, &max_len));
+  Workspace& W = c->ws;
+  CUDA_TRY(c, cudaMemcpyAsync(W.ids, W.h_ids, size_t(T) * 2, cudaMemcpyHostToDevice, c->stream));
+  CUDA_TRY(c, cudaMemcpyAsync(W.cu, W.h_cu, size_t(n + 1) * 4, cudaMemcpyHostToDevice, c->stream));
+  AE_TRY(enqueue_forward(c, W.ids, W.cu, T, int(n), max_len, W.out));
+  CUDA_TRY(c, cudaMemcpyAsync(W.h_out, W.out, size_t(n) * kHidden * 4, cudaMemcpyDeviceToHost, c->stream));
+  CUDA_TRY(c, cudaStreamSynchronize(c->stream));
+  AE_TRY(check_dev_err(c));
+  std::memcpy(out, W.h_out, size_t(n) * kHidden * 4);
+  return 0;
+}
+
+// ------------------------------------------------------------------------------------------ .ae8 parsing
+struct Ae8 {
+  std::vector<uint8_t> bytes;
+  size_t pos = 8;
+  bool ok = true;
+  std::vector<std::vector<int8_t>> i8s;
+  std::vector<std::vector<float>> f32s;
+  uint64_t u64() {
+    uint64_t v = 0;
+    if (!ok || bytes.size() - pos < 8) {
+      ok = false;
+      return 0;
+    }
+    std::memcpy(&v, &bytes[pos], 8);
+    pos += 8;
+    return v;
+  }
+  const int8_t* i8vec(uint64_t* n_out = nullptr) {
+    const uint64_t n = u64();
+    if (!ok || n > bytes.size() - pos) {
+      ok = false;
+      return nullptr;
+    }
+    i8s.emplace_back(reinterpret_cast<const int8_t*>(&bytes[pos]), reinterpret_cast<const int8_t*>(&bytes[pos]) + n);
+    pos += n;
+    if (n_out) *n_out = n;
+    return i8s.back().data();
+  }
+  const float* f32vec(uint64_t* n_out = nullptr) {
+    const uint64_t n = u64();
+    if (!ok || n > (bytes.size() - pos) / 4) {
+      ok = false;
+      return nullptr;
+    }
+    f32s.emplace_back(n);
+    std::memcpy(f32s.back().data(), &bytes[pos], n * 4);
+    pos += n * 4;
+    if (n_out) *n_out = n;
+    return f32s.back().data();
+  }
+  bool linear(ae_linear_desc& d) {
+    d.n_out = u64();
+    d.k_in = u64();
+    uint64_t nw = 0, ns = 0, nb = 0, ni = 0;
+    d.w_q = i8vec(&nw);
+    d.w_scale = f32vec(&ns);
+    d.bias = f32vec(&nb);
+    d.inv_smooth = f32vec(&ni);
+    if (ok && (nw != d.n_out * d.k_in || ns != d.n_out || nb != d.n_out || ni != d.k_in)) ok = false;
+    if (d.n_out == 0) d.w_q = nullptr;
+    return ok;
+  }
+};
+
+// Token-weighted greedy (longest first) assignment of sequences to shards. Cost of a sequence of L
+// tokens: 19,759,104 L int8 MACs + 8,448 L^2 attention MACs. Each shard lists its sequences longest
+// first, so the batches cut from it hold sequences of similar length.
+std::vector<std::vector<uint32_t>> plan_shards(const uint32_t* cu, uint32_t n, int n_shards) {
+  auto len_of = [&](uint32_t i) { return std::min<uint32_t>(cu[i + 1] - cu[i], kMaxPos); };
+  std::vector<uint32_t> order(n);
+  std::iota(order.begin(), order.end(), 0u);
+  std::stable_sort(order.begin(), order.end(), [&](uint32_t a, uint32_t b) { return len_of(a) > len_of(b); });
+  std::vector<double> load(n_shards, 0.0);
+  std::vector<std::vector<uint32_t>> shard(n_shards);
+  for (uint32_t i : order) {
+    const double L = len_of(i);
+    const int d = int(std::min_element(load.begin(), load.end()) - load.begin());
+    load[d] += 19759104.0 * L + 8448.0 * L * L;
+    shard[d].push_back(i);
+  }
+  return shard;
+}
+
+}  // namespace
+
+// ============================================================================================ C ABI
+extern "C" {
+
+int ae_ctx_create(int device, ae_ctx** out) {
+  if (!out) return fail(nullptr, AE_ERR_INVALID_ARG, "out is null");
+  *out = nullptr;
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) return fail(nullptr, AE_ERR_CUDA, "cudaGetDeviceCount: %s", cudaGetErrorString(e));
+  if (device < 0 || device >= n || device >= kMaxDevices)
+    return fail(nullptr, AE_ERR_INVALID_ARG, "device %d out of range (%d visible)", device, n);
+  cudaDeviceProp prop;
+  e = cudaGetDeviceProperties(&prop, device);
+  if (e != cudaSuccess) return fail(nullptr, AE_ERR_CUDA, "cudaGetDeviceProperties: %s", cudaGetErrorString(e));
+  if (prop.major != 10 || prop.minor != 0)
+    return fail(nullptr, AE_ERR_CUDA, "device %d is sm_%d%d; this library is built for sm_100a (B200)", device, prop.major,
+                prop.minor);
+  DeviceGuard g(device);
+  auto* c = new ae_ctx();
+  c->device = device;
+  e = cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaMalloc(&c->d_err, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(c->d_err, 0, sizeof(int));
+  if (e != cudaSuccess) {
+    if (c->own_stream) cudaStreamDestroy(c->own_stream);
+    delete c;
+    return fail(nullptr, AE_ERR_CUDA, "context setup: %s", cudaGetErrorString(e));
+  }
+  c->stream = c->own_stream;
+  const char* gm = std::getenv("ARCTIC_GELU");
+  c->gelu_erf = (gm && std::strcmp(gm, "erf") == 0) ? 1 : 0;
+  if (gemm_i8_prime() || attention_prime()) {
+    ae_ctx_destroy(c);
+    return fail(nullptr, AE_ERR_CUDA, "kernel attribute setup failed on device %d", device);
+  }
+  *out = c;
+  return 0;
+}
+
+int ae_ctx_destroy(ae_ctx* c) {
+  if (!c) return 0;
+  DeviceGuard g(c->device);
+  cudaStreamSynchronize(c->stream);
+  drop_graphs(c);
+  free_ws(c);
+  free_model(c);
+  if (c->d_err) cudaFree(c->d_err);
+  if (c->own_stream) cudaStreamDestroy(c->own_stream);
+  delete c;
+  return 0;
+}
+
+const char* ae_last_error(const ae_ctx* c) { return c ? c->err.c_str() : g_create_err.c_str(); }
+
+int ae_ctx_set_stream(ae_ctx* c, void* s) {
+  if (!c) return AE_ERR_INVALID_ARG;
+  drop_graphs(c);
+  c->stream = s ? static_cast<cudaStream_t>(s) : c->own_stream;
+  return 0;
+}
+
+int ae_ctx_device(const ae_ctx* c) { return c ? c->device : AE_ERR_INVALID_ARG; }
+
+int ae_model_load(ae_ctx* c, const ae_model_desc* d) {
+  if (!c || !d) return fail(c, AE_ERR_INVALID_ARG, "null argument");
+  DeviceGuard g(c->device);
+  // validation (the sizes src/quantize.rs:9-18 fix; the reference asserts them while packing)
+  if (!d->word_emb_q || !d->word_emb_scale || !d->pos_emb_q || !d->pos_emb_scale || !d->type_emb_q ||
+      !d->type_emb_scale || !d->emb_ln_weight || !d->emb_ln_bias)
+    return fail(c, AE_ERR_BAD_PACK, "embedding tables missing");
+  for (int l = 0; l < kLayers; ++l) {
+    const ae_layer_desc& L = d->layers[l];
+    const bool last = l == kLayers - 1;
+    if (!L.ln1_weight || !L.ln1_bias || !L.ln2_weight || !L.ln2_bias)
+      return fail(c, AE_ERR_BAD_PACK, "layer %d: LayerNorm parameters missing", l);
+    if (!check_linear(L.attn_out, kHidden, kHidden, false) || !check_linear(L.ffn_inter, kInter, kHidden, false) ||
+        !check_linear(L.ffn_out, kHidden, kInter, false))
+      return fail(c, AE_ERR_BAD_PACK, "layer %d: attn_out / ffn shapes must be 384x384, 1536x384, 384x1536", l);
+    if (!last) {
+      if (!check_linear(L.qkv, 3 * kHidden, kHidden, false))
+        return fail(c, AE_ERR_BAD_PACK, "layer %d: qkv must be 1152x384", l);
+    } else {
+      if (L.has_split != 1 || !check_linear(L.q_only, kHidden, kHidden, false) ||
+          !check_linear(L.kv_only, 2 * kHidden, kHidden, false) || L.qkv.k_in != kHidden || !L.qkv.inv_smooth)
+        return fail(c, AE_ERR_BAD_PACK, "layer 11 must carry the [CLS]-pruned split (q_only 384x384, kv_only 768x384)");
+    }
+  }
+  cudaStreamSynchronize(c->stream);
+  drop_graphs(c);
+  free_model(c);
+  size_t bytes = size_t(kVocab) * kHidden + kVocab * 4 + kMaxPos * kHidden + kMaxPos * 4 + 3 * kHidden * 4 + 64 * 1024;
+  for (int l = 0; l < kLayers; ++l) {
+    const ae_layer_desc& L = d->layers[l];
+    bytes += linear_bytes(L.qkv) + linear_bytes(L.attn_out) + linear_bytes(L.ffn_inter) + linear_bytes(L.ffn_out) +
+             4 * kHidden * 4 + 4096;
+    if (L.has_split) bytes += linear_bytes(L.q_only) + linear_bytes(L.kv_only);
+  }
+  void* arena = nullptr;
+  CUDA_TRY(c, cudaMalloc(&arena, bytes));
+  DevModel& M = c->model;
+  M.arena = arena;
+  M.arena_bytes = bytes;
+  Carve cv{static_cast<uint8_t*>(arena)};
+  M.word_q = cv.take<int8_t>(size_t(kVocab) * kHidden);
+  M.word_s = cv.take<float>(kVocab);
+  M.pos_q = cv.take<int8_t>(size_t(kMaxPos) * kHidden);
+  M.pos_s = cv.take<float>(kMaxPos);
+  M.type0 = cv.take<float>(kHidden);
+  M.emb_lnw = cv.take<float>(kHidden);
+  M.emb_lnb = cv.take<float>(kHidden);
+  int r = 0;
+  std::vector<float> type0(kHidden);
+  for (int j = 0; j < kHidden; ++j) type0[j] = float(d->type_emb_q[j]) * d->type_emb_scale[0];  // src/model.rs:50-54
+  if ((r = upload(c, M.word_q, d->word_emb_q, size_t(kVocab) * kHidden)) || (r = upload(c, M.word_s, d->word_emb_scale, kVocab)) ||
+      (r = upload(c, M.pos_q, d->pos_emb_q, size_t(kMaxPos) * kHidden)) || (r = upload(c, M.pos_s, d->pos_emb_scale, kMaxPos)) ||
+      (r = upload(c, M.type0, type0.data(), kHidden)) || (r = upload(c, M.emb_lnw, d->emb_ln_weight, kHidden)) ||
+      (r = upload(c, M.emb_lnb, d->emb_ln_bias, kHidden))) {
+    free_model(c);
+    return r;
+  }
+  for (int l = 0; l < kLayers && !r; ++l) {
+    const ae_layer_desc& L = d->layers[l];
+    DevLayer& D = M.layers[l];
+    r = upload_linear(c, cv, L.qkv, D.qkv);
+    if (!r && L.has_split) r = upload_linear(c, cv, L.q_only, D.q_only);
+    if (!r && L.has_split) r = upload_linear(c, cv, L.kv_only, D.kv_only);
+    if (!r) r = upload_linear(c, cv, L.attn_out, D.ao);
+    if (!r) r = upload_linear(c, cv, L.ffn_inter, D.fi);
+    if (!r) r = upload_linear(c, cv, L.ffn_out, D.fo);
+    if (!r) {
+      D.ln1w = cv.take<float>(kHidden);
+      D.ln1b = cv.take<float>(kHidden);
+      D.ln2w = cv.take<float>(kHidden);
+      D.ln2b = cv.take<float>(kHidden);
+      if ((r = upload(c, D.ln1w, L.ln1_weight, kHidden)) || (r = upload(c, D.ln1b, L.ln1_bias, kHidden)) ||
+          (r = upload(c, D.ln2w, L.ln2_weight, kHidden)) || (r = upload(c, D.ln2b, L.ln2_bias, kHidden))) {
+      }
+    }
+  }
+  if (r) {
+    free_model(c);
+    return r;
+  }
+  if (cv.off > bytes) {
+    free_model(c);
+    return fail(c, AE_ERR_BAD_PACK, "internal: model arena overflow");
+  }
+  c->has_model = true;
+  return 0;
+}
+
+int ae_model_load_file(ae_ctx* c, const char* path) {
+  if (!c || !path) return fail(c, AE_ERR_INVALID_ARG, "null argument");
+  std::ifstream f(path, std::ios::binary);
+  if (!f) return fail(c, AE_ERR_BAD_PACK, "cannot open %s", path);
+  Ae8 p;
+  p.bytes.assign(std::istreambuf_iterator<char>(f), std::istreambuf_iterator<char>());
+  if (p.bytes.size() < 8 || std::memcmp(p.bytes.data(), "ARCTIC8\x01", 8) != 0)
+    return fail(c, AE_ERR_BAD_PACK, "invalid .ae8 magic header");
+  p.i8s.reserve(128);
+  p.f32s.reserve(512);
+  ae_model_desc d{};
+  uint64_t n0, n1, n2, n3, n4, n5, n6, n7;
+  d.word_emb_q = p.i8vec(&n0);
+  d.word_emb_scale = p.f32vec(&n1);
+  d.pos_emb_q = p.i8vec(&n2);
+  d.pos_emb_scale = p.f32vec(&n3);
+  d.type_emb_q = p.i8vec(&n4);
+  d.type_emb_scale = p.f32vec(&n5);
+  d.emb_ln_weight = p.f32vec(&n6);
+  d.emb_ln_bias = p.f32vec(&n7);
+  if (p.ok && (n0 != uint64_t(kVocab) * kHidden || n1 != uint64_t(kVocab) || n2 != uint64_t(kMaxPos) * kHidden ||
+               n3 != uint64_t(kMaxPos) || n4 < uint64_t(kHidden) || n5 < 1 || n6 != uint64_t(kHidden) ||
+               n7 != uint64_t(kHidden)))
+    return fail(c, AE_ERR_BAD_PACK, "embedding tables have unexpected sizes");
+  for (int l = 0; l < kLayers && p.ok; ++l) {
+    ae_layer_desc& L = d.layers[l];
+    p.linear(L.qkv);
+    uint8_t split = 0;
+    if (p.pos < p.bytes.size()) split = p.bytes[p.pos++];
+    else p.ok = false;
+    L.has_split = split == 1;
+    if (L.has_split) {
+      p.linear(L.q_only);
+      p.linear(L.kv_only);
+    }
+    p.linear(L.attn_out);
+    uint64_t a, b, cc, dd;
+    L.ln1_weight = p.f32vec(&a);
+    L.ln1_bias = p.f32vec(&b);
+    p.linear(L.ffn_inter);
+    p.linear(L.ffn_out);
+    L.ln2_weight = p.f32vec(&cc);
+    L.ln2_bias = p.f32vec(&dd);
+    if (p.ok && (a != kHidden || b != kHidden || cc != kHidden || dd != kHidden))
+      return fail(c, AE_ERR_BAD_PACK, "layer %d: LayerNorm vectors must have 384 entries", l);
+  }
+  if (!p.ok) return fail(c, AE_ERR_BAD_PACK, "truncated or inconsistent .ae8 pack");
+  return ae_model_load(c, &d);
+}
+
+int ae_reserve(ae_ctx* c, uint32_t max_tokens, uint32_t max_seqs) {
+  if (!c) return AE_ERR_INVALID_ARG;
+  DeviceGuard g(c->device);
+  return reserve(c, max_tokens, max_seqs);
+}
+
+int ae_forward_ragged(ae_ctx* c, const uint16_t* ids, const uint32_t* cu, uint32_t n, float* out) {
+  if (!c) return AE_ERR_INVALID_ARG;
+  DeviceGuard g(c->device);
+  return forward_ragged_host(c, ids, cu, n, out);
+}
+
+int ae_forward_cls(ae_ctx* c, const uint16_t* ids, uint32_t len, float* out) {
+  if (!c) return AE_ERR_INVALID_ARG;
+  if (!c->has_model) return fail(c, AE_ERR_NO_MODEL, "no model loaded");
+  if (!ids || !out) return fail(c, AE_ERR_INVALID_ARG, "null pointer");
+  if (len == 0) return fail(c, AE_ERR_INVALID_ARG, "input_ids must not be empty");
+  DeviceGuard g(c->device);
+  const uint32_t L = std::min<uint32_t>(len, kMaxPos);
+  for (uint32_t j = 0; j < L; ++j)
+    if (ids[j] >= kVocab) return fail(c, AE_ERR_TOKEN_RANGE, "token id %u at position %u is >= 30522", ids[j], j);
+  AE_TRY(reserve(c, kMaxPos, 1));
+  Workspace& W = c->ws;
+  auto it = c->graphs.find(L);
+  if (it == c->graphs.end()) {
+    // capture: H2D ids + cu, forward, D2H out, all at fixed workspace addresses
+    W.h_cu[0] = 0;
+    W.h_cu[1] = L;
+    Graph gr;
+    CUDA_TRY(c, cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    int r = 0;
+    if (cudaMemcpyAsync(W.ids, W.h_ids, L * 2, cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
+        cudaMemcpyAsync(W.cu, W.h_cu, 2 * 4, cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
+      r = fail(c, AE_ERR_CUDA, "capture of input copies failed");
+    const uint64_t before = c->launches;
+    if (!r) r = enqueue_forward(c, W.ids, W.cu, int(L), 1, int(L), W.out);
+    gr.kernels = c->launches - before;
+    c->launches = before;  // captured, not launched
+    if (!r && cudaMemcpyAsync(W.h_out, W.out, kHidden * 4, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
+      r = fail(c, AE_ERR_CUDA, "capture of output copy failed");
+    cudaError_t e = cudaStreamEndCapture(c->stream, &gr.g);
+    if (r) {
+      if (gr.g) cudaGraphDestroy(gr.g);
+      return r;
+    }
+    if (e != cudaSuccess) return fail(c, AE_ERR_CUDA, "cudaStreamEndCapture: %s", cudaGetErrorString(e));
+    e = cudaGraphInstantiate(&gr.exec, gr.g, 0);
+    if (e != cudaSuccess) {
+      cudaGraphDestroy(gr.g);
+      return fail(c, AE_ERR_CUDA, "cudaGraphInstantiate: %s", cudaGetErrorString(e));
+    }
+    it = c->graphs.emplace(L, gr).first;
+  }
+  std::memcpy(W.h_ids, ids, L * 2);
+  W.h_cu[0] = 0;
+  W.h_cu[1] = L;
+  CUDA_TRY(c, cudaGraphLaunch(it->second.exec, c->stream));
+  c->launches += it->second.kernels;
+  CUDA_TRY(c, cudaStreamSynchronize(c->stream));
+  AE_TRY(check_dev_err(c));
+  std::memcpy(out, W.h_out, kHidden * 4);
+  return 0;
+}
+
+int ae_forward_ragged_device(ae_ctx* c, const uint16_t* d_ids, const uint32_t* d_cu, uint32_t n, uint32_t T,
+                             uint32_t max_len, float* d_out) {
+  if (!c) return AE_ERR_INVALID_ARG;
+  if (!c->has_model) return fail(c, AE_ERR_NO_MODEL, "no model loaded");
+  if (n == 0) return 0;
+  if (!d_ids || !d_cu || !d_out || T == 0) return fail(c, AE_ERR_INVALID_ARG, "null pointer or empty batch");
+  if (max_len == 0 || max_len > uint32_t(kMaxPos)) return fail(c, AE_ERR_INVALID_ARG, "max_len must be 1..512");
+  DeviceGuard g(c->device);
+  AE_TRY(reserve(c, T, n));
+  return enqueue_forward(c, d_ids, d_cu, int(T), int(n), int(max_len), d_out);
+}
+
+uint64_t ae_kernel_launches(const ae_ctx* c) { return c ? c->launches : 0; }
+
+int ae_plan_shards(const uint32_t* cu, uint32_t n, int n_shards, int32_t* shard_of) {
+  if (!cu || !shard_of || n_shards <= 0) return AE_ERR_INVALID_ARG;
+  for (uint32_t i = 0; i < n; ++i)
+    if (cu[i + 1] < cu[i]) return AE_ERR_INVALID_ARG;
+  const auto plan = plan_shards(cu, n, n_shards);
+  for (int d = 0; d < n_shards; ++d)
+    for (uint32_t i : plan[d]) shard_of[i] = d;
+  return 0;
+}
+
+int ae_sync(ae_ctx* c) {
+  if (!c) return AE_ERR_INVALID_ARG;
+  DeviceGuard g(c->device);
+  CUDA_TRY(c, cudaStreamSynchronize(c->stream));
+  return check_dev_err(c);
+}
+
+int ae_gemm_i8(ae_ctx* c, int epi, uint32_t M, uint32_t N, uint32_t K, const int8_t* d_a, const float* d_a_scale,
+               const int8_t* d_w, const float* d_w_scale, const float* d_bias, const float* d_res, const float* d_gamma,
+               const float* d_beta, const float* d_inv_smooth, float* d_out, int8_t* d_out_q, float* d_out_scale,
+               int32_t* d_acc) {
+  if (!c) return AE_ERR_INVALID_ARG;
+  DeviceGuard g(c->device);
+  if (!d_a || !d_a_scale || !d_w || !d_w_scale || !d_bias || M == 0 || K % 128)
+    return fail(c, AE_ERR_INVALID_ARG, "ae_gemm_i8: bad arguments");
+  CUtensorMap ta, tb;
+  if (make_tmap_i8(&ta, d_a, int(M), int(K)) || make_tmap_i8(&tb, d_w, int(N), int(K)))
+    return fail(c, AE_ERR_INVALID_ARG, "ae_gemm_i8: operands must be 16-byte aligned");
+  GemmArgs a{};
+  a.M = int(M);
+  a.N = int(N);
+  a.K = int(K);
+  a.a_scale = d_a_scale;
+  a.w_scale = d_w_scale;
+  a.bias = d_bias;
+  a.res = d_res;
+  a.ldr = int(N);
+  a.gamma = d_gamma;
+  a.beta = d_beta;
+  a.inv_smooth = d_inv_smooth;
+  a.out_f32 = d_out;
+  a.ldo = int(N);
+  a.out_q = d_out_q;
+  a.out_scale = d_out_scale;
+  a.acc_dbg = d_acc;
+  a.err = c->d_err;
+  a.gelu_erf = c->gelu_erf;
+  switch (epi) {
+    case EPI_F32:
+      if (!d_out || N % 128) return fail(c, AE_ERR_INVALID_ARG, "epilogue 0 needs out and N % 128 == 0");
+      break;
+    case EPI_LN_QUANT:
+      if (N != kHidden || !d_res || !d_gamma || !d_beta || !d_inv_smooth || !d_out || !d_out_q || !d_out_scale)
+        return fail(c, AE_ERR_INVALID_ARG, "epilogue 1 needs N = 384 and res, gamma, beta, inv_smooth, outputs");
+      break;
+    case EPI_GELU_QUANT:
+      if (N != kInter || !d_inv_smooth || !d_out_q || !d_out_scale)
+        return fail(c, AE_ERR_INVALID_ARG, "epilogue 2 needs N = 1536 and inv_smooth, out_q, out_scale");
+      break;
+    case EPI_LN_FINAL:
+      if (N != kHidden || !d_res || !d_gamma || !d_beta || !d_out)
+        return fail(c, AE_ERR_INVALID_ARG, "epilogue 3 needs N = 384 and res, gamma, beta, out");
+      break;
+    default:
+      return fail(c, AE_ERR_INVALID_ARG, "unknown epilogue %d", epi);
+  }
+  const int r = gemm_i8_launch(epi, ta, tb, a, c->stream);
+  if (r) return fail(c, AE_ERR_CUDA, "GEMM launch failed: code %d", r);
+  return 0;
+}
+
+int ae_attention_f32(ae_ctx* c, const float* d_qkv, const uint32_t* d_cu, uint32_t n, uint32_t max_len, float* d_ctx) {
+  if (!c) return AE_ERR_INVALID_ARG;
+  if (!d_qkv || !d_cu || !d_ctx || max_len == 0 || max_len > uint32_t(kMaxPos))
+    return fail(c, AE_ERR_INVALID_ARG, "ae_attention_f32: bad arguments");
+  DeviceGuard g(c->device);
+  return attention(c, d_qkv, 3 * kHidden, d_qkv + kHidden, d_qkv + 2 * kHidden, 3 * kHidden, d_ctx, d_cu, int(n),
+                   int(max_len), 0);
+}
+
+// ArcticEmbedS::embed_batch (src/lib.rs:138-260) across GPUs: token-weighted greedy shards, one host
+// thread per context; each context packs its shard (longest first) into batches of <= max_tokens.
+int ae_embed_batch_multi(ae_ctx* const* ctxs, int n_ctx, const uint16_t* ids, const uint32_t* cu, uint32_t n,
+                         uint32_t max_tokens, float* out) {
+  if (!ctxs || n_ctx <= 0) return fail(nullptr, AE_ERR_INVALID_ARG, "no contexts");
+  if (n == 0) return 0;
+  if (!ids || !cu || !out) return fail(ctxs[0], AE_ERR_INVALID_ARG, "null pointer");
+  if (max_tokens == 0) max_tokens = 65536;
+  max_tokens = std::max<uint32_t>(max_tokens, kMaxPos);
+  for (uint32_t i = 0; i < n; ++i)
+    if (cu[i + 1] < cu[i]) return fail(ctxs[0], AE_ERR_INVALID_ARG, "cu_seqlens must be non-decreasing");
+  auto len_of = [&](uint32_t i) { return std::min<uint32_t>(cu[i + 1] - cu[i], kMaxPos); };
+  std::vector<std::vector<uint32_t>> shard = plan_shards(cu, n, n_ctx);
+  std::vector<int> rc(n_ctx, 0);
+  auto worker = [&](int d) {
+    ae_ctx* c = ctxs[d];
+    DeviceGuard g(c->device);
+    std::vector<uint16_t> bids;
+    std::vector<uint32_t> bcu;
+    std::vector<float> bout;
+    const auto& s = shard[d];
+    size_t i = 0;
+    while (i < s.size() && rc[d] == 0) {
+      bids.clear();
+      bcu.assign(1, 0);
+      size_t j = i;
+      uint32_t tok = 0;
+      while (j < s.size() && tok + len_of(s[j]) <= max_tokens) {
+        const uint32_t L = len_of(s[j]);
+        bids.insert(bids.end(), ids + cu[s[j]], ids + cu[s[j]] + L);
+        tok += L;
+        bcu.push_back(tok);
+        ++j;
+      }
+      const uint32_t nb = uint32_t(j - i);
+      bout.resize(size_t(nb) * kHidden);
+      rc[d] = forward_ragged_host(c, bids.data(), bcu.data(), nb, bout.data());
+      if (rc[d]) break;
+      for (uint32_t k = 0; k < nb; ++k) std::memcpy(out + size_t(s[i + k]) * kHidden, &bout[size_t(k) * kHidden], kHidden * 4);
+      i = j;
+    }
+  };
+  std::vector<std::thread> th;
+  for (int d = 1; d < n_ctx; ++d) th.emplace_back(worker, d);
+  worker(0);
+  for (auto& t : th) t.join();
+  for (int d = 0; d < n_ctx; ++d)
+    if (rc[d]) {
+      if (d != 0) ctxs[0]->err = "context " + std::to_string(d) + ": " + ctxs[d]->err;
+      return rc[d];
+    }
+  return 0;
+}
+
+}  // extern "C"

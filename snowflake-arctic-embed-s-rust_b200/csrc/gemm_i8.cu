@@ -16,8 +16,8 @@
 //                  src/simd_math.rs:369-477)
 //   EPI_GELU_QUANT g = GELU(h) * inv_smooth, row max over all 1536 columns exchanged across a
 //                  3-CTA cluster through distributed shared memory, then row quantization
-//                  (FFN-up; gelu_smooth_quantize_row_avx2, src/simd_math.rs:1371-1435, with the
-//                  exact-erf GELU)
+//                  (FFN-up; gelu_smooth_quantize_row_avx2, src/simd_math.rs:1371-1435). GELU is the
+//                  reference's rational approximation (gelu_ref) or, on request, the exact erf.
 //   EPI_LN_FINAL   out = l2_normalize(layernorm_inplace_row(h))  (layer-11 FFN-down of the [CLS]
 //                  rows; src/model.rs:496-512, src/simd_math.rs:481-497, :2892-2903)
 #include <cuda.h>
@@ -357,7 +357,7 @@ __global__ void __launch_bounds__(128, 1)
         for (int j = 0; j < 32; ++j) {
           const int n = c * 32 + j;
           const float h = fmaf(float(int(r[j])), as * s_ws[n], s_bias[n]);
-          const float gv = gelu_erf(h) * s_invs[n];
+          const float gv = (g.gelu_erf ? gelu_erf(h) : gelu_ref(h)) * s_invs[n];
           vmax = fmaxf(vmax, fabsf(gv));
           r[j] = __float_as_uint(gv);
         }
@@ -435,12 +435,6 @@ static cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const Ge
                           int cluster_x) {
   using S = GemmSmem<BN, STAGES>;
   auto kfn = k_gemm_i8<BN, EPI, STAGES>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(g.N / BN, (g.M + BM - 1) / BM, 1);
   cfg.blockDim = dim3(128, 1, 1);
@@ -457,6 +451,26 @@ static cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const Ge
     cfg.numAttrs = 1;
   }
   return cudaLaunchKernelEx(&cfg, kfn, ta, tb, g);
+}
+
+// Sets the dynamic shared-memory limit of every GEMM variant on the current device (called once per
+// device before any launch can be captured into a CUDA graph).
+int gemm_i8_prime() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  (void)dev;
+  const cudaError_t e[4] = {
+      cudaFuncSetAttribute(k_gemm_i8<128, EPI_F32, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           GemmSmem<128, 4>::TOTAL),
+      cudaFuncSetAttribute(k_gemm_i8<384, EPI_LN_QUANT, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           GemmSmem<384, 3>::TOTAL),
+      cudaFuncSetAttribute(k_gemm_i8<384, EPI_LN_FINAL, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           GemmSmem<384, 3>::TOTAL),
+      cudaFuncSetAttribute(k_gemm_i8<512, EPI_GELU_QUANT, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           GemmSmem<512, 2>::TOTAL)};
+  for (auto x : e)
+    if (x != cudaSuccess) return -1;
+  return 0;
 }
 
 int gemm_i8_launch(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, cudaStream_t st) {

@@ -29,8 +29,10 @@ struct GemmArgs {
   float* out_scale;         // [M] row scale of out_q
   int32_t* acc_dbg;         // [M, N] raw int32 accumulators, or nullptr
   int* err;                 // device error word
+  int gelu_erf;             // EPI_GELU_QUANT: 0 = the reference's rational GELU, 1 = exact erf
 };
 
+int gemm_i8_prime();
 int make_tmap_i8(CUtensorMap* map, const void* base, int rows, int K);
 int gemm_i8_launch(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, cudaStream_t st);
 

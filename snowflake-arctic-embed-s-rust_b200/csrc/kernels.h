@@ -1,0 +1,48 @@
+// Launch interfaces of the row, metadata and attention kernels (rowops.cu, attention.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace ae {
+
+struct EmbedArgs {
+  int T;                      // rows
+  const uint16_t* ids;        // [T] token ids
+  const uint16_t* pos;        // [T] position of each row inside its sequence
+  const int8_t* word_q;       // [30522, 384]
+  const float* word_s;        // [30522]
+  const int8_t* pos_q;        // [512, 384]
+  const float* pos_s;         // [512]
+  const float* type0;         // [384] dequantized token_type_embeddings[0]
+  const float* gamma;         // embedding LayerNorm
+  const float* beta;
+  const float* inv_smooth;    // layers[0].qkv.inv_smooth
+  float* hidden;              // [T, 384] out
+  int8_t* act_q;              // [T, 384] out
+  float* act_s;               // [T] out
+  int* err;
+};
+
+struct AttnArgs {
+  const float* q;             // query rows, head h at columns [32h, 32h + 32)
+  int q_stride;
+  const float* k;             // key rows of all sequences
+  const float* v;             // value rows
+  int kv_stride;
+  float* out;                 // context rows (same row index as the query)
+  int out_stride;
+  const uint32_t* cu;         // [n_seqs + 1] row offsets of the sequences in k / v
+  int max_len;                // upper bound of any sequence length (<= 512)
+  int cls_mode;               // 1: one query per sequence, at row s of q / out
+  int* err;
+};
+
+int launch_embed(const EmbedArgs& a, cudaStream_t st);
+int launch_smooth_quant(const float* x, const float* inv_s, int8_t* q, float* scale, int rows, cudaStream_t st);
+int launch_row_meta(const uint32_t* cu, int n_seqs, uint16_t* pos, int32_t* cls_row, int* err, cudaStream_t st);
+int launch_gather_cls(const int32_t* cls_row, int n, const int8_t* act_q, const float* act_s, const float* hidden,
+                      int8_t* cq, float* cs, float* ch, cudaStream_t st);
+int attention_prime();
+int launch_attention_exact(const AttnArgs& a, int n_seqs, cudaStream_t st);
+
+}  // namespace ae

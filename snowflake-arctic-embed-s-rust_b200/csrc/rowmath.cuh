@@ -15,6 +15,7 @@ constexpr int kLayers = 12;
 constexpr int kVocab = 30522;
 constexpr int kMaxPos = 512;
 constexpr float kLnEps = 1e-12f;
+constexpr int kMaxDevices = 64;
 
 // hsum256_ps(sum0 + sum1) of src/simd_math.rs:3075-3084 applied to 16 partial lanes p[0..16)
 // (p[l] accumulates elements with index % 16 == l, as the two AVX2 accumulators do).
@@ -53,6 +54,25 @@ __device__ __forceinline__ float cw_exp(float x) {
 // Scalar `f32::exp` used by the reference for softmax tail elements. Evaluated in double and
 // rounded once, which is the correctly rounded result except in rare double-rounding cases.
 __device__ __forceinline__ float scalar_expf(float x) { return static_cast<float>(exp(static_cast<double>(x))); }
+
+// avx2_gelu_f32, src/simd_math.rs:152-175: rational erf approximation on x clamped to [-4.8, 4.8],
+// with the reciprocal estimate + one Newton step of the reference. The reference's estimate comes
+// from `rcp_ps` (12-bit, implementation defined); here it is the correctly rounded reciprocal, so
+// after the Newton step the two agree to about one ulp.
+__device__ __forceinline__ float gelu_ref(float x) {
+  const float xc = fminf(fmaxf(x, -4.8f), 4.8f);
+  const float u = xc * xc;
+  float num = fmaf(u, 6.4292e-5f, 0.007572631f);
+  num = fmaf(u, num, 0.055282866f);
+  num = fmaf(u, num, 0.797882463f);
+  float den = fmaf(u, 0.001139532f, 0.02381135f);
+  den = fmaf(u, den, 0.235943093f);
+  den = fmaf(u, den, 1.0f);
+  const float est = __frcp_rn(den);
+  const float inv_den = est * fmaf(-den, est, 2.0f);
+  const float erf_a = fminf(fmaxf(xc * (num * inv_den), -1.0f), 1.0f);
+  return (x * 0.5f) * (1.0f + erf_a);
+}
 
 // GELU with the exact error function (0.5 x (1 + erf(x / sqrt 2))).
 __device__ __forceinline__ float gelu_erf(float x) {

@@ -1,0 +1,191 @@
+// Row kernels of the forward pass: token embedding + LayerNorm + SmoothQuant quantization, the
+// attention-context quantization, per-row metadata of a packed (ragged) batch and the gather of
+// the [CLS] rows for the pruned last layer.
+//
+// LayerNorm and quantization reproduce the reference's AVX2 row kernels bit for bit: 16 lanes
+// hold the 16 partial sums (element j goes to lane j % 16, as the two 8-wide AVX2 accumulators
+// do), combined with the hsum256 tree; every product and sum rounds as in the reference.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "kernels.h"
+#include "ptx.cuh"
+#include "rowmath.cuh"
+
+namespace ae {
+
+// Combines the 16 per-lane partial sums held by the 16 lanes of a half-warp exactly as
+// hsum256_ps(sum0 + sum1) does; the result is returned on all 16 lanes.
+__device__ __forceinline__ float halfwarp_tree16(float p, unsigned mask) {
+  // v[l] = p[l] + p[8 + l]            (lanes 0..7)
+  float v = p + __shfl_down_sync(mask, p, 8, 16);
+  // t[l] = v[l] + v[l + 4]            (lanes 0..3)
+  float t = v + __shfl_down_sync(mask, v, 4, 16);
+  // u0 = t0 + t1, u2 = t2 + t3        (lanes 0, 2)
+  float u = t + __shfl_down_sync(mask, t, 1, 16);
+  // (t0 + t1) + (t2 + t3)             (lane 0)
+  float r = u + __shfl_down_sync(mask, u, 2, 16);
+  return __shfl_sync(mask, r, 0, 16);
+}
+
+__device__ __forceinline__ float halfwarp_max(float v, unsigned mask) {
+#pragma unroll
+  for (int o = 8; o >= 1; o >>= 1) v = fmaxf(v, __shfl_xor_sync(mask, v, o, 16));
+  return v;
+}
+
+// One half-warp per token row: dequant_add_embeddings_row (src/simd_math.rs:1827-1881, generic
+// path) + layernorm_smooth_quantize_row (src/simd_math.rs:369-477) with the embedding LayerNorm
+// and layers[0].qkv.inv_smooth (src/model.rs:196-219).
+__global__ void __launch_bounds__(256) k_embed_ln_quant(EmbedArgs a) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 4;
+  const int l = threadIdx.x & 15;
+  const unsigned mask = 0xffffffffu;  // both half-warps stay converged (inactive rows compute row T-1)
+  const bool active = row < a.T;
+  const int hw = active ? row : a.T - 1;
+  int tok = a.ids[hw];
+  const int pos = min(int(a.pos[hw]), kMaxPos - 1);
+  if (tok >= kVocab) {
+    if (l == 0) record_err(a.err, DEV_ERR_BAD_TOKEN);
+    tok = 0;
+  }
+  const int8_t* wq = a.word_q + size_t(tok) * kHidden;
+  const int8_t* pq = a.pos_q + size_t(pos) * kHidden;
+  const float ws = a.word_s[tok], ps = a.pos_s[pos];
+  float h[24];
+  float p = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 24; ++i) {
+    const int j = l + 16 * i;
+    h[i] = (float(wq[j]) * ws + float(pq[j]) * ps) + a.type0[j];
+    p = p + h[i];
+  }
+  const float mean = halfwarp_tree16(p, mask) / float(kHidden);
+  p = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 24; ++i) {
+    const float d = h[i] - mean;
+    p = fmaf(d, d, p);
+  }
+  const float var = halfwarp_tree16(p, mask) / float(kHidden);
+  const float rstd = 1.0f / sqrtf(var + kLnEps);
+  float vmax = 1e-8f;
+  float* hrow = a.hidden + size_t(hw) * kHidden;
+#pragma unroll
+  for (int i = 0; i < 24; ++i) {
+    const int j = l + 16 * i;
+    h[i] = fmaf((h[i] - mean) * rstd, a.gamma[j], a.beta[j]);
+    if (active) hrow[j] = h[i];
+    vmax = fmaxf(vmax, fabsf(h[i] * a.inv_smooth[j]));
+  }
+  const float max_abs = halfwarp_max(vmax, mask);
+  const float inv_scale = 127.0f / max_abs;
+  int8_t* qrow = a.act_q + size_t(hw) * kHidden;
+#pragma unroll
+  for (int i = 0; i < 24; ++i) {
+    const int j = l + 16 * i;
+    const int8_t qv = int8_t(quant_i8(h[i] * (a.inv_smooth[j] * inv_scale)));
+    if (active) qrow[j] = qv;
+  }
+  if (active && l == 0) a.act_s[hw] = max_abs / 127.0f;
+}
+
+// One warp per row: smooth_quantize_row_avx2 (src/simd_math.rs:584-649), the quantization of the
+// attention context with attn_out.inv_smooth (src/model.rs:324-328).
+__global__ void __launch_bounds__(256) k_smooth_quant(const float* __restrict__ x, const float* __restrict__ inv_s,
+                                                      int8_t* __restrict__ q, float* __restrict__ scale, int rows) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float* xr = x + size_t(row) * kHidden;
+  float v[12];
+  float vmax = 1e-8f;
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    const float4 t = reinterpret_cast<const float4*>(xr)[lane + 32 * i];
+    v[4 * i] = t.x;
+    v[4 * i + 1] = t.y;
+    v[4 * i + 2] = t.z;
+    v[4 * i + 3] = t.w;
+  }
+#pragma unroll
+  for (int i = 0; i < 12; ++i) {
+    const int j = 4 * (lane + 32 * (i / 4)) + (i % 4);
+    vmax = fmaxf(vmax, fabsf(v[i] * inv_s[j]));
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, o));
+  const float inv_scale = 127.0f / vmax;
+  int8_t* qr = q + size_t(row) * kHidden;
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    uint32_t w = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int j = 4 * (lane + 32 * i) + e;
+      w |= (uint32_t(quant_i8(v[4 * i + e] * (inv_s[j] * inv_scale))) & 0xFFu) << (8 * e);
+    }
+    reinterpret_cast<uint32_t*>(qr)[lane + 32 * i] = w;
+  }
+  if (lane == 0) scale[row] = vmax / 127.0f;
+}
+
+// Per-row metadata of a packed batch: position of each row inside its sequence (positions restart
+// at 0 for every sequence, src/model.rs:557-567) and the row of each sequence's [CLS] token.
+// One block per sequence. Sequences must have 1..512 rows.
+__global__ void k_row_meta(const uint32_t* __restrict__ cu, int n_seqs, uint16_t* __restrict__ pos,
+                           int32_t* __restrict__ cls_row, int* err) {
+  const int s = blockIdx.x;
+  if (s >= n_seqs) return;
+  const uint32_t b = cu[s], e = cu[s + 1];
+  if (e <= b || e - b > uint32_t(kMaxPos)) {
+    if (threadIdx.x == 0) record_err(err, DEV_ERR_BAD_SHAPE);
+    return;
+  }
+  for (uint32_t r = b + threadIdx.x; r < e; r += blockDim.x) pos[r] = uint16_t(r - b);
+  if (threadIdx.x == 0) cls_row[s] = int32_t(b);
+}
+
+// Gathers the [CLS] rows (act_q, act_scale, hidden) of every sequence into rows 0..n-1
+// (the compaction of src/model.rs:786-800, into separate buffers).
+__global__ void k_gather_cls(const int32_t* __restrict__ cls_row, int n, const int8_t* __restrict__ act_q,
+                             const float* __restrict__ act_s, const float* __restrict__ hidden,
+                             int8_t* __restrict__ cq, float* __restrict__ cs, float* __restrict__ ch) {
+  const int b = blockIdx.x;
+  if (b >= n) return;
+  const int r = cls_row[b];
+  const int t = threadIdx.x;  // 96 threads
+  reinterpret_cast<float4*>(ch + size_t(b) * kHidden)[t] = reinterpret_cast<const float4*>(hidden + size_t(r) * kHidden)[t];
+  reinterpret_cast<uint32_t*>(cq + size_t(b) * kHidden)[t] =
+      reinterpret_cast<const uint32_t*>(act_q + size_t(r) * kHidden)[t];
+  if (t == 0) cs[b] = act_s[r];
+}
+
+int launch_embed(const EmbedArgs& a, cudaStream_t st) {
+  if (a.T <= 0) return 0;
+  const int rows_per_block = 16;
+  k_embed_ln_quant<<<(a.T + rows_per_block - 1) / rows_per_block, 256, 0, st>>>(a);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int launch_smooth_quant(const float* x, const float* inv_s, int8_t* q, float* scale, int rows, cudaStream_t st) {
+  if (rows <= 0) return 0;
+  k_smooth_quant<<<(rows + 7) / 8, 256, 0, st>>>(x, inv_s, q, scale, rows);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int launch_row_meta(const uint32_t* cu, int n_seqs, uint16_t* pos, int32_t* cls_row, int* err, cudaStream_t st) {
+  if (n_seqs <= 0) return 0;
+  k_row_meta<<<n_seqs, 128, 0, st>>>(cu, n_seqs, pos, cls_row, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int launch_gather_cls(const int32_t* cls_row, int n, const int8_t* act_q, const float* act_s, const float* hidden,
+                      int8_t* cq, float* cs, float* ch, cudaStream_t st) {
+  if (n <= 0) return 0;
+  k_gather_cls<<<n, 96, 0, st>>>(cls_row, n, act_q, act_s, hidden, cq, cs, ch);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+}  // namespace ae

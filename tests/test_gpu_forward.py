@@ -1,0 +1,133 @@
+"""Full forward pass on the B200 vs the CPU oracle on the same seeded synthetic pack and token
+ids: cosine >= 0.9999 and max-abs <= 2e-3 on the L2-normalised [CLS] embedding (the north-star
+tolerance), for the reference's own length set (tests/parallel_test.rs:21), ragged batches, the
+layer-wise int32 accumulators, determinism and the error paths."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import COS_MIN, MAXABS_MAX, REF_LENGTHS, rng
+from arctic_embed_s_int8 import AeError, Engine, synth
+
+pytestmark = pytest.mark.gpu
+
+
+def close(a, b):
+    cos = float(np.dot(a, b) / (np.linalg.norm(a) * np.linalg.norm(b)))
+    return cos, float(np.abs(a - b).max())
+
+
+@pytest.mark.parametrize("L", REF_LENGTHS)
+def test_forward_cls_matches_oracle(engine, oracle_model, L):
+    ids = synth.token_ids(L, rng(1000 + L))
+    got = engine.forward_cls(ids)
+    ref = oracle_model.forward_cls(ids)
+    cos, mx = close(got, ref)
+    assert cos >= COS_MIN and mx <= MAXABS_MAX, (L, cos, mx)
+    # replayed graph gives the same bits
+    np.testing.assert_array_equal(engine.forward_cls(ids), got)
+
+
+def test_ragged_batch_matches_oracle(engine, oracle_model):
+    r = rng(7)
+    lens = [1, 2, 3, 8, 12, 16, 31, 64, 100, 128, 200, 333, 512, 5, 1, 77]
+    seqs = [synth.token_ids(L, r) for L in lens]
+    got = engine.forward_ragged(seqs)
+    for s, g in zip(seqs, got):
+        cos, mx = close(g, oracle_model.forward_cls(s))
+        assert cos >= COS_MIN and mx <= MAXABS_MAX, (len(s), cos, mx)
+    # packed == single on the GPU as well
+    single = np.stack([engine.forward_cls(s) for s in seqs])
+    np.testing.assert_array_equal(got, single)
+
+
+def test_reference_ragged_packing(engine, oracle_model):
+    """embed_batch packs short sequences (< 16 tokens) into forward_ragged_cls (src/lib.rs:161-238)."""
+    r = rng(8)
+    seqs = [synth.token_ids(L, r) for L in [5, 9, 3, 12, 7, 2, 15, 4]]
+    ref = oracle_model.forward_ragged(seqs[:4])
+    got = engine.forward_ragged(seqs[:4])
+    for g, o in zip(got, ref):
+        cos, mx = close(g, o)
+        assert cos >= COS_MIN and mx <= MAXABS_MAX
+
+
+def test_layerwise_int32_accumulators_bit_exact(engine, oracle_model, quantized):
+    """Given the oracle's own int8 activations of every layer, the GPU GEMM reproduces the int32
+    accumulators exactly (QKV of layers 0-10, KV-only of layer 11, FFN-down of layers 0-10)."""
+    ids = synth.token_ids(48, rng(3))
+    tr = oracle_model.trace(ids)
+    L = len(ids)
+    for l in range(12):
+        ly = quantized.layers[l]
+        lin = ly.kv_only if l == 11 else ly.qkv
+        a = torch.from_numpy(tr["gemm_in_q"][l].copy()).cuda()
+        acc = torch.zeros(L, lin.n_out, dtype=torch.int32, device="cuda")
+        out = torch.zeros(L, lin.n_out, dtype=torch.float32, device="cuda")
+        engine.gemm_i8(0, a, torch.from_numpy(tr["gemm_in_s"][l].copy()).cuda(), torch.from_numpy(lin.w_q).cuda(),
+                       torch.from_numpy(lin.w_scale).cuda(), torch.from_numpy(lin.bias).cuda(), out=out, acc=acc)
+        engine.sync()
+        ref = tr["gemm_in_q"][l].astype(np.int64) @ lin.w_q.astype(np.int64).T
+        np.testing.assert_array_equal(acc.cpu().numpy(), ref)
+        if l < 11:
+            np.testing.assert_array_equal(out.cpu().numpy(), tr["qkv_out"][l])
+    for l in range(11):
+        lin = quantized.layers[l].ffn_out
+        a = torch.from_numpy(tr["down_in_q"][l].copy()).cuda()
+        acc = torch.zeros(L, 384, dtype=torch.int32, device="cuda")
+        out = torch.zeros(L, 384, dtype=torch.float32, device="cuda")
+        engine.gemm_i8(0, a, torch.from_numpy(tr["down_in_s"][l].copy()).cuda(), torch.from_numpy(lin.w_q).cuda(),
+                       torch.from_numpy(lin.w_scale).cuda(), torch.from_numpy(lin.bias).cuda(), out=out, acc=acc)
+        engine.sync()
+        np.testing.assert_array_equal(acc.cpu().numpy(), tr["down_in_q"][l].astype(np.int64) @ lin.w_q.astype(np.int64).T)
+
+
+def test_fresh_engines_deterministic(pack_path):
+    """Regression idea of tests/parallel_test.rs:54-64: the first call on a fresh context completes
+    and is bit-identical to another fresh context's."""
+    ids = synth.token_ids(33, rng(5))
+    e1 = Engine(0).load_file(pack_path)
+    e2 = Engine(0).load_file(pack_path)
+    a, b = e1.forward_cls(ids), e2.forward_cls(ids)
+    np.testing.assert_array_equal(a, b)
+    np.testing.assert_array_equal(e1.forward_ragged([ids])[0], a)
+    e1.close()
+    e2.close()
+
+
+def test_truncation_to_512(engine):
+    ids = synth.token_ids(700, rng(6))
+    np.testing.assert_array_equal(engine.forward_cls(ids), engine.forward_cls(ids[:512]))
+    got = engine.forward_ragged([ids, ids[:10]])
+    np.testing.assert_array_equal(got[0], engine.forward_cls(ids[:512]))
+
+
+def test_error_paths(engine, pack_path):
+    with pytest.raises(AeError, match="TOKEN_RANGE"):
+        engine.forward_cls(np.array([101, 30522, 102], np.uint16))
+    with pytest.raises(AeError, match="INVALID_ARG"):
+        engine.forward_cls(np.zeros(0, np.uint16))
+    with pytest.raises(AeError, match="INVALID_ARG"):
+        engine.forward_ragged([np.array([101, 102], np.uint16), np.zeros(0, np.uint16)])
+    e = Engine(0)
+    with pytest.raises(AeError, match="NO_MODEL"):
+        e.forward_cls(np.array([101, 102], np.uint16))
+    with pytest.raises(AeError, match="BAD_PACK"):
+        e.load_file(pack_path + ".missing")
+    e.close()
+    # the engine still works after the errors
+    assert np.isfinite(engine.forward_cls(np.array([101, 2000, 102], np.uint16))).all()
+
+
+def test_device_resident_forward(engine):
+    r = rng(11)
+    seqs = [synth.token_ids(L, r) for L in [128] * 8 + [3, 500]]
+    from arctic_embed_s_int8 import pack_sequences
+
+    ids, cu = pack_sequences(seqs)
+    d_ids = torch.from_numpy(ids.view(np.int16)).cuda()
+    d_cu = torch.from_numpy(cu.view(np.int32)).cuda()
+    out = torch.zeros(len(seqs), 384, dtype=torch.float32, device="cuda")
+    engine.forward_device(d_ids, d_cu, len(seqs), int(cu[-1]), 512, out)
+    engine.sync()
+    np.testing.assert_array_equal(out.cpu().numpy(), engine.forward_ragged(seqs))
