@@ -190,11 +190,11 @@ def run_reference(args, rank, world):
     return 0
 
 
-def kernel_breakdown(eng, T: int, n: int, L: int, reps: int = 5):
-    """Times each kernel of a step alone (CUDA events on the engine's stream) at the step's shapes."""
+def kernel_breakdown(eng, stream, T: int, n: int, L: int, reps: int = 5):
+    """Times each kernel of a step alone (CUDA events on the engine's launch stream) at the step's shapes."""
     import torch
 
-    st = torch.cuda.current_stream()
+    st = stream
     dev = "cuda"
     g = torch.Generator(device="cpu").manual_seed(0)
     a384 = torch.randint(-127, 128, (T, 384), dtype=torch.int8, generator=g).to(dev)
@@ -228,12 +228,14 @@ def kernel_breakdown(eng, T: int, n: int, L: int, reps: int = 5):
         "attention": lambda: eng.attention_f32(qkv, cu, n, L, ctx),
     }
     flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
+    torch.cuda.synchronize()
     res_ms = {}
     for name, fn in kernels.items():
         fn()
         ts = []
         for _ in range(reps):
-            flush.fill_(1.0)
+            with torch.cuda.stream(st):
+                flush.fill_(1.0)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(st)
             fn()
@@ -384,7 +386,7 @@ def main() -> int:
             lat[f"runs@{L}"] = runs
         result["latency"] = lat
         # kernel breakdown and roofline of the dominant kernel
-        kb = kernel_breakdown(eng, T, BATCH_SEQS, SEQ_LEN)
+        kb = kernel_breakdown(eng, stream, T, BATCH_SEQS, SEQ_LEN)
         per_step = {k: v["ms"] * 11 for k, v in kb.items()}
         dom = max(per_step, key=per_step.get)
         peaks = {}
