@@ -144,6 +144,21 @@ int ae_gemm_i8(ae_ctx* ctx, int epi, uint32_t M, uint32_t N, uint32_t K, const i
 int ae_attention_f32(ae_ctx* ctx, const float* d_qkv, const uint32_t* d_cu_seqlens, uint32_t n_seqs,
                      uint32_t max_len, float* d_ctx);
 
+/* Allocation-free variant of the single-sequence forward, for callers that cannot call cudaMalloc
+ * when they embed: code recording into a CUDA graph it is capturing, hosts that hand out device
+ * memory once at start-up from their own pool, latency paths that must not wait on the allocator.
+ * No counterpart in the reference (the CPU crate gets the same effect from a reusable Workspace).
+ * d_ids: 1..512 token ids in device memory of ctx's GPU (longer inputs are rejected with
+ * AE_ERR_CAPACITY: truncate to the first 512 first); d_out384: device float[384]. Asynchronous on
+ * the context's stream. The model must already be loaded (ae_model_load allocates; this call
+ * does not). Scratch: a file-scope 8 MiB device array in the library, which every GPU that loads
+ * the library holds until the process exits. The first call on a device looks up that array's
+ * device address (cudaGetSymbolAddress) and builds its tensor maps; make that first call before
+ * any stream capture. Every call shares the one array and nothing in it has to start at zero (the
+ * call writes every row it reads); calls that overlap on the GPU, from any context on the same
+ * device, race on it. */
+int ae_forward_cls_noalloc(ae_ctx* ctx, const uint16_t* d_ids, uint32_t len, float* d_out384);
+
 /* Number of this library's kernels the context has launched so far (graph replays included). */
 uint64_t ae_kernel_launches(const ae_ctx* ctx);
 

@@ -953,3 +953,95 @@ int ae_embed_batch_multi(ae_ctx* const* ctxs, int n_ctx, const uint16_t* ids, co
 }
 
 }  // extern "C"
+
+// ============================================================================================
+// Allocation-free single-sequence forward.
+//
+// Some callers cannot call cudaMalloc at the time they embed: code that records the call into a
+// CUDA graph it is capturing (allocation breaks the capture), hosts whose device memory is handed
+// out once at start-up by their own pool, and real-time paths that must not block on the
+// allocator. ae_forward_cls_noalloc serves them: its scratch (the activations of one <= 512-token
+// sequence, about 6 MB) lives in the file-scope device array below instead of the context's
+// cudaMalloc'd workspace, so the call itself allocates nothing.
+namespace {
+
+constexpr size_t kNoAllocBytes = size_t(8) << 20;  // 8 MiB: holds the workspace of one 512-token sequence
+__device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
+
+// Per-device view of g_noalloc_scratch: its device address (from cudaGetSymbolAddress, not the
+// host-side name) carved into a Workspace, with tensor maps for the GEMM A operands.
+struct NoAllocState {
+  bool ready = false;
+  Workspace ws;
+};
+NoAllocState g_noalloc[kMaxDevices];
+std::mutex g_noalloc_mu;
+
+__global__ void k_noalloc_cu(uint32_t* cu, uint32_t len) {
+  cu[0] = 0;
+  cu[1] = len;
+}
+
+int noalloc_setup(ae_ctx* c, NoAllocState& st) {
+  void* base = nullptr;
+  CUDA_TRY(c, cudaGetSymbolAddress(&base, g_noalloc_scratch));
+  Workspace& w = st.ws;
+  const size_t T = kMaxPos, B = 128;  // one sequence; [CLS] buffers keep the 128-row tile height
+  Carve cv{static_cast<uint8_t*>(base)};
+  w.ids = cv.take<uint16_t>(T);
+  w.cu = cv.take<uint32_t>(B + 1);
+  w.pos = cv.take<uint16_t>(T);
+  w.cls_row = cv.take<int32_t>(B);
+  w.hidden = cv.take<float>(T * kHidden);
+  w.act_q = cv.take<int8_t>(T * kHidden);
+  w.act_s = cv.take<float>(T);
+  w.qkv = cv.take<float>(T * 3 * kHidden);
+  w.ctx = cv.take<float>(T * kHidden);
+  w.inter_q = cv.take<int8_t>(T * kInter);
+  w.inter_s = cv.take<float>(T);
+  w.cq = cv.take<int8_t>(B * kHidden);
+  w.cs = cv.take<float>(B);
+  w.ch = cv.take<float>(B * kHidden);
+  w.q_cls = cv.take<float>(B * kHidden);
+  w.cctx = cv.take<float>(B * kHidden);
+  w.cinter_q = cv.take<int8_t>(B * kInter);
+  w.cinter_s = cv.take<float>(B);
+  w.out = cv.take<float>(B * kHidden);
+  if (cv.off > kNoAllocBytes) return fail(c, AE_ERR_CAPACITY, "internal: static scratch too small");
+  w.cap_tokens = uint32_t(T);
+  w.cap_seqs = uint32_t(B);
+  if (make_tmap_i8(&w.tm_act_q, w.act_q, int(T), kHidden) || make_tmap_i8(&w.tm_inter_q, w.inter_q, int(T), kInter) ||
+      make_tmap_i8(&w.tm_cq, w.cq, int(B), kHidden) || make_tmap_i8(&w.tm_cinter_q, w.cinter_q, int(B), kInter))
+    return fail(c, AE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the static scratch");
+  st.ready = true;
+  return 0;
+}
+
+}  // namespace
+
+extern "C" int ae_forward_cls_noalloc(ae_ctx* c, const uint16_t* d_ids, uint32_t len, float* d_out384) {
+  if (!c) return AE_ERR_INVALID_ARG;
+  if (!c->has_model) return fail(c, AE_ERR_NO_MODEL, "no model loaded");
+  if (!d_ids || !d_out384) return fail(c, AE_ERR_INVALID_ARG, "null pointer");
+  if (len == 0 || len > uint32_t(kMaxPos))
+    return fail(c, AE_ERR_CAPACITY,
+                "ae_forward_cls_noalloc takes 1..512 token ids (its static scratch holds one 512-token sequence); "
+                "got %u",
+                len);
+  DeviceGuard g(c->device);
+  NoAllocState& st = g_noalloc[c->device];
+  {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!st.ready) AE_TRY(noalloc_setup(c, st));
+  }
+  Workspace& W = st.ws;
+  k_noalloc_cu<<<1, 1, 0, c->stream>>>(W.cu, len);
+  CUDA_TRY(c, cudaGetLastError());
+  ++c->launches;
+  // run the forward on the static scratch: the context's own workspace is set aside for the call
+  Workspace saved = c->ws;
+  c->ws = W;
+  const int r = enqueue_forward(c, d_ids, W.cu, int(len), 1, int(len), d_out384);
+  c->ws = saved;
+  return r;
+}
