@@ -1,15 +1,23 @@
 // Segment-masked multi-head attention (12 heads x d32, <= 512 keys per sequence) in fp32 on the
 // CUDA cores, in the exact operation order of the reference's AVX2 kernels:
 //   compute_scores_head32_avx2   src/simd_math.rs:2953-2984  (q pre-scaled by 1/sqrt(32),
-//                                 dot32x4 + hadd tree for keys in groups of 4, hsum256 for the rest)
+//                                 dot32x4 + hadd tree for keys in complete groups of 4, hsum256
+//                                 for the rest)
 //   softmax_inplace_avx2         src/simd_math.rs:2989-3042  (Cody-Waite exp on 8-wide chunks with
 //                                 two 8-lane accumulators, scalar exp for the tail, then * 1/sum)
-//   weighted_sum_head32_avx2     src/simd_math.rs:3047-3070  (two accumulators, even/odd keys)
+//   weighted_sum_head32_avx2     src/simd_math.rs:3047-3070  (two accumulators: even / odd keys)
 // driven as in src/model.rs:294-321 (all rows) and :814-843 ([CLS] rows of the pruned layer 11).
 //
-// One CTA per (sequence, head, query tile of 128); one thread per query. The sequence's K and V
-// head slices are staged in shared memory and read as broadcasts. Scores are recomputed in each
-// of the three softmax passes instead of being stored, which keeps shared memory at 2 x L x 128 B.
+// k_attention_rows: one CTA per (sequence, head, tile of QT queries), one thread per query. The
+// head's K and V are staged in shared memory as key pairs (k[2i][d], k[2i+1][d]) so that every
+// operation works on two keys at once with the sm_100 packed f32x2 instructions: each lane of a
+// packed FMA / add / multiply is an ordinary IEEE single-precision operation, so the results are
+// the same bits as the scalar sequence, and the reference's even/odd weighted-sum accumulators are
+// exactly the two lanes. Sequences of up to kStoreMaxLen keys keep their scores (then
+// exponentials) in shared memory; longer ones recompute the scores in each softmax pass.
+//
+// k_attention_cls: one warp per (sequence, head) for the single [CLS] query of layer 11: lanes
+// split the keys for the scores, 16 lanes run the 16 exp-sum chains, lane d accumulates dim d.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -20,31 +28,76 @@
 
 namespace ae {
 
-// One score in the reference order; `grouped` selects the hadd-tree order used for keys inside a
-// complete group of four.
-__device__ __forceinline__ float score_ref(const float (&q)[32], const float* __restrict__ k, bool grouped) {
-  float s8[8];
-  const float4* k4 = reinterpret_cast<const float4*>(k);
-  float kk[32];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float4 t = k4[i];
-    kk[4 * i] = t.x;
-    kk[4 * i + 1] = t.y;
-    kk[4 * i + 2] = t.z;
-    kk[4 * i + 3] = t.w;
-  }
+constexpr int kStoreMaxLen = 256;  // longest sequence whose scores stay in shared memory
+
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+
+// Scores of the key pair (2i, 2i+1) stored as kp[d] = (k[2i][d], k[2i+1][d]).
+__device__ __forceinline__ float2 score_pair(const float (&q)[32], const float2* __restrict__ kp, bool grouped) {
+  float2 s8[8];
 #pragma unroll
   for (int l = 0; l < 8; ++l) {
-    const float a = fmaf(q[8 + l], kk[8 + l], q[l] * kk[l]);
-    const float b = fmaf(q[24 + l], kk[24 + l], q[16 + l] * kk[16 + l]);
-    s8[l] = a + b;
+    const float2 a = fma2(f2(q[8 + l], q[8 + l]), kp[8 + l], mul2(f2(q[l], q[l]), kp[l]));
+    const float2 b = fma2(f2(q[24 + l], q[24 + l]), kp[24 + l], mul2(f2(q[16 + l], q[16 + l]), kp[16 + l]));
+    s8[l] = add2(a, b);
   }
-  if (grouped) return ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
-  return ((s8[0] + s8[4]) + (s8[1] + s8[5])) + ((s8[2] + s8[6]) + (s8[3] + s8[7]));
+  if (grouped)
+    return add2(add2(add2(s8[0], s8[1]), add2(s8[2], s8[3])), add2(add2(s8[4], s8[5]), add2(s8[6], s8[7])));
+  return add2(add2(add2(s8[0], s8[4]), add2(s8[1], s8[5])), add2(add2(s8[2], s8[6]), add2(s8[3], s8[7])));
 }
 
-__global__ void __launch_bounds__(128) k_attention_exact(AttnArgs a) {
+// cw_exp (rowmath.cuh) on two lanes.
+__device__ __forceinline__ float2 cw_exp2(float2 x) {
+  const float2 y = f2(fmaxf(fminf(x.x, 88.0f), -87.3f), fmaxf(fminf(x.y, 88.0f), -87.3f));
+  const float2 t = mul2(y, f2(1.44269504088896341f, 1.44269504088896341f));
+  const float2 n = f2(rintf(t.x), rintf(t.y));
+  const float2 nn = f2(-n.x, -n.y);
+  const float2 r = fma2(nn, f2(1.428606765330187e-6f, 1.428606765330187e-6f),
+                        fma2(nn, f2(0.693145751953125f, 0.693145751953125f), y));
+  float2 p = fma2(r, f2(0.008333334f, 0.008333334f), f2(0.041666668f, 0.041666668f));
+  p = fma2(r, p, f2(0.16666667f, 0.16666667f));
+  p = fma2(r, p, f2(0.5f, 0.5f));
+  p = fma2(r, p, f2(1.0f, 1.0f));
+  p = fma2(r, p, f2(1.0f, 1.0f));
+  const float2 pw =
+      f2(__int_as_float((__float2int_rn(n.x) + 127) << 23), __int_as_float((__float2int_rn(n.y) + 127) << 23));
+  return mul2(p, pw);
+}
+
+// Stages the head's K and V of rows [s0, s0 + L) as key pairs (odd L: the last pair's second key is 0).
+__device__ __forceinline__ void stage_kv_pairs(const AttnArgs& a, int s0, int L, int h, float2* kp, float2* vp) {
+  const int pairs = (L + 1) >> 1;
+  for (int i = threadIdx.x; i < pairs * 8; i += blockDim.x) {
+    const int pr = i >> 3, c = (i & 7) * 4;
+    const int t0 = 2 * pr, t1 = t0 + 1;
+    const size_t b0 = size_t(s0 + t0) * a.kv_stride + h * 32 + c;
+    const float4 k0 = *reinterpret_cast<const float4*>(a.k + b0);
+    const float4 v0 = *reinterpret_cast<const float4*>(a.v + b0);
+    float4 k1 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = k1;
+    if (t1 < L) {
+      const size_t b1 = b0 + a.kv_stride;
+      k1 = *reinterpret_cast<const float4*>(a.k + b1);
+      v1 = *reinterpret_cast<const float4*>(a.v + b1);
+    }
+    float2* kd = kp + pr * 32 + c;
+    float2* vd = vp + pr * 32 + c;
+    kd[0] = f2(k0.x, k1.x);
+    kd[1] = f2(k0.y, k1.y);
+    kd[2] = f2(k0.z, k1.z);
+    kd[3] = f2(k0.w, k1.w);
+    vd[0] = f2(v0.x, v1.x);
+    vd[1] = f2(v0.y, v1.y);
+    vd[2] = f2(v0.z, v1.z);
+    vd[3] = f2(v0.w, v1.w);
+  }
+}
+
+// STORE = true serves sequences of 1..kStoreMaxLen keys, STORE = false the longer ones.
+template <int QT, bool STORE>
+__global__ void __launch_bounds__(QT) k_attention_rows(AttnArgs a) {
   extern __shared__ float4 smem4[];
   const int s = blockIdx.x;
   const int h = blockIdx.y;
@@ -53,25 +106,22 @@ __global__ void __launch_bounds__(128) k_attention_exact(AttnArgs a) {
   const int s0 = int(a.cu[s]);
   const int L = int(a.cu[s + 1]) - s0;
   if (L <= 0 || L > a.max_len) {
-    if (tid == 0 && tile == 0 && h == 0) record_err(a.err, DEV_ERR_BAD_SHAPE);
+    if (STORE && tid == 0 && tile == 0 && h == 0) record_err(a.err, DEV_ERR_BAD_SHAPE);
     return;
   }
-  const int nq = a.cls_mode ? 1 : L;
-  if (tile * 128 >= nq) return;
+  if (STORE ? (L > kStoreMaxLen) : (L <= kStoreMaxLen)) return;  // the other variant's sequence
+  if (tile * QT >= L) return;
 
-  float* ks = reinterpret_cast<float*>(smem4);
-  float* vs = ks + size_t(L) * 32;
-  for (int i = tid; i < L * 8; i += blockDim.x) {
-    const int t = i >> 3, c = (i & 7) * 4;
-    const size_t base = size_t(s0 + t) * a.kv_stride + h * 32 + c;
-    *reinterpret_cast<float4*>(ks + t * 32 + c) = *reinterpret_cast<const float4*>(a.k + base);
-    *reinterpret_cast<float4*>(vs + t * 32 + c) = *reinterpret_cast<const float4*>(a.v + base);
-  }
+  const int pairs = (L + 1) >> 1;
+  float2* kp = reinterpret_cast<float2*>(smem4);
+  float2* vp = kp + pairs * 32;
+  float* sc = reinterpret_cast<float*>(vp + pairs * 32);  // [L][QT] scores, then exponentials (STORE)
+  stage_kv_pairs(a, s0, L, h, kp, vp);
   __syncthreads();
 
-  const int qi = tile * 128 + tid;
-  if (qi >= nq) return;
-  const int qrow = a.cls_mode ? s : s0 + qi;
+  const int qi = tile * QT + tid;
+  if (qi >= L) return;
+  const int qrow = s0 + qi;
   const float scale = 1.0f / sqrtf(32.0f);
   float q[32];
   {
@@ -87,78 +137,233 @@ __global__ void __launch_bounds__(128) k_attention_exact(AttnArgs a) {
   }
   const int L4 = L & ~3, L8 = L & ~7, L16 = L & ~15;
 
-  // pass 1: row max
+  // pass 1: scores and their max
   float mx = -INFINITY;
-  for (int t = 0; t < L; ++t) mx = fmaxf(mx, score_ref(q, ks + t * 32, t < L4));
+  for (int i = 0; i < pairs; ++i) {
+    const float2 sp = score_pair(q, kp + i * 32, 2 * i < L4);
+    if (STORE) {
+      sc[(2 * i) * QT + tid] = sp.x;
+      if (2 * i + 1 < L) sc[(2 * i + 1) * QT + tid] = sp.y;
+    }
+    mx = fmaxf(mx, sp.x);
+    if (2 * i + 1 < L) mx = fmaxf(mx, sp.y);
+  }
+  const float2 neg_mx = f2(-mx, -mx);
 
-  // pass 2: sum of exponentials in the reference's accumulation order
-  float vs0[8], vs1[8];
+  auto score2 = [&](int t) -> float2 {  // scores of keys t, t+1 (t even)
+    if (STORE) return f2(sc[t * QT + tid], (t + 1 < L) ? sc[(t + 1) * QT + tid] : 0.0f);
+    return score_pair(q, kp + (t >> 1) * 32, t < L4);
+  };
+  auto put2 = [&](int t, float2 e) {
+    if (STORE) {
+      sc[t * QT + tid] = e.x;
+      sc[(t + 1) * QT + tid] = e.y;
+    }
+  };
+
+  // pass 2: exponentials and their sum in the reference's accumulation order
+  float2 vs0[4], vs1[4];  // lanes (2j, 2j+1) of the reference's two 8-lane accumulators
 #pragma unroll
-  for (int j = 0; j < 8; ++j) vs0[j] = vs1[j] = 0.0f;
+  for (int j = 0; j < 4; ++j) vs0[j] = vs1[j] = f2(0.0f, 0.0f);
   for (int t0 = 0; t0 < L16; t0 += 16) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) vs0[j] = vs0[j] + cw_exp(score_ref(q, ks + (t0 + j) * 32, t0 + j < L4) - mx);
+    for (int j = 0; j < 4; ++j) {
+      const float2 e = cw_exp2(add2(score2(t0 + 2 * j), neg_mx));
+      put2(t0 + 2 * j, e);
+      vs0[j] = add2(vs0[j], e);
+    }
 #pragma unroll
-    for (int j = 0; j < 8; ++j) vs1[j] = vs1[j] + cw_exp(score_ref(q, ks + (t0 + 8 + j) * 32, t0 + 8 + j < L4) - mx);
+    for (int j = 0; j < 4; ++j) {
+      const float2 e = cw_exp2(add2(score2(t0 + 8 + 2 * j), neg_mx));
+      put2(t0 + 8 + 2 * j, e);
+      vs1[j] = add2(vs1[j], e);
+    }
   }
   if (L8 > L16) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) vs0[j] = vs0[j] + cw_exp(score_ref(q, ks + (L16 + j) * 32, L16 + j < L4) - mx);
+    for (int j = 0; j < 4; ++j) {
+      const float2 e = cw_exp2(add2(score2(L16 + 2 * j), neg_mx));
+      put2(L16 + 2 * j, e);
+      vs0[j] = add2(vs0[j], e);
+    }
   }
   float v8[8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) v8[j] = vs0[j] + vs1[j];
-  float sum = tree8(v8);
-  for (int t = L8; t < L; ++t) sum = sum + scalar_expf(score_ref(q, ks + t * 32, t < L4) - mx);
-  const float inv = 1.0f / sum;
-
-  // pass 3: probabilities and the weighted sum of V (accumulator a: even keys, b: odd keys)
-  float acc_a[32], acc_b[32];
-#pragma unroll
-  for (int d = 0; d < 32; ++d) acc_a[d] = acc_b[d] = 0.0f;
-  auto prob = [&](int t) {
-    const float x = score_ref(q, ks + t * 32, t < L4) - mx;
-    return (t < L8 ? cw_exp(x) : scalar_expf(x)) * inv;
-  };
-  int t = 0;
-  for (; t + 2 <= L; t += 2) {
-    const float pa = prob(t), pb = prob(t + 1);
-    const float* va = vs + t * 32;
-    const float* vb = va + 32;
-#pragma unroll
-    for (int d = 0; d < 32; ++d) {
-      acc_a[d] = fmaf(va[d], pa, acc_a[d]);
-      acc_b[d] = fmaf(vb[d], pb, acc_b[d]);
-    }
+  for (int j = 0; j < 4; ++j) {
+    const float2 t = add2(vs0[j], vs1[j]);
+    v8[2 * j] = t.x;
+    v8[2 * j + 1] = t.y;
   }
-  if (t < L) {
-    const float pa = prob(t);
-    const float* va = vs + t * 32;
+  float sum = tree8(v8);
+  for (int t = L8; t < L; ++t) {
+    const float x = STORE ? sc[t * QT + tid] : ((t & 1) ? score2(t - 1).y : score2(t).x);
+    const float e = scalar_expf(x - mx);
+    if (STORE) sc[t * QT + tid] = e;
+    sum = sum + e;
+  }
+  const float inv = 1.0f / sum;
+  const float2 inv2 = f2(inv, inv);
+
+  // pass 3: probabilities and the weighted sum of V; lane x = even keys (a), lane y = odd keys (b)
+  auto exps2 = [&](int t) -> float2 {  // exponentials of keys t, t+1 (t even; 0 past the end)
+    if (STORE) return f2(sc[t * QT + tid], (t + 1 < L) ? sc[(t + 1) * QT + tid] : 0.0f);
+    const float2 x = add2(score_pair(q, kp + (t >> 1) * 32, t < L4), neg_mx);
+    if (t + 1 < L8) return cw_exp2(x);
+    return f2(scalar_expf(x.x), (t + 1 < L) ? scalar_expf(x.y) : 0.0f);  // t >= L8 here
+  };
+  float2 acc[32];
 #pragma unroll
-    for (int d = 0; d < 32; ++d) acc_a[d] = fmaf(va[d], pa, acc_a[d]);
+  for (int d = 0; d < 32; ++d) acc[d] = f2(0.0f, 0.0f);
+  const int full_pairs = L >> 1;
+  for (int i = 0; i < full_pairs; ++i) {
+    const float2 p = mul2(exps2(2 * i), inv2);
+    const float2* v = vp + i * 32;
+#pragma unroll
+    for (int d = 0; d < 32; ++d) acc[d] = fma2(v[d], p, acc[d]);
+  }
+  if (L & 1) {
+    const float pa = exps2(L - 1).x * inv;
+    const float2* v = vp + (L >> 1) * 32;
+#pragma unroll
+    for (int d = 0; d < 32; ++d) acc[d].x = fmaf(v[d].x, pa, acc[d].x);
   }
   float4* o = reinterpret_cast<float4*>(a.out + size_t(qrow) * a.out_stride + h * 32);
 #pragma unroll
   for (int i = 0; i < 8; ++i)
-    o[i] = make_float4(acc_a[4 * i] + acc_b[4 * i], acc_a[4 * i + 1] + acc_b[4 * i + 1],
-                       acc_a[4 * i + 2] + acc_b[4 * i + 2], acc_a[4 * i + 3] + acc_b[4 * i + 3]);
+    o[i] = make_float4(acc[4 * i].x + acc[4 * i].y, acc[4 * i + 1].x + acc[4 * i + 1].y,
+                       acc[4 * i + 2].x + acc[4 * i + 2].y, acc[4 * i + 3].x + acc[4 * i + 3].y);
+}
+
+// One warp per (sequence, head): the single [CLS] query (row s of q / out) over the sequence's keys.
+__global__ void __launch_bounds__(128) k_attention_cls(AttnArgs a, int n_seqs) {
+  extern __shared__ float4 smem4[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int item = blockIdx.x * 4 + warp;  // (sequence, head)
+  if (item >= n_seqs * kHeads) return;
+  const int s = item / kHeads, h = item % kHeads;
+  const int s0 = int(a.cu[s]);
+  const int L = int(a.cu[s + 1]) - s0;
+  if (L <= 0 || L > a.max_len) {
+    if (lane == 0) record_err(a.err, DEV_ERR_BAD_SHAPE);
+    return;
+  }
+  float* sc = reinterpret_cast<float*>(smem4) + warp * kMaxPos;  // scores, then exponentials
+  const float scale = 1.0f / sqrtf(32.0f);
+  float q[32];
+  {
+    const float4* qp = reinterpret_cast<const float4*>(a.q + size_t(s) * a.q_stride + h * 32);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 t = qp[i];
+      q[4 * i] = t.x * scale;
+      q[4 * i + 1] = t.y * scale;
+      q[4 * i + 2] = t.z * scale;
+      q[4 * i + 3] = t.w * scale;
+    }
+  }
+  const int L4 = L & ~3, L8 = L & ~7, L16 = L & ~15;
+  float mx = -INFINITY;
+  for (int t = lane; t < L; t += 32) {
+    const float4* k4 = reinterpret_cast<const float4*>(a.k + size_t(s0 + t) * a.kv_stride + h * 32);
+    float kk[32];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 v = k4[i];
+      kk[4 * i] = v.x;
+      kk[4 * i + 1] = v.y;
+      kk[4 * i + 2] = v.z;
+      kk[4 * i + 3] = v.w;
+    }
+    float s8[8];
+#pragma unroll
+    for (int l = 0; l < 8; ++l)
+      s8[l] = fmaf(q[8 + l], kk[8 + l], q[l] * kk[l]) + fmaf(q[24 + l], kk[24 + l], q[16 + l] * kk[16 + l]);
+    const float sv = (t < L4) ? ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]))
+                              : ((s8[0] + s8[4]) + (s8[1] + s8[5])) + ((s8[2] + s8[6]) + (s8[3] + s8[7]));
+    sc[t] = sv;
+    mx = fmaxf(mx, sv);
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  __syncwarp();
+  for (int t = lane; t < L; t += 32) sc[t] = (t < L8) ? cw_exp(sc[t] - mx) : scalar_expf(sc[t] - mx);
+  __syncwarp();
+  // lane l < 16 runs the chain of the reference's lane slot l (keys t0 + l of every 16-key chunk;
+  // slots 0-7 then also take the trailing 8-key chunk), as the two 8-lane AVX2 accumulators do
+  float part = 0.0f;
+  if (lane < 16) {
+    for (int t0 = 0; t0 < L16; t0 += 16) part = part + sc[t0 + lane];
+    if (L8 > L16 && lane < 8) part = part + sc[L16 + lane];
+  }
+  const float v = part + __shfl_down_sync(0xffffffffu, part, 8);  // vs0[l] + vs1[l]
+  const float t4 = v + __shfl_down_sync(0xffffffffu, v, 4);
+  const float u = t4 + __shfl_down_sync(0xffffffffu, t4, 1);
+  float sum = u + __shfl_down_sync(0xffffffffu, u, 2);
+  sum = __shfl_sync(0xffffffffu, sum, 0);
+  for (int t = L8; t < L; ++t) sum = sum + sc[t];
+  const float inv = 1.0f / sum;
+  // weighted sum: lane = dim, accumulator a (even keys) and b (odd keys)
+  float acc_a = 0.0f, acc_b = 0.0f;
+  const float* vcol = a.v + size_t(s0) * a.kv_stride + h * 32 + lane;
+  int t = 0;
+  for (; t + 2 <= L; t += 2) {
+    acc_a = fmaf(vcol[size_t(t) * a.kv_stride], sc[t] * inv, acc_a);
+    acc_b = fmaf(vcol[size_t(t + 1) * a.kv_stride], sc[t + 1] * inv, acc_b);
+  }
+  if (t < L) acc_a = fmaf(vcol[size_t(t) * a.kv_stride], sc[t] * inv, acc_a);
+  a.out[size_t(s) * a.out_stride + h * 32 + lane] = acc_a + acc_b;
+}
+
+template <int QT, bool STORE>
+static size_t rows_smem(int max_len) {
+  const int L = STORE ? (max_len < kStoreMaxLen ? max_len : kStoreMaxLen) : max_len;
+  return size_t((L + 1) / 2) * 32 * 8 * 2 + (STORE ? size_t(L) * QT * 4 : 0);
+}
+
+template <int QT, bool STORE>
+static int launch_rows(const AttnArgs& a, int n_seqs, cudaStream_t st) {
+  const int L = STORE ? (a.max_len < kStoreMaxLen ? a.max_len : kStoreMaxLen) : a.max_len;
+  dim3 grid(n_seqs, kHeads, (L + QT - 1) / QT);
+  k_attention_rows<QT, STORE><<<grid, QT, rows_smem<QT, STORE>(a.max_len), st>>>(a);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+template <int QT>
+static int launch_qt(const AttnArgs& a, int n_seqs, cudaStream_t st) {
+  int r = launch_rows<QT, true>(a, n_seqs, st);
+  if (!r && a.max_len > kStoreMaxLen) r = launch_rows<QT, false>(a, n_seqs, st);
+  return r;
+}
+
+static int smem_attr(const void* fn, size_t bytes) {
+  return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes)) == cudaSuccess ? 0 : -1;
 }
 
 int attention_prime() {
-  return cudaFuncSetAttribute(k_attention_exact, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxPos * 32 * 4 * 2) ==
-                 cudaSuccess
-             ? 0
-             : -1;
+  int r = 0;
+  r |= smem_attr((const void*)k_attention_rows<128, true>, rows_smem<128, true>(kMaxPos));
+  r |= smem_attr((const void*)k_attention_rows<64, true>, rows_smem<64, true>(kMaxPos));
+  r |= smem_attr((const void*)k_attention_rows<32, true>, rows_smem<32, true>(kMaxPos));
+  r |= smem_attr((const void*)k_attention_rows<128, false>, rows_smem<128, false>(kMaxPos));
+  r |= smem_attr((const void*)k_attention_rows<64, false>, rows_smem<64, false>(kMaxPos));
+  r |= smem_attr((const void*)k_attention_rows<32, false>, rows_smem<32, false>(kMaxPos));
+  r |= smem_attr((const void*)k_attention_cls, 4 * kMaxPos * 4);
+  return r;
 }
 
 int launch_attention_exact(const AttnArgs& a, int n_seqs, cudaStream_t st) {
   if (n_seqs <= 0) return 0;
   if (a.max_len <= 0 || a.max_len > kMaxPos) return -1;
-  const size_t smem = size_t(a.max_len) * 32 * 4 * 2;
-  const int nq = a.cls_mode ? 1 : a.max_len;
-  dim3 grid(n_seqs, kHeads, (nq + 127) / 128);
-  k_attention_exact<<<grid, 128, smem, st>>>(a);
-  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+  if (a.cls_mode) {
+    const int items = n_seqs * kHeads;
+    k_attention_cls<<<(items + 3) / 4, 128, 4 * kMaxPos * 4, st>>>(a, n_seqs);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+  }
+  // query tile: 128 threads when the grid fills the GPU, smaller tiles for few sequences
+  const long ctas128 = long(n_seqs) * kHeads * ((a.max_len + 127) / 128);
+  if (ctas128 >= 2 * 148) return launch_qt<128>(a, n_seqs, st);
+  if (ctas128 * 2 >= 2 * 148) return launch_qt<64>(a, n_seqs, st);
+  return launch_qt<32>(a, n_seqs, st);
 }
 
 }  // namespace ae

@@ -191,7 +191,7 @@ int upload_linear(ae_ctx* c, Carve& cv, const ae_linear_desc& d, DevLinear& o) {
   CUDA_TRY(c, cudaMemcpy(o.w, d.w_q, d.n_out * d.k_in, cudaMemcpyHostToDevice));
   CUDA_TRY(c, cudaMemcpy(o.ws, d.w_scale, d.n_out * 4, cudaMemcpyHostToDevice));
   CUDA_TRY(c, cudaMemcpy(o.bias, d.bias, d.n_out * 4, cudaMemcpyHostToDevice));
-  if (make_tmap_i8(&o.tmap, o.w, o.n, o.k) != 0) return fail(c, AE_ERR_CUDA, "cuTensorMapEncodeTiled failed for weights");
+  if (make_tmap_i8(&o.tmap, o.w, o.n, o.k, kBoxB) != 0) return fail(c, AE_ERR_CUDA, "cuTensorMapEncodeTiled failed for weights");
   return 0;
 }
 
@@ -283,8 +283,8 @@ int reserve(ae_ctx* c, uint32_t tokens, uint32_t seqs) {
   w.out = cv.take<float>(B * kHidden);
   w.cap_tokens = tokens;
   w.cap_seqs = seqs;
-  if (make_tmap_i8(&w.tm_act_q, w.act_q, int(T), kHidden) || make_tmap_i8(&w.tm_inter_q, w.inter_q, int(T), kInter) ||
-      make_tmap_i8(&w.tm_cq, w.cq, int(B), kHidden) || make_tmap_i8(&w.tm_cinter_q, w.cinter_q, int(B), kInter))
+  if (make_tmap_i8(&w.tm_act_q, w.act_q, int(T), kHidden, kBoxA) || make_tmap_i8(&w.tm_inter_q, w.inter_q, int(T), kInter, kBoxA) ||
+      make_tmap_i8(&w.tm_cq, w.cq, int(B), kHidden, kBoxA) || make_tmap_i8(&w.tm_cinter_q, w.cinter_q, int(B), kInter, kBoxA))
     return fail(c, AE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the workspace");
   CUDA_TRY(c, cudaMallocHost(&w.h_ids, T * 2));
   CUDA_TRY(c, cudaMallocHost(&w.h_cu, (B + 1) * 4));
@@ -844,7 +844,7 @@ int ae_gemm_i8(ae_ctx* c, int epi, uint32_t M, uint32_t N, uint32_t K, const int
   if (!d_a || !d_a_scale || !d_w || !d_w_scale || !d_bias || M == 0 || K % 128)
     return fail(c, AE_ERR_INVALID_ARG, "ae_gemm_i8: bad arguments");
   CUtensorMap ta, tb;
-  if (make_tmap_i8(&ta, d_a, int(M), int(K)) || make_tmap_i8(&tb, d_w, int(N), int(K)))
+  if (make_tmap_i8(&ta, d_a, int(M), int(K), kBoxA) || make_tmap_i8(&tb, d_w, int(N), int(K), kBoxB))
     return fail(c, AE_ERR_INVALID_ARG, "ae_gemm_i8: operands must be 16-byte aligned");
   GemmArgs a{};
   a.M = int(M);
@@ -867,7 +867,7 @@ int ae_gemm_i8(ae_ctx* c, int epi, uint32_t M, uint32_t N, uint32_t K, const int
   a.gelu_erf = c->gelu_erf;
   switch (epi) {
     case EPI_F32:
-      if (!d_out || N % 128) return fail(c, AE_ERR_INVALID_ARG, "epilogue 0 needs out and N % 128 == 0");
+      if (!d_out || N % 64) return fail(c, AE_ERR_INVALID_ARG, "epilogue 0 needs out and N a multiple of 128 or 192");
       break;
     case EPI_LN_QUANT:
       if (N != kHidden || !d_res || !d_gamma || !d_beta || !d_inv_smooth || !d_out || !d_out_q || !d_out_scale)
@@ -1010,8 +1010,8 @@ int noalloc_setup(ae_ctx* c, NoAllocState& st) {
   if (cv.off > kNoAllocBytes) return fail(c, AE_ERR_CAPACITY, "internal: static scratch too small");
   w.cap_tokens = uint32_t(T);
   w.cap_seqs = uint32_t(B);
-  if (make_tmap_i8(&w.tm_act_q, w.act_q, int(T), kHidden) || make_tmap_i8(&w.tm_inter_q, w.inter_q, int(T), kInter) ||
-      make_tmap_i8(&w.tm_cq, w.cq, int(B), kHidden) || make_tmap_i8(&w.tm_cinter_q, w.cinter_q, int(B), kInter))
+  if (make_tmap_i8(&w.tm_act_q, w.act_q, int(T), kHidden, kBoxA) || make_tmap_i8(&w.tm_inter_q, w.inter_q, int(T), kInter, kBoxA) ||
+      make_tmap_i8(&w.tm_cq, w.cq, int(B), kHidden, kBoxA) || make_tmap_i8(&w.tm_cinter_q, w.cinter_q, int(B), kInter, kBoxA))
     return fail(c, AE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the static scratch");
   st.ready = true;
   return 0;

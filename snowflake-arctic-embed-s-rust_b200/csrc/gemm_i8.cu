@@ -4,22 +4,36 @@
 //   acc[m,n] = sum_k A[m,k] * W[n,k]                      (exact int32)
 //   h[m,n]   = fma(float(acc), a_scale[m] * w_scale[n], bias[n] (+ res[m,n]))
 // A is [M,K] row-major int8, W is [N,K] row-major int8 (out_features x in_features), both K-major
-// operands for tcgen05. Tiles are 128 rows of A; K is consumed in 128-byte blocks staged by TMA
-// (128-byte swizzle, no multicast) through a STAGES-deep mbarrier ring; one thread issues the MMAs,
-// the int32 accumulator lives in TMEM, and the 128 epilogue threads each own one output row.
+// operands for tcgen05.
+//
+// Structure: a persistent, warp-specialised kernel, one CTA per SM (576 threads).
+//   warp 0      TMA producer: the CTA's slice of W (BN rows) is loaded once and stays in shared
+//               memory when K = 384 ("resident"); A tiles (128 rows) stream through a STAGES-deep
+//               ring of 128-byte K blocks (128-byte swizzle, no multicast).
+//   warp 1      MMA issuer: one thread issues the tcgen05.mma of each tile into a TMEM accumulator;
+//               two accumulators alternate when 2 x BN <= 512 TMEM columns, so the epilogue of one
+//               tile overlaps the MMAs of the next.
+//   warps 2-17  epilogue: 4 warps per TMEM lane quadrant (32 rows), each with a quarter of the
+//               columns, so the FP32 epilogue work runs on 16 warps.
+// Each CTA keeps one N slice and walks the M tiles m0 = start, start + stride, ...
 //
 // Epilogues:
 //   EPI_F32        out[m,n] = h                                   (QKV, KV-only, Q-only projections)
 //   EPI_LN_QUANT   hidden = LayerNorm(h) written back as the new residual, then the SmoothQuant
-//                  dynamic row quantization for the next GEMM       (attention-out and FFN-down;
+//                  dynamic row quantization for the next GEMM (attention-out and FFN-down;
 //                  src/model.rs:330-353, :375-397 with layernorm_smooth_quantize_row_avx2,
-//                  src/simd_math.rs:369-477)
-//   EPI_GELU_QUANT g = GELU(h) * inv_smooth, row max over all 1536 columns exchanged across a
-//                  3-CTA cluster through distributed shared memory, then row quantization
-//                  (FFN-up; gelu_smooth_quantize_row_avx2, src/simd_math.rs:1371-1435). GELU is the
-//                  reference's rational approximation (gelu_ref) or, on request, the exact erf.
+//                  src/simd_math.rs:369-477). The full 384-wide row is in one CTA; warp q of a
+//                  quadrant owns the reduction lanes 4q..4q+3 (columns 16k + 4q + e) so every
+//                  exact-order partial-sum chain stays inside one thread, and the 16 lanes are
+//                  combined through shared memory with the reference's hsum256 tree.
+//   EPI_GELU_QUANT g = GELU(h) * inv_smooth, row max over all 1536 columns, row quantization
+//                  (FFN-up; gelu_smooth_quantize_row_avx2, src/simd_math.rs:1371-1435). A cluster
+//                  of 6 CTAs holds the 6 slices of 256 columns of the same 128 rows; each CTA sends
+//                  its partial row maxima into its peers' shared memory with st.async, which
+//                  completes on the peers' mbarriers. GELU is the reference's rational
+//                  approximation (gelu_ref) or, on request, the exact erf.
 //   EPI_LN_FINAL   out = l2_normalize(layernorm_inplace_row(h))  (layer-11 FFN-down of the [CLS]
-//                  rows; src/model.rs:496-512, src/simd_math.rs:481-497, :2892-2903)
+//                  rows; src/model.rs:496-512, src/simd_math.rs:481-497, :2892-2903; sequential sums)
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -33,53 +47,65 @@
 
 namespace ae {
 
-constexpr int BM = 128;        // rows per tile
-constexpr int BK = 128;        // K bytes per stage (one 128-byte swizzle atom wide)
-constexpr int A_STAGE = BM * BK;  // 16 KB
+constexpr int BM = 128;            // rows per tile
+constexpr int BK = 128;            // K bytes per block (one 128-byte swizzle atom wide)
+constexpr int A_STAGE = BM * BK;   // 16 KB
+constexpr int kEpiWarps = 16;
+constexpr int kThreads = (2 + kEpiWarps) * 32;
+constexpr int kResK = 384;         // K of the GEMMs whose weight slice stays resident
+constexpr int kResKB = kResK / BK;
+constexpr int kGeluCluster = 6;
 
-template <int BN, int STAGES>
-struct GemmSmem {
-  static constexpr int B_STAGE = BN * BK;
-  static constexpr int STAGE = A_STAGE + B_STAGE;
-  static constexpr int TILES = STAGES * STAGE;
-  // per-column parameters: w_scale, bias, gamma, beta, inv_smooth
-  static constexpr int PARAMS = 5 * BN * 4;
-  static constexpr int ROWMAX = 3 * BM * 4;
-  static constexpr int BARS = (2 * STAGES + 1) * 8 + 16;
-  static constexpr int TOTAL = 1024 + TILES + PARAMS + ROWMAX + BARS;
+template <int BN, int EPI, bool RES, int STAGES>
+struct Layout {
+  static constexpr bool LN = EPI == EPI_LN_QUANT || EPI == EPI_LN_FINAL;
+  static constexpr int NB = (2 * BN <= 512) ? 2 : 1;                   // TMEM accumulators
+  static constexpr uint32_t TCOLS = (NB * BN <= 128) ? 128 : (NB * BN <= 256 ? 256 : 512);
+  static constexpr int NSUB = BN <= 256 ? BN : BN / 2;                  // N of one MMA
+  static constexpr int B_RES = RES ? kResKB * BN * BK : 0;
+  static constexpr int STAGE = A_STAGE + (RES ? 0 : BN * BK);
+  static constexpr int RING = STAGES * STAGE;
+  static constexpr int PARAM_FLOATS = 3 * BN + 2 * kHidden;             // ws, bias, invs | gamma, beta
+  static constexpr int XCH_FLOATS =
+      LN ? (2 * BM * 16 + BM * 4) : (EPI == EPI_GELU_QUANT ? (2 * 4 * BM + 2 * kGeluCluster * BM) : 0);
+  static constexpr int NBARS = 2 * STAGES + 1 + 2 * 2 + 2;
+  static constexpr int TOTAL = 1024 + B_RES + RING + 4 * (PARAM_FLOATS + XCH_FLOATS) + 8 * NBARS + 16;
 };
 
-__host__ __device__ constexpr uint32_t tmem_cols_for(int bn) {
-  return bn <= 32 ? 32 : bn <= 64 ? 64 : bn <= 128 ? 128 : bn <= 256 ? 256 : 512;
-}
-
-template <int BN, int EPI, int STAGES>
-__global__ void __launch_bounds__(128, 1)
-    k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs g) {
-  using S = GemmSmem<BN, STAGES>;
+template <int BN, int EPI, bool RES, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm_i8(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs g,
+              int n_tiles_n, int m_tiles) {
+  using Ly = Layout<BN, EPI, RES, STAGES>;
+  constexpr int NB = Ly::NB;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  float* s_ws = reinterpret_cast<float*>(smem + S::TILES);
+  uint8_t* b_res = smem;
+  uint8_t* ring = smem + Ly::B_RES;
+  float* s_ws = reinterpret_cast<float*>(ring + Ly::RING);
   float* s_bias = s_ws + BN;
-  float* s_gamma = s_bias + BN;
-  float* s_beta = s_gamma + BN;
-  float* s_invs = s_beta + BN;
-  float* s_rowmax = s_invs + BN;  // [3][BM], written by the cluster peers (EPI_GELU_QUANT)
-  uint64_t* full = reinterpret_cast<uint64_t*>(s_rowmax + 3 * BM);
+  float* s_invs = s_bias + BN;
+  float* s_gamma = s_invs + BN;
+  float* s_beta = s_gamma + kHidden;
+  float* xch = s_beta + kHidden;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xch + Ly::XCH_FLOATS);
+  uint64_t* full = bars;
   uint64_t* empty = full + STAGES;
-  uint64_t* accfull = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accfull + 1);
+  uint64_t* bfull = empty + STAGES;
+  uint64_t* acc_full = bfull + 1;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* rmx_bar = acc_empty + 2;  // EPI_GELU_QUANT: peers' row maxima arrived (per tile parity)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + Ly::NBARS);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int n_tile = blockIdx.x;
-  const int m0 = blockIdx.y * BM;
+  const int n_tile = blockIdx.x % n_tiles_n;
   const int n0 = n_tile * BN;
+  const int m_first = blockIdx.x / n_tiles_n;
+  const int m_stride = gridDim.x / n_tiles_n;
+  const int my_tiles = m_first < m_tiles ? (m_tiles - 1 - m_first) / m_stride + 1 : 0;
   const int KB = g.K / BK;
-  constexpr uint32_t TCOLS = tmem_cols_for(BN);
-
-  if constexpr (EPI == EPI_GELU_QUANT) cluster_arrive_release();  // peers must be running before DSMEM use
 
   if (tid == 0) {
     tma_prefetch_desc(&tmA);
@@ -88,317 +114,422 @@ __global__ void __launch_bounds__(128, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accfull, 1);
+    mbar_init(bfull, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], kEpiWarps);
+      mbar_init(&rmx_bar[b], 1);
+    }
     fence_mbar_init();
   }
   if (warp == 0) {
-    tmem_alloc(tmem_slot, TCOLS);
+    tmem_alloc(tmem_slot, Ly::TCOLS);
     tmem_relinquish();
   }
-  // per-column epilogue parameters
   for (int i = tid; i < BN; i += blockDim.x) {
     const int n = n0 + i;
     s_ws[i] = g.w_scale[n];
     s_bias[i] = g.bias[n];
-    if constexpr (EPI == EPI_LN_QUANT || EPI == EPI_LN_FINAL) {
+    if constexpr (EPI == EPI_LN_QUANT || EPI == EPI_GELU_QUANT) s_invs[i] = g.inv_smooth[n];
+  }
+  if constexpr (Ly::LN) {
+    for (int i = tid; i < kHidden; i += blockDim.x) {
       s_gamma[i] = g.gamma[i];
       s_beta[i] = g.beta[i];
     }
-    if constexpr (EPI == EPI_LN_QUANT || EPI == EPI_GELU_QUANT) s_invs[i] = g.inv_smooth[n];
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (EPI == EPI_GELU_QUANT) {  // peers' barriers are initialised before any st.async
+    cluster_arrive_release();
+    cluster_wait_acquire();
+  }
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  bool ok = true;
-  if (warp == 0 && lane == 0) {
-    // ---------------- TMA producer
-    for (int kb = 0; kb < KB && ok; ++kb) {
-      const int s = kb % STAGES;
-      if (kb >= STAGES) ok = mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1, g.err, DEV_ERR_TIMEOUT_PRODUCER);
-      if (!ok) break;
-      uint8_t* a_s = smem + s * S::STAGE;
-      uint8_t* b_s = a_s + A_STAGE;
-      mbar_arrive_expect_tx(&full[s], S::STAGE);
-      tma_load_2d(a_s, &tmA, &full[s], kb * BK, m0);
-#pragma unroll
-      for (int j = 0; j < BN / 128; ++j) tma_load_2d(b_s + j * 128 * BK, &tmB, &full[s], kb * BK, n0 + j * 128);
-    }
-  } else if (warp == 1 && lane == 0) {
-    // ---------------- MMA issuer
-    constexpr uint32_t idesc = idesc_i8(128, 128);
-    for (int kb = 0; kb < KB && ok; ++kb) {
-      const int s = kb % STAGES;
-      ok = mbar_wait(&full[s], (kb / STAGES) & 1, g.err, DEV_ERR_TIMEOUT_MMA);
-      if (!ok) break;
-      tc_fence_after();
-      const uint32_t a_addr = smem_u32(smem + s * S::STAGE);
-      const uint32_t b_addr = a_addr + A_STAGE;
-#pragma unroll
-      for (int ks = 0; ks < BK / 32; ++ks) {
-        const uint64_t ad = sdesc_sw128(a_addr + ks * 32);
-#pragma unroll
-        for (int j = 0; j < BN / 128; ++j) {
-          const uint64_t bd = sdesc_sw128(b_addr + j * 128 * BK + ks * 32);
-          mma_i8(tmem + j * 128, ad, bd, idesc, (kb | ks) != 0);
+  if (warp == 0) {
+    // ------------------------------------------------ TMA producer
+    if (lane == 0) {
+      bool ok = true;
+      if constexpr (RES) {
+        mbar_arrive_expect_tx(bfull, Ly::B_RES);
+        for (int kb = 0; kb < kResKB; ++kb)
+          for (int j = 0; j < BN / 64; ++j)
+            tma_load_2d(b_res + (kb * BN + j * 64) * BK, &tmB, bfull, kb * BK, n0 + j * 64);
+      }
+      int kc = 0;
+      for (int it = 0; it < my_tiles && ok; ++it) {
+        const int m0 = (m_first + it * m_stride) * BM;
+        for (int kb = 0; kb < KB; ++kb, ++kc) {
+          const int s = kc % STAGES;
+          if (kc >= STAGES && !(ok = mbar_wait(&empty[s], ((kc / STAGES) - 1) & 1, g.err, DEV_ERR_TIMEOUT_PRODUCER)))
+            break;
+          uint8_t* st = ring + s * Ly::STAGE;
+          mbar_arrive_expect_tx(&full[s], Ly::STAGE);
+          tma_load_2d(st, &tmA, &full[s], kb * BK, m0);
+          if constexpr (!RES) {
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(st + A_STAGE + j * 64 * BK, &tmB, &full[s], kb * BK, n0 + j * 64);
+          }
         }
       }
-      mma_commit(&empty[s]);
     }
-    if (ok) mma_commit(accfull);
-  }
-  __syncwarp();
-
-  // ---------------- epilogue: thread = row
-  ok = mbar_wait(accfull, 0, g.err, DEV_ERR_TIMEOUT_EPILOGUE);
-  ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld/st are warp-collective: keep the warp uniform
-  tc_fence_after();
-  const int row = m0 + warp * 32 + lane;
-  const bool valid = ok && row < g.M;
-  const uint32_t trow = tmem + (uint32_t(warp * 32) << 16);
-  const float as = valid ? g.a_scale[row] : 0.0f;
-  uint32_t r[32];
-
-  if constexpr (EPI == EPI_F32) {
-    if (ok) {
-      for (int c = 0; c < BN / 32; ++c) {
-        tmem_ld32(trow + c * 32, r);
-        tmem_ld_wait();
-        if (valid) {
-          float* o = g.out_f32 + size_t(row) * g.ldo + n0 + c * 32;
-          const float* rs = g.res ? g.res + size_t(row) * g.ldr + n0 + c * 32 : nullptr;
-          if (g.acc_dbg) {
-            int4* ad = reinterpret_cast<int4*>(g.acc_dbg + size_t(row) * g.N + n0 + c * 32);
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      bool ok = true;
+      if constexpr (RES) ok = mbar_wait(bfull, 0, g.err, DEV_ERR_TIMEOUT_MMA);
+      constexpr uint32_t idesc = idesc_i8(BM, Ly::NSUB);
+      int kc = 0;
+      for (int it = 0; it < my_tiles && ok; ++it) {
+        const int b = it % NB, u = it / NB;
+        if (u >= 1 && !(ok = mbar_wait(&acc_empty[b], (u - 1) & 1, g.err, DEV_ERR_TIMEOUT_MMA))) break;
+        tc_fence_after();
+        const uint32_t d = tmem + uint32_t(b * BN);
+        for (int kb = 0; kb < KB; ++kb, ++kc) {
+          const int s = kc % STAGES;
+          if (!(ok = mbar_wait(&full[s], (kc / STAGES) & 1, g.err, DEV_ERR_TIMEOUT_MMA))) break;
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(ring + s * Ly::STAGE);
+          const uint32_t b_addr = RES ? smem_u32(b_res + kb * BN * BK) : a_addr + A_STAGE;
 #pragma unroll
-            for (int q = 0; q < 8; ++q)
+          for (int ks = 0; ks < BK / 32; ++ks) {
+            const uint64_t ad = sdesc_sw128(a_addr + ks * 32);
+#pragma unroll
+            for (int j = 0; j < BN / Ly::NSUB; ++j)
+              mma_i8(d + j * Ly::NSUB, ad, sdesc_sw128(b_addr + j * Ly::NSUB * BK + ks * 32), idesc, (kb | ks) != 0);
+          }
+          mma_commit(&empty[s]);
+        }
+        if (ok) mma_commit(&acc_full[b]);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------ epilogue
+    const int ew = warp - 2;       // 0..15
+    const int Q = warp & 3;        // TMEM lane quadrant this warp may access
+    const int qq = ew >> 2;        // column quarter (F32, GELU) / reduction-lane group (LN)
+    const int rt = Q * 32 + lane;  // row within the tile
+    const uint32_t tq = tmem + (uint32_t(Q * 32) << 16);
+    bool ok = true;
+    for (int it = 0; it < my_tiles; ++it) {
+      const int b = it % NB, u = it / NB;
+      if (ok) ok = mbar_wait(&acc_full[b], u & 1, g.err, DEV_ERR_TIMEOUT_EPILOGUE);
+      ok = __all_sync(0xffffffffu, ok);
+      tc_fence_after();
+      const int m0 = (m_first + it * m_stride) * BM;
+      const int row = m0 + rt;
+      const bool valid = ok && row < g.M;
+      const float as = valid ? g.a_scale[row] : 0.0f;
+      const uint32_t tb = tq + uint32_t(b * BN);
+
+      if constexpr (EPI == EPI_F32) {
+        constexpr int CW = BN / 4;
+        const int c0 = qq * CW;
+        uint32_t r[CW];
+        if (ok) {
+#pragma unroll
+          for (int ch = 0; ch < CW / 16; ++ch) tmem_ld16(tb + c0 + ch * 16, r + ch * 16);
+          tmem_ld_wait();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[b]);
+        if (valid) {
+          if (g.acc_dbg) {
+            int4* ad = reinterpret_cast<int4*>(g.acc_dbg + size_t(row) * g.N + n0 + c0);
+#pragma unroll
+            for (int q = 0; q < CW / 4; ++q)
               ad[q] = make_int4(int(r[4 * q]), int(r[4 * q + 1]), int(r[4 * q + 2]), int(r[4 * q + 3]));
           }
+          float* o = g.out_f32 + size_t(row) * g.ldo + n0 + c0;
+          const float* rs = g.res ? g.res + size_t(row) * g.ldr + n0 + c0 : nullptr;
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
+          for (int q = 0; q < CW / 4; ++q) {
             float v[4];
+            float4 rr = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (rs) rr = reinterpret_cast<const float4*>(rs)[q];
+            const float rv[4] = {rr.x, rr.y, rr.z, rr.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const int j = 4 * q + e;
-              const int n = c * 32 + j;
-              float b = s_bias[n];
-              if (rs) b = b + rs[j];
-              v[e] = fmaf(float(int(r[j])), as * s_ws[n], b);
+              float bb = s_bias[c0 + j];
+              if (rs) bb = bb + rv[e];
+              v[e] = fmaf(float(int(r[j])), as * s_ws[c0 + j], bb);
             }
             reinterpret_cast<float4*>(o)[q] = make_float4(v[0], v[1], v[2], v[3]);
           }
         }
-      }
-    }
-  } else if constexpr (EPI == EPI_LN_QUANT || EPI == EPI_LN_FINAL) {
-    static_assert(BN == kHidden, "row-LayerNorm epilogue needs the full 384-wide row");
-    if (ok) {
-      // pass 1: h = fma(acc, as*ws, bias + res); partial sums; h -> TMEM
-      float p[16];
-      float seq = 0.0f;
+      } else if constexpr (EPI == EPI_GELU_QUANT) {
+        constexpr int CW = BN / 4;  // 64
+        const int c0 = qq * CW;
+        const int par = it & 1;
+        const uint32_t rank = cluster_ctarank();
+        float* xg = xch + par * 4 * BM;                           // [4][BM] maxima of the column quarters
+        float* rmx = xch + 2 * 4 * BM + par * kGeluCluster * BM;  // [6][BM] maxima of the cluster CTAs
+        uint32_t r[CW];
+        if (ok) {
 #pragma unroll
-      for (int l = 0; l < 16; ++l) p[l] = 0.0f;
-      for (int c = 0; c < BN / 32; ++c) {
-        tmem_ld32(trow + c * 32, r);
-        tmem_ld_wait();
-        float h[32];
-        if (valid) {
-          const float* rs = g.res + size_t(row) * g.ldr + c * 32;
-          if (g.acc_dbg) {
-            int4* ad = reinterpret_cast<int4*>(g.acc_dbg + size_t(row) * g.N + c * 32);
-#pragma unroll
-            for (int q = 0; q < 8; ++q)
-              ad[q] = make_int4(int(r[4 * q]), int(r[4 * q + 1]), int(r[4 * q + 2]), int(r[4 * q + 3]));
-          }
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const float4 rv = reinterpret_cast<const float4*>(rs)[q];
-            const float rr[4] = {rv.x, rv.y, rv.z, rv.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int j = 4 * q + e;
-              const int n = c * 32 + j;
-              h[j] = fmaf(float(int(r[j])), as * s_ws[n], s_bias[n] + rr[e]);
-            }
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) h[j] = 0.0f;
-        }
-        if constexpr (EPI == EPI_LN_QUANT) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) p[j] = p[j] + h[j];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) p[j] = p[j] + h[16 + j];
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) seq = seq + h[j];
-        }
-#pragma unroll
-        for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(h[j]);
-        tmem_st32(trow + c * 32, r);
-      }
-      tmem_st_wait();
-      const float mean = (EPI == EPI_LN_QUANT ? tree16(p) : seq) / float(kHidden);
-      // pass 2: variance
-#pragma unroll
-      for (int l = 0; l < 16; ++l) p[l] = 0.0f;
-      seq = 0.0f;
-      for (int c = 0; c < BN / 32; ++c) {
-        tmem_ld32(trow + c * 32, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float d = __uint_as_float(r[j]) - mean;
-          if constexpr (EPI == EPI_LN_QUANT) p[j & 15] = fmaf(d, d, p[j & 15]);
-          else seq = seq + d * d;
-        }
-      }
-      const float var = (EPI == EPI_LN_QUANT ? tree16(p) : seq) / float(kHidden);
-      const float rstd = 1.0f / sqrtf(var + kLnEps);
-      if constexpr (EPI == EPI_LN_QUANT) {
-        // pass 3: y = LN(h) -> residual out and TMEM; row max of |y * inv_smooth|
-        float vmax = 1e-8f;
-        for (int c = 0; c < BN / 32; ++c) {
-          tmem_ld32(trow + c * 32, r);
+          for (int ch = 0; ch < CW / 16; ++ch) tmem_ld16(tb + c0 + ch * 16, r + ch * 16);
           tmem_ld_wait();
-          float y[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int n = c * 32 + j;
-            y[j] = fmaf((__uint_as_float(r[j]) - mean) * rstd, s_gamma[n], s_beta[n]);
-            vmax = fmaxf(vmax, fabsf(y[j] * s_invs[n]));
-            r[j] = __float_as_uint(y[j]);
-          }
-          if (valid) {
-            float4* o = reinterpret_cast<float4*>(g.out_f32 + size_t(row) * g.ldo + c * 32);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) o[q] = make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
-          }
-          tmem_st32(trow + c * 32, r);
         }
-        tmem_st_wait();
-        // pass 4: quantize
-        const float max_abs = vmax;
-        const float inv_scale = 127.0f / max_abs;
-        for (int c = 0; c < BN / 32; ++c) {
-          tmem_ld32(trow + c * 32, r);
-          tmem_ld_wait();
-          uint32_t pk[8];
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            uint32_t w = 0;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int n = c * 32 + 4 * q + e;
-              const int qi = quant_i8(__uint_as_float(r[4 * q + e]) * (s_invs[n] * inv_scale));
-              w |= (uint32_t(qi) & 0xFFu) << (8 * e);
-            }
-            pk[q] = w;
-          }
-          if (valid) {
-            uint4* qo = reinterpret_cast<uint4*>(g.out_q + size_t(row) * kHidden + c * 32);
-            qo[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-            qo[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-          }
-        }
-        if (valid) g.out_scale[row] = max_abs / 127.0f;
-      } else {
-        // EPI_LN_FINAL: y = (h - mean) * rstd * gamma + beta (unfused), then L2 normalize
-        float ss = 0.0f;
-        for (int c = 0; c < BN / 32; ++c) {
-          tmem_ld32(trow + c * 32, r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int n = c * 32 + j;
-            const float y = (__uint_as_float(r[j]) - mean) * rstd * s_gamma[n] + s_beta[n];
-            ss = ss + y * y;
-            r[j] = __float_as_uint(y);
-          }
-          tmem_st32(trow + c * 32, r);
-        }
-        tmem_st_wait();
-        const float inv_norm = ss > 0.0f ? 1.0f / sqrtf(ss) : 1.0f;
-        for (int c = 0; c < BN / 32; ++c) {
-          tmem_ld32(trow + c * 32, r);
-          tmem_ld_wait();
-          if (valid) {
-            float4* o = reinterpret_cast<float4*>(g.out_f32 + size_t(row) * g.ldo + c * 32);
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              float v[4];
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float y = __uint_as_float(r[4 * q + e]);
-                v[e] = ss > 0.0f ? y * inv_norm : y;
-              }
-              o[q] = make_float4(v[0], v[1], v[2], v[3]);
-            }
-          }
-        }
-      }
-    }
-  } else if constexpr (EPI == EPI_GELU_QUANT) {
-    // 3 CTAs of a cluster hold columns [512 r, 512 r + 512) of the same 128 rows.
-    const uint32_t rank = cluster_ctarank();
-    float vmax = 1e-8f;
-    if (ok) {
-      for (int c = 0; c < BN / 32; ++c) {
-        tmem_ld32(trow + c * 32, r);
-        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[b]);
         if (valid && g.acc_dbg) {
-          int4* ad = reinterpret_cast<int4*>(g.acc_dbg + size_t(row) * g.N + n0 + c * 32);
+          int4* ad = reinterpret_cast<int4*>(g.acc_dbg + size_t(row) * g.N + n0 + c0);
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
+          for (int q = 0; q < CW / 4; ++q)
             ad[q] = make_int4(int(r[4 * q]), int(r[4 * q + 1]), int(r[4 * q + 2]), int(r[4 * q + 3]));
         }
+        float vmax = 1e-8f;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int n = c * 32 + j;
-          const float h = fmaf(float(int(r[j])), as * s_ws[n], s_bias[n]);
-          const float gv = (g.gelu_erf ? gelu_erf(h) : gelu_ref(h)) * s_invs[n];
+        for (int j = 0; j < CW; ++j) {
+          const int c = c0 + j;
+          const float h = fmaf(float(int(r[j])), as * s_ws[c], s_bias[c]);
+          const float gv = (g.gelu_erf ? gelu_erf(h) : gelu_ref(h)) * s_invs[c];
           vmax = fmaxf(vmax, fabsf(gv));
           r[j] = __float_as_uint(gv);
         }
-        tmem_st32(trow + c * 32, r);
-      }
-      tmem_st_wait();
-    }
-    // exchange the partial row maxima across the cluster (every thread takes part, error or not)
-    cluster_wait_acquire();  // all peers have started
+        xg[qq * BM + rt] = vmax;
+        named_bar(1 + Q, 128);
+        const float cta_max = fmaxf(fmaxf(xg[rt], xg[BM + rt]), fmaxf(xg[2 * BM + rt], xg[3 * BM + rt]));
+        if (ew == 0 && lane == 0) mbar_arrive_expect_tx(&rmx_bar[par], kGeluCluster * BM * 4);
+        if (qq == 0) {
 #pragma unroll
-    for (uint32_t q = 0; q < 3; ++q) st_cluster_f32(map_peer(&s_rowmax[rank * BM + tid], q), vmax);
-    cluster_arrive_release();
-    cluster_wait_acquire();
-    const float max_abs = fmaxf(fmaxf(s_rowmax[tid], s_rowmax[BM + tid]), s_rowmax[2 * BM + tid]);
-    const float inv_scale = 127.0f / max_abs;
-    if (ok) {
-      for (int c = 0; c < BN / 32; ++c) {
-        tmem_ld32(trow + c * 32, r);
-        tmem_ld_wait();
-        uint32_t pk[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          uint32_t w = 0;
-#pragma unroll
-          for (int e = 0; e < 4; ++e)
-            w |= (uint32_t(quant_i8(__uint_as_float(r[4 * q + e]) * inv_scale)) & 0xFFu) << (8 * e);
-          pk[q] = w;
+          for (uint32_t q = 0; q < kGeluCluster; ++q)
+            st_async_f32(map_peer(&rmx[rank * BM + rt], q), cta_max, map_peer(&rmx_bar[par], q));
         }
+        if (ok) ok = mbar_wait(&rmx_bar[par], (it >> 1) & 1, g.err, DEV_ERR_TIMEOUT_EPILOGUE);
+        float max_abs = rmx[rt];
+#pragma unroll
+        for (int q = 1; q < kGeluCluster; ++q) max_abs = fmaxf(max_abs, rmx[q * BM + rt]);
+        const float inv_scale = 127.0f / max_abs;
         if (valid) {
-          uint4* qo = reinterpret_cast<uint4*>(g.out_q + size_t(row) * g.N + n0 + c * 32);
-          qo[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-          qo[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          uint32_t pk[CW / 4];
+#pragma unroll
+          for (int q = 0; q < CW / 4; ++q) {
+            uint32_t w = 0;
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              w |= (uint32_t(quant_i8(__uint_as_float(r[4 * q + e]) * inv_scale)) & 0xFFu) << (8 * e);
+            pk[q] = w;
+          }
+          uint4* qo = reinterpret_cast<uint4*>(g.out_q + size_t(row) * g.N + n0 + c0);
+#pragma unroll
+          for (int q = 0; q < CW / 16; ++q) qo[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          if (rank == 0 && qq == 0) g.out_scale[row] = max_abs / 127.0f;
         }
+      } else if constexpr (EPI == EPI_LN_QUANT) {
+        static_assert(BN == kHidden, "row-LayerNorm epilogue needs the full 384-wide row");
+        float* xs = xch;                 // [BM][16] partial sums
+        float* xv = xch + BM * 16;       // [BM][16] partial sums of squares
+        float* xm = xch + 2 * BM * 16;   // [BM][4]  partial maxima
+        const int cq = 4 * qq;           // first owned column of every 16-column block
+        uint32_t r[24];
+        float p[4] = {0.f, 0.f, 0.f, 0.f};
+        // pass 1: h = fma(acc, as * ws, bias + res) -> TMEM; partial sums (chains of lanes cq..cq+3)
+        if (ok) {
+          for (int k0 = 0; k0 < 24; k0 += 6) {
+#pragma unroll
+            for (int k = 0; k < 6; ++k) tmem_ld4(tb + 16 * (k0 + k) + cq, r + 4 * k);
+            tmem_ld_wait();
+#pragma unroll
+            for (int k = 0; k < 6; ++k) {
+              const int c = 16 * (k0 + k) + cq;
+              float4 rr = make_float4(0.f, 0.f, 0.f, 0.f);
+              if (valid) rr = *reinterpret_cast<const float4*>(g.res + size_t(row) * g.ldr + c);
+              const float rv[4] = {rr.x, rr.y, rr.z, rr.w};
+              if (valid && g.acc_dbg)
+                *reinterpret_cast<int4*>(g.acc_dbg + size_t(row) * g.N + c) =
+                    make_int4(int(r[4 * k]), int(r[4 * k + 1]), int(r[4 * k + 2]), int(r[4 * k + 3]));
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float h = fmaf(float(int(r[4 * k + e])), as * s_ws[c + e], s_bias[c + e] + rv[e]);
+                p[e] = p[e] + h;
+                r[4 * k + e] = __float_as_uint(h);
+              }
+              tmem_st4(tb + c, r + 4 * k);
+            }
+          }
+          tmem_st_wait();
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) xs[rt * 16 + cq + e] = p[e];
+        named_bar(1 + Q, 128);
+        float pp[16];
+#pragma unroll
+        for (int l = 0; l < 16; ++l) pp[l] = xs[rt * 16 + l];
+        const float mean = tree16(pp) / float(kHidden);
+        // pass 2: variance
+#pragma unroll
+        for (int e = 0; e < 4; ++e) p[e] = 0.0f;
+        if (ok) {
+          for (int k0 = 0; k0 < 24; k0 += 6) {
+#pragma unroll
+            for (int k = 0; k < 6; ++k) tmem_ld4(tb + 16 * (k0 + k) + cq, r + 4 * k);
+            tmem_ld_wait();
+#pragma unroll
+            for (int k = 0; k < 6; ++k)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float d = __uint_as_float(r[4 * k + e]) - mean;
+                p[e] = fmaf(d, d, p[e]);
+              }
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) xv[rt * 16 + cq + e] = p[e];
+        named_bar(1 + Q, 128);
+#pragma unroll
+        for (int l = 0; l < 16; ++l) pp[l] = xv[rt * 16 + l];
+        const float var = tree16(pp) / float(kHidden);
+        const float rstd = 1.0f / sqrtf(var + kLnEps);
+        // pass 3: y = LN(h) -> residual out and TMEM; max |y * inv_smooth|
+        float vmax = 1e-8f;
+        if (ok) {
+          for (int k0 = 0; k0 < 24; k0 += 6) {
+#pragma unroll
+            for (int k = 0; k < 6; ++k) tmem_ld4(tb + 16 * (k0 + k) + cq, r + 4 * k);
+            tmem_ld_wait();
+#pragma unroll
+            for (int k = 0; k < 6; ++k) {
+              const int c = 16 * (k0 + k) + cq;
+              float y[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                y[e] = fmaf((__uint_as_float(r[4 * k + e]) - mean) * rstd, s_gamma[c + e], s_beta[c + e]);
+                vmax = fmaxf(vmax, fabsf(y[e] * s_invs[c + e]));
+                r[4 * k + e] = __float_as_uint(y[e]);
+              }
+              if (valid) *reinterpret_cast<float4*>(g.out_f32 + size_t(row) * g.ldo + c) = make_float4(y[0], y[1], y[2], y[3]);
+              tmem_st4(tb + c, r + 4 * k);
+            }
+          }
+          tmem_st_wait();
+        }
+        xm[rt * 4 + qq] = vmax;
+        named_bar(1 + Q, 128);
+        const float max_abs = fmaxf(fmaxf(xm[rt * 4], xm[rt * 4 + 1]), fmaxf(xm[rt * 4 + 2], xm[rt * 4 + 3]));
+        const float inv_scale = 127.0f / max_abs;
+        // pass 4: quantize
+        if (ok) {
+          for (int k0 = 0; k0 < 24; k0 += 6) {
+#pragma unroll
+            for (int k = 0; k < 6; ++k) tmem_ld4(tb + 16 * (k0 + k) + cq, r + 4 * k);
+            tmem_ld_wait();
+#pragma unroll
+            for (int k = 0; k < 6; ++k) {
+              const int c = 16 * (k0 + k) + cq;
+              uint32_t w = 0;
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                w |= (uint32_t(quant_i8(__uint_as_float(r[4 * k + e]) * (s_invs[c + e] * inv_scale))) & 0xFFu) << (8 * e);
+              if (valid) *reinterpret_cast<uint32_t*>(g.out_q + size_t(row) * kHidden + c) = w;
+            }
+          }
+        }
+        if (valid && qq == 0) g.out_scale[row] = max_abs / 127.0f;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[b]);
+      } else {  // EPI_LN_FINAL
+        static_assert(BN == kHidden, "row-LayerNorm epilogue needs the full 384-wide row");
+        const int cq = 4 * qq;
+        uint32_t r[32];
+        // pass 1 (all 4 warps of the quadrant): h = fma(acc, as * ws, bias + res) -> TMEM
+        if (ok) {
+          for (int k0 = 0; k0 < 24; k0 += 6) {
+#pragma unroll
+            for (int k = 0; k < 6; ++k) tmem_ld4(tb + 16 * (k0 + k) + cq, r + 4 * k);
+            tmem_ld_wait();
+#pragma unroll
+            for (int k = 0; k < 6; ++k) {
+              const int c = 16 * (k0 + k) + cq;
+              float4 rr = make_float4(0.f, 0.f, 0.f, 0.f);
+              if (valid) rr = *reinterpret_cast<const float4*>(g.res + size_t(row) * g.ldr + c);
+              const float rv[4] = {rr.x, rr.y, rr.z, rr.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                r[4 * k + e] = __float_as_uint(fmaf(float(int(r[4 * k + e])), as * s_ws[c + e], s_bias[c + e] + rv[e]));
+              tmem_st4(tb + c, r + 4 * k);
+            }
+          }
+          tmem_st_wait();
+        }
+        tc_fence_before();
+        named_bar(1 + Q, 128);
+        tc_fence_after();
+        // the sequential sums of layernorm_inplace_row / l2_normalize_inplace: one warp per quadrant
+        if (qq == 0 && ok) {
+          float seq = 0.0f;
+          for (int c = 0; c < kHidden; c += 32) {
+            tmem_ld16(tb + c, r);
+            tmem_ld16(tb + c + 16, r + 16);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) seq = seq + __uint_as_float(r[j]);
+          }
+          const float mean = seq / float(kHidden);
+          seq = 0.0f;
+          for (int c = 0; c < kHidden; c += 32) {
+            tmem_ld16(tb + c, r);
+            tmem_ld16(tb + c + 16, r + 16);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float d = __uint_as_float(r[j]) - mean;
+              seq = seq + d * d;
+            }
+          }
+          const float rstd = 1.0f / sqrtf(seq / float(kHidden) + kLnEps);
+          float ss = 0.0f;
+          for (int c = 0; c < kHidden; c += 32) {
+            tmem_ld16(tb + c, r);
+            tmem_ld16(tb + c + 16, r + 16);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float y = (__uint_as_float(r[j]) - mean) * rstd * s_gamma[c + j] + s_beta[c + j];
+              ss = ss + y * y;
+            }
+          }
+          const float inv_norm = ss > 0.0f ? 1.0f / sqrtf(ss) : 1.0f;
+          for (int c = 0; c < kHidden; c += 32) {
+            tmem_ld16(tb + c, r);
+            tmem_ld16(tb + c + 16, r + 16);
+            tmem_ld_wait();
+            if (valid) {
+              float4* o = reinterpret_cast<float4*>(g.out_f32 + size_t(row) * g.ldo + c);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                float v[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int j = 4 * q + e;
+                  const float y = (__uint_as_float(r[j]) - mean) * rstd * s_gamma[c + j] + s_beta[c + j];
+                  v[e] = ss > 0.0f ? y * inv_norm : y;
+                }
+                o[q] = make_float4(v[0], v[1], v[2], v[3]);
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[b]);
       }
-      if (valid && rank == 0) g.out_scale[row] = max_abs / 127.0f;
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, TCOLS);
+  if constexpr (EPI == EPI_GELU_QUANT) {  // no CTA leaves while a peer may still write into it
+    cluster_arrive_release();
+    cluster_wait_acquire();
+  }
+  if (warp == 0) tmem_dealloc(tmem, Ly::TCOLS);
 }
 
 // ------------------------------------------------------------------------------------ host side
@@ -415,14 +546,14 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   return fn;
 }
 
-// Tensor map of a [rows, K] row-major int8 matrix, 128 x 128-byte boxes, 128-byte swizzle.
-int make_tmap_i8(CUtensorMap* map, const void* base, int rows, int K) {
+// Tensor map of a [rows, K] row-major int8 matrix: boxes of box_rows x 128 bytes, 128-byte swizzle.
+int make_tmap_i8(CUtensorMap* map, const void* base, int rows, int K, int box_rows) {
   auto enc = get_encode();
   if (!enc) return -1;
-  if ((reinterpret_cast<uintptr_t>(base) & 15) || (K % 16)) return -2;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (K % 16) || rows <= 0) return -2;
   cuuint64_t dims[2] = {cuuint64_t(K), cuuint64_t(rows)};
   cuuint64_t strides[1] = {cuuint64_t(K)};
-  cuuint32_t box[2] = {128, 128};
+  cuuint32_t box[2] = {128, cuuint32_t(box_rows)};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -430,69 +561,109 @@ int make_tmap_i8(CUtensorMap* map, const void* base, int rows, int K) {
   return r == CUDA_SUCCESS ? 0 : -3;
 }
 
-template <int BN, int EPI, int STAGES>
-static cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, cudaStream_t st,
-                          int cluster_x) {
-  using S = GemmSmem<BN, STAGES>;
-  auto kfn = k_gemm_i8<BN, EPI, STAGES>;
+static int num_sms() {
+  static int cache[kMaxDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDevices) return 148;
+  if (!cache[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+template <int BN, int EPI, bool RES, int STAGES>
+static int set_smem() {
+  return cudaFuncSetAttribute(k_gemm_i8<BN, EPI, RES, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              Layout<BN, EPI, RES, STAGES>::TOTAL) == cudaSuccess
+             ? 0
+             : -1;
+}
+
+template <int BN, int EPI, bool RES, int STAGES>
+static cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, cudaStream_t st) {
+  using Ly = Layout<BN, EPI, RES, STAGES>;
+  auto kfn = k_gemm_i8<BN, EPI, RES, STAGES>;
+  const int nt = g.N / BN;
+  const int mt = (g.M + BM - 1) / BM;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(g.N / BN, (g.M + BM - 1) / BM, 1);
-  cfg.blockDim = dim3(128, 1, 1);
-  cfg.dynamicSmemBytes = S::TOTAL;
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Ly::TOTAL;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
-  cfg.numAttrs = 0;
-  if (cluster_x > 1) {
+  int ctas;
+  if constexpr (EPI == EPI_GELU_QUANT) {
+    // nt == cluster size: the 6 CTAs of a cluster hold the 6 column slices of one 128-row tile
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = cluster_x;
+    attr[0].val.clusterDim.x = kGeluCluster;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    static int max_clusters[kMaxDevices] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!max_clusters[dev]) {
+      cfg.gridDim = dim3(kGeluCluster * 8, 1, 1);
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kfn, &cfg) != cudaSuccess || n <= 0) n = num_sms() / kGeluCluster;
+      max_clusters[dev] = n;
+    }
+    const int clusters = mt < max_clusters[dev] ? mt : max_clusters[dev];
+    ctas = kGeluCluster * clusters;
+  } else {
+    cfg.numAttrs = 0;
+    const int per_n = num_sms() / nt > 0 ? num_sms() / nt : 1;
+    ctas = nt * (mt < per_n ? mt : per_n);
   }
-  return cudaLaunchKernelEx(&cfg, kfn, ta, tb, g);
+  cfg.gridDim = dim3(ctas, 1, 1);
+  return cudaLaunchKernelEx(&cfg, kfn, ta, tb, g, nt, mt);
 }
 
 // Sets the dynamic shared-memory limit of every GEMM variant on the current device (called once per
 // device before any launch can be captured into a CUDA graph).
 int gemm_i8_prime() {
-  int dev = 0;
-  cudaGetDevice(&dev);
-  (void)dev;
-  const cudaError_t e[4] = {
-      cudaFuncSetAttribute(k_gemm_i8<128, EPI_F32, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           GemmSmem<128, 4>::TOTAL),
-      cudaFuncSetAttribute(k_gemm_i8<384, EPI_LN_QUANT, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           GemmSmem<384, 3>::TOTAL),
-      cudaFuncSetAttribute(k_gemm_i8<384, EPI_LN_FINAL, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           GemmSmem<384, 3>::TOTAL),
-      cudaFuncSetAttribute(k_gemm_i8<512, EPI_GELU_QUANT, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           GemmSmem<512, 2>::TOTAL)};
-  for (auto x : e)
-    if (x != cudaSuccess) return -1;
-  return 0;
+  int r = 0;
+  r |= set_smem<128, EPI_F32, true, 4>();
+  r |= set_smem<192, EPI_F32, true, 4>();
+  r |= set_smem<256, EPI_F32, true, 4>();
+  r |= set_smem<128, EPI_F32, false, 4>();
+  r |= set_smem<192, EPI_F32, false, 4>();
+  r |= set_smem<256, EPI_F32, false, 4>();
+  r |= set_smem<384, EPI_LN_QUANT, true, 3>();
+  r |= set_smem<384, EPI_LN_QUANT, false, 3>();
+  r |= set_smem<384, EPI_LN_FINAL, true, 3>();
+  r |= set_smem<384, EPI_LN_FINAL, false, 3>();
+  r |= set_smem<256, EPI_GELU_QUANT, true, 4>();
+  r |= set_smem<256, EPI_GELU_QUANT, false, 4>();
+  return r;
 }
 
 int gemm_i8_launch(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, cudaStream_t st) {
   if (g.M <= 0) return 0;
-  if (g.K % BK) return -10;
+  if (g.K % BK || g.K <= 0) return -10;
+  const bool res = g.K == kResK;
   cudaError_t e = cudaSuccess;
   switch (epi) {
     case EPI_F32:
-      if (g.N % 128) return -11;
-      e = launch<128, EPI_F32, 4>(ta, tb, g, st, 1);
+      if (g.N % 256 == 0) e = res ? launch<256, EPI_F32, true, 4>(ta, tb, g, st) : launch<256, EPI_F32, false, 4>(ta, tb, g, st);
+      else if (g.N % 192 == 0) e = res ? launch<192, EPI_F32, true, 4>(ta, tb, g, st) : launch<192, EPI_F32, false, 4>(ta, tb, g, st);
+      else if (g.N % 128 == 0) e = res ? launch<128, EPI_F32, true, 4>(ta, tb, g, st) : launch<128, EPI_F32, false, 4>(ta, tb, g, st);
+      else return -11;
       break;
     case EPI_LN_QUANT:
       if (g.N != kHidden) return -11;
-      e = launch<384, EPI_LN_QUANT, 3>(ta, tb, g, st, 1);
+      e = res ? launch<384, EPI_LN_QUANT, true, 3>(ta, tb, g, st) : launch<384, EPI_LN_QUANT, false, 3>(ta, tb, g, st);
       break;
     case EPI_LN_FINAL:
       if (g.N != kHidden) return -11;
-      e = launch<384, EPI_LN_FINAL, 3>(ta, tb, g, st, 1);
+      e = res ? launch<384, EPI_LN_FINAL, true, 3>(ta, tb, g, st) : launch<384, EPI_LN_FINAL, false, 3>(ta, tb, g, st);
       break;
     case EPI_GELU_QUANT:
-      if (g.N != 3 * 512) return -11;
-      e = launch<512, EPI_GELU_QUANT, 2>(ta, tb, g, st, 3);
+      if (g.N != kGeluCluster * 256) return -11;
+      e = res ? launch<256, EPI_GELU_QUANT, true, 4>(ta, tb, g, st) : launch<256, EPI_GELU_QUANT, false, 4>(ta, tb, g, st);
       break;
     default:
       return -12;

@@ -33,7 +33,11 @@ struct GemmArgs {
 };
 
 int gemm_i8_prime();
-int make_tmap_i8(CUtensorMap* map, const void* base, int rows, int K);
+// Tensor map of a [rows, K] row-major int8 matrix with boxes of box_rows x 128 bytes: 128 for
+// activations (A operands), 64 for weights (B operands, loaded in 64-row slices).
+int make_tmap_i8(CUtensorMap* map, const void* base, int rows, int K, int box_rows);
+constexpr int kBoxA = 128;
+constexpr int kBoxB = 64;
 int gemm_i8_launch(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, cudaStream_t st);
 
 }  // namespace ae
