@@ -37,11 +37,19 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __
 
 // Scores of the key pair (2i, 2i+1) stored as kp[d] = (k[2i][d], k[2i+1][d]).
 __device__ __forceinline__ float2 score_pair(const float (&q)[32], const float2* __restrict__ kp, bool grouped) {
+  float2 k[32];
+  const float4* k4 = reinterpret_cast<const float4*>(kp);  // 128-bit shared loads: two dims per load
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float4 t = k4[i];
+    k[2 * i] = f2(t.x, t.y);
+    k[2 * i + 1] = f2(t.z, t.w);
+  }
   float2 s8[8];
 #pragma unroll
   for (int l = 0; l < 8; ++l) {
-    const float2 a = fma2(f2(q[8 + l], q[8 + l]), kp[8 + l], mul2(f2(q[l], q[l]), kp[l]));
-    const float2 b = fma2(f2(q[24 + l], q[24 + l]), kp[24 + l], mul2(f2(q[16 + l], q[16 + l]), kp[16 + l]));
+    const float2 a = fma2(f2(q[8 + l], q[8 + l]), k[8 + l], mul2(f2(q[l], q[l]), k[l]));
+    const float2 b = fma2(f2(q[24 + l], q[24 + l]), k[24 + l], mul2(f2(q[16 + l], q[16 + l]), k[16 + l]));
     s8[l] = add2(a, b);
   }
   if (grouped)
@@ -67,31 +75,53 @@ __device__ __forceinline__ float2 cw_exp2(float2 x) {
   return mul2(p, pw);
 }
 
-// Stages the head's K and V of rows [s0, s0 + L) as key pairs (odd L: the last pair's second key is 0).
+constexpr int KPS = 34;  // float2 per staged key pair (32 dims + 2 pad: 16-byte aligned, fewer bank conflicts)
+
+__device__ __forceinline__ float ld_act(const float* p, int C, int tt, int t, int c) {
+  return tt ? p[tt_index(t, c, C)] : p[size_t(t) * C + c];
+}
+
+// Stages the head's K and V of rows [s0, s0 + L) as key pairs kp[p][d] = (k[2p][d], k[2p+1][d])
+// (odd L: the last pair's second key is 0). A warp covers 8 pairs x 4 dims per step, so the
+// tile-transposed rows it reads are contiguous.
 __device__ __forceinline__ void stage_kv_pairs(const AttnArgs& a, int s0, int L, int h, float2* kp, float2* vp) {
   const int pairs = (L + 1) >> 1;
-  for (int i = threadIdx.x; i < pairs * 8; i += blockDim.x) {
-    const int pr = i >> 3, c = (i & 7) * 4;
-    const int t0 = 2 * pr, t1 = t0 + 1;
-    const size_t b0 = size_t(s0 + t0) * a.kv_stride + h * 32 + c;
-    const float4 k0 = *reinterpret_cast<const float4*>(a.k + b0);
-    const float4 v0 = *reinterpret_cast<const float4*>(a.v + b0);
-    float4 k1 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = k1;
+  const int kc = a.k_col + 32 * h, vc = a.v_col + 32 * h;
+  const int groups = (pairs + 7) >> 3;  // 8-pair groups
+  for (int i = threadIdx.x; i < groups * 256; i += blockDim.x) {
+    const int w = i >> 5, l = i & 31;
+    const int g = w >> 3, dgrp = w & 7;  // warp-step: pair group g, dims 4*dgrp .. 4*dgrp+3
+    const int p = 8 * g + (l & 7), d = 4 * dgrp + (l >> 3);
+    if (p >= pairs) continue;
+    const int t0 = 2 * p, t1 = t0 + 1;
+    const float k0 = ld_act(a.kv, a.kv_C, a.kv_tt, s0 + t0, kc + d);
+    const float v0 = ld_act(a.kv, a.kv_C, a.kv_tt, s0 + t0, vc + d);
+    float k1 = 0.0f, v1 = 0.0f;
     if (t1 < L) {
-      const size_t b1 = b0 + a.kv_stride;
-      k1 = *reinterpret_cast<const float4*>(a.k + b1);
-      v1 = *reinterpret_cast<const float4*>(a.v + b1);
+      k1 = ld_act(a.kv, a.kv_C, a.kv_tt, s0 + t1, kc + d);
+      v1 = ld_act(a.kv, a.kv_C, a.kv_tt, s0 + t1, vc + d);
     }
-    float2* kd = kp + pr * 32 + c;
-    float2* vd = vp + pr * 32 + c;
-    kd[0] = f2(k0.x, k1.x);
-    kd[1] = f2(k0.y, k1.y);
-    kd[2] = f2(k0.z, k1.z);
-    kd[3] = f2(k0.w, k1.w);
-    vd[0] = f2(v0.x, v1.x);
-    vd[1] = f2(v0.y, v1.y);
-    vd[2] = f2(v0.z, v1.z);
-    vd[3] = f2(v0.w, v1.w);
+    kp[p * KPS + d] = f2(k0, k1);
+    vp[p * KPS + d] = f2(v0, v1);
+  }
+}
+
+__device__ __forceinline__ void load_query(const AttnArgs& a, int qrow, int h, float (&q)[32]) {
+  const float scale = 1.0f / sqrtf(32.0f);
+  if (a.q_tt) {
+    const float* qp = a.q + tt_index(qrow, a.q_col + 32 * h, a.q_C);
+#pragma unroll
+    for (int d = 0; d < 32; ++d) q[d] = qp[size_t(d) << 7] * scale;
+  } else {
+    const float4* qp = reinterpret_cast<const float4*>(a.q + size_t(qrow) * a.q_C + a.q_col + 32 * h);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 t = qp[i];
+      q[4 * i] = t.x * scale;
+      q[4 * i + 1] = t.y * scale;
+      q[4 * i + 2] = t.z * scale;
+      q[4 * i + 3] = t.w * scale;
+    }
   }
 }
 
@@ -114,33 +144,22 @@ __global__ void __launch_bounds__(QT) k_attention_rows(AttnArgs a) {
 
   const int pairs = (L + 1) >> 1;
   float2* kp = reinterpret_cast<float2*>(smem4);
-  float2* vp = kp + pairs * 32;
-  float* sc = reinterpret_cast<float*>(vp + pairs * 32);  // [L][QT] scores, then exponentials (STORE)
+  float2* vp = kp + pairs * KPS;
+  float* sc = reinterpret_cast<float*>(vp + pairs * KPS);  // [L][QT] scores, then exponentials (STORE)
   stage_kv_pairs(a, s0, L, h, kp, vp);
   __syncthreads();
 
   const int qi = tile * QT + tid;
   if (qi >= L) return;
   const int qrow = s0 + qi;
-  const float scale = 1.0f / sqrtf(32.0f);
   float q[32];
-  {
-    const float4* qp = reinterpret_cast<const float4*>(a.q + size_t(qrow) * a.q_stride + h * 32);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float4 t = qp[i];
-      q[4 * i] = t.x * scale;
-      q[4 * i + 1] = t.y * scale;
-      q[4 * i + 2] = t.z * scale;
-      q[4 * i + 3] = t.w * scale;
-    }
-  }
+  load_query(a, qrow, h, q);
   const int L4 = L & ~3, L8 = L & ~7, L16 = L & ~15;
 
   // pass 1: scores and their max
   float mx = -INFINITY;
   for (int i = 0; i < pairs; ++i) {
-    const float2 sp = score_pair(q, kp + i * 32, 2 * i < L4);
+    const float2 sp = score_pair(q, kp + i * KPS, 2 * i < L4);
     if (STORE) {
       sc[(2 * i) * QT + tid] = sp.x;
       if (2 * i + 1 < L) sc[(2 * i + 1) * QT + tid] = sp.y;
@@ -152,7 +171,7 @@ __global__ void __launch_bounds__(QT) k_attention_rows(AttnArgs a) {
 
   auto score2 = [&](int t) -> float2 {  // scores of keys t, t+1 (t even)
     if (STORE) return f2(sc[t * QT + tid], (t + 1 < L) ? sc[(t + 1) * QT + tid] : 0.0f);
-    return score_pair(q, kp + (t >> 1) * 32, t < L4);
+    return score_pair(q, kp + (t >> 1) * KPS, t < L4);
   };
   auto put2 = [&](int t, float2 e) {
     if (STORE) {
@@ -207,7 +226,7 @@ __global__ void __launch_bounds__(QT) k_attention_rows(AttnArgs a) {
   // pass 3: probabilities and the weighted sum of V; lane x = even keys (a), lane y = odd keys (b)
   auto exps2 = [&](int t) -> float2 {  // exponentials of keys t, t+1 (t even; 0 past the end)
     if (STORE) return f2(sc[t * QT + tid], (t + 1 < L) ? sc[(t + 1) * QT + tid] : 0.0f);
-    const float2 x = add2(score_pair(q, kp + (t >> 1) * 32, t < L4), neg_mx);
+    const float2 x = add2(score_pair(q, kp + (t >> 1) * KPS, t < L4), neg_mx);
     if (t + 1 < L8) return cw_exp2(x);
     return f2(scalar_expf(x.x), (t + 1 < L) ? scalar_expf(x.y) : 0.0f);  // t >= L8 here
   };
@@ -217,17 +236,21 @@ __global__ void __launch_bounds__(QT) k_attention_rows(AttnArgs a) {
   const int full_pairs = L >> 1;
   for (int i = 0; i < full_pairs; ++i) {
     const float2 p = mul2(exps2(2 * i), inv2);
-    const float2* v = vp + i * 32;
+    const float4* v4 = reinterpret_cast<const float4*>(vp + i * KPS);
 #pragma unroll
-    for (int d = 0; d < 32; ++d) acc[d] = fma2(v[d], p, acc[d]);
+    for (int j = 0; j < 16; ++j) {
+      const float4 t = v4[j];
+      acc[2 * j] = fma2(f2(t.x, t.y), p, acc[2 * j]);
+      acc[2 * j + 1] = fma2(f2(t.z, t.w), p, acc[2 * j + 1]);
+    }
   }
   if (L & 1) {
     const float pa = exps2(L - 1).x * inv;
-    const float2* v = vp + (L >> 1) * 32;
+    const float2* v = vp + (L >> 1) * KPS;
 #pragma unroll
     for (int d = 0; d < 32; ++d) acc[d].x = fmaf(v[d].x, pa, acc[d].x);
   }
-  float4* o = reinterpret_cast<float4*>(a.out + size_t(qrow) * a.out_stride + h * 32);
+  float4* o = reinterpret_cast<float4*>(a.out + size_t(qrow) * kHidden + h * 32);
 #pragma unroll
   for (int i = 0; i < 8; ++i)
     o[i] = make_float4(acc[4 * i].x + acc[4 * i].y, acc[4 * i + 1].x + acc[4 * i + 1].y,
@@ -235,6 +258,9 @@ __global__ void __launch_bounds__(QT) k_attention_rows(AttnArgs a) {
 }
 
 // One warp per (sequence, head): the single [CLS] query (row s of q / out) over the sequence's keys.
+// Shared memory per warp: the scores / exponentials (512 floats) and a 32-key x 32-dim V chunk.
+constexpr int kClsWarpFloats = kMaxPos + 32 * 33;
+
 __global__ void __launch_bounds__(128) k_attention_cls(AttnArgs a, int n_seqs) {
   extern __shared__ float4 smem4[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -247,33 +273,17 @@ __global__ void __launch_bounds__(128) k_attention_cls(AttnArgs a, int n_seqs) {
     if (lane == 0) record_err(a.err, DEV_ERR_BAD_SHAPE);
     return;
   }
-  float* sc = reinterpret_cast<float*>(smem4) + warp * kMaxPos;  // scores, then exponentials
-  const float scale = 1.0f / sqrtf(32.0f);
+  float* sc = reinterpret_cast<float*>(smem4) + warp * kClsWarpFloats;  // scores, then exponentials
+  float* vs = sc + kMaxPos;                                              // [32 keys][33]
   float q[32];
-  {
-    const float4* qp = reinterpret_cast<const float4*>(a.q + size_t(s) * a.q_stride + h * 32);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float4 t = qp[i];
-      q[4 * i] = t.x * scale;
-      q[4 * i + 1] = t.y * scale;
-      q[4 * i + 2] = t.z * scale;
-      q[4 * i + 3] = t.w * scale;
-    }
-  }
+  load_query(a, s, h, q);
+  const int kc = a.k_col + 32 * h, vc = a.v_col + 32 * h;
   const int L4 = L & ~3, L8 = L & ~7, L16 = L & ~15;
   float mx = -INFINITY;
   for (int t = lane; t < L; t += 32) {
-    const float4* k4 = reinterpret_cast<const float4*>(a.k + size_t(s0 + t) * a.kv_stride + h * 32);
     float kk[32];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float4 v = k4[i];
-      kk[4 * i] = v.x;
-      kk[4 * i + 1] = v.y;
-      kk[4 * i + 2] = v.z;
-      kk[4 * i + 3] = v.w;
-    }
+    for (int d = 0; d < 32; ++d) kk[d] = ld_act(a.kv, a.kv_C, a.kv_tt, s0 + t, kc + d);
     float s8[8];
 #pragma unroll
     for (int l = 0; l < 8; ++l)
@@ -302,22 +312,30 @@ __global__ void __launch_bounds__(128) k_attention_cls(AttnArgs a, int n_seqs) {
   sum = __shfl_sync(0xffffffffu, sum, 0);
   for (int t = L8; t < L; ++t) sum = sum + sc[t];
   const float inv = 1.0f / sum;
-  // weighted sum: lane = dim, accumulator a (even keys) and b (odd keys)
+  // weighted sum: lane = dim, accumulator a (even keys) and b (odd keys); V staged 32 keys at a time
   float acc_a = 0.0f, acc_b = 0.0f;
-  const float* vcol = a.v + size_t(s0) * a.kv_stride + h * 32 + lane;
-  int t = 0;
-  for (; t + 2 <= L; t += 2) {
-    acc_a = fmaf(vcol[size_t(t) * a.kv_stride], sc[t] * inv, acc_a);
-    acc_b = fmaf(vcol[size_t(t + 1) * a.kv_stride], sc[t + 1] * inv, acc_b);
+  for (int t0 = 0; t0 < L; t0 += 32) {
+    const int t = t0 + lane;
+    __syncwarp();
+    if (t < L) {
+#pragma unroll
+      for (int d = 0; d < 32; ++d) vs[lane * 33 + d] = ld_act(a.kv, a.kv_C, a.kv_tt, s0 + t, vc + d);
+    }
+    __syncwarp();
+    const int n = L - t0 < 32 ? L - t0 : 32;
+    for (int j = 0; j < n; ++j) {
+      const float p = sc[t0 + j] * inv;
+      if ((t0 + j) & 1) acc_b = fmaf(vs[j * 33 + lane], p, acc_b);
+      else acc_a = fmaf(vs[j * 33 + lane], p, acc_a);
+    }
   }
-  if (t < L) acc_a = fmaf(vcol[size_t(t) * a.kv_stride], sc[t] * inv, acc_a);
-  a.out[size_t(s) * a.out_stride + h * 32 + lane] = acc_a + acc_b;
+  a.out[size_t(s) * kHidden + h * 32 + lane] = acc_a + acc_b;
 }
 
 template <int QT, bool STORE>
 static size_t rows_smem(int max_len) {
   const int L = STORE ? (max_len < kStoreMaxLen ? max_len : kStoreMaxLen) : max_len;
-  return size_t((L + 1) / 2) * 32 * 8 * 2 + (STORE ? size_t(L) * QT * 4 : 0);
+  return size_t((L + 1) / 2) * KPS * 8 * 2 + (STORE ? size_t(L) * QT * 4 : 0);
 }
 
 template <int QT, bool STORE>
@@ -347,7 +365,7 @@ int attention_prime() {
   r |= smem_attr((const void*)k_attention_rows<128, false>, rows_smem<128, false>(kMaxPos));
   r |= smem_attr((const void*)k_attention_rows<64, false>, rows_smem<64, false>(kMaxPos));
   r |= smem_attr((const void*)k_attention_rows<32, false>, rows_smem<32, false>(kMaxPos));
-  r |= smem_attr((const void*)k_attention_cls, 4 * kMaxPos * 4);
+  r |= smem_attr((const void*)k_attention_cls, 4 * kClsWarpFloats * 4);
   return r;
 }
 
@@ -356,7 +374,7 @@ int launch_attention_exact(const AttnArgs& a, int n_seqs, cudaStream_t st) {
   if (a.max_len <= 0 || a.max_len > kMaxPos) return -1;
   if (a.cls_mode) {
     const int items = n_seqs * kHeads;
-    k_attention_cls<<<(items + 3) / 4, 128, 4 * kMaxPos * 4, st>>>(a, n_seqs);
+    k_attention_cls<<<(items + 3) / 4, 128, 4 * kClsWarpFloats * 4, st>>>(a, n_seqs);
     return cudaGetLastError() == cudaSuccess ? 0 : -3;
   }
   // query tile: 128 threads when the grid fills the GPU, smaller tiles for few sequences

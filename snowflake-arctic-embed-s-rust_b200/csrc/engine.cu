@@ -293,10 +293,14 @@ int reserve(ae_ctx* c, uint32_t tokens, uint32_t seqs) {
 }
 
 // ------------------------------------------------------------------------------------------ forward
+// `tt` selects the tile-transposed layout for the fp32 residual and output (the hidden state and
+// the QKV / KV outputs of the packed rows; the [CLS]-row buffers stay row-major).
 int gemm(ae_ctx* c, int epi, const CUtensorMap& ta, const DevLinear& L, int M, const float* a_scale, const float* res,
          int ldr, const float* gamma, const float* beta, const float* inv_next, float* out, int ldo, int8_t* out_q,
-         float* out_s) {
+         float* out_s, int tt = 0) {
   GemmArgs g{};
+  g.out_tt = tt;
+  g.res_tt = tt;
   g.M = M;
   g.N = L.n;
   g.K = L.k;
@@ -321,16 +325,19 @@ int gemm(ae_ctx* c, int epi, const CUtensorMap& ta, const DevLinear& L, int M, c
   return 0;
 }
 
-int attention(ae_ctx* c, const float* q, int qs, const float* k, const float* v, int kvs, float* out,
-              const uint32_t* cu, int n, int max_len, int cls) {
+int attention(ae_ctx* c, const float* q, int q_C, int q_col, int q_tt, const float* kv, int kv_C, int k_col,
+              int v_col, int kv_tt, float* out, const uint32_t* cu, int n, int max_len, int cls) {
   AttnArgs a{};
   a.q = q;
-  a.q_stride = qs;
-  a.k = k;
-  a.v = v;
-  a.kv_stride = kvs;
+  a.q_C = q_C;
+  a.q_col = q_col;
+  a.q_tt = q_tt;
+  a.kv = kv;
+  a.kv_C = kv_C;
+  a.k_col = k_col;
+  a.v_col = v_col;
+  a.kv_tt = kv_tt;
   a.out = out;
-  a.out_stride = kHidden;
   a.cu = cu;
   a.max_len = max_len;
   a.cls_mode = cls;
@@ -369,28 +376,28 @@ int enqueue_forward(ae_ctx* c, const uint16_t* d_ids, const uint32_t* d_cu, int 
   for (int l = 0; l + 1 < kLayers; ++l) {
     const DevLayer& Ly = M.layers[l];
     AE_TRY(gemm(c, EPI_F32, W.tm_act_q, Ly.qkv, T, W.act_s, nullptr, 0, nullptr, nullptr, nullptr, W.qkv, 3 * kHidden,
-                nullptr, nullptr));
-    AE_TRY(attention(c, W.qkv, 3 * kHidden, W.qkv + kHidden, W.qkv + 2 * kHidden, 3 * kHidden, W.ctx, d_cu, n, max_len,
+                nullptr, nullptr, 1));
+    AE_TRY(attention(c, W.qkv, 3 * kHidden, 0, 1, W.qkv, 3 * kHidden, kHidden, 2 * kHidden, 1, W.ctx, d_cu, n, max_len,
                      0));
     ++c->launches;
     if (launch_smooth_quant(W.ctx, Ly.ao.inv_s, W.act_q, W.act_s, T, st))
       return fail(c, AE_ERR_CUDA, "context quantization launch failed");
     AE_TRY(gemm(c, EPI_LN_QUANT, W.tm_act_q, Ly.ao, T, W.act_s, W.hidden, kHidden, Ly.ln1w, Ly.ln1b, Ly.fi.inv_s,
-                W.hidden, kHidden, W.act_q, W.act_s));
+                W.hidden, kHidden, W.act_q, W.act_s, 1));
     AE_TRY(gemm(c, EPI_GELU_QUANT, W.tm_act_q, Ly.fi, T, W.act_s, nullptr, 0, nullptr, nullptr, Ly.fo.inv_s, nullptr, 0,
                 W.inter_q, W.inter_s));
     AE_TRY(gemm(c, EPI_LN_QUANT, W.tm_inter_q, Ly.fo, T, W.inter_s, W.hidden, kHidden, Ly.ln2w, Ly.ln2b,
-                M.layers[l + 1].qkv.inv_s, W.hidden, kHidden, W.act_q, W.act_s));
+                M.layers[l + 1].qkv.inv_s, W.hidden, kHidden, W.act_q, W.act_s, 1));
   }
   const DevLayer& Z = M.layers[kLayers - 1];
   AE_TRY(gemm(c, EPI_F32, W.tm_act_q, Z.kv_only, T, W.act_s, nullptr, 0, nullptr, nullptr, nullptr, W.qkv, 2 * kHidden,
-              nullptr, nullptr));
+              nullptr, nullptr, 1));
   c->launches += 2;  // gather + [CLS] context quantization
   if (launch_gather_cls(W.cls_row, n, W.act_q, W.act_s, W.hidden, W.cq, W.cs, W.ch, st))
     return fail(c, AE_ERR_CUDA, "gather launch failed");
   AE_TRY(gemm(c, EPI_F32, W.tm_cq, Z.q_only, n, W.cs, nullptr, 0, nullptr, nullptr, nullptr, W.q_cls, kHidden, nullptr,
               nullptr));
-  AE_TRY(attention(c, W.q_cls, kHidden, W.qkv, W.qkv + kHidden, 2 * kHidden, W.cctx, d_cu, n, max_len, 1));
+  AE_TRY(attention(c, W.q_cls, kHidden, 0, 0, W.qkv, 2 * kHidden, 0, kHidden, 1, W.cctx, d_cu, n, max_len, 1));
   if (launch_smooth_quant(W.cctx, Z.ao.inv_s, W.cq, W.cs, n, st))
     return fail(c, AE_ERR_CUDA, "context quantization launch failed");
   AE_TRY(gemm(c, EPI_LN_QUANT, W.tm_cq, Z.ao, n, W.cs, W.ch, kHidden, Z.ln1w, Z.ln1b, Z.fi.inv_s, W.ch, kHidden, W.cq,
@@ -894,7 +901,7 @@ int ae_attention_f32(ae_ctx* c, const float* d_qkv, const uint32_t* d_cu, uint32
   if (!d_qkv || !d_cu || !d_ctx || max_len == 0 || max_len > uint32_t(kMaxPos))
     return fail(c, AE_ERR_INVALID_ARG, "ae_attention_f32: bad arguments");
   DeviceGuard g(c->device);
-  return attention(c, d_qkv, 3 * kHidden, d_qkv + kHidden, d_qkv + 2 * kHidden, 3 * kHidden, d_ctx, d_cu, int(n),
+  return attention(c, d_qkv, 3 * kHidden, 0, 0, d_qkv, 3 * kHidden, kHidden, 2 * kHidden, 0, d_ctx, d_cu, int(n),
                    int(max_len), 0);
 }
 

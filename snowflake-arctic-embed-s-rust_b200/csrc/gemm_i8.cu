@@ -66,10 +66,13 @@ struct Layout {
   static constexpr int STAGE = A_STAGE + (RES ? 0 : BN * BK);
   static constexpr int RING = STAGES * STAGE;
   static constexpr int PARAM_FLOATS = 3 * BN + 2 * kHidden;             // ws, bias, invs | gamma, beta
+  static constexpr int XCH_FLOATS_GELU = 2 * 4 * BM + 2 * kGeluCluster * BM;
+  static constexpr int STAGING_BYTES = EPI == EPI_GELU_QUANT ? kEpiWarps * 32 * 80 : 0;  // int8 output rows
   static constexpr int XCH_FLOATS =
-      LN ? (2 * BM * 16 + BM * 4) : (EPI == EPI_GELU_QUANT ? (2 * 4 * BM + 2 * kGeluCluster * BM) : 0);
+      LN ? (2 * BM * 16 + BM * 4) : (EPI == EPI_GELU_QUANT ? XCH_FLOATS_GELU + STAGING_BYTES / 4 : 0);
   static constexpr int NBARS = 2 * STAGES + 1 + 2 * 2 + 2;
   static constexpr int TOTAL = 1024 + B_RES + RING + 4 * (PARAM_FLOATS + XCH_FLOATS) + 8 * NBARS + 16;
+  static_assert(TOTAL <= 232448, "shared memory of one CTA exceeds the sm_100 limit");
 };
 
 template <int BN, int EPI, bool RES, int STAGES>
@@ -243,6 +246,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int q = 0; q < CW / 4; ++q)
               ad[q] = make_int4(int(r[4 * q]), int(r[4 * q + 1]), int(r[4 * q + 2]), int(r[4 * q + 3]));
           }
+          if (g.out_tt && !g.res) {  // one 128-byte line per column for the warp's 32 rows
+            float* o = g.out_f32 + tt_index(row, n0 + c0, g.ldo);
+#pragma unroll
+            for (int j = 0; j < CW; ++j)
+              o[size_t(j) << 7] = fmaf(float(int(r[j])), as * s_ws[c0 + j], s_bias[c0 + j]);
+            continue;
+          }
           float* o = g.out_f32 + size_t(row) * g.ldo + n0 + c0;
           const float* rs = g.res ? g.res + size_t(row) * g.ldr + n0 + c0 : nullptr;
 #pragma unroll
@@ -284,13 +294,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             ad[q] = make_int4(int(r[4 * q]), int(r[4 * q + 1]), int(r[4 * q + 2]), int(r[4 * q + 3]));
         }
         float vmax = 1e-8f;
+        if (g.gelu_erf) {
 #pragma unroll
-        for (int j = 0; j < CW; ++j) {
-          const int c = c0 + j;
-          const float h = fmaf(float(int(r[j])), as * s_ws[c], s_bias[c]);
-          const float gv = (g.gelu_erf ? gelu_erf(h) : gelu_ref(h)) * s_invs[c];
-          vmax = fmaxf(vmax, fabsf(gv));
-          r[j] = __float_as_uint(gv);
+          for (int j = 0; j < CW; ++j) {
+            const int c = c0 + j;
+            const float gv = gelu_erf(fmaf(float(int(r[j])), as * s_ws[c], s_bias[c])) * s_invs[c];
+            vmax = fmaxf(vmax, fabsf(gv));
+            r[j] = __float_as_uint(gv);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < CW; j += 2) {
+            const int c = c0 + j;
+            const float2 h = __ffma2_rn(make_float2(float(int(r[j])), float(int(r[j + 1]))),
+                                        __fmul2_rn(make_float2(as, as), make_float2(s_ws[c], s_ws[c + 1])),
+                                        make_float2(s_bias[c], s_bias[c + 1]));
+            const float2 gv = __fmul2_rn(gelu_ref2(h), make_float2(s_invs[c], s_invs[c + 1]));
+            vmax = fmaxf(vmax, fmaxf(fabsf(gv.x), fabsf(gv.y)));
+            r[j] = __float_as_uint(gv.x);
+            r[j + 1] = __float_as_uint(gv.y);
+          }
         }
         xg[qq * BM + rt] = vmax;
         named_bar(1 + Q, 128);
@@ -306,7 +329,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int q = 1; q < kGeluCluster; ++q) max_abs = fmaxf(max_abs, rmx[q * BM + rt]);
         const float inv_scale = 127.0f / max_abs;
-        if (valid) {
+        {
+          // quantize into this warp's staging slot (32 rows x 64 bytes, rows padded to 80 bytes),
+          // then write 8 rows x 64 contiguous bytes per store instruction
+          uint8_t* stg = reinterpret_cast<uint8_t*>(xch + Ly::XCH_FLOATS_GELU) + ew * (32 * 80);
           uint32_t pk[CW / 4];
 #pragma unroll
           for (int q = 0; q < CW / 4; ++q) {
@@ -316,10 +342,19 @@ __global__ void __launch_bounds__(kThreads, 1)
               w |= (uint32_t(quant_i8(__uint_as_float(r[4 * q + e]) * inv_scale)) & 0xFFu) << (8 * e);
             pk[q] = w;
           }
-          uint4* qo = reinterpret_cast<uint4*>(g.out_q + size_t(row) * g.N + n0 + c0);
 #pragma unroll
-          for (int q = 0; q < CW / 16; ++q) qo[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-          if (rank == 0 && qq == 0) g.out_scale[row] = max_abs / 127.0f;
+          for (int q = 0; q < CW / 16; ++q)
+            *reinterpret_cast<uint4*>(stg + lane * 80 + 16 * q) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int rr = 8 * i + (lane >> 2), q = lane & 3;
+            const int grow = m0 + Q * 32 + rr;
+            const uint4 v = *reinterpret_cast<const uint4*>(stg + rr * 80 + 16 * q);
+            if (ok && grow < g.M) *reinterpret_cast<uint4*>(g.out_q + size_t(grow) * g.N + n0 + c0 + 16 * q) = v;
+          }
+          __syncwarp();
+          if (valid && rank == 0 && qq == 0) g.out_scale[row] = max_abs / 127.0f;
         }
       } else if constexpr (EPI == EPI_LN_QUANT) {
         static_assert(BN == kHidden, "row-LayerNorm epilogue needs the full 384-wide row");
@@ -338,9 +373,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int k = 0; k < 6; ++k) {
               const int c = 16 * (k0 + k) + cq;
-              float4 rr = make_float4(0.f, 0.f, 0.f, 0.f);
-              if (valid) rr = *reinterpret_cast<const float4*>(g.res + size_t(row) * g.ldr + c);
-              const float rv[4] = {rr.x, rr.y, rr.z, rr.w};
+              float rv[4] = {0.f, 0.f, 0.f, 0.f};
+              if (valid) {
+                if (g.res_tt) {
+                  const float* rp = g.res + tt_index(row, c, g.ldr);
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) rv[e] = rp[e << 7];
+                } else {
+                  const float4 rr = *reinterpret_cast<const float4*>(g.res + size_t(row) * g.ldr + c);
+                  rv[0] = rr.x;
+                  rv[1] = rr.y;
+                  rv[2] = rr.z;
+                  rv[3] = rr.w;
+                }
+              }
               if (valid && g.acc_dbg)
                 *reinterpret_cast<int4*>(g.acc_dbg + size_t(row) * g.N + c) =
                     make_int4(int(r[4 * k]), int(r[4 * k + 1]), int(r[4 * k + 2]), int(r[4 * k + 3]));
@@ -403,7 +449,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 vmax = fmaxf(vmax, fabsf(y[e] * s_invs[c + e]));
                 r[4 * k + e] = __float_as_uint(y[e]);
               }
-              if (valid) *reinterpret_cast<float4*>(g.out_f32 + size_t(row) * g.ldo + c) = make_float4(y[0], y[1], y[2], y[3]);
+              if (valid) {
+                if (g.out_tt) {
+                  float* op = g.out_f32 + tt_index(row, c, g.ldo);
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) op[e << 7] = y[e];
+                } else {
+                  *reinterpret_cast<float4*>(g.out_f32 + size_t(row) * g.ldo + c) = make_float4(y[0], y[1], y[2], y[3]);
+                }
+              }
               tmem_st4(tb + c, r + 4 * k);
             }
           }
@@ -637,7 +691,7 @@ int gemm_i8_prime() {
   r |= set_smem<384, EPI_LN_FINAL, true, 3>();
   r |= set_smem<384, EPI_LN_FINAL, false, 3>();
   r |= set_smem<256, EPI_GELU_QUANT, true, 4>();
-  r |= set_smem<256, EPI_GELU_QUANT, false, 4>();
+  r |= set_smem<256, EPI_GELU_QUANT, false, 3>();
   return r;
 }
 
@@ -663,7 +717,7 @@ int gemm_i8_launch(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const 
       break;
     case EPI_GELU_QUANT:
       if (g.N != kGeluCluster * 256) return -11;
-      e = res ? launch<256, EPI_GELU_QUANT, true, 4>(ta, tb, g, st) : launch<256, EPI_GELU_QUANT, false, 4>(ta, tb, g, st);
+      e = res ? launch<256, EPI_GELU_QUANT, true, 4>(ta, tb, g, st) : launch<256, EPI_GELU_QUANT, false, 3>(ta, tb, g, st);
       break;
     default:
       return -12;

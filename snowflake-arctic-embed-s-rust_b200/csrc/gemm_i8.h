@@ -30,6 +30,8 @@ struct GemmArgs {
   int32_t* acc_dbg;         // [M, N] raw int32 accumulators, or nullptr
   int* err;                 // device error word
   int gelu_erf;             // EPI_GELU_QUANT: 0 = the reference's rational GELU, 1 = exact erf
+  int out_tt;               // out_f32 in the tile-transposed layout (ldo = its column count)
+  int res_tt;               // res in the tile-transposed layout (ldr = its column count)
 };
 
 int gemm_i8_prime();

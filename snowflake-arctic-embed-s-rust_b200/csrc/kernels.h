@@ -17,21 +17,23 @@ struct EmbedArgs {
   const float* gamma;         // embedding LayerNorm
   const float* beta;
   const float* inv_smooth;    // layers[0].qkv.inv_smooth
-  float* hidden;              // [T, 384] out
+  float* hidden;              // [T, 384] out, tile-transposed
   int8_t* act_q;              // [T, 384] out
   float* act_s;               // [T] out
   int* err;
 };
 
 struct AttnArgs {
-  const float* q;             // query rows, head h at columns [32h, 32h + 32)
-  int q_stride;
-  const float* k;             // key rows of all sequences
-  const float* v;             // value rows
-  int kv_stride;
-  float* out;                 // context rows (same row index as the query)
-  int out_stride;
-  const uint32_t* cu;         // [n_seqs + 1] row offsets of the sequences in k / v
+  // Q: tile-transposed [rows, q_C] when q_tt, else row-major with row stride q_C; head h of the
+  // query at columns q_col + 32h ... + 31.
+  const float* q;
+  int q_C, q_col, q_tt;
+  // K and V: columns k_col + 32h and v_col + 32h of kv ([rows, kv_C], tile-transposed when kv_tt,
+  // else row-major with row stride kv_C); rows of sequence s are cu[s] .. cu[s+1]-1.
+  const float* kv;
+  int kv_C, k_col, v_col, kv_tt;
+  float* out;                 // context rows, row-major [rows, 384] (row of the query)
+  const uint32_t* cu;         // [n_seqs + 1] row offsets of the sequences
   int max_len;                // upper bound of any sequence length (<= 512)
   int cls_mode;               // 1: one query per sequence, at row s of q / out
   int* err;

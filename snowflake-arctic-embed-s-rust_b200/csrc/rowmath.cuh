@@ -17,6 +17,13 @@ constexpr int kMaxPos = 512;
 constexpr float kLnEps = 1e-12f;
 constexpr int kMaxDevices = 64;
 
+// Tile-transposed layout of the large fp32 activations ([T, C] matrices such as the QKV output and
+// the hidden state): element (t, c) is stored at ((t / 128) * C + c) * 128 + t % 128, so the 32
+// consecutive rows a warp's epilogue threads own write one contiguous 128-byte line per column.
+__host__ __device__ __forceinline__ size_t tt_index(int t, int c, int C) {
+  return ((size_t(t >> 7) * size_t(C) + size_t(c)) << 7) + size_t(t & 127);
+}
+
 // hsum256_ps(sum0 + sum1) of src/simd_math.rs:3075-3084 applied to 16 partial lanes p[0..16)
 // (p[l] accumulates elements with index % 16 == l, as the two AVX2 accumulators do).
 __device__ __forceinline__ float tree16(const float (&p)[16]) {
@@ -55,10 +62,17 @@ __device__ __forceinline__ float cw_exp(float x) {
 // rounded once, which is the correctly rounded result except in rare double-rounding cases.
 __device__ __forceinline__ float scalar_expf(float x) { return static_cast<float>(exp(static_cast<double>(x))); }
 
+// Hardware reciprocal approximation (MUFU, within one ulp), the estimate GELU refines.
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
 // avx2_gelu_f32, src/simd_math.rs:152-175: rational erf approximation on x clamped to [-4.8, 4.8],
-// with the reciprocal estimate + one Newton step of the reference. The reference's estimate comes
-// from `rcp_ps` (12-bit, implementation defined); here it is the correctly rounded reciprocal, so
-// after the Newton step the two agree to about one ulp.
+// with a reciprocal estimate refined by one Newton step, as the reference does. The reference's
+// estimate comes from `rcp_ps` (12-bit, implementation defined); here it is the hardware
+// reciprocal (about 23-bit), so after the Newton step the two agree to about one ulp.
 __device__ __forceinline__ float gelu_ref(float x) {
   const float xc = fminf(fmaxf(x, -4.8f), 4.8f);
   const float u = xc * xc;
@@ -68,10 +82,28 @@ __device__ __forceinline__ float gelu_ref(float x) {
   float den = fmaf(u, 0.001139532f, 0.02381135f);
   den = fmaf(u, den, 0.235943093f);
   den = fmaf(u, den, 1.0f);
-  const float est = __frcp_rn(den);
+  const float est = rcp_approx(den);
   const float inv_den = est * fmaf(-den, est, 2.0f);
   const float erf_a = fminf(fmaxf(xc * (num * inv_den), -1.0f), 1.0f);
   return (x * 0.5f) * (1.0f + erf_a);
+}
+
+// gelu_ref on two lanes with the packed f32x2 arithmetic of sm_100 (each lane rounds exactly as
+// the scalar sequence does).
+__device__ __forceinline__ float2 gelu_ref2(float2 x) {
+  const float2 xc = make_float2(fminf(fmaxf(x.x, -4.8f), 4.8f), fminf(fmaxf(x.y, -4.8f), 4.8f));
+  const float2 u = __fmul2_rn(xc, xc);
+  float2 num = __ffma2_rn(u, make_float2(6.4292e-5f, 6.4292e-5f), make_float2(0.007572631f, 0.007572631f));
+  num = __ffma2_rn(u, num, make_float2(0.055282866f, 0.055282866f));
+  num = __ffma2_rn(u, num, make_float2(0.797882463f, 0.797882463f));
+  float2 den = __ffma2_rn(u, make_float2(0.001139532f, 0.001139532f), make_float2(0.02381135f, 0.02381135f));
+  den = __ffma2_rn(u, den, make_float2(0.235943093f, 0.235943093f));
+  den = __ffma2_rn(u, den, make_float2(1.0f, 1.0f));
+  const float2 est = make_float2(rcp_approx(den.x), rcp_approx(den.y));
+  const float2 inv_den = __fmul2_rn(est, __ffma2_rn(make_float2(-den.x, -den.y), est, make_float2(2.0f, 2.0f)));
+  const float2 t = __fmul2_rn(xc, __fmul2_rn(num, inv_den));
+  const float2 erf_a = make_float2(fminf(fmaxf(t.x, -1.0f), 1.0f), fminf(fmaxf(t.y, -1.0f), 1.0f));
+  return __fmul2_rn(__fmul2_rn(x, make_float2(0.5f, 0.5f)), __fadd2_rn(make_float2(1.0f, 1.0f), erf_a));
 }
 
 // GELU with the exact error function (0.5 x (1 + erf(x / sqrt 2))).

@@ -35,11 +35,16 @@ __device__ __forceinline__ float halfwarp_max(float v, unsigned mask) {
   return v;
 }
 
-// One half-warp per token row: dequant_add_embeddings_row (src/simd_math.rs:1827-1881, generic
-// path) + layernorm_smooth_quantize_row (src/simd_math.rs:369-477) with the embedding LayerNorm
-// and layers[0].qkv.inv_smooth (src/model.rs:196-219).
+// One half-warp per token row, 16 rows per block: dequant_add_embeddings_row
+// (src/simd_math.rs:1827-1881, generic path) + layernorm_smooth_quantize_row (src/simd_math.rs:369-477)
+// with the embedding LayerNorm and layers[0].qkv.inv_smooth (src/model.rs:196-219). The hidden
+// rows go through a shared-memory tile so that the tile-transposed store of a column covers the
+// block's 16 consecutive rows (64 contiguous bytes).
 __global__ void __launch_bounds__(256) k_embed_ln_quant(EmbedArgs a) {
-  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 4;
+  __shared__ float tile[kHidden][17];
+  const int r0 = blockIdx.x * 16;
+  const int lr = threadIdx.x >> 4;  // row within the block
+  const int row = r0 + lr;
   const int l = threadIdx.x & 15;
   const unsigned mask = 0xffffffffu;  // both half-warps stay converged (inactive rows compute row T-1)
   const bool active = row < a.T;
@@ -71,12 +76,11 @@ __global__ void __launch_bounds__(256) k_embed_ln_quant(EmbedArgs a) {
   const float var = halfwarp_tree16(p, mask) / float(kHidden);
   const float rstd = 1.0f / sqrtf(var + kLnEps);
   float vmax = 1e-8f;
-  float* hrow = a.hidden + size_t(hw) * kHidden;
 #pragma unroll
   for (int i = 0; i < 24; ++i) {
     const int j = l + 16 * i;
     h[i] = fmaf((h[i] - mean) * rstd, a.gamma[j], a.beta[j]);
-    if (active) hrow[j] = h[i];
+    tile[j][lr] = h[i];
     vmax = fmaxf(vmax, fabsf(h[i] * a.inv_smooth[j]));
   }
   const float max_abs = halfwarp_max(vmax, mask);
@@ -89,6 +93,12 @@ __global__ void __launch_bounds__(256) k_embed_ln_quant(EmbedArgs a) {
     if (active) qrow[j] = qv;
   }
   if (active && l == 0) a.act_s[hw] = max_abs / 127.0f;
+  __syncthreads();
+  // tile-transposed store: thread -> (column, row), rows fastest
+  for (int i = threadIdx.x; i < kHidden * 16; i += blockDim.x) {
+    const int j = i >> 4, rr = i & 15;
+    if (r0 + rr < a.T) a.hidden[tt_index(r0 + rr, j, kHidden)] = tile[j][rr];
+  }
 }
 
 // One warp per row: smooth_quantize_row_avx2 (src/simd_math.rs:584-649), the quantization of the
@@ -148,7 +158,8 @@ __global__ void k_row_meta(const uint32_t* __restrict__ cu, int n_seqs, uint16_t
 }
 
 // Gathers the [CLS] rows (act_q, act_scale, hidden) of every sequence into rows 0..n-1
-// (the compaction of src/model.rs:786-800, into separate buffers).
+// (the compaction of src/model.rs:786-800, into separate buffers); hidden is tile-transposed,
+// the gathered rows are row-major.
 __global__ void k_gather_cls(const int32_t* __restrict__ cls_row, int n, const int8_t* __restrict__ act_q,
                              const float* __restrict__ act_s, const float* __restrict__ hidden,
                              int8_t* __restrict__ cq, float* __restrict__ cs, float* __restrict__ ch) {
@@ -156,7 +167,8 @@ __global__ void k_gather_cls(const int32_t* __restrict__ cls_row, int n, const i
   if (b >= n) return;
   const int r = cls_row[b];
   const int t = threadIdx.x;  // 96 threads
-  reinterpret_cast<float4*>(ch + size_t(b) * kHidden)[t] = reinterpret_cast<const float4*>(hidden + size_t(r) * kHidden)[t];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) ch[size_t(b) * kHidden + 4 * t + e] = hidden[tt_index(r, 4 * t + e, kHidden)];
   reinterpret_cast<uint32_t*>(cq + size_t(b) * kHidden)[t] =
       reinterpret_cast<const uint32_t*>(act_q + size_t(r) * kHidden)[t];
   if (t == 0) cs[b] = act_s[r];
