@@ -159,6 +159,25 @@ int ae_attention_f32(ae_ctx* ctx, const float* d_qkv, const uint32_t* d_cu_seqle
  * device, race on it. */
 int ae_forward_cls_noalloc(ae_ctx* ctx, const uint16_t* d_ids, uint32_t len, float* d_out384);
 
+/* Per-kernel timing of the forward pass (CUDA events around every launch on the context's stream).
+ * Kinds, in the order of the forward pass: */
+enum {
+  AE_KERNEL_ROW_META = 0,   /* positions and [CLS] rows of a packed batch */
+  AE_KERNEL_EMBED = 1,      /* embedding + LayerNorm + quantization */
+  AE_KERNEL_QKV = 2,        /* QKV GEMM (layers 0-10), KV GEMM (layer 11) */
+  AE_KERNEL_ATTENTION = 3,  /* attention of all rows (layers 0-10) */
+  AE_KERNEL_CTX_QUANT = 4,  /* attention-context quantization */
+  AE_KERNEL_ATTN_OUT = 5,   /* attention-out GEMM + residual + LayerNorm + quantization */
+  AE_KERNEL_FFN_UP = 6,     /* FFN-up GEMM + GELU + quantization */
+  AE_KERNEL_FFN_DOWN = 7,   /* FFN-down GEMM + residual + LayerNorm + quantization */
+  AE_KERNEL_CLS = 8,        /* layer-11 [CLS] tail: gather, Q GEMM, attention, quantization, GEMMs */
+  AE_KERNEL_KINDS = 9
+};
+/* enable != 0 starts recording (and clears earlier records); 0 stops. */
+int ae_profile(ae_ctx* ctx, int enable);
+/* After ae_sync: total milliseconds and launch counts per kind over everything recorded. */
+int ae_profile_read(ae_ctx* ctx, float* total_ms, uint32_t* launches);
+
 /* Number of this library's kernels the context has launched so far (graph replays included). */
 uint64_t ae_kernel_launches(const ae_ctx* ctx);
 

@@ -110,7 +110,10 @@ class Engine:
 
     def close(self):
         if getattr(self, "_h", None):
-            lib().ae_ctx_destroy(self._h)
+            try:
+                lib().ae_ctx_destroy(self._h)
+            except Exception:  # interpreter shutdown: modules may already be torn down
+                pass
             self._h = None
 
     def __del__(self):
@@ -174,6 +177,19 @@ class Engine:
 
     def kernel_launches(self) -> int:
         return int(lib().ae_kernel_launches(self._h))
+
+    KERNEL_KINDS = ("row_meta", "embed", "qkv", "attention", "ctx_quant", "attn_out", "ffn_up", "ffn_down", "cls_tail")
+
+    def profile(self, enable: bool) -> None:
+        """Start (clearing earlier records) or stop per-kernel CUDA-event timing of the forward pass."""
+        self._check(lib().ae_profile(self._h, 1 if enable else 0))
+
+    def profile_read(self) -> dict:
+        """{kind: (total_ms, launches)} of everything recorded since profile(True); call after sync()."""
+        ms = np.zeros(len(self.KERNEL_KINDS), np.float32)
+        n = np.zeros(len(self.KERNEL_KINDS), np.uint32)
+        self._check(lib().ae_profile_read(self._h, _ptr(ms), _ptr(n)))
+        return {k: (float(ms[i]), int(n[i])) for i, k in enumerate(self.KERNEL_KINDS)}
 
 
 def embed_batch_multi(engines, seqs=None, ids=None, cu=None, max_batch_tokens: int = 0) -> np.ndarray:

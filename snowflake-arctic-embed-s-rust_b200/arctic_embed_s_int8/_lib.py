@@ -30,7 +30,7 @@ SYMBOLS = [
     "ae_ctx_create", "ae_ctx_destroy", "ae_last_error", "ae_ctx_set_stream", "ae_ctx_device",
     "ae_model_load", "ae_model_load_file", "ae_reserve", "ae_forward_cls", "ae_forward_ragged",
     "ae_forward_ragged_device", "ae_embed_batch_multi", "ae_gemm_i8", "ae_attention_f32", "ae_kernel_launches",
-    "ae_plan_shards", "ae_forward_cls_noalloc", "ae_sync",
+    "ae_plan_shards", "ae_forward_cls_noalloc", "ae_profile", "ae_profile_read", "ae_sync",
 ]
 
 
@@ -103,6 +103,8 @@ def lib():
     L.ae_kernel_launches.argtypes = [P]
     L.ae_plan_shards.argtypes = [P, u32, C.c_int, P]
     L.ae_forward_cls_noalloc.argtypes = [P, P, u32, P]
+    L.ae_profile.argtypes = [P, C.c_int]
+    L.ae_profile_read.argtypes = [P, P, P]
     for name in SYMBOLS:
         if name not in ("ae_last_error", "ae_kernel_launches"):
             getattr(L, name).restype = C.c_int

@@ -28,8 +28,6 @@
 
 namespace ae {
 
-constexpr int kStoreMaxLen = 256;  // longest sequence whose scores stay in shared memory
-
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
 __device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
 __device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
@@ -125,87 +123,110 @@ __device__ __forceinline__ void load_query(const AttnArgs& a, int qrow, int h, f
   }
 }
 
-// STORE = true serves sequences of 1..kStoreMaxLen keys, STORE = false the longer ones.
-template <int QT, bool STORE>
+// TMEM columns of one CTA: the scores of a sequence of L keys (power of two, >= 32).
+__host__ __device__ constexpr uint32_t tmem_cols_for_len(int L) {
+  return L <= 32 ? 32 : L <= 64 ? 64 : L <= 128 ? 128 : L <= 256 ? 256 : 512;
+}
+
+// One CTA per (sequence, head, tile of QT queries); thread = query = TMEM lane. Every thread keeps
+// the scores, then the exponentials, of its query in its TMEM lane (column t = key t), so shared
+// memory holds only the head's K / V pairs. Threads whose query lies past the sequence still take
+// part in the warp-collective TMEM loads and stores and write nothing.
+template <int QT>
 __global__ void __launch_bounds__(QT) k_attention_rows(AttnArgs a) {
   extern __shared__ float4 smem4[];
+  __shared__ uint32_t tmem_slot;
   const int s = blockIdx.x;
   const int h = blockIdx.y;
   const int tile = blockIdx.z;
   const int tid = threadIdx.x;
+  const int warp = tid >> 5;
   const int s0 = int(a.cu[s]);
   const int L = int(a.cu[s + 1]) - s0;
   if (L <= 0 || L > a.max_len) {
-    if (STORE && tid == 0 && tile == 0 && h == 0) record_err(a.err, DEV_ERR_BAD_SHAPE);
+    if (tid == 0 && tile == 0 && h == 0) record_err(a.err, DEV_ERR_BAD_SHAPE);
     return;
   }
-  if (STORE ? (L > kStoreMaxLen) : (L <= kStoreMaxLen)) return;  // the other variant's sequence
   if (tile * QT >= L) return;
-
+  const uint32_t cols = tmem_cols_for_len(L);
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, cols);
+    tmem_relinquish();
+  }
   const int pairs = (L + 1) >> 1;
   float2* kp = reinterpret_cast<float2*>(smem4);
   float2* vp = kp + pairs * KPS;
-  float* sc = reinterpret_cast<float*>(vp + pairs * KPS);  // [L][QT] scores, then exponentials (STORE)
   stage_kv_pairs(a, s0, L, h, kp, vp);
+  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tl = tmem_slot + (uint32_t(warp * 32) << 16);  // this warp's 32 lanes
 
   const int qi = tile * QT + tid;
-  if (qi >= L) return;
-  const int qrow = s0 + qi;
+  const bool active = qi < L;
+  const int qrow = s0 + (active ? qi : L - 1);
   float q[32];
   load_query(a, qrow, h, q);
   const int L4 = L & ~3, L8 = L & ~7, L16 = L & ~15;
+  uint32_t r[16];
 
-  // pass 1: scores and their max
+  // pass 1: scores -> TMEM (16 keys per store) and their max
   float mx = -INFINITY;
-  for (int i = 0; i < pairs; ++i) {
-    const float2 sp = score_pair(q, kp + i * KPS, 2 * i < L4);
-    if (STORE) {
-      sc[(2 * i) * QT + tid] = sp.x;
-      if (2 * i + 1 < L) sc[(2 * i + 1) * QT + tid] = sp.y;
+  for (int t0 = 0; t0 < L; t0 += 16) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int t = t0 + 2 * j;
+      float2 sp = f2(0.0f, 0.0f);
+      if (t < L) {
+        sp = score_pair(q, kp + (t >> 1) * KPS, t < L4);
+        mx = fmaxf(mx, sp.x);
+        if (t + 1 < L) mx = fmaxf(mx, sp.y);
+      }
+      r[2 * j] = __float_as_uint(sp.x);
+      r[2 * j + 1] = __float_as_uint(sp.y);
     }
-    mx = fmaxf(mx, sp.x);
-    if (2 * i + 1 < L) mx = fmaxf(mx, sp.y);
+    tmem_st16(tl + t0, r);
   }
+  tmem_st_wait();
   const float2 neg_mx = f2(-mx, -mx);
 
-  auto score2 = [&](int t) -> float2 {  // scores of keys t, t+1 (t even)
-    if (STORE) return f2(sc[t * QT + tid], (t + 1 < L) ? sc[(t + 1) * QT + tid] : 0.0f);
-    return score_pair(q, kp + (t >> 1) * KPS, t < L4);
-  };
-  auto put2 = [&](int t, float2 e) {
-    if (STORE) {
-      sc[t * QT + tid] = e.x;
-      sc[(t + 1) * QT + tid] = e.y;
-    }
-  };
-
-  // pass 2: exponentials and their sum in the reference's accumulation order
-  float2 vs0[4], vs1[4];  // lanes (2j, 2j+1) of the reference's two 8-lane accumulators
+  // pass 2: exponentials (back into TMEM) and their sum in the reference's accumulation order:
+  // full 16-key chunks feed the two 8-lane accumulators, a trailing 8-key chunk the first one,
+  // the last L % 8 keys a scalar exp added in order after the tree
+  float2 vs0[4], vs1[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) vs0[j] = vs1[j] = f2(0.0f, 0.0f);
-  for (int t0 = 0; t0 < L16; t0 += 16) {
+  for (int t0 = 0; t0 < L; t0 += 16) {
+    tmem_ld16(tl + t0, r);
+    tmem_ld_wait();
+    if (t0 + 16 <= L16) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 e = cw_exp2(add2(score2(t0 + 2 * j), neg_mx));
-      put2(t0 + 2 * j, e);
-      vs0[j] = add2(vs0[j], e);
-    }
+      for (int j = 0; j < 8; ++j) {
+        const float2 e = cw_exp2(add2(f2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), neg_mx));
+        if (j < 4) vs0[j] = add2(vs0[j], e);
+        else vs1[j - 4] = add2(vs1[j - 4], e);
+        r[2 * j] = __float_as_uint(e.x);
+        r[2 * j + 1] = __float_as_uint(e.y);
+      }
+    } else {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 e = cw_exp2(add2(score2(t0 + 8 + 2 * j), neg_mx));
-      put2(t0 + 8 + 2 * j, e);
-      vs1[j] = add2(vs1[j], e);
+      for (int j = 0; j < 8; ++j) {
+        const int t = t0 + 2 * j;
+        const float2 x = add2(f2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), neg_mx);
+        float2 e;
+        if (j < 4 && t + 1 < L8) {  // the trailing 8-key chunk (keys L16 .. L16 + 7)
+          e = cw_exp2(x);
+          vs0[j & 3] = add2(vs0[j & 3], e);
+        } else {  // the last L % 8 keys: scalar exp, summed after the tree
+          e = f2(t < L ? scalar_expf(x.x) : 0.0f, t + 1 < L ? scalar_expf(x.y) : 0.0f);
+        }
+        r[2 * j] = __float_as_uint(e.x);
+        r[2 * j + 1] = __float_as_uint(e.y);
+      }
     }
+    tmem_st16(tl + t0, r);
   }
-  if (L8 > L16) {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 e = cw_exp2(add2(score2(L16 + 2 * j), neg_mx));
-      put2(L16 + 2 * j, e);
-      vs0[j] = add2(vs0[j], e);
-    }
-  }
+  tmem_st_wait();
   float v8[8];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -214,47 +235,53 @@ __global__ void __launch_bounds__(QT) k_attention_rows(AttnArgs a) {
     v8[2 * j + 1] = t.y;
   }
   float sum = tree8(v8);
-  for (int t = L8; t < L; ++t) {
-    const float x = STORE ? sc[t * QT + tid] : ((t & 1) ? score2(t - 1).y : score2(t).x);
-    const float e = scalar_expf(x - mx);
-    if (STORE) sc[t * QT + tid] = e;
-    sum = sum + e;
+  if (L8 < L) {  // ((tree + e[L8]) + e[L8 + 1]) + ..., the keys re-read from TMEM
+    tmem_ld16(tl + L16, r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (L16 + j >= L8 && L16 + j < L) sum = sum + __uint_as_float(r[j]);
   }
   const float inv = 1.0f / sum;
   const float2 inv2 = f2(inv, inv);
 
   // pass 3: probabilities and the weighted sum of V; lane x = even keys (a), lane y = odd keys (b)
-  auto exps2 = [&](int t) -> float2 {  // exponentials of keys t, t+1 (t even; 0 past the end)
-    if (STORE) return f2(sc[t * QT + tid], (t + 1 < L) ? sc[(t + 1) * QT + tid] : 0.0f);
-    const float2 x = add2(score_pair(q, kp + (t >> 1) * KPS, t < L4), neg_mx);
-    if (t + 1 < L8) return cw_exp2(x);
-    return f2(scalar_expf(x.x), (t + 1 < L) ? scalar_expf(x.y) : 0.0f);  // t >= L8 here
-  };
   float2 acc[32];
 #pragma unroll
   for (int d = 0; d < 32; ++d) acc[d] = f2(0.0f, 0.0f);
-  const int full_pairs = L >> 1;
-  for (int i = 0; i < full_pairs; ++i) {
-    const float2 p = mul2(exps2(2 * i), inv2);
-    const float4* v4 = reinterpret_cast<const float4*>(vp + i * KPS);
+  for (int t0 = 0; t0 < L; t0 += 16) {
+    tmem_ld16(tl + t0, r);
+    tmem_ld_wait();
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const float4 t = v4[j];
-      acc[2 * j] = fma2(f2(t.x, t.y), p, acc[2 * j]);
-      acc[2 * j + 1] = fma2(f2(t.z, t.w), p, acc[2 * j + 1]);
+    for (int j = 0; j < 8; ++j) {
+      const int t = t0 + 2 * j;
+      if (t + 1 < L) {
+        const float2 p = mul2(f2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), inv2);
+        const float4* v4 = reinterpret_cast<const float4*>(vp + (t >> 1) * KPS);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float4 vv = v4[i];
+          acc[2 * i] = fma2(f2(vv.x, vv.y), p, acc[2 * i]);
+          acc[2 * i + 1] = fma2(f2(vv.z, vv.w), p, acc[2 * i + 1]);
+        }
+      } else if (t < L) {  // odd L: the last key goes to the even accumulator
+        const float pa = __uint_as_float(r[2 * j]) * inv;
+        const float2* v = vp + (t >> 1) * KPS;
+#pragma unroll
+        for (int d = 0; d < 32; ++d) acc[d].x = fmaf(v[d].x, pa, acc[d].x);
+      }
     }
   }
-  if (L & 1) {
-    const float pa = exps2(L - 1).x * inv;
-    const float2* v = vp + (L >> 1) * KPS;
+  if (active) {
+    float4* o = reinterpret_cast<float4*>(a.out + size_t(s0 + qi) * kHidden + h * 32);
 #pragma unroll
-    for (int d = 0; d < 32; ++d) acc[d].x = fmaf(v[d].x, pa, acc[d].x);
+    for (int i = 0; i < 8; ++i)
+      o[i] = make_float4(acc[4 * i].x + acc[4 * i].y, acc[4 * i + 1].x + acc[4 * i + 1].y,
+                         acc[4 * i + 2].x + acc[4 * i + 2].y, acc[4 * i + 3].x + acc[4 * i + 3].y);
   }
-  float4* o = reinterpret_cast<float4*>(a.out + size_t(qrow) * kHidden + h * 32);
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-    o[i] = make_float4(acc[4 * i].x + acc[4 * i].y, acc[4 * i + 1].x + acc[4 * i + 1].y,
-                       acc[4 * i + 2].x + acc[4 * i + 2].y, acc[4 * i + 3].x + acc[4 * i + 3].y);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem_slot, cols);
 }
 
 // One warp per (sequence, head): the single [CLS] query (row s of q / out) over the sequence's keys.
@@ -332,25 +359,24 @@ __global__ void __launch_bounds__(128) k_attention_cls(AttnArgs a, int n_seqs) {
   a.out[size_t(s) * kHidden + h * 32 + lane] = acc_a + acc_b;
 }
 
-template <int QT, bool STORE>
-static size_t rows_smem(int max_len) {
-  const int L = STORE ? (max_len < kStoreMaxLen ? max_len : kStoreMaxLen) : max_len;
-  return size_t((L + 1) / 2) * KPS * 8 * 2 + (STORE ? size_t(L) * QT * 4 : 0);
-}
+constexpr size_t kRowsSmemMax = 220 * 1024;  // dynamic shared memory cap (static smem comes on top)
 
-template <int QT, bool STORE>
-static int launch_rows(const AttnArgs& a, int n_seqs, cudaStream_t st) {
-  const int L = STORE ? (a.max_len < kStoreMaxLen ? a.max_len : kStoreMaxLen) : a.max_len;
-  dim3 grid(n_seqs, kHeads, (L + QT - 1) / QT);
-  k_attention_rows<QT, STORE><<<grid, QT, rows_smem<QT, STORE>(a.max_len), st>>>(a);
-  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+// Shared memory of a rows CTA: the K / V pairs, padded so that at most 512 / cols CTAs share an SM
+// (their TMEM allocations then always fit; a CTA never waits in tcgen05.alloc).
+static size_t rows_smem(int max_len) {
+  const size_t kv = size_t((max_len + 1) / 2) * KPS * 8 * 2;
+  const uint32_t cols = tmem_cols_for_len(max_len);
+  const size_t per_sm = 227 * 1024;
+  size_t floor_bytes = per_sm / (512 / cols) - 2048 + 1;  // no more than 512 / cols CTAs fit
+  if (floor_bytes > kRowsSmemMax) floor_bytes = kRowsSmemMax;
+  return kv > floor_bytes ? kv : floor_bytes;
 }
 
 template <int QT>
-static int launch_qt(const AttnArgs& a, int n_seqs, cudaStream_t st) {
-  int r = launch_rows<QT, true>(a, n_seqs, st);
-  if (!r && a.max_len > kStoreMaxLen) r = launch_rows<QT, false>(a, n_seqs, st);
-  return r;
+static int launch_rows(const AttnArgs& a, int n_seqs, cudaStream_t st) {
+  dim3 grid(n_seqs, kHeads, (a.max_len + QT - 1) / QT);
+  k_attention_rows<QT><<<grid, QT, rows_smem(a.max_len), st>>>(a);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
 static int smem_attr(const void* fn, size_t bytes) {
@@ -359,12 +385,10 @@ static int smem_attr(const void* fn, size_t bytes) {
 
 int attention_prime() {
   int r = 0;
-  r |= smem_attr((const void*)k_attention_rows<128, true>, rows_smem<128, true>(kMaxPos));
-  r |= smem_attr((const void*)k_attention_rows<64, true>, rows_smem<64, true>(kMaxPos));
-  r |= smem_attr((const void*)k_attention_rows<32, true>, rows_smem<32, true>(kMaxPos));
-  r |= smem_attr((const void*)k_attention_rows<128, false>, rows_smem<128, false>(kMaxPos));
-  r |= smem_attr((const void*)k_attention_rows<64, false>, rows_smem<64, false>(kMaxPos));
-  r |= smem_attr((const void*)k_attention_rows<32, false>, rows_smem<32, false>(kMaxPos));
+  const size_t most = kRowsSmemMax;
+  r |= smem_attr((const void*)k_attention_rows<128>, most);
+  r |= smem_attr((const void*)k_attention_rows<64>, most);
+  r |= smem_attr((const void*)k_attention_rows<32>, most);
   r |= smem_attr((const void*)k_attention_cls, 4 * kClsWarpFloats * 4);
   return r;
 }
@@ -379,9 +403,9 @@ int launch_attention_exact(const AttnArgs& a, int n_seqs, cudaStream_t st) {
   }
   // query tile: 128 threads when the grid fills the GPU, smaller tiles for few sequences
   const long ctas128 = long(n_seqs) * kHeads * ((a.max_len + 127) / 128);
-  if (ctas128 >= 2 * 148) return launch_qt<128>(a, n_seqs, st);
-  if (ctas128 * 2 >= 2 * 148) return launch_qt<64>(a, n_seqs, st);
-  return launch_qt<32>(a, n_seqs, st);
+  if (ctas128 >= 2 * 148) return launch_rows<128>(a, n_seqs, st);
+  if (ctas128 * 2 >= 2 * 148) return launch_rows<64>(a, n_seqs, st);
+  return launch_rows<32>(a, n_seqs, st);
 }
 
 }  // namespace ae

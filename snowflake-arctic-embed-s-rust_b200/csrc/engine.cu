@@ -111,6 +111,10 @@ struct ae_ctx {
   std::map<uint32_t, Graph> graphs;  // forward_cls graph per sequence length
   std::string err;
   int gelu_erf = 0;       // ARCTIC_GELU=erf selects the exact-erf GELU (outside the parity tolerance)
+  bool prof = false;      // record CUDA events around every launch (ae_profile)
+  int prof_kind = 0;      // kind of the launches being enqueued
+  std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> prof_events;
+  std::vector<cudaEvent_t> prof_pool;
   uint64_t launches = 0;  // kernels enqueued (or replayed from a graph) on this context
   uint64_t graph_kernels = 0;
 };
@@ -293,6 +297,34 @@ int reserve(ae_ctx* c, uint32_t tokens, uint32_t seqs) {
 }
 
 // ------------------------------------------------------------------------------------------ forward
+// Profiling: a pair of events around the next launch(es) of the current kind.
+cudaEvent_t prof_event(ae_ctx* c) {
+  if (!c->prof_pool.empty()) {
+    cudaEvent_t e = c->prof_pool.back();
+    c->prof_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+struct ProfScope {
+  ae_ctx* c;
+  cudaEvent_t a = nullptr, b = nullptr;
+  ProfScope(ae_ctx* cc, int kind) : c(cc) {
+    if (!c->prof) return;
+    c->prof_kind = kind;
+    a = prof_event(c);
+    b = prof_event(c);
+    cudaEventRecord(a, c->stream);
+  }
+  ~ProfScope() {
+    if (!c->prof || !a) return;
+    cudaEventRecord(b, c->stream);
+    c->prof_events.push_back({c->prof_kind, {a, b}});
+  }
+};
+
 // `tt` selects the tile-transposed layout for the fp32 residual and output (the hidden state and
 // the QKV / KV outputs of the packed rows; the [CLS]-row buffers stay row-major).
 int gemm(ae_ctx* c, int epi, const CUtensorMap& ta, const DevLinear& L, int M, const float* a_scale, const float* res,
@@ -354,7 +386,11 @@ int enqueue_forward(ae_ctx* c, const uint16_t* d_ids, const uint32_t* d_cu, int 
   cudaStream_t st = c->stream;
   const uint64_t launches0 = c->launches;
   c->launches += 2;  // row metadata + embedding
-  if (launch_row_meta(d_cu, n, W.pos, W.cls_row, c->d_err, st)) return fail(c, AE_ERR_CUDA, "row metadata launch failed");
+  {
+    ProfScope ps(c, AE_KERNEL_ROW_META);
+    if (launch_row_meta(d_cu, n, W.pos, W.cls_row, c->d_err, st))
+      return fail(c, AE_ERR_CUDA, "row metadata launch failed");
+  }
   EmbedArgs e{};
   e.T = T;
   e.ids = d_ids;
@@ -371,27 +407,52 @@ int enqueue_forward(ae_ctx* c, const uint16_t* d_ids, const uint32_t* d_cu, int 
   e.act_q = W.act_q;
   e.act_s = W.act_s;
   e.err = c->d_err;
-  if (launch_embed(e, st)) return fail(c, AE_ERR_CUDA, "embedding launch failed");
+  {
+    ProfScope ps(c, AE_KERNEL_EMBED);
+    if (launch_embed(e, st)) return fail(c, AE_ERR_CUDA, "embedding launch failed");
+  }
 
   for (int l = 0; l + 1 < kLayers; ++l) {
     const DevLayer& Ly = M.layers[l];
-    AE_TRY(gemm(c, EPI_F32, W.tm_act_q, Ly.qkv, T, W.act_s, nullptr, 0, nullptr, nullptr, nullptr, W.qkv, 3 * kHidden,
-                nullptr, nullptr, 1));
-    AE_TRY(attention(c, W.qkv, 3 * kHidden, 0, 1, W.qkv, 3 * kHidden, kHidden, 2 * kHidden, 1, W.ctx, d_cu, n, max_len,
-                     0));
+    {
+      ProfScope ps(c, AE_KERNEL_QKV);
+      AE_TRY(gemm(c, EPI_F32, W.tm_act_q, Ly.qkv, T, W.act_s, nullptr, 0, nullptr, nullptr, nullptr, W.qkv, 3 * kHidden,
+                  nullptr, nullptr, 1));
+    }
+    {
+      ProfScope ps(c, AE_KERNEL_ATTENTION);
+      AE_TRY(attention(c, W.qkv, 3 * kHidden, 0, 1, W.qkv, 3 * kHidden, kHidden, 2 * kHidden, 1, W.ctx, d_cu, n,
+                       max_len, 0));
+    }
     ++c->launches;
-    if (launch_smooth_quant(W.ctx, Ly.ao.inv_s, W.act_q, W.act_s, T, st))
-      return fail(c, AE_ERR_CUDA, "context quantization launch failed");
-    AE_TRY(gemm(c, EPI_LN_QUANT, W.tm_act_q, Ly.ao, T, W.act_s, W.hidden, kHidden, Ly.ln1w, Ly.ln1b, Ly.fi.inv_s,
-                W.hidden, kHidden, W.act_q, W.act_s, 1));
-    AE_TRY(gemm(c, EPI_GELU_QUANT, W.tm_act_q, Ly.fi, T, W.act_s, nullptr, 0, nullptr, nullptr, Ly.fo.inv_s, nullptr, 0,
-                W.inter_q, W.inter_s));
-    AE_TRY(gemm(c, EPI_LN_QUANT, W.tm_inter_q, Ly.fo, T, W.inter_s, W.hidden, kHidden, Ly.ln2w, Ly.ln2b,
-                M.layers[l + 1].qkv.inv_s, W.hidden, kHidden, W.act_q, W.act_s, 1));
+    {
+      ProfScope ps(c, AE_KERNEL_CTX_QUANT);
+      if (launch_smooth_quant(W.ctx, Ly.ao.inv_s, W.act_q, W.act_s, T, st))
+        return fail(c, AE_ERR_CUDA, "context quantization launch failed");
+    }
+    {
+      ProfScope ps(c, AE_KERNEL_ATTN_OUT);
+      AE_TRY(gemm(c, EPI_LN_QUANT, W.tm_act_q, Ly.ao, T, W.act_s, W.hidden, kHidden, Ly.ln1w, Ly.ln1b, Ly.fi.inv_s,
+                  W.hidden, kHidden, W.act_q, W.act_s, 1));
+    }
+    {
+      ProfScope ps(c, AE_KERNEL_FFN_UP);
+      AE_TRY(gemm(c, EPI_GELU_QUANT, W.tm_act_q, Ly.fi, T, W.act_s, nullptr, 0, nullptr, nullptr, Ly.fo.inv_s, nullptr,
+                  0, W.inter_q, W.inter_s));
+    }
+    {
+      ProfScope ps(c, AE_KERNEL_FFN_DOWN);
+      AE_TRY(gemm(c, EPI_LN_QUANT, W.tm_inter_q, Ly.fo, T, W.inter_s, W.hidden, kHidden, Ly.ln2w, Ly.ln2b,
+                  M.layers[l + 1].qkv.inv_s, W.hidden, kHidden, W.act_q, W.act_s, 1));
+    }
   }
   const DevLayer& Z = M.layers[kLayers - 1];
-  AE_TRY(gemm(c, EPI_F32, W.tm_act_q, Z.kv_only, T, W.act_s, nullptr, 0, nullptr, nullptr, nullptr, W.qkv, 2 * kHidden,
-              nullptr, nullptr, 1));
+  {
+    ProfScope ps(c, AE_KERNEL_QKV);
+    AE_TRY(gemm(c, EPI_F32, W.tm_act_q, Z.kv_only, T, W.act_s, nullptr, 0, nullptr, nullptr, nullptr, W.qkv,
+                2 * kHidden, nullptr, nullptr, 1));
+  }
+  ProfScope ps_cls(c, AE_KERNEL_CLS);
   c->launches += 2;  // gather + [CLS] context quantization
   if (launch_gather_cls(W.cls_row, n, W.act_q, W.act_s, W.hidden, W.cq, W.cs, W.ch, st))
     return fail(c, AE_ERR_CUDA, "gather launch failed");
@@ -592,6 +653,11 @@ int ae_ctx_destroy(ae_ctx* c) {
   drop_graphs(c);
   free_ws(c);
   free_model(c);
+  for (auto& e : c->prof_events) {
+    cudaEventDestroy(e.second.first);
+    cudaEventDestroy(e.second.second);
+  }
+  for (auto e : c->prof_pool) cudaEventDestroy(e);
   if (c->d_err) cudaFree(c->d_err);
   if (c->own_stream) cudaStreamDestroy(c->own_stream);
   delete c;
@@ -782,7 +848,10 @@ int ae_forward_cls(ae_ctx* c, const uint16_t* ids, uint32_t len, float* out) {
         cudaMemcpyAsync(W.cu, W.h_cu, 2 * 4, cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
       r = fail(c, AE_ERR_CUDA, "capture of input copies failed");
     const uint64_t before = c->launches;
+    const bool prof = c->prof;
+    c->prof = false;  // no event records inside the graph
     if (!r) r = enqueue_forward(c, W.ids, W.cu, int(L), 1, int(L), W.out);
+    c->prof = prof;
     gr.kernels = c->launches - before;
     c->launches = before;  // captured, not launched
     if (!r && cudaMemcpyAsync(W.h_out, W.out, kHidden * 4, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
@@ -824,6 +893,34 @@ int ae_forward_ragged_device(ae_ctx* c, const uint16_t* d_ids, const uint32_t* d
 }
 
 uint64_t ae_kernel_launches(const ae_ctx* c) { return c ? c->launches : 0; }
+
+int ae_profile(ae_ctx* c, int enable) {
+  if (!c) return AE_ERR_INVALID_ARG;
+  DeviceGuard g(c->device);
+  for (auto& e : c->prof_events) {
+    c->prof_pool.push_back(e.second.first);
+    c->prof_pool.push_back(e.second.second);
+  }
+  c->prof_events.clear();
+  c->prof = enable != 0;
+  return 0;
+}
+
+int ae_profile_read(ae_ctx* c, float* total_ms, uint32_t* launches) {
+  if (!c || !total_ms || !launches) return AE_ERR_INVALID_ARG;
+  DeviceGuard g(c->device);
+  for (int k = 0; k < AE_KERNEL_KINDS; ++k) {
+    total_ms[k] = 0.0f;
+    launches[k] = 0;
+  }
+  for (auto& e : c->prof_events) {
+    float ms = 0.0f;
+    CUDA_TRY(c, cudaEventElapsedTime(&ms, e.second.first, e.second.second));
+    total_ms[e.first] += ms;
+    launches[e.first] += 1;
+  }
+  return 0;
+}
 
 int ae_plan_shards(const uint32_t* cu, uint32_t n, int n_shards, int32_t* shard_of) {
   if (!cu || !shard_of || n_shards <= 0) return AE_ERR_INVALID_ARG;
