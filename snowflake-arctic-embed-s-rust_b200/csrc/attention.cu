@@ -59,7 +59,8 @@ __device__ __forceinline__ float2 score_pair(const float (&q)[32], const float2*
 __device__ __forceinline__ float2 cw_exp2(float2 x) {
   const float2 y = f2(fmaxf(fminf(x.x, 88.0f), -87.3f), fmaxf(fminf(x.y, 88.0f), -87.3f));
   const float2 t = mul2(y, f2(1.44269504088896341f, 1.44269504088896341f));
-  const float2 n = f2(rintf(t.x), rintf(t.y));
+  const float2 big = add2(t, f2(kRoundMagic, kRoundMagic));    // round half to even (rowmath.cuh)
+  const float2 n = add2(big, f2(-kRoundMagic, -kRoundMagic));
   const float2 nn = f2(-n.x, -n.y);
   const float2 r = fma2(nn, f2(1.428606765330187e-6f, 1.428606765330187e-6f),
                         fma2(nn, f2(0.693145751953125f, 0.693145751953125f), y));
@@ -68,8 +69,8 @@ __device__ __forceinline__ float2 cw_exp2(float2 x) {
   p = fma2(r, p, f2(0.5f, 0.5f));
   p = fma2(r, p, f2(1.0f, 1.0f));
   p = fma2(r, p, f2(1.0f, 1.0f));
-  const float2 pw =
-      f2(__int_as_float((__float2int_rn(n.x) + 127) << 23), __int_as_float((__float2int_rn(n.y) + 127) << 23));
+  const float2 pw = f2(__int_as_float(((__float_as_int(big.x) - kRoundMagicBits) + 127) << 23),
+                       __int_as_float(((__float_as_int(big.y) - kRoundMagicBits) + 127) << 23));
   return mul2(p, pw);
 }
 

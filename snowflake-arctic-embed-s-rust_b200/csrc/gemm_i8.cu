@@ -163,6 +163,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       int kc = 0;
       for (int it = 0; it < my_tiles && ok; ++it) {
         const int m0 = (m_first + it * m_stride) * BM;
+        if constexpr (Ly::LN) {
+          // the epilogue reads this tile's residual: one contiguous block in the tile-transposed layout
+          if (g.res_tt && g.res && m0 < g.M) prefetch_l2_bulk(g.res + size_t(m0) * g.ldr, uint32_t(BM) * g.ldr * 4);
+        }
         for (int kb = 0; kb < KB; ++kb, ++kc) {
           const int s = kc % STAGES;
           if (kc >= STAGES && !(ok = mbar_wait(&empty[s], ((kc / STAGES) - 1) & 1, g.err, DEV_ERR_TIMEOUT_PRODUCER)))
@@ -365,34 +369,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t r[24];
         float p[4] = {0.f, 0.f, 0.f, 0.f};
         // pass 1: h = fma(acc, as * ws, bias + res) -> TMEM; partial sums (chains of lanes cq..cq+3)
+        const float* res_row = nullptr;  // column c of this row at res_row[c * rstep]
+        size_t rstep = 1;
+        if (valid) {
+          res_row = g.res_tt ? g.res + tt_index(row, 0, g.ldr) : g.res + size_t(row) * g.ldr;
+          rstep = g.res_tt ? 128 : 1;
+        }
         if (ok) {
-          for (int k0 = 0; k0 < 24; k0 += 6) {
+          for (int k0 = 0; k0 < 24; k0 += 4) {
+            float rv[16];
 #pragma unroll
-            for (int k = 0; k < 6; ++k) tmem_ld4(tb + 16 * (k0 + k) + cq, r + 4 * k);
+            for (int k = 0; k < 4; ++k)
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                rv[4 * k + e] = valid ? res_row[size_t(16 * (k0 + k) + cq + e) * rstep] : 0.0f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) tmem_ld4(tb + 16 * (k0 + k) + cq, r + 4 * k);
             tmem_ld_wait();
 #pragma unroll
-            for (int k = 0; k < 6; ++k) {
+            for (int k = 0; k < 4; ++k) {
               const int c = 16 * (k0 + k) + cq;
-              float rv[4] = {0.f, 0.f, 0.f, 0.f};
-              if (valid) {
-                if (g.res_tt) {
-                  const float* rp = g.res + tt_index(row, c, g.ldr);
-#pragma unroll
-                  for (int e = 0; e < 4; ++e) rv[e] = rp[e << 7];
-                } else {
-                  const float4 rr = *reinterpret_cast<const float4*>(g.res + size_t(row) * g.ldr + c);
-                  rv[0] = rr.x;
-                  rv[1] = rr.y;
-                  rv[2] = rr.z;
-                  rv[3] = rr.w;
-                }
-              }
               if (valid && g.acc_dbg)
                 *reinterpret_cast<int4*>(g.acc_dbg + size_t(row) * g.N + c) =
                     make_int4(int(r[4 * k]), int(r[4 * k + 1]), int(r[4 * k + 2]), int(r[4 * k + 3]));
+              const float4 wv = *reinterpret_cast<const float4*>(s_ws + c);
+              const float4 bv = *reinterpret_cast<const float4*>(s_bias + c);
+              const float wsv[4] = {wv.x, wv.y, wv.z, wv.w};
+              const float bsv[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
-                const float h = fmaf(float(int(r[4 * k + e])), as * s_ws[c + e], s_bias[c + e] + rv[e]);
+                const float h = fmaf(float(int(r[4 * k + e])), as * wsv[e], bsv[e] + rv[4 * k + e]);
                 p[e] = p[e] + h;
                 r[4 * k + e] = __float_as_uint(h);
               }
@@ -434,6 +440,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float rstd = 1.0f / sqrtf(var + kLnEps);
         // pass 3: y = LN(h) -> residual out and TMEM; max |y * inv_smooth|
         float vmax = 1e-8f;
+        float* out_row = valid ? (g.out_tt ? g.out_f32 + tt_index(row, 0, g.ldo) : g.out_f32 + size_t(row) * g.ldo)
+                               : nullptr;
         if (ok) {
           for (int k0 = 0; k0 < 24; k0 += 6) {
 #pragma unroll
@@ -442,20 +450,26 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int k = 0; k < 6; ++k) {
               const int c = 16 * (k0 + k) + cq;
+              const float4 gv4 = *reinterpret_cast<const float4*>(s_gamma + c);
+              const float4 bv4 = *reinterpret_cast<const float4*>(s_beta + c);
+              const float4 iv4 = *reinterpret_cast<const float4*>(s_invs + c);
+              const float gv[4] = {gv4.x, gv4.y, gv4.z, gv4.w};
+              const float bv[4] = {bv4.x, bv4.y, bv4.z, bv4.w};
+              const float iv[4] = {iv4.x, iv4.y, iv4.z, iv4.w};
               float y[4];
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
-                y[e] = fmaf((__uint_as_float(r[4 * k + e]) - mean) * rstd, s_gamma[c + e], s_beta[c + e]);
-                vmax = fmaxf(vmax, fabsf(y[e] * s_invs[c + e]));
+                y[e] = fmaf((__uint_as_float(r[4 * k + e]) - mean) * rstd, gv[e], bv[e]);
+                vmax = fmaxf(vmax, fabsf(y[e] * iv[e]));
                 r[4 * k + e] = __float_as_uint(y[e]);
               }
               if (valid) {
                 if (g.out_tt) {
-                  float* op = g.out_f32 + tt_index(row, c, g.ldo);
+                  float* op = out_row + size_t(c) * 128;
 #pragma unroll
                   for (int e = 0; e < 4; ++e) op[e << 7] = y[e];
                 } else {
-                  *reinterpret_cast<float4*>(g.out_f32 + size_t(row) * g.ldo + c) = make_float4(y[0], y[1], y[2], y[3]);
+                  *reinterpret_cast<float4*>(out_row + c) = make_float4(y[0], y[1], y[2], y[3]);
                 }
               }
               tmem_st4(tb + c, r + 4 * k);
@@ -476,10 +490,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int k = 0; k < 6; ++k) {
               const int c = 16 * (k0 + k) + cq;
+              const float4 iv4 = *reinterpret_cast<const float4*>(s_invs + c);
+              const float iv[4] = {iv4.x, iv4.y, iv4.z, iv4.w};
               uint32_t w = 0;
 #pragma unroll
               for (int e = 0; e < 4; ++e)
-                w |= (uint32_t(quant_i8(__uint_as_float(r[4 * k + e]) * (s_invs[c + e] * inv_scale))) & 0xFFu) << (8 * e);
+                w |= (uint32_t(quant_i8(__uint_as_float(r[4 * k + e]) * (iv[e] * inv_scale))) & 0xFFu) << (8 * e);
               if (valid) *reinterpret_cast<uint32_t*>(g.out_q + size_t(row) * kHidden + c) = w;
             }
           }

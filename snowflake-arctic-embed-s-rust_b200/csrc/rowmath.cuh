@@ -38,23 +38,30 @@ __device__ __forceinline__ float tree8(const float (&v)[8]) {
   return ((v[0] + v[4]) + (v[1] + v[5])) + ((v[2] + v[6]) + (v[3] + v[7]));
 }
 
+// Round-to-nearest-even of |x| < 2^22 on the FP32 pipe: adding 1.5 * 2^23 leaves the rounded
+// integer in the low mantissa bits (the add itself rounds half to even), subtracting it back gives
+// the rounded value exactly. Same result as rintf / cvt.rni without the conversion pipe.
+constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
+constexpr int kRoundMagicBits = 0x4B400000;
+
 // Clamp-and-round of the AVX2 quantizers: min(max(v, -127), 127) then cvtps_epi32 (half-even).
 __device__ __forceinline__ int quant_i8(float v) {
   v = fminf(fmaxf(v, -127.0f), 127.0f);
-  return __float2int_rn(v);
+  return __float_as_int(v + kRoundMagic) - kRoundMagicBits;
 }
 
 // avx2_exp_f32, src/simd_math.rs:113-143 (Cody-Waite range reduction + degree-5 polynomial).
 __device__ __forceinline__ float cw_exp(float x) {
-  float y = fmaxf(fminf(x, 88.0f), -87.3f);
-  float n = rintf(y * 1.44269504088896341f);  // LOG2_E rounded to f32
-  float r = fmaf(-n, 1.428606765330187e-6f, fmaf(-n, 0.693145751953125f, y));
+  const float y = fmaxf(fminf(x, 88.0f), -87.3f);
+  const float big = y * 1.44269504088896341f + kRoundMagic;  // LOG2_E rounded to f32; two roundings
+  const float n = big - kRoundMagic;                          // round(y * log2e), half to even
+  const float r = fmaf(-n, 1.428606765330187e-6f, fmaf(-n, 0.693145751953125f, y));
   float p = fmaf(r, 0.008333334f, 0.041666668f);
   p = fmaf(r, p, 0.16666667f);
   p = fmaf(r, p, 0.5f);
   p = fmaf(r, p, 1.0f);
   p = fmaf(r, p, 1.0f);
-  int ni = __float2int_rn(n) + 127;
+  const int ni = (__float_as_int(big) - kRoundMagicBits) + 127;
   return p * __int_as_float(ni << 23);
 }
 
