@@ -226,6 +226,101 @@ def measure_fp32_peak() -> float:
     return 2.0 * 8192 ** 3 / best / 1e9
 
 
+def microbench(eng, stream, peaks: dict) -> dict:
+    """Config 5: the four int8 GEMM shapes x M in {512, 8192, 65536} (plain dequant epilogue, and the
+    fused model epilogue where the shape has one) and the masked attention over 64 x 12 x 512 x 32
+    fp32. CUDA events on the launch stream, median of 5 after warm-up, L2 flushed before each."""
+    import torch
+
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    i8peak = 2.0 * peaks.get("bf16_tflops", 1590.0)
+    g = torch.Generator(device="cpu").manual_seed(5)
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
+
+    def timed(fn, reps=5):
+        fn()
+        ts = []
+        for _ in range(reps):
+            with torch.cuda.stream(stream):
+                flush.fill_(1.0)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        eng.sync()
+        return float(np.median(ts))
+
+    out = {"gemm": [], "attention": None}
+    for K, N in ((384, 1152), (384, 384), (384, 1536), (1536, 384)):
+        w = torch.clamp(torch.round(torch.randn(N, K, generator=g) * 40), -127, 127).to(torch.int8).cuda()
+        ws = (torch.rand(N, generator=g) * 9e-3 + 1e-3).cuda()
+        bias = (torch.randn(N, generator=g) * 0.02).cuda()
+        for M in (512, 8192, 65536):
+            a = torch.randint(-127, 128, (M, K), dtype=torch.int8, generator=g).cuda()
+            asc = (torch.rand(M, generator=g) * 9e-3 + 1e-3).cuda()
+            o = torch.empty(M, N, device="cuda")
+            ops = 2.0 * M * K * N
+            ms = timed(lambda: eng.gemm_i8(0, a, asc, w, ws, bias, out=o))
+            byt = M * K + K * N + 4 * N + 4 * M + 4 * M * N
+            bound_ms = max(ops / (i8peak * 1e12), byt / (hbm * 1e9)) * 1e3
+            row = {"K": K, "N": N, "M": M, "epilogue": "dequant f32", "ms": ms, "tops": ops / ms / 1e9,
+                   "roofline_ms": bound_ms, "frac": bound_ms / ms}
+            out["gemm"].append(row)
+            fused = None
+            if N == 384:
+                res = torch.randn(M, N, device="cuda")
+                gam, bet = torch.ones(384, device="cuda"), torch.zeros(384, device="cuda")
+                inv = torch.ones(384, device="cuda")
+                q = torch.empty(M, N, dtype=torch.int8, device="cuda")
+                sc = torch.empty(M, device="cuda")
+                fused = ("residual+LayerNorm+requant", lambda: eng.gemm_i8(1, a, asc, w, ws, bias, res=res, gamma=gam,
+                                                                         beta=bet, inv_smooth=inv, out=res, out_q=q,
+                                                                         out_scale=sc),
+                         M * K + K * N + 8 * M + 2 * 4 * M * N + M * N)
+            elif N == 1536:
+                inv = torch.ones(1536, device="cuda")
+                q = torch.empty(M, N, dtype=torch.int8, device="cuda")
+                sc = torch.empty(M, device="cuda")
+                fused = ("GELU+requant", lambda: eng.gemm_i8(2, a, asc, w, ws, bias, inv_smooth=inv, out_q=q,
+                                                            out_scale=sc), M * K + K * N + 8 * M + M * N)
+            if fused:
+                ms = timed(fused[1])
+                bound_ms = max(ops / (i8peak * 1e12), fused[2] / (hbm * 1e9)) * 1e3
+                out["gemm"].append({"K": K, "N": N, "M": M, "epilogue": fused[0], "ms": ms, "tops": ops / ms / 1e9,
+                                    "roofline_ms": bound_ms, "frac": bound_ms / ms})
+    n, L = 64, 512
+    qkv = torch.randn(n * L, 1152, device="cuda")
+    cu = torch.arange(0, n + 1, dtype=torch.int32, device="cuda") * L
+    ctx = torch.empty(n * L, 384, device="cuda")
+    ms = timed(lambda: eng.attention_f32(qkv, cu, n, L, ctx))
+    fl = n * 12 * 2.0 * 2.0 * L * L * 32
+    out["attention"] = {"shape": "64 x 12 heads x 512 x 32, fp32, exact reference order", "ms": ms,
+                        "tflops": fl / ms / 1e9}
+    out["basis"] = (f"roofline_ms = max(ops / int8 peak (2 x measured bf16 = {i8peak:.0f} TOPS), bytes / measured "
+                    f"HBM {hbm} GB/s); frac = roofline_ms / ms")
+    return out
+
+
+def ragged_throughput(eng) -> dict:
+    """Config 4: 131,072 sequences, lengths log-uniform on [8, 512], through ae_embed_batch_multi
+    (host ids in, embeddings out) on this process's GPU."""
+    from arctic_embed_s_int8 import embed_batch_multi, pack_sequences, synth
+
+    r = np.random.Generator(np.random.PCG64(4))
+    lens = np.exp(r.uniform(np.log(8), np.log(512), 131072)).astype(np.int64)
+    seqs = [synth.token_ids(int(L), r) for L in lens]
+    ids, cu = pack_sequences(seqs)
+    embed_batch_multi([eng], ids=ids[: int(cu[2048])], cu=cu[:2049])  # warm-up
+    t0 = time.perf_counter()
+    embed_batch_multi([eng], ids=ids, cu=cu)
+    dt = time.perf_counter() - t0
+    return {"sequences": len(seqs), "tokens": int(cu[-1]), "mean_len": float(lens.mean()), "seconds": dt,
+            "embeddings_per_s": len(seqs) / dt, "tokens_per_s": float(cu[-1]) / dt,
+            "api": "ae_embed_batch_multi, host buffers (wall clock, includes packing and copies)"}
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -236,6 +331,8 @@ def main() -> int:
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seqs-per-step", type=int, default=64)
     ap.add_argument("--no-extras", action="store_true", help="skip latency, kernel breakdown and CPU baseline")
+    ap.add_argument("--micro", action="store_true", help="also run the config-5 kernel microbenchmarks")
+    ap.add_argument("--ragged", action="store_true", help="also run config 4 (131,072 ragged sequences)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -339,7 +436,8 @@ def main() -> int:
         # latency (config 2 subset): p50/p99 of forward_cls, host buffers, CUDA-graph replay
         lat = {}
         r = np.random.Generator(np.random.PCG64(42))
-        for L, runs in ((32, args.latency_runs), (512, max(50, args.latency_runs // 3))):
+        for L, runs in ((8, args.latency_runs), (32, args.latency_runs), (128, args.latency_runs),
+                        (512, max(50, args.latency_runs // 3))):
             ids = synth.token_ids(L, r)
             for _ in range(20):
                 eng.forward_cls(ids)
@@ -400,6 +498,10 @@ def main() -> int:
                                   "frac": ach / hbm, "traffic": None, "ms_per_launch": ms_launch,
                                   "peak_basis": f"HBM copy bandwidth {src}"}
         result["int8_tops_whole_step"] = BATCH_SEQS * int8_ops_per_seq(SEQ_LEN) / (total_s / args.steps) / 1e12
+        if args.micro:
+            result["micro"] = microbench(eng, stream, peaks)
+        if args.ragged:
+            result["ragged"] = ragged_throughput(eng)
         try:
             result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
         except Exception as e:  # reported, not fatal

@@ -379,6 +379,40 @@ int attention(ae_ctx* c, const float* q, int q_C, int q_col, int q_tt, const flo
   return 0;
 }
 
+// Residual GEMM followed by LayerNorm + SmoothQuant quantization (attention-out, FFN-down):
+// fused into the GEMM epilogue when the batch has enough 128-row tiles to fill the GPU; otherwise
+// a plain-epilogue GEMM split over narrow column slices writes h = fma(acc, as*ws, bias + res)
+// into `scratch` (row-major) and a row kernel applies the same LayerNorm + quantization.
+int gemm_ln(ae_ctx* c, const CUtensorMap& ta, const DevLinear& L, int M, const float* a_scale, float* hidden,
+            int hidden_tt, const float* gamma, const float* beta, const float* inv_next, int8_t* out_q, float* out_s,
+            float* scratch) {
+  const int m_tiles = (M + 127) / 128;
+  if (m_tiles >= 74) {
+    return gemm(c, EPI_LN_QUANT, ta, L, M, a_scale, hidden, kHidden, gamma, beta, inv_next, hidden, kHidden, out_q,
+                out_s, hidden_tt);
+  }
+  GemmArgs g{};
+  g.M = M;
+  g.N = L.n;
+  g.K = L.k;
+  g.a_scale = a_scale;
+  g.w_scale = L.ws;
+  g.bias = L.bias;
+  g.res = hidden;
+  g.ldr = kHidden;
+  g.res_tt = hidden_tt;
+  g.out_f32 = scratch;
+  g.ldo = kHidden;
+  g.err = c->d_err;
+  ++c->launches;
+  int r = gemm_i8_launch(EPI_F32, ta, L.tmap, g, c->stream);
+  if (r) return fail(c, AE_ERR_CUDA, "GEMM launch failed (split residual path): code %d", r);
+  ++c->launches;
+  if (launch_ln_quant_rows(scratch, M, gamma, beta, inv_next, hidden, hidden_tt, out_q, out_s, c->stream))
+    return fail(c, AE_ERR_CUDA, "LayerNorm row kernel launch failed");
+  return 0;
+}
+
 // Enqueues the whole forward pass of a packed batch on the context's stream.
 int enqueue_forward(ae_ctx* c, const uint16_t* d_ids, const uint32_t* d_cu, int T, int n, int max_len, float* d_out) {
   Workspace& W = c->ws;
@@ -432,8 +466,8 @@ int enqueue_forward(ae_ctx* c, const uint16_t* d_ids, const uint32_t* d_cu, int 
     }
     {
       ProfScope ps(c, AE_KERNEL_ATTN_OUT);
-      AE_TRY(gemm(c, EPI_LN_QUANT, W.tm_act_q, Ly.ao, T, W.act_s, W.hidden, kHidden, Ly.ln1w, Ly.ln1b, Ly.fi.inv_s,
-                  W.hidden, kHidden, W.act_q, W.act_s, 1));
+      AE_TRY(gemm_ln(c, W.tm_act_q, Ly.ao, T, W.act_s, W.hidden, 1, Ly.ln1w, Ly.ln1b, Ly.fi.inv_s, W.act_q, W.act_s,
+                     W.ctx));
     }
     {
       ProfScope ps(c, AE_KERNEL_FFN_UP);
@@ -442,8 +476,8 @@ int enqueue_forward(ae_ctx* c, const uint16_t* d_ids, const uint32_t* d_cu, int 
     }
     {
       ProfScope ps(c, AE_KERNEL_FFN_DOWN);
-      AE_TRY(gemm(c, EPI_LN_QUANT, W.tm_inter_q, Ly.fo, T, W.inter_s, W.hidden, kHidden, Ly.ln2w, Ly.ln2b,
-                  M.layers[l + 1].qkv.inv_s, W.hidden, kHidden, W.act_q, W.act_s, 1));
+      AE_TRY(gemm_ln(c, W.tm_inter_q, Ly.fo, T, W.inter_s, W.hidden, 1, Ly.ln2w, Ly.ln2b, M.layers[l + 1].qkv.inv_s,
+                     W.act_q, W.act_s, W.ctx));
     }
   }
   const DevLayer& Z = M.layers[kLayers - 1];
@@ -461,12 +495,19 @@ int enqueue_forward(ae_ctx* c, const uint16_t* d_ids, const uint32_t* d_cu, int 
   AE_TRY(attention(c, W.q_cls, kHidden, 0, 0, W.qkv, 2 * kHidden, 0, kHidden, 1, W.cctx, d_cu, n, max_len, 1));
   if (launch_smooth_quant(W.cctx, Z.ao.inv_s, W.cq, W.cs, n, st))
     return fail(c, AE_ERR_CUDA, "context quantization launch failed");
-  AE_TRY(gemm(c, EPI_LN_QUANT, W.tm_cq, Z.ao, n, W.cs, W.ch, kHidden, Z.ln1w, Z.ln1b, Z.fi.inv_s, W.ch, kHidden, W.cq,
-              W.cs));
+  AE_TRY(gemm_ln(c, W.tm_cq, Z.ao, n, W.cs, W.ch, 0, Z.ln1w, Z.ln1b, Z.fi.inv_s, W.cq, W.cs, W.cctx));
   AE_TRY(gemm(c, EPI_GELU_QUANT, W.tm_cq, Z.fi, n, W.cs, nullptr, 0, nullptr, nullptr, Z.fo.inv_s, nullptr, 0, W.cinter_q,
               W.cinter_s));
-  AE_TRY(gemm(c, EPI_LN_FINAL, W.tm_cinter_q, Z.fo, n, W.cinter_s, W.ch, kHidden, Z.ln2w, Z.ln2b, nullptr, d_out,
-              kHidden, nullptr, nullptr));
+  if ((n + 127) / 128 >= 74) {
+    AE_TRY(gemm(c, EPI_LN_FINAL, W.tm_cinter_q, Z.fo, n, W.cinter_s, W.ch, kHidden, Z.ln2w, Z.ln2b, nullptr, d_out,
+                kHidden, nullptr, nullptr));
+  } else {
+    AE_TRY(gemm(c, EPI_F32, W.tm_cinter_q, Z.fo, n, W.cinter_s, W.ch, kHidden, nullptr, nullptr, nullptr, W.cctx,
+                kHidden, nullptr, nullptr));
+    ++c->launches;
+    if (launch_ln_final_rows(W.cctx, n, Z.ln2w, Z.ln2b, d_out, st))
+      return fail(c, AE_ERR_CUDA, "final LayerNorm row kernel launch failed");
+  }
   c->graph_kernels = c->launches - launches0;
   return 0;
 }

@@ -259,11 +259,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           float* o = g.out_f32 + size_t(row) * g.ldo + n0 + c0;
           const float* rs = g.res ? g.res + size_t(row) * g.ldr + n0 + c0 : nullptr;
+          const float* rs_tt = (g.res && g.res_tt) ? g.res + tt_index(row, n0 + c0, g.ldr) : nullptr;
 #pragma unroll
           for (int q = 0; q < CW / 4; ++q) {
             float v[4];
             float4 rr = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (rs) rr = reinterpret_cast<const float4*>(rs)[q];
+            if (rs_tt)
+              rr = make_float4(rs_tt[(4 * q) << 7], rs_tt[(4 * q + 1) << 7], rs_tt[(4 * q + 2) << 7],
+                               rs_tt[(4 * q + 3) << 7]);
+            else if (rs)
+              rr = reinterpret_cast<const float4*>(rs)[q];
             const float rv[4] = {rr.x, rr.y, rr.z, rr.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
@@ -696,6 +701,8 @@ static cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const Ge
 // device before any launch can be captured into a CUDA graph).
 int gemm_i8_prime() {
   int r = 0;
+  r |= set_smem<64, EPI_F32, true, 4>();
+  r |= set_smem<64, EPI_F32, false, 4>();
   r |= set_smem<128, EPI_F32, true, 4>();
   r |= set_smem<192, EPI_F32, true, 4>();
   r |= set_smem<256, EPI_F32, true, 4>();
@@ -717,12 +724,26 @@ int gemm_i8_launch(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const 
   const bool res = g.K == kResK;
   cudaError_t e = cudaSuccess;
   switch (epi) {
-    case EPI_F32:
-      if (g.N % 256 == 0) e = res ? launch<256, EPI_F32, true, 4>(ta, tb, g, st) : launch<256, EPI_F32, false, 4>(ta, tb, g, st);
-      else if (g.N % 192 == 0) e = res ? launch<192, EPI_F32, true, 4>(ta, tb, g, st) : launch<192, EPI_F32, false, 4>(ta, tb, g, st);
-      else if (g.N % 128 == 0) e = res ? launch<128, EPI_F32, true, 4>(ta, tb, g, st) : launch<128, EPI_F32, false, 4>(ta, tb, g, st);
-      else return -11;
+    case EPI_F32: {
+      // wide slices for large M; for few M tiles, narrower slices spread the work over more SMs
+      const int mt = (g.M + BM - 1) / BM;
+      const bool few = mt * (g.N / 128) < num_sms();
+      if (few && g.N % 64 == 0 && mt * (g.N / 64) <= num_sms())
+        e = res ? launch<64, EPI_F32, true, 4>(ta, tb, g, st) : launch<64, EPI_F32, false, 4>(ta, tb, g, st);
+      else if (few && g.N % 128 == 0)
+        e = res ? launch<128, EPI_F32, true, 4>(ta, tb, g, st) : launch<128, EPI_F32, false, 4>(ta, tb, g, st);
+      else if (g.N % 256 == 0)
+        e = res ? launch<256, EPI_F32, true, 4>(ta, tb, g, st) : launch<256, EPI_F32, false, 4>(ta, tb, g, st);
+      else if (g.N % 192 == 0)
+        e = res ? launch<192, EPI_F32, true, 4>(ta, tb, g, st) : launch<192, EPI_F32, false, 4>(ta, tb, g, st);
+      else if (g.N % 128 == 0)
+        e = res ? launch<128, EPI_F32, true, 4>(ta, tb, g, st) : launch<128, EPI_F32, false, 4>(ta, tb, g, st);
+      else if (g.N % 64 == 0)
+        e = res ? launch<64, EPI_F32, true, 4>(ta, tb, g, st) : launch<64, EPI_F32, false, 4>(ta, tb, g, st);
+      else
+        return -11;
       break;
+    }
     case EPI_LN_QUANT:
       if (g.N != kHidden) return -11;
       e = res ? launch<384, EPI_LN_QUANT, true, 3>(ta, tb, g, st) : launch<384, EPI_LN_QUANT, false, 3>(ta, tb, g, st);

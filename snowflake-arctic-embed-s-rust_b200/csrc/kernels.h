@@ -40,6 +40,10 @@ struct AttnArgs {
 };
 
 int launch_embed(const EmbedArgs& a, cudaStream_t st);
+int launch_ln_quant_rows(const float* h_in, int M, const float* gamma, const float* beta, const float* inv_s,
+                         float* hidden, int hidden_tt, int8_t* q, float* scale, cudaStream_t st);
+int launch_ln_final_rows(const float* h_in, int M, const float* gamma, const float* beta, float* out,
+                         cudaStream_t st);
 int launch_smooth_quant(const float* x, const float* inv_s, int8_t* q, float* scale, int rows, cudaStream_t st);
 int launch_row_meta(const uint32_t* cu, int n_seqs, uint16_t* pos, int32_t* cls_row, int* err, cudaStream_t st);
 int launch_gather_cls(const int32_t* cls_row, int n, const int8_t* act_q, const float* act_s, const float* hidden,

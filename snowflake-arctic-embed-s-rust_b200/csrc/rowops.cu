@@ -101,6 +101,87 @@ __global__ void __launch_bounds__(256) k_embed_ln_quant(EmbedArgs a) {
   }
 }
 
+// One half-warp per row: layernorm_smooth_quantize_row_avx2 (src/simd_math.rs:369-477) on rows of
+// h = fma(acc, a_scale * w_scale, bias + residual) that a GEMM with the plain epilogue wrote
+// (row-major [M, 384]); the LayerNorm output goes to hidden (tile-transposed when hidden_tt, else
+// row-major), the quantized row to q / scale. Used when a batch has too few row tiles for the fused
+// LayerNorm epilogue to fill the GPU.
+__global__ void __launch_bounds__(256) k_ln_quant_rows(const float* __restrict__ h_in, int M,
+                                                       const float* __restrict__ gamma,
+                                                       const float* __restrict__ beta,
+                                                       const float* __restrict__ inv_s, float* __restrict__ hidden,
+                                                       int hidden_tt, int8_t* __restrict__ q,
+                                                       float* __restrict__ scale) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 4;
+  const int l = threadIdx.x & 15;
+  const unsigned mask = 0xffffffffu;
+  const bool active = row < M;
+  const int hw = active ? row : M - 1;
+  const float* x = h_in + size_t(hw) * kHidden;
+  float h[24];
+  float p = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 24; ++i) {
+    h[i] = x[l + 16 * i];
+    p = p + h[i];
+  }
+  const float mean = halfwarp_tree16(p, mask) / float(kHidden);
+  p = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 24; ++i) {
+    const float d = h[i] - mean;
+    p = fmaf(d, d, p);
+  }
+  const float var = halfwarp_tree16(p, mask) / float(kHidden);
+  const float rstd = 1.0f / sqrtf(var + kLnEps);
+  float vmax = 1e-8f;
+#pragma unroll
+  for (int i = 0; i < 24; ++i) {
+    const int j = l + 16 * i;
+    h[i] = fmaf((h[i] - mean) * rstd, gamma[j], beta[j]);
+    if (active) hidden[hidden_tt ? tt_index(hw, j, kHidden) : size_t(hw) * kHidden + j] = h[i];
+    vmax = fmaxf(vmax, fabsf(h[i] * inv_s[j]));
+  }
+  const float max_abs = halfwarp_max(vmax, mask);
+  const float inv_scale = 127.0f / max_abs;
+#pragma unroll
+  for (int i = 0; i < 24; ++i) {
+    const int j = l + 16 * i;
+    const int8_t qv = int8_t(quant_i8(h[i] * (inv_s[j] * inv_scale)));
+    if (active) q[size_t(hw) * kHidden + j] = qv;
+  }
+  if (active && l == 0) scale[hw] = max_abs / 127.0f;
+}
+
+// One thread per row: layernorm_inplace_row + l2_normalize_inplace (src/simd_math.rs:481-497,
+// :2892-2903), whose sums are sequential over the 384 elements, on rows of h (row-major [M, 384]).
+__global__ void k_ln_final_rows(const float* __restrict__ h_in, int M, const float* __restrict__ gamma,
+                                const float* __restrict__ beta, float* __restrict__ out) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= M) return;
+  const float* x = h_in + size_t(row) * kHidden;
+  float sum = 0.0f;
+  for (int j = 0; j < kHidden; ++j) sum = sum + x[j];
+  const float mean = sum / float(kHidden);
+  float var = 0.0f;
+  for (int j = 0; j < kHidden; ++j) {
+    const float d = x[j] - mean;
+    var = var + d * d;
+  }
+  const float rstd = 1.0f / sqrtf(var / float(kHidden) + kLnEps);
+  float ss = 0.0f;
+  for (int j = 0; j < kHidden; ++j) {
+    const float y = (x[j] - mean) * rstd * gamma[j] + beta[j];
+    ss = ss + y * y;
+  }
+  const float inv = ss > 0.0f ? 1.0f / sqrtf(ss) : 1.0f;
+  float* o = out + size_t(row) * kHidden;
+  for (int j = 0; j < kHidden; ++j) {
+    const float y = (x[j] - mean) * rstd * gamma[j] + beta[j];
+    o[j] = ss > 0.0f ? y * inv : y;
+  }
+}
+
 // One warp per row: smooth_quantize_row_avx2 (src/simd_math.rs:584-649), the quantization of the
 // attention context with attn_out.inv_smooth (src/model.rs:324-328).
 __global__ void __launch_bounds__(256) k_smooth_quant(const float* __restrict__ x, const float* __restrict__ inv_s,
@@ -178,6 +259,20 @@ int launch_embed(const EmbedArgs& a, cudaStream_t st) {
   if (a.T <= 0) return 0;
   const int rows_per_block = 16;
   k_embed_ln_quant<<<(a.T + rows_per_block - 1) / rows_per_block, 256, 0, st>>>(a);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int launch_ln_quant_rows(const float* h_in, int M, const float* gamma, const float* beta, const float* inv_s,
+                         float* hidden, int hidden_tt, int8_t* q, float* scale, cudaStream_t st) {
+  if (M <= 0) return 0;
+  k_ln_quant_rows<<<(M + 15) / 16, 256, 0, st>>>(h_in, M, gamma, beta, inv_s, hidden, hidden_tt, q, scale);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
+int launch_ln_final_rows(const float* h_in, int M, const float* gamma, const float* beta, float* out,
+                         cudaStream_t st) {
+  if (M <= 0) return 0;
+  k_ln_final_rows<<<(M + 127) / 128, 128, 0, st>>>(h_in, M, gamma, beta, out);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 

@@ -41,6 +41,20 @@ def test_ragged_batch_matches_oracle(engine, oracle_model):
     np.testing.assert_array_equal(got, single)
 
 
+def test_fused_and_split_layernorm_paths_agree(engine, oracle_model):
+    """A batch of >= 74 row tiles takes the fused LayerNorm GEMM epilogue; a single sequence takes the
+    narrow-slice GEMM + LayerNorm row kernel. Both compute the same formulas in the same order, so
+    every embedding is bit-identical across the two paths."""
+    r = rng(9)
+    seqs = [synth.token_ids(512, r) for _ in range(19)] + [synth.token_ids(L, r) for L in (1, 7, 130)]
+    assert sum(len(s) for s in seqs) >= 74 * 128
+    got = engine.forward_ragged(seqs)
+    for i in (0, 7, 18, 19, 20, 21):
+        np.testing.assert_array_equal(got[i], engine.forward_cls(seqs[i]))
+    cos, mx = close(got[21], oracle_model.forward_cls(seqs[21]))
+    assert cos >= COS_MIN and mx <= MAXABS_MAX
+
+
 def test_reference_ragged_packing(engine, oracle_model):
     """embed_batch packs short sequences (< 16 tokens) into forward_ragged_cls (src/lib.rs:161-238)."""
     r = rng(8)
