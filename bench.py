@@ -316,8 +316,15 @@ def ragged_throughput(eng) -> dict:
     t0 = time.perf_counter()
     embed_batch_multi([eng], ids=ids, cu=cu)
     dt = time.perf_counter() - t0
+    # a second, profiled pass: device time per kernel kind next to the wall clock
+    eng.profile(True)
+    embed_batch_multi([eng], ids=ids, cu=cu)
+    eng.sync()
+    prof = eng.profile_read()
+    eng.profile(False)
     return {"sequences": len(seqs), "tokens": int(cu[-1]), "mean_len": float(lens.mean()), "seconds": dt,
             "embeddings_per_s": len(seqs) / dt, "tokens_per_s": float(cu[-1]) / dt,
+            "kernels_s": {k: round(v[0] / 1e3, 4) for k, v in prof.items()},
             "api": "ae_embed_batch_multi, host buffers (wall clock, includes packing and copies)"}
 
 
@@ -498,14 +505,20 @@ def main() -> int:
                                   "frac": ach / hbm, "traffic": None, "ms_per_launch": ms_launch,
                                   "peak_basis": f"HBM copy bandwidth {src}"}
         result["int8_tops_whole_step"] = BATCH_SEQS * int8_ops_per_seq(SEQ_LEN) / (total_s / args.steps) / 1e12
-        if args.micro:
-            result["micro"] = microbench(eng, stream, peaks)
-        if args.ragged:
-            result["ragged"] = ragged_throughput(eng)
         try:
             result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
         except Exception as e:  # reported, not fatal
             result["cpu_baseline"] = {"error": str(e)}
+    if rank == 0 and args.micro:
+        peaks = {}
+        try:
+            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+                peaks = json.load(f)
+        except OSError:
+            pass
+        result["micro"] = microbench(eng, stream, peaks)
+    if rank == 0 and args.ragged:
+        result["ragged"] = ragged_throughput(eng)
     if rank == 0:
         print(json.dumps(result), flush=True)
     eng.close()

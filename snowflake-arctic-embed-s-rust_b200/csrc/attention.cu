@@ -13,8 +13,11 @@
 // operation works on two keys at once with the sm_100 packed f32x2 instructions: each lane of a
 // packed FMA / add / multiply is an ordinary IEEE single-precision operation, so the results are
 // the same bits as the scalar sequence, and the reference's even/odd weighted-sum accumulators are
-// exactly the two lanes. Sequences of up to kStoreMaxLen keys keep their scores (then
-// exponentials) in shared memory; longer ones recompute the scores in each softmax pass.
+// exactly the two lanes. Each thread keeps the scores, then the exponentials, of its query in its
+// TMEM lane (column t = key t), so every score is computed once and shared memory holds only K / V.
+//
+// k_attention_wide: the same with two or four warpgroups on one tile's TMEM lanes, for sequences
+// of more than 128 keys (whose score columns leave room for only 1-2 CTAs per SM).
 //
 // k_attention_cls: one warp per (sequence, head) for the single [CLS] query of layer 11: lanes
 // split the keys for the scores, 16 lanes run the 16 exp-sum chains, lane d accumulates dim d.
@@ -28,26 +31,29 @@
 
 namespace ae {
 
+#ifndef ATTN_WIDE_256_NWG
+#define ATTN_WIDE_256_NWG 2
+#define ATTN_WIDE_256_MINB 2
+#endif
+#define ATTN_WIDE_256 ATTN_WIDE_256_NWG, ATTN_WIDE_256_MINB
+
 __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
 __device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
 __device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
 __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 
-// Scores of the key pair (2i, 2i+1) stored as kp[d] = (k[2i][d], k[2i+1][d]).
+// Scores of the key pair (2i, 2i+1). K pairs are staged with the dims that one 8-lane partial
+// sum of the reference's dot32x4 uses side by side: kp[4l + j] = (k[2i][l + 8j], k[2i+1][l + 8j]),
+// so lane l's four products come from two 128-bit shared loads.
 __device__ __forceinline__ float2 score_pair(const float (&q)[32], const float2* __restrict__ kp, bool grouped) {
-  float2 k[32];
-  const float4* k4 = reinterpret_cast<const float4*>(kp);  // 128-bit shared loads: two dims per load
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const float4 t = k4[i];
-    k[2 * i] = f2(t.x, t.y);
-    k[2 * i + 1] = f2(t.z, t.w);
-  }
+  const float4* k4 = reinterpret_cast<const float4*>(kp);
   float2 s8[8];
 #pragma unroll
   for (int l = 0; l < 8; ++l) {
-    const float2 a = fma2(f2(q[8 + l], q[8 + l]), k[8 + l], mul2(f2(q[l], q[l]), k[l]));
-    const float2 b = fma2(f2(q[24 + l], q[24 + l]), k[24 + l], mul2(f2(q[16 + l], q[16 + l]), k[16 + l]));
+    const float4 t0 = k4[2 * l];      // dims l, l + 8 of both keys
+    const float4 t1 = k4[2 * l + 1];  // dims l + 16, l + 24
+    const float2 a = fma2(f2(q[8 + l], q[8 + l]), f2(t0.z, t0.w), mul2(f2(q[l], q[l]), f2(t0.x, t0.y)));
+    const float2 b = fma2(f2(q[24 + l], q[24 + l]), f2(t1.z, t1.w), mul2(f2(q[16 + l], q[16 + l]), f2(t1.x, t1.y)));
     s8[l] = add2(a, b);
   }
   if (grouped)
@@ -80,9 +86,9 @@ __device__ __forceinline__ float ld_act(const float* p, int C, int tt, int t, in
   return tt ? p[tt_index(t, c, C)] : p[size_t(t) * C + c];
 }
 
-// Stages the head's K and V of rows [s0, s0 + L) as key pairs kp[p][d] = (k[2p][d], k[2p+1][d])
-// (odd L: the last pair's second key is 0). A warp covers 8 pairs x 4 dims per step, so the
-// tile-transposed rows it reads are contiguous.
+// Stages the head's K and V of rows [s0, s0 + L) as key pairs (k[2p][d], k[2p+1][d]), K dims in
+// score_pair's order, V dims in order (odd L: the last pair's second key is 0). A warp covers
+// 8 pairs x 4 dims per step, so the tile-transposed rows it reads are contiguous.
 __device__ __forceinline__ void stage_kv_pairs(const AttnArgs& a, int s0, int L, int h, float2* kp, float2* vp) {
   const int pairs = (L + 1) >> 1;
   const int kc = a.k_col + 32 * h, vc = a.v_col + 32 * h;
@@ -100,7 +106,7 @@ __device__ __forceinline__ void stage_kv_pairs(const AttnArgs& a, int s0, int L,
       k1 = ld_act(a.kv, a.kv_C, a.kv_tt, s0 + t1, kc + d);
       v1 = ld_act(a.kv, a.kv_C, a.kv_tt, s0 + t1, vc + d);
     }
-    kp[p * KPS + d] = f2(k0, k1);
+    kp[p * KPS + (d & 7) * 4 + (d >> 3)] = f2(k0, k1);  // score_pair's order
     vp[p * KPS + d] = f2(v0, v1);
   }
 }
@@ -285,6 +291,185 @@ __global__ void __launch_bounds__(QT) k_attention_rows(AttnArgs a) {
   if (warp == 0) tmem_dealloc(tmem_slot, cols);
 }
 
+// NWG warpgroups per 128-query tile: warps w, w + 4, ... share TMEM lane quadrant w & 3 (the same
+// queries). Scores and exponentials: group g takes keys t0 + g KPG .. t0 + (g + 1) KPG - 1 of
+// every 16-key chunk (KPG = 16 / NWG), so each of the reference's 16 sum slots is summed in order
+// by one group; P.V: group g accumulates dims g DPG .. (g + 1) DPG - 1 (DPG = 32 / NWG) over all
+// keys in order.
+template <int NWG, int MINB>
+__global__ void __launch_bounds__(128 * NWG, MINB) k_attention_wide(AttnArgs a) {
+  constexpr int KPG = 16 / NWG;  // keys of a 16-key chunk per group (8 or 4)
+  constexpr int DPG = 32 / NWG;  // dims of V per group (16 or 8)
+  extern __shared__ float4 smem4[];
+  __shared__ uint32_t tmem_slot;
+  __shared__ float xmx[NWG][128];
+  __shared__ float xsl[16][128];  // the 16 slot sums of every query
+  const int s = blockIdx.x;
+  const int h = blockIdx.y;
+  const int tile = blockIdx.z;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int grp = warp >> 2;
+  const int qt = tid & 127;
+  const int s0 = int(a.cu[s]);
+  const int L = int(a.cu[s + 1]) - s0;
+  if (L <= 0 || L > a.max_len) {
+    if (tid == 0 && tile == 0 && h == 0) record_err(a.err, DEV_ERR_BAD_SHAPE);
+    return;
+  }
+  if (tile * 128 >= L) return;
+  const uint32_t cols = tmem_cols_for_len(L);
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, cols);
+    tmem_relinquish();
+  }
+  const int pairs = (L + 1) >> 1;
+  float2* kp = reinterpret_cast<float2*>(smem4);
+  float2* vp = kp + pairs * KPS;
+  stage_kv_pairs(a, s0, L, h, kp, vp);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tl = tmem_slot + (uint32_t((warp & 3) * 32) << 16);
+
+  const int qi = tile * 128 + qt;
+  const bool active = qi < L;
+  const int qrow = s0 + (active ? qi : L - 1);
+  const int L4 = L & ~3, L8 = L & ~7, L16 = L & ~15;
+  const int ko = KPG * grp;  // this group's keys within a 16-key chunk
+  uint32_t r[16];
+
+  // pass 1: scores -> TMEM and their max
+  float mx = -INFINITY;
+  {
+    float q[32];
+    load_query(a, qrow, h, q);
+    for (int t0 = 0; t0 < L; t0 += 16) {
+#pragma unroll
+      for (int j = 0; j < KPG / 2; ++j) {
+        const int t = t0 + ko + 2 * j;
+        float2 sp = f2(0.0f, 0.0f);
+        if (t < L) {
+          sp = score_pair(q, kp + (t >> 1) * KPS, t < L4);
+          mx = fmaxf(mx, sp.x);
+          if (t + 1 < L) mx = fmaxf(mx, sp.y);
+        }
+        r[2 * j] = __float_as_uint(sp.x);
+        r[2 * j + 1] = __float_as_uint(sp.y);
+      }
+      if constexpr (KPG == 8) tmem_st8(tl + t0 + ko, r);
+      else tmem_st4(tl + t0 + ko, r);
+    }
+  }
+  tmem_st_wait();
+  xmx[grp][qt] = mx;
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < NWG; ++g) mx = fmaxf(mx, xmx[g][qt]);
+  const float2 neg_mx = f2(-mx, -mx);
+
+  // pass 2: exponentials -> TMEM; this group's sum slots (and, for slots 0-7, the trailing
+  // 8-key chunk) accumulated in chunk order
+  float2 vs[KPG / 2];
+#pragma unroll
+  for (int j = 0; j < KPG / 2; ++j) vs[j] = f2(0.0f, 0.0f);
+  for (int t0 = 0; t0 < L; t0 += 16) {
+    if constexpr (KPG == 8) tmem_ld8(tl + t0 + ko, r);
+    else tmem_ld4(tl + t0 + ko, r);
+    tmem_ld_wait();
+    if (t0 + 16 <= L16) {
+#pragma unroll
+      for (int j = 0; j < KPG / 2; ++j) {
+        const float2 e = cw_exp2(add2(f2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), neg_mx));
+        vs[j] = add2(vs[j], e);
+        r[2 * j] = __float_as_uint(e.x);
+        r[2 * j + 1] = __float_as_uint(e.y);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < KPG / 2; ++j) {
+        const int t = t0 + ko + 2 * j;
+        const float2 x = add2(f2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), neg_mx);
+        float2 e;
+        if (ko < 8 && t + 1 < L8) {  // the trailing 8-key chunk (keys L16 .. L16 + 7): slots 0-7
+          e = cw_exp2(x);
+          vs[j] = add2(vs[j], e);
+        } else {  // the last L % 8 keys: scalar exp, summed after the tree
+          e = f2(t < L ? scalar_expf(x.x) : 0.0f, t + 1 < L ? scalar_expf(x.y) : 0.0f);
+        }
+        r[2 * j] = __float_as_uint(e.x);
+        r[2 * j + 1] = __float_as_uint(e.y);
+      }
+    }
+    if constexpr (KPG == 8) tmem_st8(tl + t0 + ko, r);
+    else tmem_st4(tl + t0 + ko, r);
+  }
+  tmem_st_wait();
+#pragma unroll
+  for (int j = 0; j < KPG / 2; ++j) {
+    xsl[ko + 2 * j][qt] = vs[j].x;
+    xsl[ko + 2 * j + 1][qt] = vs[j].y;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (grp == 0) {
+    float v8[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v8[j] = xsl[j][qt] + xsl[8 + j][qt];  // acc0 + acc1
+    float sum = tree8(v8);
+    if (L8 < L) {  // ((tree + e[L8]) + e[L8 + 1]) + ..., the keys re-read from TMEM
+      tmem_ld16(tl + L16, r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (L16 + j >= L8 && L16 + j < L) sum = sum + __uint_as_float(r[j]);
+    }
+    xmx[0][qt] = 1.0f / sum;
+  }
+  __syncthreads();
+  const float inv = xmx[0][qt];
+  const float2 inv2 = f2(inv, inv);
+
+  // pass 3: probabilities and the weighted sum of this group's dims of V
+  float2 acc[DPG];
+#pragma unroll
+  for (int d = 0; d < DPG; ++d) acc[d] = f2(0.0f, 0.0f);
+  for (int t0 = 0; t0 < L; t0 += 16) {
+    tmem_ld16(tl + t0, r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int t = t0 + 2 * j;
+      if (t + 1 < L) {
+        const float2 p = mul2(f2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), inv2);
+        const float4* v4 = reinterpret_cast<const float4*>(vp + (t >> 1) * KPS + DPG * grp);
+#pragma unroll
+        for (int i = 0; i < DPG / 2; ++i) {
+          const float4 vv = v4[i];
+          acc[2 * i] = fma2(f2(vv.x, vv.y), p, acc[2 * i]);
+          acc[2 * i + 1] = fma2(f2(vv.z, vv.w), p, acc[2 * i + 1]);
+        }
+      } else if (t < L) {  // odd L: the last key goes to the even accumulator
+        const float pa = __uint_as_float(r[2 * j]) * inv;
+        const float2* v = vp + (t >> 1) * KPS + DPG * grp;
+#pragma unroll
+        for (int d = 0; d < DPG; ++d) acc[d].x = fmaf(v[d].x, pa, acc[d].x);
+      }
+    }
+  }
+  if (active) {
+    float4* o = reinterpret_cast<float4*>(a.out + size_t(s0 + qi) * kHidden + h * 32 + DPG * grp);
+#pragma unroll
+    for (int i = 0; i < DPG / 4; ++i)
+      o[i] = make_float4(acc[4 * i].x + acc[4 * i].y, acc[4 * i + 1].x + acc[4 * i + 1].y,
+                         acc[4 * i + 2].x + acc[4 * i + 2].y, acc[4 * i + 3].x + acc[4 * i + 3].y);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem_slot, cols);
+}
+
 // One warp per (sequence, head): the single [CLS] query (row s of q / out) over the sequence's keys.
 // Shared memory per warp: the scores / exponentials (512 floats) and a 32-key x 32-dim V chunk.
 constexpr int kClsWarpFloats = kMaxPos + 32 * 33;
@@ -362,21 +547,37 @@ __global__ void __launch_bounds__(128) k_attention_cls(AttnArgs a, int n_seqs) {
 
 constexpr size_t kRowsSmemMax = 220 * 1024;  // dynamic shared memory cap (static smem comes on top)
 
-// Shared memory of a rows CTA: the K / V pairs, padded so that at most 512 / cols CTAs share an SM
-// (their TMEM allocations then always fit; a CTA never waits in tcgen05.alloc).
-static size_t rows_smem(int max_len) {
+// Static shared memory of the kernels (cudaFuncGetAttributes at setup), counted by rows_smem.
+static size_t g_static_rows = 0, g_static_wide2 = 0, g_static_wide4 = 0;
+
+// Dynamic shared memory of a CTA: the K / V pairs, padded so that at most 512 / cols CTAs share an
+// SM (their TMEM allocations then always fit; a CTA never waits in tcgen05.alloc). static_bytes:
+// the kernel's static shared memory, which shares the SM's 228 KB with the dynamic part.
+static size_t rows_smem_cap(size_t static_bytes) {  // a CTA holds at most 227 KB, static included
+  const size_t cap = 227 * 1024 - static_bytes;
+  return cap < kRowsSmemMax ? cap : kRowsSmemMax;
+}
+static size_t rows_smem(int max_len, size_t static_bytes) {
   const size_t kv = size_t((max_len + 1) / 2) * KPS * 8 * 2;
   const uint32_t cols = tmem_cols_for_len(max_len);
   const size_t per_sm = 227 * 1024;
-  size_t floor_bytes = per_sm / (512 / cols) - 2048 + 1;  // no more than 512 / cols CTAs fit
-  if (floor_bytes > kRowsSmemMax) floor_bytes = kRowsSmemMax;
+  size_t floor_bytes = per_sm / (512 / cols) - 2048 + 1 - static_bytes;  // no more than 512 / cols CTAs fit
+  if (floor_bytes > rows_smem_cap(static_bytes)) floor_bytes = rows_smem_cap(static_bytes);
   return kv > floor_bytes ? kv : floor_bytes;
 }
 
 template <int QT>
 static int launch_rows(const AttnArgs& a, int n_seqs, cudaStream_t st) {
   dim3 grid(n_seqs, kHeads, (a.max_len + QT - 1) / QT);
-  k_attention_rows<QT><<<grid, QT, rows_smem(a.max_len), st>>>(a);
+  if (QT == 128 && tmem_cols_for_len(a.max_len) == 256) {  // 2 CTAs per SM: two warpgroups each
+    k_attention_wide<ATTN_WIDE_256><<<grid, 128 * ATTN_WIDE_256_NWG, rows_smem(a.max_len, g_static_wide2), st>>>(a);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+  }
+  if (QT == 128 && tmem_cols_for_len(a.max_len) == 512) {  // 1 CTA per SM: four warpgroups
+    k_attention_wide<4, 1><<<grid, 512, rows_smem(a.max_len, g_static_wide4), st>>>(a);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+  }
+  k_attention_rows<QT><<<grid, QT, rows_smem(a.max_len, g_static_rows), st>>>(a);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
@@ -384,12 +585,24 @@ static int smem_attr(const void* fn, size_t bytes) {
   return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes)) == cudaSuccess ? 0 : -1;
 }
 
+static int static_smem(const void* fn, size_t* out) {
+  cudaFuncAttributes at{};
+  if (cudaFuncGetAttributes(&at, fn) != cudaSuccess) return -1;
+  *out = at.sharedSizeBytes;
+  return 0;
+}
+
 int attention_prime() {
   int r = 0;
-  const size_t most = kRowsSmemMax;
-  r |= smem_attr((const void*)k_attention_rows<128>, most);
-  r |= smem_attr((const void*)k_attention_rows<64>, most);
-  r |= smem_attr((const void*)k_attention_rows<32>, most);
+  r |= static_smem((const void*)k_attention_rows<128>, &g_static_rows);
+  r |= static_smem((const void*)k_attention_wide<ATTN_WIDE_256>, &g_static_wide2);
+  r |= static_smem((const void*)k_attention_wide<4, 1>, &g_static_wide4);
+  if (r) return r;
+  r |= smem_attr((const void*)k_attention_rows<128>, rows_smem_cap(g_static_rows));
+  r |= smem_attr((const void*)k_attention_rows<64>, rows_smem_cap(g_static_rows));
+  r |= smem_attr((const void*)k_attention_rows<32>, rows_smem_cap(g_static_rows));
+  r |= smem_attr((const void*)k_attention_wide<ATTN_WIDE_256>, rows_smem_cap(g_static_wide2));
+  r |= smem_attr((const void*)k_attention_wide<4, 1>, rows_smem_cap(g_static_wide4));
   r |= smem_attr((const void*)k_attention_cls, 4 * kClsWarpFloats * 4);
   return r;
 }
@@ -402,10 +615,12 @@ int launch_attention_exact(const AttnArgs& a, int n_seqs, cudaStream_t st) {
     k_attention_cls<<<(items + 3) / 4, 128, 4 * kClsWarpFloats * 4, st>>>(a, n_seqs);
     return cudaGetLastError() == cudaSuccess ? 0 : -3;
   }
-  // query tile: 128 threads when the grid fills the GPU, smaller tiles for few sequences
-  const long ctas128 = long(n_seqs) * kHeads * ((a.max_len + 127) / 128);
-  if (ctas128 >= 2 * 148) return launch_rows<128>(a, n_seqs, st);
-  if (ctas128 * 2 >= 2 * 148) return launch_rows<64>(a, n_seqs, st);
+  // query tile: no wider than the sequences (32 / 64 threads for short ones, whose TMEM then packs
+  // 16 / 8 CTAs per SM), and narrower while the grid has fewer than two CTAs per SM
+  const int cap = a.max_len <= 32 ? 32 : a.max_len <= 64 ? 64 : 128;
+  const long heads = long(n_seqs) * kHeads;
+  if (cap == 128 && heads * ((a.max_len + 127) / 128) >= 2 * 148) return launch_rows<128>(a, n_seqs, st);
+  if (cap >= 64 && heads * ((a.max_len + 63) / 64) >= 2 * 148) return launch_rows<64>(a, n_seqs, st);
   return launch_rows<32>(a, n_seqs, st);
 }
 

@@ -117,6 +117,9 @@ struct ae_ctx {
   std::vector<cudaEvent_t> prof_pool;
   uint64_t launches = 0;  // kernels enqueued (or replayed from a graph) on this context
   uint64_t graph_kernels = 0;
+  // host packing of the last ragged batch: sequences grouped by attention length class
+  std::vector<uint32_t> order;       // packed position -> caller's sequence index
+  std::vector<ae::AttnSegment> segs;  // consecutive packed sequences of one class
 };
 
 namespace {
@@ -232,6 +235,11 @@ void drop_graphs(ae_ctx* c) {
 int reserve(ae_ctx* c, uint32_t tokens, uint32_t seqs) {
   Workspace& w = c->ws;
   if (tokens <= w.cap_tokens && seqs <= w.cap_seqs && w.arena) return 0;
+  // grow geometrically, so that a stream of slowly growing batches reallocates a few times only
+  if (w.arena) {
+    if (tokens > w.cap_tokens) tokens = std::max<uint32_t>(tokens, w.cap_tokens + w.cap_tokens / 2);
+    if (seqs > w.cap_seqs) seqs = std::max<uint32_t>(seqs, w.cap_seqs + w.cap_seqs / 2);
+  }
   tokens = std::max(tokens, w.cap_tokens);
   seqs = std::max(seqs, w.cap_seqs);
   tokens = std::max<uint32_t>(align_up(tokens, 128), 128);
@@ -358,7 +366,8 @@ int gemm(ae_ctx* c, int epi, const CUtensorMap& ta, const DevLinear& L, int M, c
 }
 
 int attention(ae_ctx* c, const float* q, int q_C, int q_col, int q_tt, const float* kv, int kv_C, int k_col,
-              int v_col, int kv_tt, float* out, const uint32_t* cu, int n, int max_len, int cls) {
+              int v_col, int kv_tt, float* out, const uint32_t* cu, int n, int max_len, int cls,
+              const std::vector<AttnSegment>* segs = nullptr) {
   AttnArgs a{};
   a.q = q;
   a.q_C = q_C;
@@ -374,6 +383,16 @@ int attention(ae_ctx* c, const float* q, int q_C, int q_col, int q_tt, const flo
   a.max_len = max_len;
   a.cls_mode = cls;
   a.err = c->d_err;
+  if (segs && segs->size() > 1) {  // one launch per length class, sized for that class
+    for (const AttnSegment& g : *segs) {
+      AttnArgs b = a;
+      b.cu = cu + g.first;
+      b.max_len = g.max_len;
+      ++c->launches;
+      if (launch_attention_exact(b, g.count, c->stream)) return fail(c, AE_ERR_CUDA, "attention launch failed");
+    }
+    return 0;
+  }
   ++c->launches;
   if (launch_attention_exact(a, n, c->stream)) return fail(c, AE_ERR_CUDA, "attention launch failed");
   return 0;
@@ -414,7 +433,11 @@ int gemm_ln(ae_ctx* c, const CUtensorMap& ta, const DevLinear& L, int M, const f
 }
 
 // Enqueues the whole forward pass of a packed batch on the context's stream.
-int enqueue_forward(ae_ctx* c, const uint16_t* d_ids, const uint32_t* d_cu, int T, int n, int max_len, float* d_out) {
+//
+// segs (optional): the packed sequences as runs of one attention length class each (host packing
+// knows the lengths); the attention of layers 0-10 then launches once per run.
+int enqueue_forward(ae_ctx* c, const uint16_t* d_ids, const uint32_t* d_cu, int T, int n, int max_len, float* d_out,
+                    const std::vector<AttnSegment>* segs = nullptr) {
   Workspace& W = c->ws;
   const DevModel& M = c->model;
   cudaStream_t st = c->stream;
@@ -456,7 +479,7 @@ int enqueue_forward(ae_ctx* c, const uint16_t* d_ids, const uint32_t* d_cu, int 
     {
       ProfScope ps(c, AE_KERNEL_ATTENTION);
       AE_TRY(attention(c, W.qkv, 3 * kHidden, 0, 1, W.qkv, 3 * kHidden, kHidden, 2 * kHidden, 1, W.ctx, d_cu, n,
-                       max_len, 0));
+                       max_len, 0, segs));
     }
     ++c->launches;
     {
@@ -539,17 +562,36 @@ int pack_host(ae_ctx* c, const uint16_t* ids, const uint32_t* cu, uint32_t n, in
   if (T > 0x7fffffffu) return fail(c, AE_ERR_CAPACITY, "batch too large");
   AE_TRY(reserve(c, uint32_t(T), n));
   Workspace& W = c->ws;
+  // Sequences are packed grouped by attention length class (stable inside a class), so that each
+  // class's attention launch is sized for its own longest sequence; rows are independent, so the
+  // order changes no result, and the output is written back in the caller's order.
+  auto len_of = [&](uint32_t i) { return std::min<uint32_t>(cu[i + 1] - cu[i], kMaxPos); };
+  c->order.resize(n);
+  c->segs.clear();
+  uint32_t filled = 0;
+  for (int cls = 0; cls < kAttnClasses; ++cls) {
+    const uint32_t first = filled;
+    int seg_max = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+      const uint32_t len = len_of(i);
+      if (attn_class(int(len)) != cls) continue;
+      c->order[filled++] = i;
+      seg_max = std::max<int>(seg_max, int(len));
+    }
+    if (filled > first) c->segs.push_back(AttnSegment{int(first), int(filled - first), seg_max});
+  }
   uint32_t off = 0;
   W.h_cu[0] = 0;
-  for (uint32_t i = 0; i < n; ++i) {
-    const uint32_t len = std::min<uint32_t>(cu[i + 1] - cu[i], kMaxPos);
+  for (uint32_t k = 0; k < n; ++k) {
+    const uint32_t i = c->order[k];
+    const uint32_t len = len_of(i);
     const uint16_t* src = ids + cu[i];
     for (uint32_t j = 0; j < len; ++j) {
       if (src[j] >= kVocab) return fail(c, AE_ERR_TOKEN_RANGE, "token id %u at sequence %u is >= 30522", src[j], i);
     }
     std::memcpy(W.h_ids + off, src, len * 2);
     off += len;
-    W.h_cu[i + 1] = off;
+    W.h_cu[k + 1] = off;
   }
   *T_out = int(T);
   *maxlen_out = max_len;
@@ -565,11 +607,12 @@ int forward_ragged_host(ae_ctx* c, const uint16_t* ids, const uint32_t* cu, uint
   Workspace& W = c->ws;
   CUDA_TRY(c, cudaMemcpyAsync(W.ids, W.h_ids, size_t(T) * 2, cudaMemcpyHostToDevice, c->stream));
   CUDA_TRY(c, cudaMemcpyAsync(W.cu, W.h_cu, size_t(n + 1) * 4, cudaMemcpyHostToDevice, c->stream));
-  AE_TRY(enqueue_forward(c, W.ids, W.cu, T, int(n), max_len, W.out));
+  AE_TRY(enqueue_forward(c, W.ids, W.cu, T, int(n), max_len, W.out, &c->segs));
   CUDA_TRY(c, cudaMemcpyAsync(W.h_out, W.out, size_t(n) * kHidden * 4, cudaMemcpyDeviceToHost, c->stream));
   CUDA_TRY(c, cudaStreamSynchronize(c->stream));
   AE_TRY(check_dev_err(c));
-  std::memcpy(out, W.h_out, size_t(n) * kHidden * 4);
+  for (uint32_t k = 0; k < n; ++k)
+    std::memcpy(out + size_t(c->order[k]) * kHidden, W.h_out + size_t(k) * kHidden, kHidden * 4);
   return 0;
 }
 
@@ -1063,19 +1106,33 @@ int ae_embed_batch_multi(ae_ctx* const* ctxs, int n_ctx, const uint16_t* ids, co
     std::vector<uint16_t> bids;
     std::vector<uint32_t> bcu;
     std::vector<float> bout;
-    const auto& s = shard[d];
-    size_t i = 0;
-    while (i < s.size() && rc[d] == 0) {
-      bids.clear();
-      bcu.assign(1, 0);
+    // longest first: each batch then holds sequences of similar length (tight attention launches)
+    std::vector<uint32_t> s = shard[d];
+    std::stable_sort(s.begin(), s.end(), [&](uint32_t x, uint32_t y) { return len_of(x) > len_of(y); });
+    // batch boundaries first, so that the workspace is sized once for the largest batch
+    std::vector<size_t> ends;
+    uint32_t most_tok = 0, most_seqs = 0;
+    for (size_t i = 0; i < s.size();) {
       size_t j = i;
       uint32_t tok = 0;
-      while (j < s.size() && tok + len_of(s[j]) <= max_tokens) {
-        const uint32_t L = len_of(s[j]);
-        bids.insert(bids.end(), ids + cu[s[j]], ids + cu[s[j]] + L);
+      while (j < s.size() && tok + len_of(s[j]) <= max_tokens) tok += len_of(s[j++]);
+      ends.push_back(j);
+      most_tok = std::max(most_tok, tok);
+      most_seqs = std::max<uint32_t>(most_seqs, uint32_t(j - i));
+      i = j;
+    }
+    if (!s.empty()) rc[d] = reserve(c, most_tok, most_seqs);
+    size_t i = 0;
+    for (size_t bi = 0; bi < ends.size() && rc[d] == 0; ++bi) {
+      bids.clear();
+      bcu.assign(1, 0);
+      const size_t j = ends[bi];
+      uint32_t tok = 0;
+      for (size_t k = i; k < j; ++k) {
+        const uint32_t L = len_of(s[k]);
+        bids.insert(bids.end(), ids + cu[s[k]], ids + cu[s[k]] + L);
         tok += L;
         bcu.push_back(tok);
-        ++j;
       }
       const uint32_t nb = uint32_t(j - i);
       bout.resize(size_t(nb) * kHidden);

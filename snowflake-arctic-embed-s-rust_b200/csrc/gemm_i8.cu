@@ -344,13 +344,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* stg = reinterpret_cast<uint8_t*>(xch + Ly::XCH_FLOATS_GELU) + ew * (32 * 80);
           uint32_t pk[CW / 4];
 #pragma unroll
-          for (int q = 0; q < CW / 4; ++q) {
-            uint32_t w = 0;
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              w |= (uint32_t(quant_i8(__uint_as_float(r[4 * q + e]) * inv_scale)) & 0xFFu) << (8 * e);
-            pk[q] = w;
-          }
+          for (int q = 0; q < CW / 4; ++q)
+            pk[q] = pack_i8x4(quant_bits_scaled(__uint_as_float(r[4 * q]) * inv_scale),
+                              quant_bits_scaled(__uint_as_float(r[4 * q + 1]) * inv_scale),
+                              quant_bits_scaled(__uint_as_float(r[4 * q + 2]) * inv_scale),
+                              quant_bits_scaled(__uint_as_float(r[4 * q + 3]) * inv_scale));
 #pragma unroll
           for (int q = 0; q < CW / 16; ++q)
             *reinterpret_cast<uint4*>(stg + lane * 80 + 16 * q) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
@@ -497,10 +495,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int c = 16 * (k0 + k) + cq;
               const float4 iv4 = *reinterpret_cast<const float4*>(s_invs + c);
               const float iv[4] = {iv4.x, iv4.y, iv4.z, iv4.w};
-              uint32_t w = 0;
-#pragma unroll
-              for (int e = 0; e < 4; ++e)
-                w |= (uint32_t(quant_i8(__uint_as_float(r[4 * k + e]) * (iv[e] * inv_scale))) & 0xFFu) << (8 * e);
+              const uint32_t w = pack_i8x4(quant_bits_scaled(__uint_as_float(r[4 * k]) * (iv[0] * inv_scale)),
+                                           quant_bits_scaled(__uint_as_float(r[4 * k + 1]) * (iv[1] * inv_scale)),
+                                           quant_bits_scaled(__uint_as_float(r[4 * k + 2]) * (iv[2] * inv_scale)),
+                                           quant_bits_scaled(__uint_as_float(r[4 * k + 3]) * (iv[3] * inv_scale)));
               if (valid) *reinterpret_cast<uint32_t*>(g.out_q + size_t(row) * kHidden + c) = w;
             }
           }

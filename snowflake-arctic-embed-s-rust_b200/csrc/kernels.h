@@ -49,6 +49,17 @@ int launch_row_meta(const uint32_t* cu, int n_seqs, uint16_t* pos, int32_t* cls_
 int launch_gather_cls(const int32_t* cls_row, int n, const int8_t* act_q, const float* act_s, const float* hidden,
                       int8_t* cq, float* cs, float* ch, cudaStream_t st);
 int attention_prime();
+// A run of consecutive packed sequences [first, first + count) whose lengths are at most max_len
+// and fall in one attention length class.
+struct AttnSegment {
+  int first;
+  int count;
+  int max_len;
+};
+// Length classes of the attention launch: 1-32, 33-64, 65-128, 129-256, 257-512 keys (the TMEM
+// columns a CTA allocates for its scores).
+constexpr int kAttnClasses = 5;
+inline int attn_class(int len) { return len <= 32 ? 0 : len <= 64 ? 1 : len <= 128 ? 2 : len <= 256 ? 3 : 4; }
 int launch_attention_exact(const AttnArgs& a, int n_seqs, cudaStream_t st);
 
 }  // namespace ae

@@ -50,6 +50,16 @@ __device__ __forceinline__ int quant_i8(float v) {
   return __float_as_int(v + kRoundMagic) - kRoundMagicBits;
 }
 
+// quant_i8 for a value already scaled by 127 / max|x| of its row: |v| <= 127 (1 + 3 * 2^-24) < 127.5
+// for finite inputs, so the clamp to [-127, 127] never changes the rounded result. Returns the bits
+// of v + 1.5 * 2^23, whose low byte is the int8 (the magic constant's low 22 bits are zero).
+__device__ __forceinline__ uint32_t quant_bits_scaled(float v) { return __float_as_uint(v + kRoundMagic); }
+
+// Four quant_bits_scaled results -> four int8 bytes (element 0 in the lowest byte).
+__device__ __forceinline__ uint32_t pack_i8x4(uint32_t b0, uint32_t b1, uint32_t b2, uint32_t b3) {
+  return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
+}
+
 // avx2_exp_f32, src/simd_math.rs:113-143 (Cody-Waite range reduction + degree-5 polynomial).
 __device__ __forceinline__ float cw_exp(float x) {
   const float y = fmaxf(fminf(x, 88.0f), -87.3f);
@@ -109,8 +119,11 @@ __device__ __forceinline__ float2 gelu_ref2(float2 x) {
   const float2 est = make_float2(rcp_approx(den.x), rcp_approx(den.y));
   const float2 inv_den = __fmul2_rn(est, __ffma2_rn(make_float2(-den.x, -den.y), est, make_float2(2.0f, 2.0f)));
   const float2 t = __fmul2_rn(xc, __fmul2_rn(num, inv_den));
-  const float2 erf_a = make_float2(fminf(fmaxf(t.x, -1.0f), 1.0f), fminf(fmaxf(t.y, -1.0f), 1.0f));
-  return __fmul2_rn(__fmul2_rn(x, make_float2(0.5f, 0.5f)), __fadd2_rn(make_float2(1.0f, 1.0f), erf_a));
+  // (x * 0.5) * (1 + clamp(t, -1, 1)): 1 + clamp(t, -1, 1) = clamp(RN(1 + t), 0, 2) = 2 v with
+  // v = sat(RN(0.5 t + 0.5)) (halving is exact), and RN(RN(x * 0.5) * 2v) = RN(x * v) because
+  // x * 0.5 is exact for |x| >= 2^-125 (below that the result is far under the quantization step).
+  const float2 v = make_float2(__saturatef(fmaf(t.x, 0.5f, 0.5f)), __saturatef(fmaf(t.y, 0.5f, 0.5f)));
+  return __fmul2_rn(x, v);
 }
 
 // GELU with the exact error function (0.5 x (1 + erf(x / sqrt 2))).
