@@ -92,6 +92,20 @@ __device__ __forceinline__ float ld_act(const float* p, int C, int tt, int t, in
 __device__ __forceinline__ void stage_kv_pairs(const AttnArgs& a, int s0, int L, int h, float2* kp, float2* vp) {
   const int pairs = (L + 1) >> 1;
   const int kc = a.k_col + 32 * h, vc = a.v_col + 32 * h;
+  if (a.kv_tt && !(s0 & 1)) {
+    // tile-transposed rows with an even first row: keys (2p, 2p+1) of one dim are 8 adjacent bytes
+    // in the same 128-row block, copied asynchronously (all in flight at once); lanes take
+    // consecutive pairs of one dim. The second key of an odd L's last pair is zero-filled.
+    for (int i = threadIdx.x; i < pairs * 32; i += blockDim.x) {
+      const int d = i / pairs, p = i - d * pairs;
+      const int t = s0 + 2 * p;
+      const uint32_t bytes = (2 * p + 1 < L) ? 8u : 4u;
+      cp_async8(kp + p * KPS + (d & 7) * 4 + (d >> 3), a.kv + tt_index(t, kc + d, a.kv_C), bytes);
+      cp_async8(vp + p * KPS + d, a.kv + tt_index(t, vc + d, a.kv_C), bytes);
+    }
+    cp_async_wait_all();
+    return;
+  }
   const int groups = (pairs + 7) >> 3;  // 8-pair groups
   for (int i = threadIdx.x; i < groups * 256; i += blockDim.x) {
     const int w = i >> 5, l = i & 31;

@@ -168,6 +168,14 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, uint32_t ab_type)
   return (1u << 4) | (ab_type << 7) | (ab_type << 10) | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
 }
 
+// Asynchronous global -> shared copy of 8 bytes (src_bytes of them read, the rest zero-filled);
+// complete after cp_async_wait_all.
+__device__ __forceinline__ void cp_async8(void* smem, const void* gmem, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(smem_u32(smem)), "l"(gmem), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // Shared-memory matrix descriptor for a K-major operand in the 128-byte swizzle layout: rows of
 // 128 bytes, 8-row swizzle atoms of 1024 bytes stacked along M/N (stride byte offset 1024).
 __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
