@@ -51,6 +51,31 @@ def attn_flops_per_seq(L: int) -> float:
     return 2.0 * (8448.0 * L * L + 768.0 * L)
 
 
+# ncu summaries (committed under profiles/) with the measured DRAM bytes per launch of a kernel kind
+NCU_TRAFFIC = {"attention": "k_attention_rows128_config3_ncu.md"}
+
+
+def ncu_traffic(kind: str):
+    """dram__bytes_read.sum + dram__bytes_write.sum per launch from the kernel's ncu summary."""
+    name = NCU_TRAFFIC.get(kind)
+    if not name:
+        return None, None
+    try:
+        with open(os.path.join(ROOT, "profiles", name)) as f:
+            for ln in f:
+                if ln.startswith("| traffic_bytes_per_launch |"):
+                    return int(ln.split("|")[2].strip()), "profiles/" + name
+    except (OSError, ValueError):
+        pass
+    return None, None
+
+
+def attn_bytes_per_launch(T: int) -> int:
+    """Algorithmic DRAM bytes of one layer's attention: read Q, K, V (T x 1,152 fp32), write the
+    context (T x 384 fp32)."""
+    return T * (3 * H + H) * 4
+
+
 def make_batches(n_batches: int, seed: int, seqs: int = BATCH_SEQS, L: int = SEQ_LEN):
     from arctic_embed_s_int8 import synth
 
@@ -492,8 +517,10 @@ def main() -> int:
         elif dom == "attention":
             ach = work[dom] / (per_step_ms[dom] * 1e-3) / 1e12
             fp32 = measure_fp32_peak()
+            traffic, tsrc = ncu_traffic(dom)
             result["roofline"] = {"kernel": dom, "bound": "fp32", "achieved": ach, "peak": fp32,
-                                  "unit": "TFLOP/s (fp32 CUDA cores)", "frac": ach / fp32, "traffic": None,
+                                  "unit": "TFLOP/s (fp32 CUDA cores)", "frac": ach / fp32, "traffic": traffic,
+                                  "traffic_source": tsrc, "algorithmic_bytes_per_launch": attn_bytes_per_launch(T),
                                   "ms_per_launch": ms_launch,
                                   "peak_basis": "measured here: cuBLAS SGEMM 8192^3, TF32 off (the attention keeps "
                                                 "the reference's fp32 operation order, so it runs on the CUDA cores)",

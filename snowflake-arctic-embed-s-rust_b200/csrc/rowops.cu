@@ -153,32 +153,51 @@ __global__ void __launch_bounds__(256) k_ln_quant_rows(const float* __restrict__
   if (active && l == 0) scale[hw] = max_abs / 127.0f;
 }
 
-// One thread per row: layernorm_inplace_row + l2_normalize_inplace (src/simd_math.rs:481-497,
-// :2892-2903), whose sums are sequential over the 384 elements, on rows of h (row-major [M, 384]).
-__global__ void k_ln_final_rows(const float* __restrict__ h_in, int M, const float* __restrict__ gamma,
-                                const float* __restrict__ beta, float* __restrict__ out) {
-  const int row = blockIdx.x * blockDim.x + threadIdx.x;
-  if (row >= M) return;
-  const float* x = h_in + size_t(row) * kHidden;
-  float sum = 0.0f;
-  for (int j = 0; j < kHidden; ++j) sum = sum + x[j];
-  const float mean = sum / float(kHidden);
-  float var = 0.0f;
-  for (int j = 0; j < kHidden; ++j) {
-    const float d = x[j] - mean;
-    var = var + d * d;
+// layernorm_inplace_row + l2_normalize_inplace (src/simd_math.rs:481-497, :2892-2903) on rows of
+// h (row-major [M, 384]). Their sums are sequential over the 384 elements, so one thread owns a
+// row; a block stages 16 rows in shared memory with coalesced loads (rows padded to 385 floats, so
+// the 16 owners read 16 different banks) and writes the results back the same way.
+constexpr int kLnFinalRows = 16;
+constexpr int kLnFinalPitch = kHidden + 1;
+
+__global__ void __launch_bounds__(128) k_ln_final_rows(const float* __restrict__ h_in, int M,
+                                                       const float* __restrict__ gamma,
+                                                       const float* __restrict__ beta, float* __restrict__ out) {
+  extern __shared__ float xs[];  // [kLnFinalRows][kLnFinalPitch]
+  const int r0 = blockIdx.x * kLnFinalRows;
+  const int rows = M - r0 < kLnFinalRows ? M - r0 : kLnFinalRows;
+  for (int i = threadIdx.x; i < rows * kHidden; i += blockDim.x) {
+    const int r = i / kHidden, j = i - r * kHidden;
+    xs[r * kLnFinalPitch + j] = h_in[size_t(r0 + r) * kHidden + j];
   }
-  const float rstd = 1.0f / sqrtf(var / float(kHidden) + kLnEps);
-  float ss = 0.0f;
-  for (int j = 0; j < kHidden; ++j) {
-    const float y = (x[j] - mean) * rstd * gamma[j] + beta[j];
-    ss = ss + y * y;
+  __syncthreads();
+  const int r = threadIdx.x;
+  if (r < rows) {
+    float* x = xs + r * kLnFinalPitch;
+    float sum = 0.0f;
+    for (int j = 0; j < kHidden; ++j) sum = sum + x[j];
+    const float mean = sum / float(kHidden);
+    float var = 0.0f;
+    for (int j = 0; j < kHidden; ++j) {
+      const float d = x[j] - mean;
+      var = var + d * d;
+    }
+    const float rstd = 1.0f / sqrtf(var / float(kHidden) + kLnEps);
+    float ss = 0.0f;
+    for (int j = 0; j < kHidden; ++j) {
+      const float y = (x[j] - mean) * rstd * gamma[j] + beta[j];
+      x[j] = y;
+      ss = ss + y * y;
+    }
+    if (ss > 0.0f) {
+      const float inv = 1.0f / sqrtf(ss);
+      for (int j = 0; j < kHidden; ++j) x[j] = x[j] * inv;
+    }
   }
-  const float inv = ss > 0.0f ? 1.0f / sqrtf(ss) : 1.0f;
-  float* o = out + size_t(row) * kHidden;
-  for (int j = 0; j < kHidden; ++j) {
-    const float y = (x[j] - mean) * rstd * gamma[j] + beta[j];
-    o[j] = ss > 0.0f ? y * inv : y;
+  __syncthreads();
+  for (int i = threadIdx.x; i < rows * kHidden; i += blockDim.x) {
+    const int rr = i / kHidden, j = i - rr * kHidden;
+    out[size_t(r0 + rr) * kHidden + j] = xs[rr * kLnFinalPitch + j];
   }
 }
 
@@ -272,7 +291,8 @@ int launch_ln_quant_rows(const float* h_in, int M, const float* gamma, const flo
 int launch_ln_final_rows(const float* h_in, int M, const float* gamma, const float* beta, float* out,
                          cudaStream_t st) {
   if (M <= 0) return 0;
-  k_ln_final_rows<<<(M + 127) / 128, 128, 0, st>>>(h_in, M, gamma, beta, out);
+  k_ln_final_rows<<<(M + kLnFinalRows - 1) / kLnFinalRows, 128, kLnFinalRows * kLnFinalPitch * 4, st>>>(
+      h_in, M, gamma, beta, out);
   return cudaGetLastError() == cudaSuccess ? 0 : -1;
 }
 
