@@ -1031,6 +1031,13 @@ int ae_gemm_i8(ae_ctx* c, int epi, uint32_t M, uint32_t N, uint32_t K, const int
   DeviceGuard g(c->device);
   if (!d_a || !d_a_scale || !d_w || !d_w_scale || !d_bias || M == 0 || K % 128)
     return fail(c, AE_ERR_INVALID_ARG, "ae_gemm_i8: bad arguments");
+  {  // the epilogues use 16-byte vector loads and stores
+    const void* ptrs[] = {d_a_scale, d_w_scale, d_bias, d_res, d_gamma, d_beta, d_inv_smooth, d_out, d_out_q,
+                          d_out_scale, d_acc};
+    for (const void* q : ptrs)
+      if (reinterpret_cast<uintptr_t>(q) & 15u)
+        return fail(c, AE_ERR_INVALID_ARG, "ae_gemm_i8: every device pointer must be 16-byte aligned");
+  }
   CUtensorMap ta, tb;
   if (make_tmap_i8(&ta, d_a, int(M), int(K), kBoxA) || make_tmap_i8(&tb, d_w, int(N), int(K), kBoxB))
     return fail(c, AE_ERR_INVALID_ARG, "ae_gemm_i8: operands must be 16-byte aligned");

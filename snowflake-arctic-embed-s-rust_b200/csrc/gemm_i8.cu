@@ -369,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         float* xv = xch + BM * 16;       // [BM][16] partial sums of squares
         float* xm = xch + 2 * BM * 16;   // [BM][4]  partial maxima
         const int cq = 4 * qq;           // first owned column of every 16-column block
-        uint32_t r[24];
+        uint32_t r[32];
         float p[4] = {0.f, 0.f, 0.f, 0.f};
         // pass 1: h = fma(acc, as * ws, bias + res) -> TMEM; partial sums (chains of lanes cq..cq+3)
         const float* res_row = nullptr;  // column c of this row at res_row[c * rstep]
@@ -481,25 +481,35 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st_wait();
         }
         xm[rt * 4 + qq] = vmax;
+        tc_fence_before();
         named_bar(1 + Q, 128);
+        tc_fence_after();
         const float max_abs = fmaxf(fmaxf(xm[rt * 4], xm[rt * 4 + 1]), fmaxf(xm[rt * 4 + 2], xm[rt * 4 + 3]));
         const float inv_scale = 127.0f / max_abs;
-        // pass 4: quantize
+        // pass 4: quantize. Elementwise, so this warp takes the 96 contiguous columns
+        // 96 qq .. 96 qq + 95 of its rows (written to TMEM by the quadrant's four warps in pass 3)
+        // and stores each row's bytes as six 16-byte pieces.
         if (ok) {
-          for (int k0 = 0; k0 < 24; k0 += 6) {
-#pragma unroll
-            for (int k = 0; k < 6; ++k) tmem_ld4(tb + 16 * (k0 + k) + cq, r + 4 * k);
+          const int c0 = 96 * qq;
+          for (int ch = 0; ch < 6; ch += 2) {
+            tmem_ld16(tb + c0 + 16 * ch, r);
+            tmem_ld16(tb + c0 + 16 * ch + 16, r + 16);
             tmem_ld_wait();
 #pragma unroll
-            for (int k = 0; k < 6; ++k) {
-              const int c = 16 * (k0 + k) + cq;
-              const float4 iv4 = *reinterpret_cast<const float4*>(s_invs + c);
-              const float iv[4] = {iv4.x, iv4.y, iv4.z, iv4.w};
-              const uint32_t w = pack_i8x4(quant_bits_scaled(__uint_as_float(r[4 * k]) * (iv[0] * inv_scale)),
-                                           quant_bits_scaled(__uint_as_float(r[4 * k + 1]) * (iv[1] * inv_scale)),
-                                           quant_bits_scaled(__uint_as_float(r[4 * k + 2]) * (iv[2] * inv_scale)),
-                                           quant_bits_scaled(__uint_as_float(r[4 * k + 3]) * (iv[3] * inv_scale)));
-              if (valid) *reinterpret_cast<uint32_t*>(g.out_q + size_t(row) * kHidden + c) = w;
+            for (int u = 0; u < 2; ++u) {
+              const int c = c0 + 16 * (ch + u);
+              uint32_t w[4];
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const float4 iv = *reinterpret_cast<const float4*>(s_invs + c + 4 * q);
+                const uint32_t* y = r + 16 * u + 4 * q;
+                w[q] = pack_i8x4(quant_bits_scaled(__uint_as_float(y[0]) * (iv.x * inv_scale)),
+                                 quant_bits_scaled(__uint_as_float(y[1]) * (iv.y * inv_scale)),
+                                 quant_bits_scaled(__uint_as_float(y[2]) * (iv.z * inv_scale)),
+                                 quant_bits_scaled(__uint_as_float(y[3]) * (iv.w * inv_scale)));
+              }
+              if (valid)
+                *reinterpret_cast<uint4*>(g.out_q + size_t(row) * kHidden + c) = make_uint4(w[0], w[1], w[2], w[3]);
             }
           }
         }
