@@ -154,7 +154,7 @@ __host__ __device__ constexpr uint32_t tmem_cols_for_len(int L) {
 // memory holds only the head's K / V pairs. Threads whose query lies past the sequence still take
 // part in the warp-collective TMEM loads and stores and write nothing.
 template <int QT>
-__global__ void __launch_bounds__(QT) k_attention_rows(AttnArgs a) {
+__global__ void __launch_bounds__(QT, 512 / QT) k_attention_rows(AttnArgs a) {
   extern __shared__ float4 smem4[];
   __shared__ uint32_t tmem_slot;
   const int s = blockIdx.x;
@@ -191,20 +191,33 @@ __global__ void __launch_bounds__(QT) k_attention_rows(AttnArgs a) {
   const int L4 = L & ~3, L8 = L & ~7, L16 = L & ~15;
   uint32_t r[16];
 
-  // pass 1: scores -> TMEM (16 keys per store) and their max
+  // pass 1: scores -> TMEM (16 keys per store) and their max (order-independent)
   float mx = -INFINITY;
   for (int t0 = 0; t0 < L; t0 += 16) {
+    if (t0 + 16 <= L4) {  // a full chunk of complete 4-key groups: no bounds, pairs interleave freely
+      float2 ma = f2(-INFINITY, -INFINITY), mb = ma;  // two max chains (even / odd pairs)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int t = t0 + 2 * j;
-      float2 sp = f2(0.0f, 0.0f);
-      if (t < L) {
-        sp = score_pair(q, kp + (t >> 1) * KPS, t < L4);
-        mx = fmaxf(mx, sp.x);
-        if (t + 1 < L) mx = fmaxf(mx, sp.y);
+      for (int j = 0; j < 8; ++j) {
+        const float2 sp = score_pair(q, kp + ((t0 >> 1) + j) * KPS, true);
+        if (j & 1) mb = f2(fmaxf(mb.x, sp.x), fmaxf(mb.y, sp.y));
+        else ma = f2(fmaxf(ma.x, sp.x), fmaxf(ma.y, sp.y));
+        r[2 * j] = __float_as_uint(sp.x);
+        r[2 * j + 1] = __float_as_uint(sp.y);
       }
-      r[2 * j] = __float_as_uint(sp.x);
-      r[2 * j + 1] = __float_as_uint(sp.y);
+      mx = fmaxf(mx, fmaxf(fmaxf(ma.x, ma.y), fmaxf(mb.x, mb.y)));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int t = t0 + 2 * j;
+        float2 sp = f2(0.0f, 0.0f);
+        if (t < L) {
+          sp = score_pair(q, kp + (t >> 1) * KPS, t < L4);
+          mx = fmaxf(mx, sp.x);
+          if (t + 1 < L) mx = fmaxf(mx, sp.y);
+        }
+        r[2 * j] = __float_as_uint(sp.x);
+        r[2 * j + 1] = __float_as_uint(sp.y);
+      }
     }
     tmem_st16(tl + t0, r);
   }
@@ -273,6 +286,20 @@ __global__ void __launch_bounds__(QT) k_attention_rows(AttnArgs a) {
   for (int t0 = 0; t0 < L; t0 += 16) {
     tmem_ld16(tl + t0, r);
     tmem_ld_wait();
+    if (t0 + 16 <= L) {  // a full chunk: no bounds
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float2 p = mul2(f2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), inv2);
+        const float4* v4 = reinterpret_cast<const float4*>(vp + ((t0 >> 1) + j) * KPS);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float4 vv = v4[i];
+          acc[2 * i] = fma2(f2(vv.x, vv.y), p, acc[2 * i]);
+          acc[2 * i + 1] = fma2(f2(vv.z, vv.w), p, acc[2 * i + 1]);
+        }
+      }
+      continue;
+    }
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int t = t0 + 2 * j;
