@@ -184,6 +184,37 @@ uint64_t ae_kernel_launches(const ae_ctx* ctx);
 /* Waits for the context's stream; reports a device-side error (AE_ERR_DEVICE) if one was raised. */
 int ae_sync(ae_ctx* ctx);
 
+/* ---------------------------------------------------------------------------------------------
+ * WordPiece tokenizer (host only, no GPU needed): BertTokenizer, src/tokenizer.rs:25-327.
+ * Text is UTF-8 (AE_ERR_INVALID_ARG on invalid UTF-8, which a Rust &str cannot hold). Outputs are
+ * [CLS] (+ the query prefix) + WordPiece ids + [SEP], truncated to 512 ids as encode_into does
+ * (src/tokenizer.rs:90-101). A tokenizer is immutable after creation and may be shared by threads.
+ * ------------------------------------------------------------------------------------------- */
+typedef struct ae_tokenizer ae_tokenizer;
+
+#define AE_QUERY_PREFIX "Represent this sentence for searching relevant passages: "
+
+/* BertTokenizer::from_vocab_file / from_vocab_str (src/tokenizer.rs:35-68): one token per line,
+ * id = line index (at most 65,536 lines). */
+int ae_tokenizer_create_from_file(const char* vocab_path, ae_tokenizer** out);
+int ae_tokenizer_create_from_vocab(const char* vocab_text, size_t len, ae_tokenizer** out);
+int ae_tokenizer_destroy(ae_tokenizer* tok);
+/* BertTokenizer::vocab_size (src/tokenizer.rs:70-73). */
+uint32_t ae_tokenizer_vocab_size(const ae_tokenizer* tok);
+/* Message of the last failure of ae_tokenizer_create_* on this thread. */
+const char* ae_tokenizer_last_error(void);
+
+/* encode (is_query = 0) / encode_query (is_query = 1), src/tokenizer.rs:74-101. Writes n <= 512
+ * ids to ids[0..n) and *n_ids = n; AE_ERR_CAPACITY if cap < n. */
+int ae_tokenize(const ae_tokenizer* tok, const char* text, size_t len, int is_query, uint16_t* ids,
+                uint32_t cap, uint32_t* n_ids);
+
+/* The tokenization step of ArcticEmbedS::embed_batch (src/lib.rs:138-160) over n texts on
+ * host threads: packed ids (ids_cap >= total) and cu_seqlens [n + 1], ready for
+ * ae_forward_ragged / ae_embed_batch_multi. texts[i] has lens[i] bytes. */
+int ae_tokenize_batch(const ae_tokenizer* tok, const char* const* texts, const size_t* lens, uint32_t n,
+                      int is_query, uint16_t* ids, size_t ids_cap, uint32_t* cu_seqlens);
+
 #ifdef __cplusplus
 }
 #endif

@@ -285,10 +285,10 @@ class ArcticEmbedS:
         return embed_batch_multi([self.engine], seqs=seqs, max_batch_tokens=max_batch_tokens)
 
     def embed_batch(self, texts, is_query: bool = False, num_threads: int = 0) -> np.ndarray:
-        """src/lib.rs:138-260: ``num_threads`` is accepted for API parity and ignored."""
-        tok = self._tok()
-        seqs = [tok.encode_query(t) if is_query else tok.encode(t) for t in texts]
-        return self.embed_batch_tokens(seqs)
+        """src/lib.rs:138-260: texts tokenized on host threads (ae_tokenize_batch), then sharded and
+        packed on the GPU(s). ``num_threads`` is accepted for API parity and ignored."""
+        ids, cu = self._tok().encode_batch(list(texts), is_query)
+        return embed_batch_multi([self.engine], ids=ids, cu=cu)
 
     def _tok(self):
         if self.tokenizer is None:

@@ -31,6 +31,8 @@ SYMBOLS = [
     "ae_model_load", "ae_model_load_file", "ae_reserve", "ae_forward_cls", "ae_forward_ragged",
     "ae_forward_ragged_device", "ae_embed_batch_multi", "ae_gemm_i8", "ae_attention_f32", "ae_kernel_launches",
     "ae_plan_shards", "ae_forward_cls_noalloc", "ae_profile", "ae_profile_read", "ae_sync",
+    "ae_tokenizer_create_from_file", "ae_tokenizer_create_from_vocab", "ae_tokenizer_destroy",
+    "ae_tokenizer_vocab_size", "ae_tokenizer_last_error", "ae_tokenize", "ae_tokenize_batch",
 ]
 
 
@@ -105,10 +107,19 @@ def lib():
     L.ae_forward_cls_noalloc.argtypes = [P, P, u32, P]
     L.ae_profile.argtypes = [P, C.c_int]
     L.ae_profile_read.argtypes = [P, P, P]
+    L.ae_tokenizer_create_from_file.argtypes = [C.c_char_p, C.POINTER(P)]
+    L.ae_tokenizer_create_from_vocab.argtypes = [C.c_char_p, C.c_size_t, C.POINTER(P)]
+    L.ae_tokenizer_destroy.argtypes = [P]
+    L.ae_tokenizer_vocab_size.argtypes = [P]
+    L.ae_tokenizer_last_error.argtypes = []
+    L.ae_tokenize.argtypes = [P, C.c_char_p, C.c_size_t, C.c_int, P, u32, C.POINTER(u32)]
+    L.ae_tokenize_batch.argtypes = [P, C.POINTER(C.c_char_p), P, u32, C.c_int, P, C.c_size_t, P]
     for name in SYMBOLS:
-        if name not in ("ae_last_error", "ae_kernel_launches"):
+        if name not in ("ae_last_error", "ae_kernel_launches", "ae_tokenizer_vocab_size", "ae_tokenizer_last_error"):
             getattr(L, name).restype = C.c_int
     L.ae_kernel_launches.restype = C.c_uint64
+    L.ae_tokenizer_vocab_size.restype = C.c_uint32
+    L.ae_tokenizer_last_error.restype = C.c_char_p
     _lib = L
     return L
 

@@ -58,3 +58,15 @@ def engine(pack_path):
 
 def rng(seed=0):
     return np.random.Generator(np.random.PCG64(seed))
+
+
+def golden_vocab_text() -> tuple:
+    """(vocabulary text, records) of the tokenizer fixture: the full id space with the golden subset at its ids and a
+    control character (removed by the normalizer, so never matched) on every other line."""
+    import json
+
+    with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "tokenizer_vectors.json"),
+              encoding="utf-8") as f:
+        g = json.load(f)
+    sub = g["vocab_subset"]
+    return "\n".join(sub.get(str(i), f"\x01{i}") for i in range(g["vocab_size"])) + "\n", g["records"]

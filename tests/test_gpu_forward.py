@@ -145,3 +145,24 @@ def test_device_resident_forward(engine):
     engine.forward_device(d_ids, d_cu, len(seqs), int(cu[-1]), 512, out)
     engine.sync()
     np.testing.assert_array_equal(out.cpu().numpy(), engine.forward_ragged(seqs))
+
+
+def test_text_to_embedding(engine, oracle_model):
+    """embed_query / embed_document / embed_batch (src/lib.rs:96-260): the C++ WordPiece tokenizer
+    feeding the GPU forward; ids identical to the reference's known answers, embeddings within the
+    tolerance of the oracle on the same ids, batch == one at a time."""
+    from conftest import golden_vocab_text
+    from arctic_embed_s_int8 import ArcticEmbedS
+    from arctic_embed_s_int8.tokenizer import BertTokenizer
+
+    vocab, records = golden_vocab_text()
+    model = ArcticEmbedS(engine, tokenizer=BertTokenizer.from_vocab_str(vocab))
+    picked = [r for r in records if r["kind"] == "query"][:3] + [r for r in records if r["kind"] == "document"][-2:]
+    for r in picked:
+        got = model.embed_query(r["text"]) if r["kind"] == "query" else model.embed_document(r["text"])
+        cos, mx = close(got, oracle_model.forward_cls(np.array(r["ids"], np.uint16)))
+        assert cos >= COS_MIN and mx <= MAXABS_MAX, (r["text"][:40], cos, mx)
+    docs = [r["text"] for r in records if r["kind"] == "document"]
+    batch = model.embed_batch(docs)
+    for t, b in zip(docs, batch):
+        np.testing.assert_array_equal(b, model.embed_document(t))
