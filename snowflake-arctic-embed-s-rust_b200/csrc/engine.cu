@@ -11,6 +11,10 @@
 // 512-row limits; a single sequence (forward_cls, src/model.rs:185-513) is the n = 1 case and is
 // replayed from a CUDA graph per length.
 #include <cuda.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -19,9 +23,11 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
-#include <fstream>
+
 #include <map>
+#include <memory>
 #include <mutex>
+#include <new>
 #include <numeric>
 #include <string>
 #include <thread>
@@ -186,25 +192,49 @@ bool check_linear(const ae_linear_desc& d, uint64_t n, uint64_t k, bool allow_pr
   return d.n_out == n && d.k_in == k && d.w_q && d.w_scale && d.bias && d.inv_smooth;
 }
 
-int upload_linear(ae_ctx* c, Carve& cv, const ae_linear_desc& d, DevLinear& o) {
+// Model upload. From a descriptor of host arrays: every tensor is copied to its offset in a host
+// image of the device arena, and one cudaMemcpy moves the image. From a mapped .ae8 file: the file
+// is copied to the GPU as it is, and each tensor moves to its aligned arena slot with a
+// device-to-device copy (no host-side copy of the 34 MB at all).
+struct Uploader {
+  const uint8_t* dev_base = nullptr;  // the model arena
+  uint8_t* host = nullptr;            // host image of the arena (descriptor loads), or
+  const uint8_t* file = nullptr;      // the mapped .ae8 file (file loads)
+  size_t file_size = 0;
+  const uint8_t* dev_file = nullptr;  // its copy on the device
+  struct Copy {
+    void* dst;
+    const void* src;
+    size_t n;
+  };
+  std::vector<Copy> d2d, h2d;
+  template <class T>
+  void put(T* dst, const void* src, size_t n) {
+    const size_t bytes = n * sizeof(T);
+    const auto* sp = static_cast<const uint8_t*>(src);
+    if (host) {
+      std::memcpy(host + (reinterpret_cast<const uint8_t*>(dst) - dev_base), src, bytes);
+    } else if (sp >= file && sp + bytes <= file + file_size) {
+      d2d.push_back(Copy{dst, dev_file + (sp - file), bytes});
+    } else {
+      h2d.push_back(Copy{dst, src, bytes});  // host-side values built during the load
+    }
+  }
+};
+
+int upload_linear(ae_ctx* c, Carve& cv, Uploader& img, const ae_linear_desc& d, DevLinear& o) {
   o.n = int(d.n_out);
   o.k = int(d.k_in);
   o.inv_s = cv.take<float>(d.k_in);
-  CUDA_TRY(c, cudaMemcpy(o.inv_s, d.inv_smooth, d.k_in * 4, cudaMemcpyHostToDevice));
+  img.put(o.inv_s, d.inv_smooth, d.k_in);
   if (d.n_out == 0) return 0;
   o.w = cv.take<int8_t>(d.n_out * d.k_in);
   o.ws = cv.take<float>(d.n_out);
   o.bias = cv.take<float>(d.n_out);
-  CUDA_TRY(c, cudaMemcpy(o.w, d.w_q, d.n_out * d.k_in, cudaMemcpyHostToDevice));
-  CUDA_TRY(c, cudaMemcpy(o.ws, d.w_scale, d.n_out * 4, cudaMemcpyHostToDevice));
-  CUDA_TRY(c, cudaMemcpy(o.bias, d.bias, d.n_out * 4, cudaMemcpyHostToDevice));
+  img.put(o.w, d.w_q, d.n_out * d.k_in);
+  img.put(o.ws, d.w_scale, d.n_out);
+  img.put(o.bias, d.bias, d.n_out);
   if (make_tmap_i8(&o.tmap, o.w, o.n, o.k, kBoxB) != 0) return fail(c, AE_ERR_CUDA, "cuTensorMapEncodeTiled failed for weights");
-  return 0;
-}
-
-template <class T>
-int upload(ae_ctx* c, T* dst, const T* src, size_t n) {
-  CUDA_TRY(c, cudaMemcpy(dst, src, n * sizeof(T), cudaMemcpyHostToDevice));
   return 0;
 }
 
@@ -617,44 +647,82 @@ int forward_ragged_host(ae_ctx* c, const uint16_t* ids, const uint32_t* cu, uint
 }
 
 // ------------------------------------------------------------------------------------------ .ae8 parsing
+// A read-only mapping of a whole file (pages taken from the page cache up front), or its bytes read
+// into memory where mapping fails.
+struct MappedFile {
+  const uint8_t* data = nullptr;
+  size_t size = 0;
+  void* map = nullptr;
+  std::vector<uint8_t> copy;
+  bool open(const char* path) {
+    const int fd = ::open(path, O_RDONLY);
+    if (fd < 0) return false;
+    struct stat st;
+    bool ok = fstat(fd, &st) == 0 && st.st_size >= 0;
+    if (ok && st.st_size > 0) {
+      size = size_t(st.st_size);
+      map = mmap(nullptr, size, PROT_READ, MAP_PRIVATE | MAP_POPULATE, fd, 0);
+      if (map == MAP_FAILED) {
+        map = nullptr;
+        copy.resize(size);
+        size_t got = 0;
+        while (ok && got < size) {
+          const ssize_t n = ::read(fd, copy.data() + got, size - got);
+          if (n <= 0) ok = false;
+          else got += size_t(n);
+        }
+        data = copy.data();
+      } else {
+        data = static_cast<const uint8_t*>(map);
+      }
+    }
+    ::close(fd);
+    return ok;
+  }
+  ~MappedFile() {
+    if (map) munmap(map, size);
+  }
+};
+
+// QuantizedModelRaw::load_ae8 (src/quantize.rs:76-137) over the bytes of a pack: every tensor is a
+// u64 element count followed by its data. The descriptor's pointers point into the bytes
+// themselves; float arrays may sit at any byte offset, so the loader only memcpy's from them.
 struct Ae8 {
-  std::vector<uint8_t> bytes;
+  const uint8_t* data = nullptr;
+  size_t size = 0;
   size_t pos = 8;
   bool ok = true;
-  std::vector<std::vector<int8_t>> i8s;
-  std::vector<std::vector<float>> f32s;
   uint64_t u64() {
     uint64_t v = 0;
-    if (!ok || bytes.size() - pos < 8) {
+    if (!ok || size - pos < 8) {
       ok = false;
       return 0;
     }
-    std::memcpy(&v, &bytes[pos], 8);
+    std::memcpy(&v, data + pos, 8);
     pos += 8;
     return v;
   }
   const int8_t* i8vec(uint64_t* n_out = nullptr) {
     const uint64_t n = u64();
-    if (!ok || n > bytes.size() - pos) {
+    if (!ok || n > size - pos) {
       ok = false;
       return nullptr;
     }
-    i8s.emplace_back(reinterpret_cast<const int8_t*>(&bytes[pos]), reinterpret_cast<const int8_t*>(&bytes[pos]) + n);
+    const int8_t* p = reinterpret_cast<const int8_t*>(data + pos);
     pos += n;
     if (n_out) *n_out = n;
-    return i8s.back().data();
+    return p;
   }
   const float* f32vec(uint64_t* n_out = nullptr) {
     const uint64_t n = u64();
-    if (!ok || n > (bytes.size() - pos) / 4) {
+    if (!ok || n > (size - pos) / 4) {
       ok = false;
       return nullptr;
     }
-    f32s.emplace_back(n);
-    std::memcpy(f32s.back().data(), &bytes[pos], n * 4);
+    const float* p = reinterpret_cast<const float*>(data + pos);
     pos += n * 4;
     if (n_out) *n_out = n;
-    return f32s.back().data();
+    return p;
   }
   bool linear(ae_linear_desc& d) {
     d.n_out = u64();
@@ -759,9 +827,11 @@ int ae_ctx_set_stream(ae_ctx* c, void* s) {
 
 int ae_ctx_device(const ae_ctx* c) { return c ? c->device : AE_ERR_INVALID_ARG; }
 
-int ae_model_load(ae_ctx* c, const ae_model_desc* d) {
-  if (!c || !d) return fail(c, AE_ERR_INVALID_ARG, "null argument");
-  DeviceGuard g(c->device);
+namespace {
+
+// ae_model_load with an optional source file: file / file_size is the mapped .ae8 pack that the
+// descriptor's pointers point into (then uploaded as is and sorted on the device).
+int load_model(ae_ctx* c, const ae_model_desc* d, const uint8_t* file, size_t file_size) {
   // validation (the sizes src/quantize.rs:9-18 fix; the reference asserts them while packing)
   if (!d->word_emb_q || !d->word_emb_scale || !d->pos_emb_q || !d->pos_emb_scale || !d->type_emb_q ||
       !d->type_emb_scale || !d->emb_ln_weight || !d->emb_ln_bias)
@@ -799,6 +869,28 @@ int ae_model_load(ae_ctx* c, const ae_model_desc* d) {
   M.arena = arena;
   M.arena_bytes = bytes;
   Carve cv{static_cast<uint8_t*>(arena)};
+  Uploader img;
+  img.dev_base = static_cast<const uint8_t*>(arena);
+  std::unique_ptr<uint8_t[]> host;
+  void* dev_file = nullptr;
+  if (file) {
+    if (cudaMalloc(&dev_file, file_size) != cudaSuccess ||
+        cudaMemcpy(dev_file, file, file_size, cudaMemcpyHostToDevice) != cudaSuccess) {
+      if (dev_file) cudaFree(dev_file);
+      free_model(c);
+      return fail(c, AE_ERR_CUDA, "model upload failed");
+    }
+    img.file = file;
+    img.file_size = file_size;
+    img.dev_file = static_cast<const uint8_t*>(dev_file);
+  } else {
+    host.reset(new (std::nothrow) uint8_t[bytes]);
+    if (!host) {
+      free_model(c);
+      return fail(c, AE_ERR_CAPACITY, "host memory for the model image");
+    }
+    img.host = host.get();
+  }
   M.word_q = cv.take<int8_t>(size_t(kVocab) * kHidden);
   M.word_s = cv.take<float>(kVocab);
   M.pos_q = cv.take<int8_t>(size_t(kMaxPos) * kHidden);
@@ -808,55 +900,75 @@ int ae_model_load(ae_ctx* c, const ae_model_desc* d) {
   M.emb_lnb = cv.take<float>(kHidden);
   int r = 0;
   std::vector<float> type0(kHidden);
-  for (int j = 0; j < kHidden; ++j) type0[j] = float(d->type_emb_q[j]) * d->type_emb_scale[0];  // src/model.rs:50-54
-  if ((r = upload(c, M.word_q, d->word_emb_q, size_t(kVocab) * kHidden)) || (r = upload(c, M.word_s, d->word_emb_scale, kVocab)) ||
-      (r = upload(c, M.pos_q, d->pos_emb_q, size_t(kMaxPos) * kHidden)) || (r = upload(c, M.pos_s, d->pos_emb_scale, kMaxPos)) ||
-      (r = upload(c, M.type0, type0.data(), kHidden)) || (r = upload(c, M.emb_lnw, d->emb_ln_weight, kHidden)) ||
-      (r = upload(c, M.emb_lnb, d->emb_ln_bias, kHidden))) {
-    free_model(c);
-    return r;
-  }
+  float type_scale;  // the pack's float arrays need not be 4-byte aligned in a mapped file
+  std::memcpy(&type_scale, d->type_emb_scale, 4);
+  for (int j = 0; j < kHidden; ++j) type0[j] = float(d->type_emb_q[j]) * type_scale;  // src/model.rs:50-54
+  img.put(M.word_q, d->word_emb_q, size_t(kVocab) * kHidden);
+  img.put(M.word_s, d->word_emb_scale, kVocab);
+  img.put(M.pos_q, d->pos_emb_q, size_t(kMaxPos) * kHidden);
+  img.put(M.pos_s, d->pos_emb_scale, kMaxPos);
+  img.put(M.type0, type0.data(), kHidden);
+  img.put(M.emb_lnw, d->emb_ln_weight, kHidden);
+  img.put(M.emb_lnb, d->emb_ln_bias, kHidden);
   for (int l = 0; l < kLayers && !r; ++l) {
     const ae_layer_desc& L = d->layers[l];
     DevLayer& D = M.layers[l];
-    r = upload_linear(c, cv, L.qkv, D.qkv);
-    if (!r && L.has_split) r = upload_linear(c, cv, L.q_only, D.q_only);
-    if (!r && L.has_split) r = upload_linear(c, cv, L.kv_only, D.kv_only);
-    if (!r) r = upload_linear(c, cv, L.attn_out, D.ao);
-    if (!r) r = upload_linear(c, cv, L.ffn_inter, D.fi);
-    if (!r) r = upload_linear(c, cv, L.ffn_out, D.fo);
+    r = upload_linear(c, cv, img, L.qkv, D.qkv);
+    if (!r && L.has_split) r = upload_linear(c, cv, img, L.q_only, D.q_only);
+    if (!r && L.has_split) r = upload_linear(c, cv, img, L.kv_only, D.kv_only);
+    if (!r) r = upload_linear(c, cv, img, L.attn_out, D.ao);
+    if (!r) r = upload_linear(c, cv, img, L.ffn_inter, D.fi);
+    if (!r) r = upload_linear(c, cv, img, L.ffn_out, D.fo);
     if (!r) {
       D.ln1w = cv.take<float>(kHidden);
       D.ln1b = cv.take<float>(kHidden);
       D.ln2w = cv.take<float>(kHidden);
       D.ln2b = cv.take<float>(kHidden);
-      if ((r = upload(c, D.ln1w, L.ln1_weight, kHidden)) || (r = upload(c, D.ln1b, L.ln1_bias, kHidden)) ||
-          (r = upload(c, D.ln2w, L.ln2_weight, kHidden)) || (r = upload(c, D.ln2b, L.ln2_bias, kHidden))) {
-      }
+      img.put(D.ln1w, L.ln1_weight, kHidden);
+      img.put(D.ln1b, L.ln1_bias, kHidden);
+      img.put(D.ln2w, L.ln2_weight, kHidden);
+      img.put(D.ln2b, L.ln2_bias, kHidden);
     }
   }
+  if (!r && cv.off > bytes) r = fail(c, AE_ERR_BAD_PACK, "internal: model arena overflow");
+  if (!r && host && cudaMemcpy(arena, host.get(), cv.off, cudaMemcpyHostToDevice) != cudaSuccess)
+    r = fail(c, AE_ERR_CUDA, "model upload failed");
+  for (size_t i = 0; !r && i < img.d2d.size(); ++i)
+    if (cudaMemcpyAsync(img.d2d[i].dst, img.d2d[i].src, img.d2d[i].n, cudaMemcpyDeviceToDevice, c->stream) !=
+        cudaSuccess)
+      r = fail(c, AE_ERR_CUDA, "model upload failed");
+  for (size_t i = 0; !r && i < img.h2d.size(); ++i)
+    if (cudaMemcpyAsync(img.h2d[i].dst, img.h2d[i].src, img.h2d[i].n, cudaMemcpyHostToDevice, c->stream) !=
+        cudaSuccess)
+      r = fail(c, AE_ERR_CUDA, "model upload failed");
+  if (cudaStreamSynchronize(c->stream) != cudaSuccess && !r) r = fail(c, AE_ERR_CUDA, "model upload failed");
+  if (dev_file) cudaFree(dev_file);
   if (r) {
     free_model(c);
     return r;
-  }
-  if (cv.off > bytes) {
-    free_model(c);
-    return fail(c, AE_ERR_BAD_PACK, "internal: model arena overflow");
   }
   c->has_model = true;
   return 0;
 }
 
+}  // namespace
+
+int ae_model_load(ae_ctx* c, const ae_model_desc* d) {
+  if (!c || !d) return fail(c, AE_ERR_INVALID_ARG, "null argument");
+  DeviceGuard g(c->device);
+  return load_model(c, d, nullptr, 0);
+}
+
 int ae_model_load_file(ae_ctx* c, const char* path) {
   if (!c || !path) return fail(c, AE_ERR_INVALID_ARG, "null argument");
-  std::ifstream f(path, std::ios::binary);
-  if (!f) return fail(c, AE_ERR_BAD_PACK, "cannot open %s", path);
+  DeviceGuard g(c->device);
+  MappedFile mf;
+  if (!mf.open(path)) return fail(c, AE_ERR_BAD_PACK, "cannot open %s", path);
   Ae8 p;
-  p.bytes.assign(std::istreambuf_iterator<char>(f), std::istreambuf_iterator<char>());
-  if (p.bytes.size() < 8 || std::memcmp(p.bytes.data(), "ARCTIC8\x01", 8) != 0)
+  p.data = mf.data;
+  p.size = mf.size;
+  if (p.size < 8 || std::memcmp(p.data, "ARCTIC8\x01", 8) != 0)
     return fail(c, AE_ERR_BAD_PACK, "invalid .ae8 magic header");
-  p.i8s.reserve(128);
-  p.f32s.reserve(512);
   ae_model_desc d{};
   uint64_t n0, n1, n2, n3, n4, n5, n6, n7;
   d.word_emb_q = p.i8vec(&n0);
@@ -875,7 +987,7 @@ int ae_model_load_file(ae_ctx* c, const char* path) {
     ae_layer_desc& L = d.layers[l];
     p.linear(L.qkv);
     uint8_t split = 0;
-    if (p.pos < p.bytes.size()) split = p.bytes[p.pos++];
+    if (p.pos < p.size) split = p.data[p.pos++];
     else p.ok = false;
     L.has_split = split == 1;
     if (L.has_split) {
@@ -894,7 +1006,7 @@ int ae_model_load_file(ae_ctx* c, const char* path) {
       return fail(c, AE_ERR_BAD_PACK, "layer %d: LayerNorm vectors must have 384 entries", l);
   }
   if (!p.ok) return fail(c, AE_ERR_BAD_PACK, "truncated or inconsistent .ae8 pack");
-  return ae_model_load(c, &d);
+  return load_model(c, &d, mf.data, mf.size);
 }
 
 int ae_reserve(ae_ctx* c, uint32_t max_tokens, uint32_t max_seqs) {
