@@ -155,6 +155,8 @@ __host__ __device__ constexpr uint32_t tmem_cols_for_len(int L) {
 // part in the warp-collective TMEM loads and stores and write nothing.
 template <int QT>
 __global__ void __launch_bounds__(QT, 512 / QT) k_attention_rows(AttnArgs a) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ float4 smem4[];
   __shared__ uint32_t tmem_slot;
   const int s = blockIdx.x;
@@ -339,6 +341,8 @@ __global__ void __launch_bounds__(QT, 512 / QT) k_attention_rows(AttnArgs a) {
 // keys in order.
 template <int NWG, int MINB>
 __global__ void __launch_bounds__(128 * NWG, MINB) k_attention_wide(AttnArgs a) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int KPG = 16 / NWG;  // keys of a 16-key chunk per group (8 or 4)
   constexpr int DPG = 32 / NWG;  // dims of V per group (16 or 8)
   extern __shared__ float4 smem4[];
@@ -516,6 +520,8 @@ __global__ void __launch_bounds__(128 * NWG, MINB) k_attention_wide(AttnArgs a) 
 constexpr int kClsWarpFloats = kMaxPos + 32 * 33;
 
 __global__ void __launch_bounds__(128) k_attention_cls(AttnArgs a, int n_seqs) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ float4 smem4[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int item = blockIdx.x * 4 + warp;  // (sequence, head)
@@ -611,15 +617,15 @@ template <int QT>
 static int launch_rows(const AttnArgs& a, int n_seqs, cudaStream_t st) {
   dim3 grid(n_seqs, kHeads, (a.max_len + QT - 1) / QT);
   if (QT == 128 && tmem_cols_for_len(a.max_len) == 256) {  // 2 CTAs per SM: two warpgroups each
-    k_attention_wide<ATTN_WIDE_256><<<grid, 128 * ATTN_WIDE_256_NWG, rows_smem(a.max_len, g_static_wide2), st>>>(a);
-    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+    return launch_pdl(k_attention_wide<ATTN_WIDE_256>, grid, dim3(128 * ATTN_WIDE_256_NWG),
+                      rows_smem(a.max_len, g_static_wide2), st, a) == cudaSuccess ? 0 : -3;
   }
   if (QT == 128 && tmem_cols_for_len(a.max_len) == 512) {  // 1 CTA per SM: four warpgroups
-    k_attention_wide<4, 1><<<grid, 512, rows_smem(a.max_len, g_static_wide4), st>>>(a);
-    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+    return launch_pdl(k_attention_wide<4, 1>, grid, dim3(512), rows_smem(a.max_len, g_static_wide4), st, a) == cudaSuccess
+               ? 0
+               : -3;
   }
-  k_attention_rows<QT><<<grid, QT, rows_smem(a.max_len, g_static_rows), st>>>(a);
-  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+  return launch_pdl(k_attention_rows<QT>, grid, dim3(QT), rows_smem(a.max_len, g_static_rows), st, a) == cudaSuccess ? 0 : -3;
 }
 
 static int smem_attr(const void* fn, size_t bytes) {
@@ -653,8 +659,10 @@ int launch_attention_exact(const AttnArgs& a, int n_seqs, cudaStream_t st) {
   if (a.max_len <= 0 || a.max_len > kMaxPos) return -1;
   if (a.cls_mode) {
     const int items = n_seqs * kHeads;
-    k_attention_cls<<<(items + 3) / 4, 128, 4 * kClsWarpFloats * 4, st>>>(a, n_seqs);
-    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+    return launch_pdl(k_attention_cls, dim3((items + 3) / 4), dim3(128), size_t(4 * kClsWarpFloats * 4), st, a, n_seqs) ==
+                   cudaSuccess
+               ? 0
+               : -3;
   }
   // query tile: no wider than the sequences (32 / 64 threads for short ones, whose TMEM then packs
   // 16 / 8 CTAs per SM), and narrower while the grid has fewer than two CTAs per SM

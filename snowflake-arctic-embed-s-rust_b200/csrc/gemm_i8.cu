@@ -109,6 +109,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int m_stride = gridDim.x / n_tiles_n;
   const int my_tiles = m_first < m_tiles ? (m_tiles - 1 - m_first) / m_stride + 1 : 0;
   const int KB = g.K / BK;
+  pdl_trigger();
 
   if (tid == 0) {
     tma_prefetch_desc(&tmA);
@@ -154,12 +155,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
       bool ok = true;
-      if constexpr (RES) {
+      if constexpr (RES) {  // the weights are model constants: loaded before waiting for the previous kernel
         mbar_arrive_expect_tx(bfull, Ly::B_RES);
         for (int kb = 0; kb < kResKB; ++kb)
           for (int j = 0; j < BN / 64; ++j)
             tma_load_2d(b_res + (kb * BN + j * 64) * BK, &tmB, bfull, kb * BK, n0 + j * 64);
       }
+      pdl_wait();
       int kc = 0;
       for (int it = 0; it < my_tiles && ok; ++it) {
         const int m0 = (m_first + it * m_stride) * BM;
@@ -183,6 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer
+    pdl_wait();
     if (lane == 0) {
       bool ok = true;
       if constexpr (RES) ok = mbar_wait(bfull, 0, g.err, DEV_ERR_TIMEOUT_MMA);
@@ -214,6 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------ epilogue
+    pdl_wait();
     const int ew = warp - 2;       // 0..15
     const int Q = warp & 3;        // TMEM lane quadrant this warp may access
     const int qq = ew >> 2;        // column quarter (F32, GELU) / reduction-lane group (LN)
@@ -675,15 +679,17 @@ static cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const Ge
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = Ly::TOTAL;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   int ctas;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // pdl_wait in the kernel
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
   if constexpr (EPI == EPI_GELU_QUANT) {
     // nt == cluster size: the 6 CTAs of a cluster hold the 6 column slices of one 128-row tile
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = kGeluCluster;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
     cfg.numAttrs = 1;
     static int max_clusters[kMaxDevices] = {};
     int dev = 0;
@@ -696,8 +702,10 @@ static cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const Ge
     }
     const int clusters = mt < max_clusters[dev] ? mt : max_clusters[dev];
     ctas = kGeluCluster * clusters;
+    cfg.numAttrs = 2;
   } else {
-    cfg.numAttrs = 0;
+    cfg.attrs = attr + 1;
+    cfg.numAttrs = 1;
     const int per_n = num_sms() / nt > 0 ? num_sms() / nt : 1;
     ctas = nt * (mt < per_n ? mt : per_n);
   }

@@ -39,6 +39,24 @@ struct AttnArgs {
   int* err;
 };
 
+// Launch with programmatic stream serialization (the kernel calls pdl_wait before it touches data
+// that earlier kernels produced).
+template <class... KArgs, class... Args>
+inline cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, static_cast<Args&&>(args)...);
+}
+
 int launch_embed(const EmbedArgs& a, cudaStream_t st);
 int launch_ln_quant_rows(const float* h_in, int M, const float* gamma, const float* beta, const float* inv_s,
                          float* hidden, int hidden_tt, int8_t* q, float* scale, cudaStream_t st);

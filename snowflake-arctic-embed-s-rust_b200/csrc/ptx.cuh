@@ -85,6 +85,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
   }
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// Kernels of the forward pass are launched with programmatic stream serialization: a kernel may
+// start while the previous one is finishing. pdl_trigger lets the next kernel launch once every
+// CTA of this one has issued it (or exited); pdl_wait blocks until the kernels this one depends on
+// have completed and their writes are visible. Before pdl_wait a kernel reads only model constants
+// and writes nothing to global memory. Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

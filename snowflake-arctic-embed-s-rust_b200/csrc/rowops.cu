@@ -41,6 +41,8 @@ __device__ __forceinline__ float halfwarp_max(float v, unsigned mask) {
 // rows go through a shared-memory tile so that the tile-transposed store of a column covers the
 // block's 16 consecutive rows (64 contiguous bytes).
 __global__ void __launch_bounds__(256) k_embed_ln_quant(EmbedArgs a) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float tile[kHidden][17];
   const int r0 = blockIdx.x * 16;
   const int lr = threadIdx.x >> 4;  // row within the block
@@ -112,6 +114,8 @@ __global__ void __launch_bounds__(256) k_ln_quant_rows(const float* __restrict__
                                                        const float* __restrict__ inv_s, float* __restrict__ hidden,
                                                        int hidden_tt, int8_t* __restrict__ q,
                                                        float* __restrict__ scale) {
+  pdl_trigger();
+  pdl_wait();
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 4;
   const int l = threadIdx.x & 15;
   const unsigned mask = 0xffffffffu;
@@ -163,6 +167,8 @@ constexpr int kLnFinalPitch = kHidden + 1;
 __global__ void __launch_bounds__(128) k_ln_final_rows(const float* __restrict__ h_in, int M,
                                                        const float* __restrict__ gamma,
                                                        const float* __restrict__ beta, float* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ float xs[];  // [kLnFinalRows][kLnFinalPitch]
   const int r0 = blockIdx.x * kLnFinalRows;
   const int rows = M - r0 < kLnFinalRows ? M - r0 : kLnFinalRows;
@@ -205,6 +211,8 @@ __global__ void __launch_bounds__(128) k_ln_final_rows(const float* __restrict__
 // attention context with attn_out.inv_smooth (src/model.rs:324-328).
 __global__ void __launch_bounds__(256) k_smooth_quant(const float* __restrict__ x, const float* __restrict__ inv_s,
                                                       int8_t* __restrict__ q, float* __restrict__ scale, int rows) {
+  pdl_trigger();
+  pdl_wait();
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -246,6 +254,8 @@ __global__ void __launch_bounds__(256) k_smooth_quant(const float* __restrict__ 
 // One block per sequence. Sequences must have 1..512 rows.
 __global__ void k_row_meta(const uint32_t* __restrict__ cu, int n_seqs, uint16_t* __restrict__ pos,
                            int32_t* __restrict__ cls_row, int* err) {
+  pdl_trigger();
+  pdl_wait();
   const int s = blockIdx.x;
   if (s >= n_seqs) return;
   const uint32_t b = cu[s], e = cu[s + 1];
@@ -263,6 +273,8 @@ __global__ void k_row_meta(const uint32_t* __restrict__ cu, int n_seqs, uint16_t
 __global__ void k_gather_cls(const int32_t* __restrict__ cls_row, int n, const int8_t* __restrict__ act_q,
                              const float* __restrict__ act_s, const float* __restrict__ hidden,
                              int8_t* __restrict__ cq, float* __restrict__ cs, float* __restrict__ ch) {
+  pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.x;
   if (b >= n) return;
   const int r = cls_row[b];
@@ -277,42 +289,38 @@ __global__ void k_gather_cls(const int32_t* __restrict__ cls_row, int n, const i
 int launch_embed(const EmbedArgs& a, cudaStream_t st) {
   if (a.T <= 0) return 0;
   const int rows_per_block = 16;
-  k_embed_ln_quant<<<(a.T + rows_per_block - 1) / rows_per_block, 256, 0, st>>>(a);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  const dim3 grid((a.T + rows_per_block - 1) / rows_per_block);
+  return launch_pdl(k_embed_ln_quant, grid, dim3(256), 0, st, a) == cudaSuccess ? 0 : -1;
 }
 
 int launch_ln_quant_rows(const float* h_in, int M, const float* gamma, const float* beta, const float* inv_s,
                          float* hidden, int hidden_tt, int8_t* q, float* scale, cudaStream_t st) {
   if (M <= 0) return 0;
-  k_ln_quant_rows<<<(M + 15) / 16, 256, 0, st>>>(h_in, M, gamma, beta, inv_s, hidden, hidden_tt, q, scale);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_pdl(k_ln_quant_rows, dim3((M + 15) / 16), dim3(256), 0, st, h_in, M, gamma, beta, inv_s, hidden,
+                    hidden_tt, q, scale) == cudaSuccess ? 0 : -1;
 }
 
 int launch_ln_final_rows(const float* h_in, int M, const float* gamma, const float* beta, float* out,
                          cudaStream_t st) {
   if (M <= 0) return 0;
-  k_ln_final_rows<<<(M + kLnFinalRows - 1) / kLnFinalRows, 128, kLnFinalRows * kLnFinalPitch * 4, st>>>(
-      h_in, M, gamma, beta, out);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_pdl(k_ln_final_rows, dim3((M + kLnFinalRows - 1) / kLnFinalRows), dim3(128),
+                    size_t(kLnFinalRows * kLnFinalPitch * 4), st, h_in, M, gamma, beta, out) == cudaSuccess ? 0 : -1;
 }
 
 int launch_smooth_quant(const float* x, const float* inv_s, int8_t* q, float* scale, int rows, cudaStream_t st) {
   if (rows <= 0) return 0;
-  k_smooth_quant<<<(rows + 7) / 8, 256, 0, st>>>(x, inv_s, q, scale, rows);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_pdl(k_smooth_quant, dim3((rows + 7) / 8), dim3(256), 0, st, x, inv_s, q, scale, rows) == cudaSuccess ? 0 : -1;
 }
 
 int launch_row_meta(const uint32_t* cu, int n_seqs, uint16_t* pos, int32_t* cls_row, int* err, cudaStream_t st) {
   if (n_seqs <= 0) return 0;
-  k_row_meta<<<n_seqs, 128, 0, st>>>(cu, n_seqs, pos, cls_row, err);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_pdl(k_row_meta, dim3(n_seqs), dim3(128), 0, st, cu, n_seqs, pos, cls_row, err) == cudaSuccess ? 0 : -1;
 }
 
 int launch_gather_cls(const int32_t* cls_row, int n, const int8_t* act_q, const float* act_s, const float* hidden,
                       int8_t* cq, float* cs, float* ch, cudaStream_t st) {
   if (n <= 0) return 0;
-  k_gather_cls<<<n, 96, 0, st>>>(cls_row, n, act_q, act_s, hidden, cq, cs, ch);
-  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+  return launch_pdl(k_gather_cls, dim3(n), dim3(96), 0, st, cls_row, n, act_q, act_s, hidden, cq, cs, ch) == cudaSuccess ? 0 : -1;
 }
 
 }  // namespace ae
