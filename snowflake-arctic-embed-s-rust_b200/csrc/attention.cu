@@ -665,9 +665,12 @@ int launch_attention_exact(const AttnArgs& a, int n_seqs, cudaStream_t st) {
                : -3;
   }
   // query tile: no wider than the sequences (32 / 64 threads for short ones, whose TMEM then packs
-  // 16 / 8 CTAs per SM), and narrower while the grid has fewer than two CTAs per SM
+  // 16 / 8 CTAs per SM), and narrower while the grid has fewer than two CTAs per SM.
+  // More than 128 keys: always the multi-warpgroup kernels (their score columns allow only 1-2 CTAs
+  // per SM, so one-warp tiles would leave each SM one warp for L x 32 query-key pairs).
   const int cap = a.max_len <= 32 ? 32 : a.max_len <= 64 ? 64 : 128;
   const long heads = long(n_seqs) * kHeads;
+  if (a.max_len > 128) return launch_rows<128>(a, n_seqs, st);
   if (cap == 128 && heads * ((a.max_len + 127) / 128) >= 2 * 148) return launch_rows<128>(a, n_seqs, st);
   if (cap >= 64 && heads * ((a.max_len + 63) / 64) >= 2 * 148) return launch_rows<64>(a, n_seqs, st);
   return launch_rows<32>(a, n_seqs, st);
