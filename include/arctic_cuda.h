@@ -83,7 +83,8 @@ int ae_ctx_create(int device, ae_ctx** out);
 int ae_ctx_destroy(ae_ctx* ctx);
 /* Message of the last failure on ctx (or of the last ae_ctx_create failure when ctx is NULL). */
 const char* ae_last_error(const ae_ctx* ctx);
-/* Stream the context launches on (a cudaStream_t); NULL selects the context's own stream. */
+/* Stream the context launches on (a cudaStream_t); NULL selects the context's own stream, a
+ * blocking stream (ordered with work on the legacy default stream). */
 int ae_ctx_set_stream(ae_ctx* ctx, void* cuda_stream);
 int ae_ctx_device(const ae_ctx* ctx);
 

@@ -779,7 +779,9 @@ int ae_ctx_create(int device, ae_ctx** out) {
   DeviceGuard g(device);
   auto* c = new ae_ctx();
   c->device = device;
-  e = cudaStreamCreateWithFlags(&c->own_stream, cudaStreamNonBlocking);
+  // a blocking stream: work that callers put on the legacy default stream (e.g. torch's default
+  // stream preparing the inputs of ae_forward_ragged_device) is ordered with the context's work
+  e = cudaStreamCreate(&c->own_stream);
   if (e == cudaSuccess) e = cudaMalloc(&c->d_err, sizeof(int));
   if (e == cudaSuccess) e = cudaMemset(c->d_err, 0, sizeof(int));
   if (e != cudaSuccess) {
