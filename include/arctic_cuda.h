@@ -185,6 +185,12 @@ uint64_t ae_kernel_launches(const ae_ctx* ctx);
 /* Waits for the context's stream; reports a device-side error (AE_ERR_DEVICE) if one was raised. */
 int ae_sync(ae_ctx* ctx);
 
+/* Self-test of failure detection (no reference counterpart): launches a kernel whose bounded wait
+ * on an mbarrier can never complete, with a limit of limit_us microseconds (1..1,000,000) instead
+ * of the kernels' 2 s. Returns AE_ERR_DEVICE ("epilogue wait timed out"); the context stays usable.
+ * No GPU fault or hang is involved. */
+int ae_selftest_wait_timeout(ae_ctx* ctx, uint32_t limit_us);
+
 /* ---------------------------------------------------------------------------------------------
  * WordPiece tokenizer (host only, no GPU needed): BertTokenizer, src/tokenizer.rs:25-327.
  * Text is UTF-8 (AE_ERR_INVALID_ARG on invalid UTF-8, which a Rust &str cannot hold). Outputs are

@@ -175,6 +175,10 @@ class Engine:
     def sync(self) -> None:
         self._check(lib().ae_sync(self._h))
 
+    def selftest_wait_timeout(self, limit_us: int) -> None:
+        """ae_selftest_wait_timeout: a bounded device wait that runs out; raises AeError(AE_ERR_DEVICE)."""
+        self._check(lib().ae_selftest_wait_timeout(self._h, limit_us))
+
     def kernel_launches(self) -> int:
         return int(lib().ae_kernel_launches(self._h))
 

@@ -33,6 +33,7 @@ SYMBOLS = [
     "ae_plan_shards", "ae_forward_cls_noalloc", "ae_profile", "ae_profile_read", "ae_sync",
     "ae_tokenizer_create_from_file", "ae_tokenizer_create_from_vocab", "ae_tokenizer_destroy",
     "ae_tokenizer_vocab_size", "ae_tokenizer_last_error", "ae_tokenize", "ae_tokenize_batch",
+    "ae_selftest_wait_timeout",
 ]
 
 
@@ -107,6 +108,7 @@ def lib():
     L.ae_forward_cls_noalloc.argtypes = [P, P, u32, P]
     L.ae_profile.argtypes = [P, C.c_int]
     L.ae_profile_read.argtypes = [P, P, P]
+    L.ae_selftest_wait_timeout.argtypes = [P, u32]
     L.ae_tokenizer_create_from_file.argtypes = [C.c_char_p, C.POINTER(P)]
     L.ae_tokenizer_create_from_vocab.argtypes = [C.c_char_p, C.c_size_t, C.POINTER(P)]
     L.ae_tokenizer_destroy.argtypes = [P]

@@ -1198,6 +1198,15 @@ int ae_gemm_i8(ae_ctx* c, int epi, uint32_t M, uint32_t N, uint32_t K, const int
   return 0;
 }
 
+int ae_selftest_wait_timeout(ae_ctx* c, uint32_t limit_us) {
+  if (!c || limit_us == 0 || limit_us > 1000000) return fail(c, AE_ERR_INVALID_ARG, "limit_us must be 1..1000000");
+  DeviceGuard g(c->device);
+  if (launch_wait_selftest(c->d_err, uint64_t(limit_us) * 1000, c->stream))
+    return fail(c, AE_ERR_CUDA, "self-test launch failed");
+  CUDA_TRY(c, cudaStreamSynchronize(c->stream));
+  return check_dev_err(c);
+}
+
 int ae_attention_f32(ae_ctx* c, const float* d_qkv, const uint32_t* d_cu, uint32_t n, uint32_t max_len, float* d_ctx) {
   if (!c) return AE_ERR_INVALID_ARG;
   if (!d_qkv || !d_cu || !d_ctx || max_len == 0 || max_len > uint32_t(kMaxPos))

@@ -58,6 +58,7 @@ inline cudaError_t launch_pdl(void (*k)(KArgs...), dim3 grid, dim3 block, size_t
 }
 
 int launch_embed(const EmbedArgs& a, cudaStream_t st);
+int launch_wait_selftest(int* err, uint64_t limit_ns, cudaStream_t st);
 int launch_ln_quant_rows(const float* h_in, int M, const float* gamma, const float* beta, const float* inv_s,
                          float* hidden, int hidden_tt, int8_t* q, float* scale, cudaStream_t st);
 int launch_ln_final_rows(const float* h_in, int M, const float* gamma, const float* beta, float* out,

@@ -71,14 +71,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
   return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity to complete.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+// Bounded wait for the phase with the given parity to complete: after limit_ns the wait records
+// `code` in the device error word and returns false (the caller then stops and returns).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
     if (mbar_try_wait(a, parity)) return true;
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (globaltimer() - t0 > limit_ns) {
       record_err(err, code);
       return false;
     }

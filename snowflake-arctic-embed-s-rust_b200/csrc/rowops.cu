@@ -286,6 +286,24 @@ __global__ void k_gather_cls(const int32_t* __restrict__ cls_row, int n, const i
   if (t == 0) cs[b] = act_s[r];
 }
 
+// Self-test of the bounded device waits: one thread waits for a phase of an mbarrier that nothing
+// ever completes, through the same mbar_wait the GEMM pipeline uses; the wait gives up after
+// limit_ns and records DEV_ERR_TIMEOUT_EPILOGUE. Nothing faults or hangs.
+__global__ void k_wait_selftest(int* err, uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(&bar, 0, err, DEV_ERR_TIMEOUT_EPILOGUE, limit_ns);
+}
+
+int launch_wait_selftest(int* err, uint64_t limit_ns, cudaStream_t st) {
+  k_wait_selftest<<<1, 32, 0, st>>>(err, limit_ns);
+  return cudaGetLastError() == cudaSuccess ? 0 : -1;
+}
+
 int launch_embed(const EmbedArgs& a, cudaStream_t st) {
   if (a.T <= 0) return 0;
   const int rows_per_block = 16;

@@ -166,3 +166,13 @@ def test_text_to_embedding(engine, oracle_model):
     batch = model.embed_batch(docs)
     for t, b in zip(docs, batch):
         np.testing.assert_array_equal(b, model.embed_document(t))
+
+
+def test_bounded_wait_reports_error(engine):
+    """Failure detection without a GPU fault: a device wait that can never complete gives up after
+    its limit, the host gets AE_ERR_DEVICE with the reason, and the context keeps working."""
+    with pytest.raises(AeError, match="DEVICE.*timed out"):
+        engine.selftest_wait_timeout(2000)
+    ids = synth.token_ids(20, rng(12))
+    np.testing.assert_array_equal(engine.forward_cls(ids), engine.forward_cls(ids))
+    engine.sync()
