@@ -89,7 +89,8 @@ __device__ __forceinline__ float ld_act(const float* p, int C, int tt, int t, in
 // Stages the head's K and V of rows [s0, s0 + L) as key pairs (k[2p][d], k[2p+1][d]), K dims in
 // score_pair's order, V dims in order (odd L: the last pair's second key is 0). A warp covers
 // 8 pairs x 4 dims per step, so the tile-transposed rows it reads are contiguous.
-__device__ __forceinline__ void stage_kv_pairs(const AttnArgs& a, int s0, int L, int h, float2* kp, float2* vp) {
+__device__ __forceinline__ void stage_kv_pairs(const AttnArgs& a, int s0, int L, int h, float2* kp, float2* vp,
+                                               bool wait = true) {
   const int pairs = (L + 1) >> 1;
   const int kc = a.k_col + 32 * h, vc = a.v_col + 32 * h;
   if (a.kv_tt && !(s0 & 1)) {
@@ -103,7 +104,7 @@ __device__ __forceinline__ void stage_kv_pairs(const AttnArgs& a, int s0, int L,
       cp_async8(kp + p * KPS + (d & 7) * 4 + (d >> 3), a.kv + tt_index(t, kc + d, a.kv_C), bytes);
       cp_async8(vp + p * KPS + d, a.kv + tt_index(t, vc + d, a.kv_C), bytes);
     }
-    cp_async_wait_all();
+    if (wait) cp_async_wait_all();
     return;
   }
   const int groups = (pairs + 7) >> 3;  // 8-pair groups
@@ -332,6 +333,283 @@ __global__ void __launch_bounds__(QT, 512 / QT) k_attention_rows(AttnArgs a) {
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem_slot, cols);
+}
+
+// Scores of the key pair (2i, 2i+1) for NQ queries at once: each staged K float4 is loaded once
+// and used by every query (score_pair's operations, in its order, per query).
+template <int NQ>
+__device__ __forceinline__ void score_pairs(const float (&q)[NQ][32], const float2* __restrict__ kp, bool grouped,
+                                            float2 (&sp)[NQ]) {
+  const float4* k4 = reinterpret_cast<const float4*>(kp);
+  float2 s8[NQ][8];
+#pragma unroll
+  for (int l = 0; l < 8; ++l) {
+    const float4 t0 = k4[2 * l];
+    const float4 t1 = k4[2 * l + 1];
+#pragma unroll
+    for (int u = 0; u < NQ; ++u) {
+      const float2 a = fma2(f2(q[u][8 + l], q[u][8 + l]), f2(t0.z, t0.w), mul2(f2(q[u][l], q[u][l]), f2(t0.x, t0.y)));
+      const float2 b =
+          fma2(f2(q[u][24 + l], q[u][24 + l]), f2(t1.z, t1.w), mul2(f2(q[u][16 + l], q[u][16 + l]), f2(t1.x, t1.y)));
+      s8[u][l] = add2(a, b);
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < NQ; ++u) {
+    const float2* x = s8[u];
+    sp[u] = grouped ? add2(add2(add2(x[0], x[1]), add2(x[2], x[3])), add2(add2(x[4], x[5]), add2(x[6], x[7])))
+                    : add2(add2(add2(x[0], x[4]), add2(x[1], x[5])), add2(add2(x[2], x[6]), add2(x[3], x[7])));
+  }
+}
+
+// k_attention_rows' three passes for NQ queries per thread over the same staged K / V: every
+// shared-memory load of K or V feeds NQ queries. Query u keeps its scores, then exponentials, in
+// TMEM columns tl + u * qcols .. + L - 1 of the thread's lane. q: pre-scaled by 1/sqrt(32);
+// out[u] = nullptr for a query past the sequence (which still takes part in the warp-collective
+// TMEM loads and stores).
+template <int NQ>
+__device__ __forceinline__ void attend_rows(const float (&q)[NQ][32], const float2* __restrict__ kp,
+                                            const float2* __restrict__ vp, int L, uint32_t tl, uint32_t qcols,
+                                            float* const (&out)[NQ]) {
+  const int L4 = L & ~3, L8 = L & ~7, L16 = L & ~15;
+  uint32_t r[NQ][16];
+
+  // pass 1: scores -> TMEM and their max
+  float mx[NQ];
+#pragma unroll
+  for (int u = 0; u < NQ; ++u) mx[u] = -INFINITY;
+  for (int t0 = 0; t0 < L; t0 += 16) {
+    if (t0 + 16 <= L4) {
+      float2 ma[NQ], mb[NQ];
+#pragma unroll
+      for (int u = 0; u < NQ; ++u) ma[u] = mb[u] = f2(-INFINITY, -INFINITY);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float2 sp[NQ];
+        score_pairs<NQ>(q, kp + ((t0 >> 1) + j) * KPS, true, sp);
+#pragma unroll
+        for (int u = 0; u < NQ; ++u) {
+          if (j & 1) mb[u] = f2(fmaxf(mb[u].x, sp[u].x), fmaxf(mb[u].y, sp[u].y));
+          else ma[u] = f2(fmaxf(ma[u].x, sp[u].x), fmaxf(ma[u].y, sp[u].y));
+          r[u][2 * j] = __float_as_uint(sp[u].x);
+          r[u][2 * j + 1] = __float_as_uint(sp[u].y);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < NQ; ++u) mx[u] = fmaxf(mx[u], fmaxf(fmaxf(ma[u].x, ma[u].y), fmaxf(mb[u].x, mb[u].y)));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int t = t0 + 2 * j;
+        float2 sp[NQ];
+#pragma unroll
+        for (int u = 0; u < NQ; ++u) sp[u] = f2(0.0f, 0.0f);
+        if (t < L) {
+          score_pairs<NQ>(q, kp + (t >> 1) * KPS, t < L4, sp);
+#pragma unroll
+          for (int u = 0; u < NQ; ++u) {
+            mx[u] = fmaxf(mx[u], sp[u].x);
+            if (t + 1 < L) mx[u] = fmaxf(mx[u], sp[u].y);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < NQ; ++u) {
+          r[u][2 * j] = __float_as_uint(sp[u].x);
+          r[u][2 * j + 1] = __float_as_uint(sp[u].y);
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < NQ; ++u) tmem_st16(tl + u * qcols + t0, r[u]);
+  }
+  tmem_st_wait();
+
+  // pass 2: exponentials (back into TMEM) and their sums, in k_attention_rows' order per query
+  float inv[NQ];
+  {
+    float2 vs0[NQ][4], vs1[NQ][4];
+#pragma unroll
+    for (int u = 0; u < NQ; ++u)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) vs0[u][j] = vs1[u][j] = f2(0.0f, 0.0f);
+    for (int t0 = 0; t0 < L; t0 += 16) {
+#pragma unroll
+      for (int u = 0; u < NQ; ++u) tmem_ld16(tl + u * qcols + t0, r[u]);
+      tmem_ld_wait();
+#pragma unroll
+      for (int u = 0; u < NQ; ++u) {
+        const float2 neg_mx = f2(-mx[u], -mx[u]);
+        if (t0 + 16 <= L16) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float2 e =
+                cw_exp2(add2(f2(__uint_as_float(r[u][2 * j]), __uint_as_float(r[u][2 * j + 1])), neg_mx));
+            if (j < 4) vs0[u][j] = add2(vs0[u][j], e);
+            else vs1[u][j - 4] = add2(vs1[u][j - 4], e);
+            r[u][2 * j] = __float_as_uint(e.x);
+            r[u][2 * j + 1] = __float_as_uint(e.y);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int t = t0 + 2 * j;
+            const float2 x = add2(f2(__uint_as_float(r[u][2 * j]), __uint_as_float(r[u][2 * j + 1])), neg_mx);
+            float2 e;
+            if (j < 4 && t + 1 < L8) {
+              e = cw_exp2(x);
+              vs0[u][j & 3] = add2(vs0[u][j & 3], e);
+            } else {
+              e = f2(t < L ? scalar_expf(x.x) : 0.0f, t + 1 < L ? scalar_expf(x.y) : 0.0f);
+            }
+            r[u][2 * j] = __float_as_uint(e.x);
+            r[u][2 * j + 1] = __float_as_uint(e.y);
+          }
+        }
+        tmem_st16(tl + u * qcols + t0, r[u]);
+      }
+    }
+    tmem_st_wait();
+#pragma unroll
+    for (int u = 0; u < NQ; ++u) {
+      float v8[8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 t = add2(vs0[u][j], vs1[u][j]);
+        v8[2 * j] = t.x;
+        v8[2 * j + 1] = t.y;
+      }
+      float sum = tree8(v8);
+      if (L8 < L) {
+        tmem_ld16(tl + u * qcols + L16, r[u]);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (L16 + j >= L8 && L16 + j < L) sum = sum + __uint_as_float(r[u][j]);
+      }
+      inv[u] = 1.0f / sum;
+    }
+  }
+
+  // pass 3: probabilities and the weighted sum of V; lane x = even keys, lane y = odd keys
+  float2 acc[NQ][32];
+#pragma unroll
+  for (int u = 0; u < NQ; ++u)
+#pragma unroll
+    for (int d = 0; d < 32; ++d) acc[u][d] = f2(0.0f, 0.0f);
+  for (int t0 = 0; t0 < L; t0 += 16) {
+#pragma unroll
+    for (int u = 0; u < NQ; ++u) tmem_ld16(tl + u * qcols + t0, r[u]);
+    tmem_ld_wait();
+    if (t0 + 16 <= L) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float2 p[NQ];
+#pragma unroll
+        for (int u = 0; u < NQ; ++u)
+          p[u] = mul2(f2(__uint_as_float(r[u][2 * j]), __uint_as_float(r[u][2 * j + 1])), f2(inv[u], inv[u]));
+        const float4* v4 = reinterpret_cast<const float4*>(vp + ((t0 >> 1) + j) * KPS);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float4 vv = v4[i];
+#pragma unroll
+          for (int u = 0; u < NQ; ++u) {
+            acc[u][2 * i] = fma2(f2(vv.x, vv.y), p[u], acc[u][2 * i]);
+            acc[u][2 * i + 1] = fma2(f2(vv.z, vv.w), p[u], acc[u][2 * i + 1]);
+          }
+        }
+      }
+      continue;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int t = t0 + 2 * j;
+      if (t + 1 < L) {
+        float2 p[NQ];
+#pragma unroll
+        for (int u = 0; u < NQ; ++u)
+          p[u] = mul2(f2(__uint_as_float(r[u][2 * j]), __uint_as_float(r[u][2 * j + 1])), f2(inv[u], inv[u]));
+        const float4* v4 = reinterpret_cast<const float4*>(vp + (t >> 1) * KPS);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float4 vv = v4[i];
+#pragma unroll
+          for (int u = 0; u < NQ; ++u) {
+            acc[u][2 * i] = fma2(f2(vv.x, vv.y), p[u], acc[u][2 * i]);
+            acc[u][2 * i + 1] = fma2(f2(vv.z, vv.w), p[u], acc[u][2 * i + 1]);
+          }
+        }
+      } else if (t < L) {  // odd L: the last key goes to the even accumulator
+        const float2* v = vp + (t >> 1) * KPS;
+#pragma unroll
+        for (int u = 0; u < NQ; ++u) {
+          const float pa = __uint_as_float(r[u][2 * j]) * inv[u];
+#pragma unroll
+          for (int d = 0; d < 32; ++d) acc[u][d].x = fmaf(v[d].x, pa, acc[u][d].x);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < NQ; ++u) {
+    if (out[u]) {
+      float4* o = reinterpret_cast<float4*>(out[u]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        o[i] = make_float4(acc[u][4 * i].x + acc[u][4 * i].y, acc[u][4 * i + 1].x + acc[u][4 * i + 1].y,
+                           acc[u][4 * i + 2].x + acc[u][4 * i + 2].y, acc[u][4 * i + 3].x + acc[u][4 * i + 3].y);
+    }
+  }
+}
+
+// Sequences of 65..128 keys in wide batches: one CTA per (sequence, pair of heads), 128 threads.
+// Warps 0-1 take head 2y, warps 2-3 head 2y + 1 (TMEM lanes 0-63 / 64-127); thread j of a head
+// takes queries j and j + 64, so every staged K / V load feeds two queries. The scores of query
+// j + 64 sit 128 TMEM columns after those of query j (256 columns: two CTAs per SM).
+__global__ void __launch_bounds__(128, 2) k_attention_rows2(AttnArgs a) {
+  pdl_trigger();
+  pdl_wait();
+  extern __shared__ float4 smem4[];
+  __shared__ uint32_t tmem_slot;
+  const int s = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int unit = warp >> 1;
+  const int h = 2 * blockIdx.y + unit;
+  const int s0 = int(a.cu[s]);
+  const int L = int(a.cu[s + 1]) - s0;
+  if (L <= 0 || L > a.max_len || L > 128) {
+    if (tid == 0 && blockIdx.y == 0) record_err(a.err, DEV_ERR_BAD_SHAPE);
+    return;
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, 256);
+    tmem_relinquish();
+  }
+  const int pairs = (L + 1) >> 1;
+  float2* kp0 = reinterpret_cast<float2*>(smem4);
+  float2* kp1 = kp0 + 2 * pairs * KPS;
+  stage_kv_pairs(a, s0, L, 2 * blockIdx.y, kp0, kp0 + pairs * KPS, false);
+  stage_kv_pairs(a, s0, L, 2 * blockIdx.y + 1, kp1, kp1 + pairs * KPS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tl = tmem_slot + (uint32_t(warp * 32) << 16);
+  const float2* kp = unit ? kp1 : kp0;
+
+  const int j = (warp & 1) * 32 + (tid & 31);
+  float q[2][32];
+  float* out[2];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int qi = j + 64 * u;
+    const bool active = qi < L;
+    load_query(a, s0 + (active ? qi : L - 1), h, q[u]);
+    out[u] = active ? a.out + size_t(s0 + qi) * kHidden + h * 32 : nullptr;
+  }
+  attend_rows<2>(q, kp, kp + pairs * KPS, L, tl, 128, out);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem_slot, 256);
 }
 
 // NWG warpgroups per 128-query tile: warps w, w + 4, ... share TMEM lane quadrant w & 3 (the same
@@ -595,7 +873,7 @@ __global__ void __launch_bounds__(128) k_attention_cls(AttnArgs a, int n_seqs) {
 constexpr size_t kRowsSmemMax = 220 * 1024;  // dynamic shared memory cap (static smem comes on top)
 
 // Static shared memory of the kernels (cudaFuncGetAttributes at setup), counted by rows_smem.
-static size_t g_static_rows = 0, g_static_wide2 = 0, g_static_wide4 = 0;
+static size_t g_static_rows = 0, g_static_wide2 = 0, g_static_wide4 = 0, g_static_rows2 = 0;
 
 // Dynamic shared memory of a CTA: the K / V pairs, padded so that at most 512 / cols CTAs share an
 // SM (their TMEM allocations then always fit; a CTA never waits in tcgen05.alloc). static_bytes:
@@ -628,6 +906,15 @@ static int launch_rows(const AttnArgs& a, int n_seqs, cudaStream_t st) {
   return launch_pdl(k_attention_rows<QT>, grid, dim3(QT), rows_smem(a.max_len, g_static_rows), st, a) == cudaSuccess ? 0 : -3;
 }
 
+// k_attention_rows2: K / V pairs of two heads; at least half an SM's shared memory, so that no
+// more CTAs share an SM than its TMEM holds (2 x 256 columns).
+static int launch_rows2(const AttnArgs& a, int n_seqs, cudaStream_t st) {
+  const size_t kv = size_t((a.max_len + 1) / 2) * KPS * 8 * 4;
+  const size_t floor_bytes = 227 * 1024 / 2 - 2048 + 1 - g_static_rows2;
+  const size_t bytes = kv > floor_bytes ? kv : floor_bytes;
+  return launch_pdl(k_attention_rows2, dim3(n_seqs, kHeads / 2), dim3(128), bytes, st, a) == cudaSuccess ? 0 : -3;
+}
+
 static int smem_attr(const void* fn, size_t bytes) {
   return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes)) == cudaSuccess ? 0 : -1;
 }
@@ -644,7 +931,9 @@ int attention_prime() {
   r |= static_smem((const void*)k_attention_rows<128>, &g_static_rows);
   r |= static_smem((const void*)k_attention_wide<ATTN_WIDE_256>, &g_static_wide2);
   r |= static_smem((const void*)k_attention_wide<4, 1>, &g_static_wide4);
+  r |= static_smem((const void*)k_attention_rows2, &g_static_rows2);
   if (r) return r;
+  r |= smem_attr((const void*)k_attention_rows2, rows_smem_cap(g_static_rows2));
   r |= smem_attr((const void*)k_attention_rows<128>, rows_smem_cap(g_static_rows));
   r |= smem_attr((const void*)k_attention_rows<64>, rows_smem_cap(g_static_rows));
   r |= smem_attr((const void*)k_attention_rows<32>, rows_smem_cap(g_static_rows));
@@ -671,7 +960,10 @@ int launch_attention_exact(const AttnArgs& a, int n_seqs, cudaStream_t st) {
   const int cap = a.max_len <= 32 ? 32 : a.max_len <= 64 ? 64 : 128;
   const long heads = long(n_seqs) * kHeads;
   if (a.max_len > 128) return launch_rows<128>(a, n_seqs, st);
-  if (cap == 128 && heads * ((a.max_len + 127) / 128) >= 2 * 148) return launch_rows<128>(a, n_seqs, st);
+#ifndef ATTN_PAIRS
+#define ATTN_PAIRS 1
+#endif
+  if (cap == 128 && heads >= 2 * 148) return ATTN_PAIRS ? launch_rows2(a, n_seqs, st) : launch_rows<128>(a, n_seqs, st);
   if (cap >= 64 && heads * ((a.max_len + 63) / 64) >= 2 * 148) return launch_rows<64>(a, n_seqs, st);
   return launch_rows<32>(a, n_seqs, st);
 }

@@ -52,6 +52,7 @@ constexpr int BK = 128;            // K bytes per block (one 128-byte swizzle at
 constexpr int A_STAGE = BM * BK;   // 16 KB
 constexpr int kEpiWarps = 16;
 constexpr int kThreads = (2 + kEpiWarps) * 32;
+constexpr int kTmemBar = 8;  // named barrier of the MMA and epilogue warps (the epilogue uses 1..4)
 constexpr int kResK = 384;         // K of the GEMMs whose weight slice stays resident
 constexpr int kResKB = kResK / BK;
 constexpr int kGeluCluster = 6;
@@ -126,10 +127,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     fence_mbar_init();
   }
-  if (warp == 0) {
-    tmem_alloc(tmem_slot, Ly::TCOLS);
-    tmem_relinquish();
-  }
   for (int i = tid; i < BN; i += blockDim.x) {
     const int n = n0 + i;
     s_ws[i] = g.w_scale[n];
@@ -142,26 +139,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       s_beta[i] = g.beta[i];
     }
   }
-  tc_fence_before();
   __syncthreads();
   if constexpr (EPI == EPI_GELU_QUANT) {  // peers' barriers are initialised before any st.async
     cluster_arrive_release();
     cluster_wait_acquire();
   }
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
+  if constexpr (RES) {  // the weights are model constants: requested before waiting for the previous kernel
+    if (tid == 0) {
+      mbar_arrive_expect_tx(bfull, Ly::B_RES);
+      for (int kb = 0; kb < kResKB; ++kb)
+        for (int j = 0; j < BN / 64; ++j)
+          tma_load_2d(b_res + (kb * BN + j * 64) * BK, &tmB, bfull, kb * BK, n0 + j * 64);
+    }
+  }
+  pdl_wait();
+  // TMEM is allocated only after the wait: a CTA waiting for the previous kernel holds none, so that
+  // kernel's CTAs can always allocate theirs. The producer needs no TMEM and starts loading at once;
+  // the MMA warp allocates while the first stage is in flight and hands the address to the epilogue.
+  uint32_t tmem = 0;
+  if (warp >= 1) {
+    if (warp == 1) {
+      tmem_alloc(tmem_slot, Ly::TCOLS);
+      tmem_relinquish();
+    }
+    tc_fence_before();
+    named_bar(kTmemBar, kThreads - 32);
+    tc_fence_after();
+    tmem = *tmem_slot;
+  }
 
   if (warp == 0) {
     // ------------------------------------------------ TMA producer
     if (lane == 0) {
       bool ok = true;
-      if constexpr (RES) {  // the weights are model constants: loaded before waiting for the previous kernel
-        mbar_arrive_expect_tx(bfull, Ly::B_RES);
-        for (int kb = 0; kb < kResKB; ++kb)
-          for (int j = 0; j < BN / 64; ++j)
-            tma_load_2d(b_res + (kb * BN + j * 64) * BK, &tmB, bfull, kb * BK, n0 + j * 64);
-      }
-      pdl_wait();
       int kc = 0;
       for (int it = 0; it < my_tiles && ok; ++it) {
         const int m0 = (m_first + it * m_stride) * BM;
@@ -185,7 +195,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer
-    pdl_wait();
     if (lane == 0) {
       bool ok = true;
       if constexpr (RES) ok = mbar_wait(bfull, 0, g.err, DEV_ERR_TIMEOUT_MMA);
@@ -217,7 +226,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------ epilogue
-    pdl_wait();
     const int ew = warp - 2;       // 0..15
     const int Q = warp & 3;        // TMEM lane quadrant this warp may access
     const int qq = ew >> 2;        // column quarter (F32, GELU) / reduction-lane group (LN)
@@ -616,7 +624,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     cluster_arrive_release();
     cluster_wait_acquire();
   }
-  if (warp == 0) tmem_dealloc(tmem, Ly::TCOLS);
+  if (warp == 1) tmem_dealloc(tmem, Ly::TCOLS);
 }
 
 // ------------------------------------------------------------------------------------ host side

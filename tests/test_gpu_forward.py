@@ -41,6 +41,22 @@ def test_ragged_batch_matches_oracle(engine, oracle_model):
     np.testing.assert_array_equal(got, single)
 
 
+def test_query_tile_widths_agree(engine, oracle_model):
+    """Attention runs in 128-, 64- or 32-query tiles, chosen by how many (sequence, head) pairs a
+    launch has. Every width evaluates the same formulas in the same order, so an embedding is the
+    same bits whichever width its batch takes: 25 sequences (300 pairs) take 128- / 64-query tiles,
+    the same sequences alone (12 pairs) 32-query tiles."""
+    r = rng(21)
+    for lo, hi in ((97, 128), (33, 64)):
+        seqs = [synth.token_ids(int(L), r) for L in r.integers(lo, hi + 1, 25)]
+        got = engine.forward_ragged(seqs)
+        np.testing.assert_array_equal(engine.forward_ragged(seqs), got)
+        for i in (0, 11, 24):
+            np.testing.assert_array_equal(engine.forward_cls(seqs[i]), got[i])
+        cos, mx = close(got[0], oracle_model.forward_cls(seqs[0]))
+        assert cos >= COS_MIN and mx <= MAXABS_MAX, (lo, cos, mx)
+
+
 def test_fused_and_split_layernorm_paths_agree(engine, oracle_model):
     """A batch of >= 74 row tiles takes the fused LayerNorm GEMM epilogue; a single sequence takes the
     narrow-slice GEMM + LayerNorm row kernel. Both compute the same formulas in the same order, so
