@@ -89,8 +89,7 @@ __device__ __forceinline__ float ld_act(const float* p, int C, int tt, int t, in
 // Stages the head's K and V of rows [s0, s0 + L) as key pairs (k[2p][d], k[2p+1][d]), K dims in
 // score_pair's order, V dims in order (odd L: the last pair's second key is 0). A warp covers
 // 8 pairs x 4 dims per step, so the tile-transposed rows it reads are contiguous.
-__device__ __forceinline__ void stage_kv_pairs(const AttnArgs& a, int s0, int L, int h, float2* kp, float2* vp,
-                                               bool wait = true) {
+__device__ __forceinline__ void stage_kv_pairs(const AttnArgs& a, int s0, int L, int h, float2* kp, float2* vp) {
   const int pairs = (L + 1) >> 1;
   const int kc = a.k_col + 32 * h, vc = a.v_col + 32 * h;
   if (a.kv_tt && !(s0 & 1)) {
@@ -104,7 +103,7 @@ __device__ __forceinline__ void stage_kv_pairs(const AttnArgs& a, int s0, int L,
       cp_async8(kp + p * KPS + (d & 7) * 4 + (d >> 3), a.kv + tt_index(t, kc + d, a.kv_C), bytes);
       cp_async8(vp + p * KPS + d, a.kv + tt_index(t, vc + d, a.kv_C), bytes);
     }
-    if (wait) cp_async_wait_all();
+    cp_async_wait_all();
     return;
   }
   const int groups = (pairs + 7) >> 3;  // 8-pair groups
@@ -335,87 +334,103 @@ __global__ void __launch_bounds__(QT, 512 / QT) k_attention_rows(AttnArgs a) {
   if (warp == 0) tmem_dealloc(tmem_slot, cols);
 }
 
-// Scores of the key pair (2i, 2i+1) for NQ queries at once: each staged K float4 is loaded once
-// and used by every query (score_pair's operations, in its order, per query).
+// ---------------------------------------------------------------------------------------------
+// Dim-major staging: K (and V) of a head as 32 rows (dims) of RS floats, key t at column t -- the
+// tile-transposed activation layout itself, so a sequence that starts a 128-row tile arrives by
+// one bulk copy. A float4 holds one dim of four keys (a "quad"), which feeds the same packed
+// operations as the key-pair layout: lanes (x, y) are the pair (4i, 4i+1), (z, w) the pair
+// (4i+2, 4i+3).
+
+// Scores of keys 4i .. 4i+3 (kq = column 4i of dim row 0) for NQ queries, in score_pair's order:
+// each float4 loaded from shared memory feeds 2 pairs x NQ queries. grouped: the four keys form a
+// complete group (dot32x4 + hadd tree); otherwise each pair takes the hsum256 order.
 template <int NQ>
-__device__ __forceinline__ void score_pairs(const float (&q)[NQ][32], const float2* __restrict__ kp, bool grouped,
-                                            float2 (&sp)[NQ]) {
-  const float4* k4 = reinterpret_cast<const float4*>(kp);
-  float2 s8[NQ][8];
+__device__ __forceinline__ void score_quad(const float (&q)[NQ][32], const float* __restrict__ kq, int rs,
+                                           bool grouped, float2 (&sp)[NQ][2]) {
+  float2 s8[NQ][2][8];
 #pragma unroll
   for (int l = 0; l < 8; ++l) {
-    const float4 t0 = k4[2 * l];
-    const float4 t1 = k4[2 * l + 1];
+    const float4 A = *reinterpret_cast<const float4*>(kq + l * rs);
+    const float4 B = *reinterpret_cast<const float4*>(kq + (l + 8) * rs);
+    const float4 C = *reinterpret_cast<const float4*>(kq + (l + 16) * rs);
+    const float4 D = *reinterpret_cast<const float4*>(kq + (l + 24) * rs);
 #pragma unroll
     for (int u = 0; u < NQ; ++u) {
-      const float2 a = fma2(f2(q[u][8 + l], q[u][8 + l]), f2(t0.z, t0.w), mul2(f2(q[u][l], q[u][l]), f2(t0.x, t0.y)));
-      const float2 b =
-          fma2(f2(q[u][24 + l], q[u][24 + l]), f2(t1.z, t1.w), mul2(f2(q[u][16 + l], q[u][16 + l]), f2(t1.x, t1.y)));
-      s8[u][l] = add2(a, b);
+      const float2 ql = f2(q[u][l], q[u][l]), ql8 = f2(q[u][l + 8], q[u][l + 8]);
+      const float2 ql16 = f2(q[u][l + 16], q[u][l + 16]), ql24 = f2(q[u][l + 24], q[u][l + 24]);
+      s8[u][0][l] = add2(fma2(ql8, f2(B.x, B.y), mul2(ql, f2(A.x, A.y))), fma2(ql24, f2(D.x, D.y), mul2(ql16, f2(C.x, C.y))));
+      s8[u][1][l] = add2(fma2(ql8, f2(B.z, B.w), mul2(ql, f2(A.z, A.w))), fma2(ql24, f2(D.z, D.w), mul2(ql16, f2(C.z, C.w))));
     }
   }
 #pragma unroll
-  for (int u = 0; u < NQ; ++u) {
-    const float2* x = s8[u];
-    sp[u] = grouped ? add2(add2(add2(x[0], x[1]), add2(x[2], x[3])), add2(add2(x[4], x[5]), add2(x[6], x[7])))
-                    : add2(add2(add2(x[0], x[4]), add2(x[1], x[5])), add2(add2(x[2], x[6]), add2(x[3], x[7])));
-  }
+  for (int u = 0; u < NQ; ++u)
+#pragma unroll
+    for (int pr = 0; pr < 2; ++pr) {
+      const float2* x = s8[u][pr];
+      sp[u][pr] = grouped ? add2(add2(add2(x[0], x[1]), add2(x[2], x[3])), add2(add2(x[4], x[5]), add2(x[6], x[7])))
+                          : add2(add2(add2(x[0], x[4]), add2(x[1], x[5])), add2(add2(x[2], x[6]), add2(x[3], x[7])));
+    }
 }
 
-// k_attention_rows' three passes for NQ queries per thread over the same staged K / V: every
-// shared-memory load of K or V feeds NQ queries. Query u keeps its scores, then exponentials, in
-// TMEM columns tl + u * qcols .. + L - 1 of the thread's lane. q: pre-scaled by 1/sqrt(32);
-// out[u] = nullptr for a query past the sequence (which still takes part in the warp-collective
-// TMEM loads and stores).
+// k_attention_rows' three passes for NQ queries per thread over one head's dim-major K / V
+// (row stride rs): every shared-memory load of K or V feeds NQ queries. Query u keeps its scores,
+// then exponentials, in TMEM columns tl + u * qcols .. + L - 1 of the thread's lane. q: pre-scaled
+// by 1/sqrt(32); out[u] = nullptr for a query past the sequence (which still takes part in the
+// warp-collective TMEM loads and stores). Columns L .. (L + 3) & ~3 of K / V must hold finite
+// values (their lanes are computed and discarded).
 template <int NQ>
-__device__ __forceinline__ void attend_rows(const float (&q)[NQ][32], const float2* __restrict__ kp,
-                                            const float2* __restrict__ vp, int L, uint32_t tl, uint32_t qcols,
-                                            float* const (&out)[NQ]) {
+__device__ __forceinline__ void attend_rows_dm(const float (&q)[NQ][32], const float* __restrict__ kd,
+                                               const float* __restrict__ vd, int rs, int L, uint32_t tl,
+                                               uint32_t qcols, float* const (&out)[NQ]) {
   const int L4 = L & ~3, L8 = L & ~7, L16 = L & ~15;
   uint32_t r[NQ][16];
 
-  // pass 1: scores -> TMEM and their max
+  // pass 1: scores -> TMEM and their max (order-independent)
   float mx[NQ];
 #pragma unroll
   for (int u = 0; u < NQ; ++u) mx[u] = -INFINITY;
   for (int t0 = 0; t0 < L; t0 += 16) {
     if (t0 + 16 <= L4) {
-      float2 ma[NQ], mb[NQ];
 #pragma unroll
-      for (int u = 0; u < NQ; ++u) ma[u] = mb[u] = f2(-INFINITY, -INFINITY);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float2 sp[NQ];
-        score_pairs<NQ>(q, kp + ((t0 >> 1) + j) * KPS, true, sp);
+      for (int c = 0; c < 4; ++c) {
+        float2 sp[NQ][2];
+        score_quad<NQ>(q, kd + t0 + 4 * c, rs, true, sp);
 #pragma unroll
         for (int u = 0; u < NQ; ++u) {
-          if (j & 1) mb[u] = f2(fmaxf(mb[u].x, sp[u].x), fmaxf(mb[u].y, sp[u].y));
-          else ma[u] = f2(fmaxf(ma[u].x, sp[u].x), fmaxf(ma[u].y, sp[u].y));
-          r[u][2 * j] = __float_as_uint(sp[u].x);
-          r[u][2 * j + 1] = __float_as_uint(sp[u].y);
+          mx[u] = fmaxf(mx[u], fmaxf(fmaxf(sp[u][0].x, sp[u][0].y), fmaxf(sp[u][1].x, sp[u][1].y)));
+          r[u][4 * c] = __float_as_uint(sp[u][0].x);
+          r[u][4 * c + 1] = __float_as_uint(sp[u][0].y);
+          r[u][4 * c + 2] = __float_as_uint(sp[u][1].x);
+          r[u][4 * c + 3] = __float_as_uint(sp[u][1].y);
         }
       }
-#pragma unroll
-      for (int u = 0; u < NQ; ++u) mx[u] = fmaxf(mx[u], fmaxf(fmaxf(ma[u].x, ma[u].y), fmaxf(mb[u].x, mb[u].y)));
     } else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int t = t0 + 2 * j;
-        float2 sp[NQ];
+      for (int c = 0; c < 4; ++c) {
+        const int t = t0 + 4 * c;
+        float2 sp[NQ][2];
 #pragma unroll
-        for (int u = 0; u < NQ; ++u) sp[u] = f2(0.0f, 0.0f);
+        for (int u = 0; u < NQ; ++u) sp[u][0] = sp[u][1] = f2(0.0f, 0.0f);
         if (t < L) {
-          score_pairs<NQ>(q, kp + (t >> 1) * KPS, t < L4, sp);
+          score_quad<NQ>(q, kd + t, rs, t < L4, sp);
 #pragma unroll
           for (int u = 0; u < NQ; ++u) {
-            mx[u] = fmaxf(mx[u], sp[u].x);
-            if (t + 1 < L) mx[u] = fmaxf(mx[u], sp[u].y);
+            // keys past the sequence: 0, outside the max
+            if (t + 1 >= L) sp[u][0].y = 0.0f;
+            if (t + 2 >= L) sp[u][1].x = 0.0f;
+            if (t + 3 >= L) sp[u][1].y = 0.0f;
+            mx[u] = fmaxf(mx[u], sp[u][0].x);
+            if (t + 1 < L) mx[u] = fmaxf(mx[u], sp[u][0].y);
+            if (t + 2 < L) mx[u] = fmaxf(mx[u], sp[u][1].x);
+            if (t + 3 < L) mx[u] = fmaxf(mx[u], sp[u][1].y);
           }
         }
 #pragma unroll
         for (int u = 0; u < NQ; ++u) {
-          r[u][2 * j] = __float_as_uint(sp[u].x);
-          r[u][2 * j + 1] = __float_as_uint(sp[u].y);
+          r[u][4 * c] = __float_as_uint(sp[u][0].x);
+          r[u][4 * c + 1] = __float_as_uint(sp[u][0].y);
+          r[u][4 * c + 2] = __float_as_uint(sp[u][1].x);
+          r[u][4 * c + 3] = __float_as_uint(sp[u][1].y);
         }
       }
     }
@@ -502,19 +517,21 @@ __device__ __forceinline__ void attend_rows(const float (&q)[NQ][32], const floa
     tmem_ld_wait();
     if (t0 + 16 <= L) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float2 p[NQ];
+      for (int c = 0; c < 4; ++c) {
+        float2 p01[NQ], p23[NQ];
 #pragma unroll
-        for (int u = 0; u < NQ; ++u)
-          p[u] = mul2(f2(__uint_as_float(r[u][2 * j]), __uint_as_float(r[u][2 * j + 1])), f2(inv[u], inv[u]));
-        const float4* v4 = reinterpret_cast<const float4*>(vp + ((t0 >> 1) + j) * KPS);
+        for (int u = 0; u < NQ; ++u) {
+          p01[u] = mul2(f2(__uint_as_float(r[u][4 * c]), __uint_as_float(r[u][4 * c + 1])), f2(inv[u], inv[u]));
+          p23[u] = mul2(f2(__uint_as_float(r[u][4 * c + 2]), __uint_as_float(r[u][4 * c + 3])), f2(inv[u], inv[u]));
+        }
+        const float* vq = vd + t0 + 4 * c;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float4 vv = v4[i];
+        for (int d = 0; d < 32; ++d) {
+          const float4 vv = *reinterpret_cast<const float4*>(vq + d * rs);
 #pragma unroll
           for (int u = 0; u < NQ; ++u) {
-            acc[u][2 * i] = fma2(f2(vv.x, vv.y), p[u], acc[u][2 * i]);
-            acc[u][2 * i + 1] = fma2(f2(vv.z, vv.w), p[u], acc[u][2 * i + 1]);
+            acc[u][d] = fma2(f2(vv.x, vv.y), p01[u], acc[u][d]);
+            acc[u][d] = fma2(f2(vv.z, vv.w), p23[u], acc[u][d]);
           }
         }
       }
@@ -528,23 +545,18 @@ __device__ __forceinline__ void attend_rows(const float (&q)[NQ][32], const floa
 #pragma unroll
         for (int u = 0; u < NQ; ++u)
           p[u] = mul2(f2(__uint_as_float(r[u][2 * j]), __uint_as_float(r[u][2 * j + 1])), f2(inv[u], inv[u]));
-        const float4* v4 = reinterpret_cast<const float4*>(vp + (t >> 1) * KPS);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float4 vv = v4[i];
+        for (int d = 0; d < 32; ++d) {
+          const float2 vv = *reinterpret_cast<const float2*>(vd + d * rs + t);
 #pragma unroll
-          for (int u = 0; u < NQ; ++u) {
-            acc[u][2 * i] = fma2(f2(vv.x, vv.y), p[u], acc[u][2 * i]);
-            acc[u][2 * i + 1] = fma2(f2(vv.z, vv.w), p[u], acc[u][2 * i + 1]);
-          }
+          for (int u = 0; u < NQ; ++u) acc[u][d] = fma2(vv, p[u], acc[u][d]);
         }
       } else if (t < L) {  // odd L: the last key goes to the even accumulator
-        const float2* v = vp + (t >> 1) * KPS;
 #pragma unroll
         for (int u = 0; u < NQ; ++u) {
           const float pa = __uint_as_float(r[u][2 * j]) * inv[u];
 #pragma unroll
-          for (int d = 0; d < 32; ++d) acc[u][d].x = fmaf(v[d].x, pa, acc[u][d].x);
+          for (int d = 0; d < 32; ++d) acc[u][d].x = fmaf(vd[d * rs + t], pa, acc[u][d].x);
         }
       }
     }
@@ -561,40 +573,81 @@ __device__ __forceinline__ void attend_rows(const float (&q)[NQ][32], const floa
   }
 }
 
+// Stages K and V of heads 2y, 2y + 1 (64 columns each) of rows [s0, s0 + L) dim-major with row
+// stride rs (>= L rounded up to 4; columns L .. rs - 1 zero) by per-thread asynchronous copies of
+// 16 bytes (four keys; s0 a multiple of 4, tile-transposed rows) or 4 bytes, or plain loads for
+// row-major activations. Complete after cp_async_wait_all.
+__device__ __forceinline__ void stage_kv_dim_major(const AttnArgs& a, int s0, int L, int y, int rs, float* kd,
+                                                   float* vd) {
+  const int kc = a.k_col + 64 * y, vc = a.v_col + 64 * y;
+  if (a.kv_tt && !(s0 & 3)) {
+    const int quads = rs >> 2;
+    for (int i = threadIdx.x; i < 128 * quads; i += blockDim.x) {
+      const int row = i / quads, c = i - row * quads;  // row: 0-63 K dims, 64-127 V dims
+      const int t = 4 * c;
+      const int col = row < 64 ? kc + row : vc + row - 64;
+      float* dst = (row < 64 ? kd + row * rs : vd + (row - 64) * rs) + t;
+      const int valid = L - t < 4 ? (L - t > 0 ? L - t : 0) : 4;
+      cp_async16(dst, a.kv + tt_index(s0 + (valid ? t : 0), col, a.kv_C), uint32_t(valid) * 4u);
+    }
+    return;
+  }
+  for (int i = threadIdx.x; i < 128 * rs; i += blockDim.x) {
+    const int row = i / rs, t = i - row * rs;
+    const int col = row < 64 ? kc + row : vc + row - 64;
+    float* dst = (row < 64 ? kd + row * rs : vd + (row - 64) * rs) + t;
+    if (a.kv_tt) {
+      cp_async4(dst, a.kv + tt_index(s0 + (t < L ? t : 0), col, a.kv_C), t < L ? 4u : 0u);
+    } else {
+      *dst = t < L ? ld_act(a.kv, a.kv_C, 0, s0 + t, col) : 0.0f;
+    }
+  }
+}
+
 // Sequences of 65..128 keys in wide batches: one CTA per (sequence, pair of heads), 128 threads.
 // Warps 0-1 take head 2y, warps 2-3 head 2y + 1 (TMEM lanes 0-63 / 64-127); thread j of a head
 // takes queries j and j + 64, so every staged K / V load feeds two queries. The scores of query
-// j + 64 sit 128 TMEM columns after those of query j (256 columns: two CTAs per SM).
+// j + 64 sit 128 TMEM columns after those of query j (256 columns: two CTAs per SM). K / V are
+// staged dim-major: a sequence that starts a 128-row tile by two bulk copies (the 64 K columns of
+// the two heads are 32 KB in a row, as are the V columns), any other by per-thread copies.
 __global__ void __launch_bounds__(128, 2) k_attention_rows2(AttnArgs a) {
   pdl_trigger();
   pdl_wait();
   extern __shared__ float4 smem4[];
   __shared__ uint32_t tmem_slot;
+  __shared__ uint64_t kv_bar;
   const int s = blockIdx.x;
+  const int y = blockIdx.y;
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int unit = warp >> 1;
-  const int h = 2 * blockIdx.y + unit;
+  const int h = 2 * y + unit;
   const int s0 = int(a.cu[s]);
   const int L = int(a.cu[s + 1]) - s0;
   if (L <= 0 || L > a.max_len || L > 128) {
-    if (tid == 0 && blockIdx.y == 0) record_err(a.err, DEV_ERR_BAD_SHAPE);
+    if (tid == 0 && y == 0) record_err(a.err, DEV_ERR_BAD_SHAPE);
     return;
+  }
+  const bool bulk = a.kv_tt && !(s0 & 127);
+  const int rs = bulk ? 128 : (L + 3) & ~3;
+  float* kd = reinterpret_cast<float*>(smem4);  // [64][rs]: K dims of heads 2y, 2y + 1
+  float* vd = kd + 64 * rs;                     // [64][rs]: V dims
+  if (bulk) {
+    if (tid == 0) {
+      mbar_init(&kv_bar, 1);
+      fence_mbar_init();
+      mbar_arrive_expect_tx(&kv_bar, 2 * 64 * 128 * 4);
+      const float* tile = a.kv + size_t(s0 >> 7) * a.kv_C * 128;
+      bulk_load(kd, tile + size_t(a.k_col + 64 * y) * 128, 64 * 128 * 4, &kv_bar);
+      bulk_load(vd, tile + size_t(a.v_col + 64 * y) * 128, 64 * 128 * 4, &kv_bar);
+    }
+  } else {
+    stage_kv_dim_major(a, s0, L, y, rs, kd, vd);
   }
   if (warp == 0) {
     tmem_alloc(&tmem_slot, 256);
     tmem_relinquish();
   }
-  const int pairs = (L + 1) >> 1;
-  float2* kp0 = reinterpret_cast<float2*>(smem4);
-  float2* kp1 = kp0 + 2 * pairs * KPS;
-  stage_kv_pairs(a, s0, L, 2 * blockIdx.y, kp0, kp0 + pairs * KPS, false);
-  stage_kv_pairs(a, s0, L, 2 * blockIdx.y + 1, kp1, kp1 + pairs * KPS);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tl = tmem_slot + (uint32_t(warp * 32) << 16);
-  const float2* kp = unit ? kp1 : kp0;
 
   const int j = (warp & 1) * 32 + (tid & 31);
   float q[2][32];
@@ -606,7 +659,19 @@ __global__ void __launch_bounds__(128, 2) k_attention_rows2(AttnArgs a) {
     load_query(a, s0 + (active ? qi : L - 1), h, q[u]);
     out[u] = active ? a.out + size_t(s0 + qi) * kHidden + h * 32 : nullptr;
   }
-  attend_rows<2>(q, kp, kp + pairs * KPS, L, tl, 128, out);
+  bool ok = true;
+  if (bulk) {
+    __syncthreads();  // kv_bar initialised
+    ok = mbar_wait(&kv_bar, 0, a.err, DEV_ERR_TIMEOUT_PRODUCER);
+  } else {
+    cp_async_wait_all();
+  }
+  tc_fence_before();
+  ok = __syncthreads_and(ok);
+  tc_fence_after();
+  if (ok)
+    attend_rows_dm<2>(q, kd + unit * 32 * rs, vd + unit * 32 * rs, rs, L, tmem_slot + (uint32_t(warp * 32) << 16), 128,
+                      out);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem_slot, 256);
@@ -906,10 +971,10 @@ static int launch_rows(const AttnArgs& a, int n_seqs, cudaStream_t st) {
   return launch_pdl(k_attention_rows<QT>, grid, dim3(QT), rows_smem(a.max_len, g_static_rows), st, a) == cudaSuccess ? 0 : -3;
 }
 
-// k_attention_rows2: K / V pairs of two heads; at least half an SM's shared memory, so that no
+// k_attention_rows2: K / V of two heads; at least half an SM's shared memory, so that no
 // more CTAs share an SM than its TMEM holds (2 x 256 columns).
 static int launch_rows2(const AttnArgs& a, int n_seqs, cudaStream_t st) {
-  const size_t kv = size_t((a.max_len + 1) / 2) * KPS * 8 * 4;
+  const size_t kv = size_t(128) * 128 * 4;  // [64][128] K + [64][128] V (row stride <= 128)
   const size_t floor_bytes = 227 * 1024 / 2 - 2048 + 1 - g_static_rows2;
   const size_t bytes = kv > floor_bytes ? kv : floor_bytes;
   return launch_pdl(k_attention_rows2, dim3(n_seqs, kHeads / 2), dim3(128), bytes, st, a) == cudaSuccess ? 0 : -3;

@@ -185,7 +185,24 @@ __device__ __forceinline__ void cp_async8(void* smem, const void* gmem, uint32_t
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(smem_u32(smem)), "l"(gmem), "r"(src_bytes)
                : "memory");
 }
+// The same for 16 bytes (L2 only; both addresses 16-byte aligned) and for 4 bytes.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(smem)), "l"(gmem), "r"(src_bytes)
+               : "memory");
+}
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Bulk asynchronous copy of `bytes` contiguous bytes global -> this CTA's shared memory (both
+// addresses 16-byte aligned, bytes a multiple of 16), completing on `bar` (complete_tx).
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(smem_dst)), "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
 
 // Shared-memory matrix descriptor for a K-major operand in the 128-byte swizzle layout: rows of
 // 128 bytes, 8-row swizzle atoms of 1024 bytes stacked along M/N (stride byte offset 1024).

@@ -39,3 +39,21 @@ def test_attention_matches_oracle(engine, lens):
     # elements (libm expf on the CPU, a correctly rounded exp on the GPU): at most a few ulp
     np.testing.assert_allclose(got, ref, rtol=0, atol=2e-6)
     assert (got == ref).mean() > 0.99
+
+
+def test_attention_two_queries_per_thread_matches_oracle(engine):
+    """25 sequences of 65..128 keys (300 (sequence, head) pairs) take the kernel whose threads hold
+    two queries each, with K / V staged dim-major; odd lengths and partial 16-key chunks included."""
+    r = rng(65)
+    lens = [128, 65, 127, 97, 100] + list(r.integers(65, 129, 20))
+    T = sum(lens)
+    qkv = r.normal(0, 1, (T, 1152)).astype(np.float32)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.uint32)
+    ctx = torch.zeros(T, 384, dtype=torch.float32, device="cuda")
+    engine.attention_f32(torch.from_numpy(qkv).cuda(), torch.from_numpy(cu.astype(np.int32)).cuda(), len(lens),
+                         max(lens), ctx)
+    engine.sync()
+    got = ctx.cpu().numpy()
+    ref = ref_attention(qkv, cu)
+    np.testing.assert_allclose(got, ref, rtol=0, atol=2e-6)
+    assert (got == ref).mean() > 0.99
