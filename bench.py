@@ -52,7 +52,7 @@ def attn_flops_per_seq(L: int) -> float:
 
 
 # ncu summaries (committed under profiles/) with the measured DRAM bytes per launch of a kernel kind
-NCU_TRAFFIC = {"attention": "k_attention_rows128_config3_ncu.md"}
+NCU_TRAFFIC = {"attention": "k_attention_rows2_config3_ncu.md"}
 
 
 def ncu_traffic(kind: str):
