@@ -608,8 +608,9 @@ __device__ __forceinline__ void stage_kv_dim_major(const AttnArgs& a, int s0, in
 // Warps 0-1 take head 2y, warps 2-3 head 2y + 1 (TMEM lanes 0-63 / 64-127); thread j of a head
 // takes queries j and j + 64, so every staged K / V load feeds two queries. The scores of query
 // j + 64 sit 128 TMEM columns after those of query j (256 columns: two CTAs per SM). K / V are
-// staged dim-major: a sequence that starts a 128-row tile by two bulk copies (the 64 K columns of
-// the two heads are 32 KB in a row, as are the V columns), any other by per-thread copies.
+// staged dim-major: a sequence that starts a 128-row tile by bulk copies (the 64 K columns of the
+// two heads are 32 KB in a row, as are the V columns and the Q columns), any other by per-thread
+// copies.
 __global__ void __launch_bounds__(128, 2) k_attention_rows2(AttnArgs a) {
   pdl_trigger();
   pdl_wait();
@@ -632,14 +633,17 @@ __global__ void __launch_bounds__(128, 2) k_attention_rows2(AttnArgs a) {
   const int rs = bulk ? 128 : (L + 3) & ~3;
   float* kd = reinterpret_cast<float*>(smem4);  // [64][rs]: K dims of heads 2y, 2y + 1
   float* vd = kd + 64 * rs;                     // [64][rs]: V dims
+  float* qd = vd + 64 * rs;                     // [64][128]: Q dims (bulk staging only)
+  const bool bulk_q = bulk && a.q_tt && a.q == a.kv && a.q_C == a.kv_C;
   if (bulk) {
     if (tid == 0) {
       mbar_init(&kv_bar, 1);
       fence_mbar_init();
-      mbar_arrive_expect_tx(&kv_bar, 2 * 64 * 128 * 4);
+      mbar_arrive_expect_tx(&kv_bar, (bulk_q ? 3 : 2) * 64 * 128 * 4);
       const float* tile = a.kv + size_t(s0 >> 7) * a.kv_C * 128;
       bulk_load(kd, tile + size_t(a.k_col + 64 * y) * 128, 64 * 128 * 4, &kv_bar);
       bulk_load(vd, tile + size_t(a.v_col + 64 * y) * 128, 64 * 128 * 4, &kv_bar);
+      if (bulk_q) bulk_load(qd, tile + size_t(a.q_col + 64 * y) * 128, 64 * 128 * 4, &kv_bar);
     }
   } else {
     stage_kv_dim_major(a, s0, L, y, rs, kd, vd);
@@ -656,7 +660,7 @@ __global__ void __launch_bounds__(128, 2) k_attention_rows2(AttnArgs a) {
   for (int u = 0; u < 2; ++u) {
     const int qi = j + 64 * u;
     const bool active = qi < L;
-    load_query(a, s0 + (active ? qi : L - 1), h, q[u]);
+    if (!bulk_q) load_query(a, s0 + (active ? qi : L - 1), h, q[u]);
     out[u] = active ? a.out + size_t(s0 + qi) * kHidden + h * 32 : nullptr;
   }
   bool ok = true;
@@ -669,6 +673,15 @@ __global__ void __launch_bounds__(128, 2) k_attention_rows2(AttnArgs a) {
   tc_fence_before();
   ok = __syncthreads_and(ok);
   tc_fence_after();
+  if (ok && bulk_q) {  // query qi of head h: column qi of dim rows 32 unit .. 32 unit + 31
+    const float scale = 1.0f / sqrtf(32.0f);
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int qi = j + 64 * u < L ? j + 64 * u : L - 1;
+#pragma unroll
+      for (int d = 0; d < 32; ++d) q[u][d] = qd[(unit * 32 + d) * 128 + qi] * scale;
+    }
+  }
   if (ok)
     attend_rows_dm<2>(q, kd + unit * 32 * rs, vd + unit * 32 * rs, rs, L, tmem_slot + (uint32_t(warp * 32) << 16), 128,
                       out);
@@ -974,7 +987,7 @@ static int launch_rows(const AttnArgs& a, int n_seqs, cudaStream_t st) {
 // k_attention_rows2: K / V of two heads; at least half an SM's shared memory, so that no
 // more CTAs share an SM than its TMEM holds (2 x 256 columns).
 static int launch_rows2(const AttnArgs& a, int n_seqs, cudaStream_t st) {
-  const size_t kv = size_t(128) * 128 * 4;  // [64][128] K + [64][128] V (row stride <= 128)
+  const size_t kv = size_t(3) * 64 * 128 * 4;  // [64][128] K, V and Q (row stride <= 128)
   const size_t floor_bytes = 227 * 1024 / 2 - 2048 + 1 - g_static_rows2;
   const size_t bytes = kv > floor_bytes ? kv : floor_bytes;
   return launch_pdl(k_attention_rows2, dim3(n_seqs, kHeads / 2), dim3(128), bytes, st, a) == cudaSuccess ? 0 : -3;
