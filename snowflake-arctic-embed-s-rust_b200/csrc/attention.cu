@@ -690,6 +690,157 @@ __global__ void __launch_bounds__(128, 2) k_attention_rows2(AttnArgs a) {
   if (warp == 0) tmem_dealloc(tmem_slot, 256);
 }
 
+// QKV projection + attention of one sequence of at most 128 keys and one pair of heads (2y, 2y + 1):
+// one CTA, 128 threads, two CTAs per SM.
+//   1. thread 0 loads the 192 weight rows of the pair (Q, K, V rows 64y .. 64y + 63 of each of the
+//      three 384-row blocks of the [1152, 384] QKV weights; k-blocks 0 and 1 before the dependency
+//      wait, they are model constants) and the sequence's 128-row activation tile (rows s0 ..
+//      s0 + 127, whatever sequences they hold beyond s0 + L), then issues the 128 x 192 x 384
+//      tcgen05 kind::i8 MMA into TMEM columns 0 .. 191;
+//   2. warp w dequantizes rows 32w .. 32w + 31 (its TMEM lanes) as the QKV GEMM's plain epilogue
+//      does, h = fma(float(acc), a_scale * w_scale, bias), into shared memory, dim-major: column n of
+//      the 192 at row n of a [192][128] array, so that Q, K and V of the pair are the [64][128]
+//      blocks k_attention_rows2 stages by bulk copies (rows past the sequence: a_scale 0, h = bias);
+//   3. k_attention_rows2's attention on those blocks, the scores in the same TMEM columns.
+// Shared memory: A (3 k-blocks x 16 KB) and a 2-stage ring of weight k-blocks (24 KB each): 96 KB,
+// which the dequantized [192][128] fp32 block reuses once the MMA has completed.
+constexpr int kQaStageA = 128 * 128;                 // one k-block of the activation tile
+constexpr int kQaStageW = 192 * 128;                 // one k-block of the pair's weight rows
+constexpr int kQaAlias = 3 * kQaStageA + 2 * kQaStageW;  // 96 KB
+static_assert(kQaAlias == 192 * 128 * 4, "the dequantized block reuses exactly the MMA operands' memory");
+constexpr size_t kQaSmem = 1024 + kQaAlias + 2 * 192 * 4 + 8 * 8;
+
+__global__ void __launch_bounds__(128, 2)
+    k_qkv_attention(const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_w,
+                    QkvAttnArgs qa) {
+  pdl_trigger();
+  extern __shared__ uint8_t qa_raw[];
+  __shared__ uint32_t tmem_slot;
+  // 1024-byte aligned (128-byte swizzle atoms) by pointer arithmetic on the shared array itself, so
+  // that the compiler keeps every access below in the shared address space
+  uint8_t* sm = qa_raw + ((1024u - (smem_u32(qa_raw) & 1023u)) & 1023u);
+  uint8_t* sa = sm;                                   // A: k-block kb at kb * 16 KB
+  uint8_t* sw = sm + 3 * kQaStageA;                   // weight ring: stage st at st * 24 KB
+  float* dm = reinterpret_cast<float*>(sm);           // after the MMA: [192][128] Q | K | V, dim-major
+  float* s_ws = reinterpret_cast<float*>(sm + kQaAlias);
+  float* s_bias = s_ws + 192;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(s_bias + 192);
+  uint64_t* w_full = bars;       // [2] weight stage loaded
+  uint64_t* a_full = bars + 2;   // activation tile loaded
+  uint64_t* w_free = bars + 3;   // stage 0 read by the MMAs of k-block 0
+  uint64_t* acc_full = bars + 4; // accumulator complete
+  const AttnArgs& a = qa.a;
+  const int s = blockIdx.x;
+  const int y = blockIdx.y;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  for (int i = tid; i < 192; i += 128) {  // column i of the pair = column gc of the QKV output
+    const int gc = (i >> 6) * kHidden + 64 * y + (i & 63);
+    s_ws[i] = qa.w_scale[gc];
+    s_bias[i] = qa.bias[gc];
+  }
+  if (tid == 0) {
+    tma_prefetch_desc(&tm_act);
+    tma_prefetch_desc(&tm_w);
+    for (int i = 0; i < 5; ++i) mbar_init(&bars[i], 1);
+    fence_mbar_init();
+    for (int kb = 0; kb < 2; ++kb) {
+      mbar_arrive_expect_tx(&w_full[kb], kQaStageW);
+      for (int p = 0; p < 3; ++p)
+        tma_load_2d(sw + kb * kQaStageW + p * 64 * 128, &tm_w, &w_full[kb], kb * 128, p * kHidden + 64 * y);
+    }
+  }
+  pdl_wait();
+  const int s0 = int(a.cu[s]);
+  const int L = int(a.cu[s + 1]) - s0;
+  const bool shape_ok = L > 0 && L <= a.max_len && L <= 128;
+  if (!shape_ok && tid == 0 && y == 0) record_err(a.err, DEV_ERR_BAD_SHAPE);
+  if (tid == 0 && shape_ok) {
+    mbar_arrive_expect_tx(a_full, 3 * kQaStageA);
+    for (int kb = 0; kb < 3; ++kb) tma_load_2d(sa + kb * kQaStageA, &tm_act, a_full, kb * 128, s0);
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, 256);
+    tmem_relinquish();
+  }
+  const float as = (shape_ok && tid < L) ? qa.a_scale[s0 + tid] : 0.0f;  // requested while the MMA runs
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  if (tid == 0) {
+    if (shape_ok) {
+      constexpr uint32_t idesc = idesc_i8(128, 192);
+      bool good = mbar_wait(a_full, 0, a.err, DEV_ERR_TIMEOUT_PRODUCER);
+      for (int kb = 0; kb < 3 && good; ++kb) {
+        const int st = kb & 1;
+        if (kb == 2) {  // k-block 2 reuses stage 0 once the MMAs of k-block 0 have read it
+          if (!(good = mbar_wait(w_free, 0, a.err, DEV_ERR_TIMEOUT_MMA))) break;
+          mbar_arrive_expect_tx(&w_full[0], kQaStageW);
+          for (int p = 0; p < 3; ++p) tma_load_2d(sw + p * 64 * 128, &tm_w, &w_full[0], 2 * 128, p * kHidden + 64 * y);
+        }
+        if (!(good = mbar_wait(&w_full[st], kb >> 1, a.err, DEV_ERR_TIMEOUT_MMA))) break;
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(sa + kb * kQaStageA);
+        const uint32_t b_addr = smem_u32(sw + st * kQaStageW);
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          mma_i8(tmem, sdesc_sw128(a_addr + ks * 32), sdesc_sw128(b_addr + ks * 32), idesc, (kb | ks) != 0);
+        if (kb == 0) mma_commit(w_free);
+      }
+      if (good) mma_commit(acc_full);
+    } else {  // no MMA: the weight copies in flight complete before the CTA exits
+      mbar_wait(&w_full[0], 0, a.err, DEV_ERR_TIMEOUT_PRODUCER);
+      mbar_wait(&w_full[1], 0, a.err, DEV_ERR_TIMEOUT_PRODUCER);
+    }
+  }
+  bool ok = shape_ok && mbar_wait(acc_full, 0, a.err, DEV_ERR_TIMEOUT_EPILOGUE);
+  ok = __all_sync(0xffffffffu, ok);  // the TMEM loads below are warp-collective
+  tc_fence_after();
+  fence_proxy_async();  // the MMAs' reads of A and the weights precede the writes that reuse that memory
+  if (ok && warp * 32 < ((L + 3) & ~3)) {  // rows the attention reads: keys 0 .. L rounded up to 4
+    const uint32_t tl = tmem + (uint32_t(warp * 32) << 16);
+    for (int c0 = 0; c0 < 192; c0 += 32) {
+      uint32_t r[32];
+      tmem_ld16(tl + c0, r);
+      tmem_ld16(tl + c0 + 16, r + 16);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int n = c0 + j;
+        dm[n * 128 + tid] = fmaf(float(int(r[j])), as * s_ws[n], s_bias[n]);
+      }
+    }
+  }
+  tc_fence_before();
+  ok = __syncthreads_and(ok);
+  tc_fence_after();
+
+  const int unit = warp >> 1;  // warps 0-1: head 2y, warps 2-3: head 2y + 1
+  const int h = 2 * y + unit;
+  const int j = (warp & 1) * 32 + (tid & 31);
+  if (ok) {
+    const float scale = 1.0f / sqrtf(32.0f);
+    float q[2][32];
+    float* out[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int qi = j + 64 * u;
+      const bool active = qi < L;
+      const int qc = active ? qi : L - 1;
+#pragma unroll
+      for (int d = 0; d < 32; ++d) q[u][d] = dm[(unit * 32 + d) * 128 + qc] * scale;
+      out[u] = active ? a.out + size_t(s0 + qi) * kHidden + h * 32 : nullptr;
+    }
+    attend_rows_dm<2>(q, dm + (64 + unit * 32) * 128, dm + (128 + unit * 32) * 128, 128, L,
+                      tmem + (uint32_t(warp * 32) << 16), 128, out);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
 // NWG warpgroups per 128-query tile: warps w, w + 4, ... share TMEM lane quadrant w & 3 (the same
 // queries). Scores and exponentials: group g takes keys t0 + g KPG .. t0 + (g + 1) KPG - 1 of
 // every 16-key chunk (KPG = 16 / NWG), so each of the reference's 16 sum slots is summed in order
@@ -1018,7 +1169,17 @@ int attention_prime() {
   r |= smem_attr((const void*)k_attention_wide<ATTN_WIDE_256>, rows_smem_cap(g_static_wide2));
   r |= smem_attr((const void*)k_attention_wide<4, 1>, rows_smem_cap(g_static_wide4));
   r |= smem_attr((const void*)k_attention_cls, 4 * kClsWarpFloats * 4);
+  r |= smem_attr((const void*)k_qkv_attention, kQaSmem);
   return r;
+}
+
+int launch_qkv_attention(const CUtensorMap& tm_act, const CUtensorMap& tm_w, const QkvAttnArgs& a, int n_seqs,
+                         cudaStream_t st) {
+  if (n_seqs <= 0) return 0;
+  if (a.a.max_len <= 0 || a.a.max_len > 128) return -1;
+  return launch_pdl(k_qkv_attention, dim3(n_seqs, kHeads / 2), dim3(128), kQaSmem, st, tm_act, tm_w, a) == cudaSuccess
+             ? 0
+             : -3;
 }
 
 int launch_attention_exact(const AttnArgs& a, int n_seqs, cudaStream_t st) {

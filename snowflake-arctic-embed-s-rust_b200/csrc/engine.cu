@@ -117,6 +117,7 @@ struct ae_ctx {
   std::map<uint32_t, Graph> graphs;  // forward_cls graph per sequence length
   std::string err;
   int gelu_erf = 0;       // ARCTIC_GELU=erf selects the exact-erf GELU (outside the parity tolerance)
+  int fused_qkv = 0;      // ARCTIC_FUSED_QKV=1: QKV projection fused into the attention (sequences <= 128 keys)
   bool prof = false;      // record CUDA events around every launch (ae_profile)
   int prof_kind = 0;      // kind of the launches being enqueued
   std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> prof_events;
@@ -499,17 +500,38 @@ int enqueue_forward(ae_ctx* c, const uint16_t* d_ids, const uint32_t* d_cu, int 
     if (launch_embed(e, st)) return fail(c, AE_ERR_CUDA, "embedding launch failed");
   }
 
+  // QKV projection fused with the attention (sequences of at most 128 keys) only on request
+  // (ARCTIC_FUSED_QKV=1): measured on config 3 it is 2 % slower than the QKV GEMM + attention
+  // kernels (its load / MMA / dequantization prologue runs while the SM's FP32 pipes idle) and
+  // 8 % slower for single sequences; by default a QKV GEMM writes the projections to global memory
+  // for the attention kernels of every length class.
+  const bool fused = max_len <= 128 && c->fused_qkv == 1;
   for (int l = 0; l + 1 < kLayers; ++l) {
     const DevLayer& Ly = M.layers[l];
-    {
-      ProfScope ps(c, AE_KERNEL_QKV);
-      AE_TRY(gemm(c, EPI_F32, W.tm_act_q, Ly.qkv, T, W.act_s, nullptr, 0, nullptr, nullptr, nullptr, W.qkv, 3 * kHidden,
-                  nullptr, nullptr, 1));
-    }
-    {
+    if (fused) {
       ProfScope ps(c, AE_KERNEL_ATTENTION);
-      AE_TRY(attention(c, W.qkv, 3 * kHidden, 0, 1, W.qkv, 3 * kHidden, kHidden, 2 * kHidden, 1, W.ctx, d_cu, n,
-                       max_len, 0, segs));
+      QkvAttnArgs qa{};
+      qa.a.out = W.ctx;
+      qa.a.cu = d_cu;
+      qa.a.max_len = max_len;
+      qa.a.err = c->d_err;
+      qa.a_scale = W.act_s;
+      qa.w_scale = Ly.qkv.ws;
+      qa.bias = Ly.qkv.bias;
+      ++c->launches;
+      if (launch_qkv_attention(W.tm_act_q, Ly.qkv.tmap, qa, n, st))
+        return fail(c, AE_ERR_CUDA, "fused QKV + attention launch failed");
+    } else {
+      {
+        ProfScope ps(c, AE_KERNEL_QKV);
+        AE_TRY(gemm(c, EPI_F32, W.tm_act_q, Ly.qkv, T, W.act_s, nullptr, 0, nullptr, nullptr, nullptr, W.qkv,
+                    3 * kHidden, nullptr, nullptr, 1));
+      }
+      {
+        ProfScope ps(c, AE_KERNEL_ATTENTION);
+        AE_TRY(attention(c, W.qkv, 3 * kHidden, 0, 1, W.qkv, 3 * kHidden, kHidden, 2 * kHidden, 1, W.ctx, d_cu, n,
+                         max_len, 0, segs));
+      }
     }
     ++c->launches;
     {
@@ -792,6 +814,8 @@ int ae_ctx_create(int device, ae_ctx** out) {
   c->stream = c->own_stream;
   const char* gm = std::getenv("ARCTIC_GELU");
   c->gelu_erf = (gm && std::strcmp(gm, "erf") == 0) ? 1 : 0;
+  const char* fq = std::getenv("ARCTIC_FUSED_QKV");
+  c->fused_qkv = (fq && std::strcmp(fq, "1") == 0) ? 1 : 0;
   if (gemm_i8_prime() || attention_prime()) {
     ae_ctx_destroy(c);
     return fail(nullptr, AE_ERR_CUDA, "kernel attribute setup failed on device %d", device);

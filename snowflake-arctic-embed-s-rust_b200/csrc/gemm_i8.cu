@@ -83,7 +83,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   using Ly = Layout<BN, EPI, RES, STAGES>;
   constexpr int NB = Ly::NB;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned (128-byte swizzle atoms) by pointer arithmetic on the shared array itself, so
+  // that the compiler keeps the parameter and exchange accesses in the shared address space
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* b_res = smem;
   uint8_t* ring = smem + Ly::B_RES;
   float* s_ws = reinterpret_cast<float*>(ring + Ly::RING);
@@ -293,48 +295,55 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else if constexpr (EPI == EPI_GELU_QUANT) {
+        // 16 columns at a time: accumulators -> g = GELU(h) * inv_smooth -> back into the same TMEM
+        // columns (few registers live, no spills); the accumulator buffer is released after the
+        // quantization pass has read g back
         constexpr int CW = BN / 4;  // 64
         const int c0 = qq * CW;
         const int par = it & 1;
         const uint32_t rank = cluster_ctarank();
         float* xg = xch + par * 4 * BM;                           // [4][BM] maxima of the column quarters
         float* rmx = xch + 2 * 4 * BM + par * kGeluCluster * BM;  // [6][BM] maxima of the cluster CTAs
-        uint32_t r[CW];
-        if (ok) {
-#pragma unroll
-          for (int ch = 0; ch < CW / 16; ++ch) tmem_ld16(tb + c0 + ch * 16, r + ch * 16);
-          tmem_ld_wait();
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[b]);
-        if (valid && g.acc_dbg) {
-          int4* ad = reinterpret_cast<int4*>(g.acc_dbg + size_t(row) * g.N + n0 + c0);
-#pragma unroll
-          for (int q = 0; q < CW / 4; ++q)
-            ad[q] = make_int4(int(r[4 * q]), int(r[4 * q + 1]), int(r[4 * q + 2]), int(r[4 * q + 3]));
-        }
+        uint32_t r[16];
         float vmax = 1e-8f;
-        if (g.gelu_erf) {
+        if (ok) {
+#pragma unroll 1
+          for (int ch = 0; ch < CW / 16; ++ch) {
+            const int cc = c0 + 16 * ch;
+            tmem_ld16(tb + cc, r);
+            tmem_ld_wait();
+            if (valid && g.acc_dbg) {
+              int4* ad = reinterpret_cast<int4*>(g.acc_dbg + size_t(row) * g.N + n0 + cc);
 #pragma unroll
-          for (int j = 0; j < CW; ++j) {
-            const int c = c0 + j;
-            const float gv = gelu_erf(fmaf(float(int(r[j])), as * s_ws[c], s_bias[c])) * s_invs[c];
-            vmax = fmaxf(vmax, fabsf(gv));
-            r[j] = __float_as_uint(gv);
-          }
-        } else {
+              for (int q = 0; q < 4; ++q)
+                ad[q] = make_int4(int(r[4 * q]), int(r[4 * q + 1]), int(r[4 * q + 2]), int(r[4 * q + 3]));
+            }
+            if (g.gelu_erf) {
 #pragma unroll
-          for (int j = 0; j < CW; j += 2) {
-            const int c = c0 + j;
-            const float2 h = __ffma2_rn(make_float2(float(int(r[j])), float(int(r[j + 1]))),
-                                        __fmul2_rn(make_float2(as, as), make_float2(s_ws[c], s_ws[c + 1])),
-                                        make_float2(s_bias[c], s_bias[c + 1]));
-            const float2 gv = __fmul2_rn(gelu_ref2(h), make_float2(s_invs[c], s_invs[c + 1]));
-            vmax = fmaxf(vmax, fmaxf(fabsf(gv.x), fabsf(gv.y)));
-            r[j] = __float_as_uint(gv.x);
-            r[j + 1] = __float_as_uint(gv.y);
+              for (int j = 0; j < 16; ++j) {
+                const int c = cc + j;
+                const float gv = gelu_erf(fmaf(float(int(r[j])), as * s_ws[c], s_bias[c])) * s_invs[c];
+                vmax = fmaxf(vmax, fabsf(gv));
+                r[j] = __float_as_uint(gv);
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; j += 2) {
+                const int c = cc + j;
+                const float2 ws2 = *reinterpret_cast<const float2*>(s_ws + c);
+                const float2 b2 = *reinterpret_cast<const float2*>(s_bias + c);
+                const float2 iv2 = *reinterpret_cast<const float2*>(s_invs + c);
+                const float2 h = __ffma2_rn(make_float2(float(int(r[j])), float(int(r[j + 1]))),
+                                            __fmul2_rn(make_float2(as, as), ws2), b2);
+                const float2 gv = __fmul2_rn(gelu_ref2(h), iv2);
+                vmax = fmaxf(vmax, fmaxf(fabsf(gv.x), fabsf(gv.y)));
+                r[j] = __float_as_uint(gv.x);
+                r[j + 1] = __float_as_uint(gv.y);
+              }
+            }
+            tmem_st16(tb + cc, r);
           }
+          tmem_st_wait();
         }
         xg[qq * BM + rt] = vmax;
         named_bar(1 + Q, 128);
@@ -354,17 +363,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           // quantize into this warp's staging slot (32 rows x 64 bytes, rows padded to 80 bytes),
           // then write 8 rows x 64 contiguous bytes per store instruction
           uint8_t* stg = reinterpret_cast<uint8_t*>(xch + Ly::XCH_FLOATS_GELU) + ew * (32 * 80);
-          uint32_t pk[CW / 4];
+          if (ok) {
+#pragma unroll 1
+            for (int ch = 0; ch < CW / 16; ++ch) {
+              tmem_ld16(tb + c0 + 16 * ch, r);
+              tmem_ld_wait();
+              uint32_t pk[4];
 #pragma unroll
-          for (int q = 0; q < CW / 4; ++q)
-            pk[q] = pack_i8x4(quant_bits_scaled(__uint_as_float(r[4 * q]) * inv_scale),
-                              quant_bits_scaled(__uint_as_float(r[4 * q + 1]) * inv_scale),
-                              quant_bits_scaled(__uint_as_float(r[4 * q + 2]) * inv_scale),
-                              quant_bits_scaled(__uint_as_float(r[4 * q + 3]) * inv_scale));
-#pragma unroll
-          for (int q = 0; q < CW / 16; ++q)
-            *reinterpret_cast<uint4*>(stg + lane * 80 + 16 * q) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+              for (int q = 0; q < 4; ++q)
+                pk[q] = pack_i8x4(quant_bits_scaled(__uint_as_float(r[4 * q]) * inv_scale),
+                                  quant_bits_scaled(__uint_as_float(r[4 * q + 1]) * inv_scale),
+                                  quant_bits_scaled(__uint_as_float(r[4 * q + 2]) * inv_scale),
+                                  quant_bits_scaled(__uint_as_float(r[4 * q + 3]) * inv_scale));
+              *reinterpret_cast<uint4*>(stg + lane * 80 + 16 * ch) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            }
+          }
+          tc_fence_before();
           __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[b]);
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int rr = 8 * i + (lane >> 2), q = lane & 3;

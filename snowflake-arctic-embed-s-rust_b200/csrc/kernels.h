@@ -1,5 +1,6 @@
 // Launch interfaces of the row, metadata and attention kernels (rowops.cu, attention.cu).
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -80,5 +81,21 @@ struct AttnSegment {
 constexpr int kAttnClasses = 5;
 inline int attn_class(int len) { return len <= 32 ? 0 : len <= 64 ? 1 : len <= 128 ? 2 : len <= 256 ? 3 : 4; }
 int launch_attention_exact(const AttnArgs& a, int n_seqs, cudaStream_t st);
+
+// QKV projection fused with the attention (sequences of at most 128 keys): the int8 GEMM
+// fma(float(acc), a_scale[row] * w_scale[n], bias[n]) of one sequence's 128-row tile against the
+// Q, K and V weight rows of two heads (tcgen05 kind::i8, the same arithmetic as the QKV GEMM's plain
+// epilogue), dequantized straight into shared memory, then k_attention_rows2's attention. The
+// projection never goes to global memory.
+struct QkvAttnArgs {
+  AttnArgs a;               // out, cu, max_len (<= 128), err; the q / kv fields are unused
+  const float* a_scale;     // [rows] row scales of the int8 activations
+  const float* w_scale;     // [1152] per-output-channel scales of the QKV weights
+  const float* bias;        // [1152]
+};
+// tm_act: the [rows, 384] int8 activations (128-row boxes); tm_w: the [1152, 384] int8 QKV weights
+// (64-row boxes).
+int launch_qkv_attention(const CUtensorMap& tm_act, const CUtensorMap& tm_w, const QkvAttnArgs& a, int n_seqs,
+                         cudaStream_t st);
 
 }  // namespace ae

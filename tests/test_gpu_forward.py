@@ -192,3 +192,31 @@ def test_bounded_wait_reports_error(engine):
     ids = synth.token_ids(20, rng(12))
     np.testing.assert_array_equal(engine.forward_cls(ids), engine.forward_cls(ids))
     engine.sync()
+
+
+def test_fused_qkv_attention_matches_split(pack_path, oracle_model, monkeypatch):
+    """The QKV projection fused into the attention kernel (sequences of at most 128 keys) computes the
+    QKV GEMM's dequantization and the attention in the same order as the split path (GEMM to global
+    memory, then the attention kernels), so every embedding is the same bits. ARCTIC_FUSED_QKV forces
+    either path at context creation; sequences start at unaligned rows and run past tile ends."""
+    r = rng(31)
+    batches = [[synth.token_ids(128, r) for _ in range(30)],
+               [synth.token_ids(int(L), r) for L in r.integers(1, 129, 40)],
+               [synth.token_ids(L, r) for L in (1, 2, 3, 4, 5, 31, 32, 33, 63, 64, 65, 127, 128)]]
+    engines = {}
+    for mode in ("0", "1"):
+        monkeypatch.setenv("ARCTIC_FUSED_QKV", mode)
+        engines[mode] = Engine(0).load_file(pack_path)
+    monkeypatch.delenv("ARCTIC_FUSED_QKV")
+    for seqs in batches:
+        split = engines["0"].forward_ragged(seqs)
+        fused = engines["1"].forward_ragged(seqs)
+        np.testing.assert_array_equal(fused, split)
+    for L in (1, 17, 64, 100, 128):
+        ids = synth.token_ids(L, rng(300 + L))
+        got = engines["1"].forward_cls(ids)
+        np.testing.assert_array_equal(got, engines["0"].forward_cls(ids))
+        cos, mx = close(got, oracle_model.forward_cls(ids))
+        assert cos >= COS_MIN and mx <= MAXABS_MAX, (L, cos, mx)
+    for e in engines.values():
+        e.close()
