@@ -236,13 +236,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int it = 0; it < my_tiles; ++it) {
       const int b = it % NB, u = it / NB;
+      const int m0 = (m_first + it * m_stride) * BM;
+      const int row = m0 + rt;
+      // inputs that do not depend on the accumulator are requested while the MMA runs: the row
+      // scale (not in the GELU epilogue, whose registers are the tighter) and, in the LayerNorm
+      // epilogue, the first 16 residual values of the row
+      float as_pre = 0.0f;
+      if constexpr (EPI != EPI_GELU_QUANT) as_pre = row < g.M ? g.a_scale[row] : 0.0f;
+      [[maybe_unused]] float rv0[16];
+      if constexpr (EPI == EPI_LN_QUANT) {
+        if (row < g.M) {
+          const float* rr = g.res_tt ? g.res + tt_index(row, 0, g.ldr) : g.res + size_t(row) * g.ldr;
+          const size_t rs = g.res_tt ? 128 : 1;
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) rv0[4 * k + e] = rr[size_t(16 * k + 4 * qq + e) * rs];
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) rv0[i] = 0.0f;
+        }
+      }
       if (ok) ok = mbar_wait(&acc_full[b], u & 1, g.err, DEV_ERR_TIMEOUT_EPILOGUE);
       ok = __all_sync(0xffffffffu, ok);
       tc_fence_after();
-      const int m0 = (m_first + it * m_stride) * BM;
-      const int row = m0 + rt;
       const bool valid = ok && row < g.M;
-      const float as = valid ? g.a_scale[row] : 0.0f;
+      const float as = !valid ? 0.0f : (EPI == EPI_GELU_QUANT ? g.a_scale[row] : as_pre);
       const uint32_t tb = tq + uint32_t(b * BN);
 
       if constexpr (EPI == EPI_F32) {
@@ -407,13 +426,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           rstep = g.res_tt ? 128 : 1;
         }
         if (ok) {
-          for (int k0 = 0; k0 < 24; k0 += 4) {
-            float rv[16];
+          // residual chunks double-buffered: chunk i + 1 (16 values) is requested before chunk i is
+          // used; chunk 0 was requested before the accumulator wait
+          float rv1[16];
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
+          for (int i = 0; i < 6; ++i) {
+            const int k0 = 4 * i;
+            float* rv = (i & 1) ? rv1 : rv0;
+            float* nx = (i & 1) ? rv0 : rv1;
+            if (i + 1 < 6) {
 #pragma unroll
-              for (int e = 0; e < 4; ++e)
-                rv[4 * k + e] = valid ? res_row[size_t(16 * (k0 + k) + cq + e) * rstep] : 0.0f;
+              for (int k = 0; k < 4; ++k)
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  nx[4 * k + e] = valid ? res_row[size_t(16 * (k0 + 4 + k) + cq + e) * rstep] : 0.0f;
+            }
 #pragma unroll
             for (int k = 0; k < 4; ++k) tmem_ld4(tb + 16 * (k0 + k) + cq, r + 4 * k);
             tmem_ld_wait();
