@@ -19,8 +19,9 @@
 // k_attention_wide: the same with two or four warpgroups on one tile's TMEM lanes, for sequences
 // of more than 128 keys (whose score columns leave room for only 1-2 CTAs per SM).
 //
-// k_attention_cls: one warp per (sequence, head) for the single [CLS] query of layer 11: lanes
-// split the keys for the scores, 16 lanes run the 16 exp-sum chains, lane d accumulates dim d.
+// k_attention_cls: one CTA per (sequence, head) for the single [CLS] query of layer 11: threads
+// split the keys for the scores (all K / V loads of a thread in flight at once), 16 lanes run the
+// 16 exp-sum chains, 64 threads the even / odd weighted-sum accumulators of the 32 dims.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -1022,81 +1023,94 @@ __global__ void __launch_bounds__(128 * NWG, MINB) k_attention_wide(AttnArgs a) 
   if (warp == 0) tmem_dealloc(tmem_slot, cols);
 }
 
-// One warp per (sequence, head): the single [CLS] query (row s of q / out) over the sequence's keys.
-// Shared memory per warp: the scores / exponentials (512 floats) and a 32-key x 32-dim V chunk.
-constexpr int kClsWarpFloats = kMaxPos + 32 * 33;
+// One CTA (128 threads) per (sequence, head): the single [CLS] query (row s of q / out) over the
+// sequence's keys. Thread t takes keys t, t + 128, ...: it loads each key's K and V row (the 32 dims
+// of a key are 32 coalesced loads across the CTA's threads in the tile-transposed layout, all in
+// flight together), computes the score in the reference's order and stages V in shared memory.
+// Warp 0 then runs the reference's 16 exp-sum chains and tree; the weighted sum takes 64 threads,
+// one per (dim, even / odd key) accumulator, each over its keys in order.
+// Shared memory: q (32), scores / exponentials (max_len), V rows (max_len x 33), two reduction slots.
+__host__ __device__ constexpr size_t cls_smem_floats(int max_len) { return 32 + 8 + size_t(max_len) * 34 + 64; }
 
 __global__ void __launch_bounds__(128) k_attention_cls(AttnArgs a, int n_seqs) {
   pdl_trigger();
   pdl_wait();
   extern __shared__ float4 smem4[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int item = blockIdx.x * 4 + warp;  // (sequence, head)
-  if (item >= n_seqs * kHeads) return;
-  const int s = item / kHeads, h = item % kHeads;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int s = blockIdx.x / kHeads, h = blockIdx.x % kHeads;
+  if (s >= n_seqs) return;
   const int s0 = int(a.cu[s]);
   const int L = int(a.cu[s + 1]) - s0;
   if (L <= 0 || L > a.max_len) {
-    if (lane == 0) record_err(a.err, DEV_ERR_BAD_SHAPE);
+    if (tid == 0) record_err(a.err, DEV_ERR_BAD_SHAPE);
     return;
   }
-  float* sc = reinterpret_cast<float*>(smem4) + warp * kClsWarpFloats;  // scores, then exponentials
-  float* vs = sc + kMaxPos;                                              // [32 keys][33]
-  float q[32];
-  load_query(a, s, h, q);
+  float* qs = reinterpret_cast<float*>(smem4);  // [32] pre-scaled query
+  float* red = qs + 32;                          // [8] warp maxima, then 1 / sum
+  float* sc = red + 8;                           // [max_len] scores, then exponentials
+  float* vs = sc + a.max_len;                    // [max_len][33] V rows
+  float* accs = vs + size_t(a.max_len) * 33;     // [64] weighted-sum accumulators
+  if (tid < 32) {
+    const float scale = 1.0f / sqrtf(32.0f);
+    qs[tid] = (a.q_tt ? a.q[tt_index(s, a.q_col + 32 * h + tid, a.q_C)]
+                      : a.q[size_t(s) * a.q_C + a.q_col + 32 * h + tid]) * scale;
+  }
+  __syncthreads();
   const int kc = a.k_col + 32 * h, vc = a.v_col + 32 * h;
   const int L4 = L & ~3, L8 = L & ~7, L16 = L & ~15;
   float mx = -INFINITY;
-  for (int t = lane; t < L; t += 32) {
-    float kk[32];
+  for (int t = tid; t < L; t += 128) {
+    float kk[32], vv[32];
 #pragma unroll
-    for (int d = 0; d < 32; ++d) kk[d] = ld_act(a.kv, a.kv_C, a.kv_tt, s0 + t, kc + d);
+    for (int d = 0; d < 32; ++d) {
+      kk[d] = ld_act(a.kv, a.kv_C, a.kv_tt, s0 + t, kc + d);
+      vv[d] = ld_act(a.kv, a.kv_C, a.kv_tt, s0 + t, vc + d);
+    }
     float s8[8];
 #pragma unroll
     for (int l = 0; l < 8; ++l)
-      s8[l] = fmaf(q[8 + l], kk[8 + l], q[l] * kk[l]) + fmaf(q[24 + l], kk[24 + l], q[16 + l] * kk[16 + l]);
+      s8[l] = fmaf(qs[8 + l], kk[8 + l], qs[l] * kk[l]) + fmaf(qs[24 + l], kk[24 + l], qs[16 + l] * kk[16 + l]);
     const float sv = (t < L4) ? ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]))
                               : ((s8[0] + s8[4]) + (s8[1] + s8[5])) + ((s8[2] + s8[6]) + (s8[3] + s8[7]));
     sc[t] = sv;
     mx = fmaxf(mx, sv);
+#pragma unroll
+    for (int d = 0; d < 32; ++d) vs[t * 33 + d] = vv[d];
   }
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  __syncwarp();
-  for (int t = lane; t < L; t += 32) sc[t] = (t < L8) ? cw_exp(sc[t] - mx) : scalar_expf(sc[t] - mx);
-  __syncwarp();
-  // lane l < 16 runs the chain of the reference's lane slot l (keys t0 + l of every 16-key chunk;
-  // slots 0-7 then also take the trailing 8-key chunk), as the two 8-lane AVX2 accumulators do
-  float part = 0.0f;
-  if (lane < 16) {
-    for (int t0 = 0; t0 < L16; t0 += 16) part = part + sc[t0 + lane];
-    if (L8 > L16 && lane < 8) part = part + sc[L16 + lane];
-  }
-  const float v = part + __shfl_down_sync(0xffffffffu, part, 8);  // vs0[l] + vs1[l]
-  const float t4 = v + __shfl_down_sync(0xffffffffu, v, 4);
-  const float u = t4 + __shfl_down_sync(0xffffffffu, t4, 1);
-  float sum = u + __shfl_down_sync(0xffffffffu, u, 2);
-  sum = __shfl_sync(0xffffffffu, sum, 0);
-  for (int t = L8; t < L; ++t) sum = sum + sc[t];
-  const float inv = 1.0f / sum;
-  // weighted sum: lane = dim, accumulator a (even keys) and b (odd keys); V staged 32 keys at a time
-  float acc_a = 0.0f, acc_b = 0.0f;
-  for (int t0 = 0; t0 < L; t0 += 32) {
-    const int t = t0 + lane;
-    __syncwarp();
-    if (t < L) {
-#pragma unroll
-      for (int d = 0; d < 32; ++d) vs[lane * 33 + d] = ld_act(a.kv, a.kv_C, a.kv_tt, s0 + t, vc + d);
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));  // the max is order-independent
+  for (int t = tid; t < L; t += 128) sc[t] = (t < L8) ? cw_exp(sc[t] - mx) : scalar_expf(sc[t] - mx);
+  __syncthreads();
+  if (warp == 0) {
+    // lane l < 16 runs the chain of the reference's lane slot l (keys t0 + l of every 16-key chunk;
+    // slots 0-7 then also take the trailing 8-key chunk), as the two 8-lane AVX2 accumulators do
+    float part = 0.0f;
+    if (lane < 16) {
+      for (int t0 = 0; t0 < L16; t0 += 16) part = part + sc[t0 + lane];
+      if (L8 > L16 && lane < 8) part = part + sc[L16 + lane];
     }
-    __syncwarp();
-    const int n = L - t0 < 32 ? L - t0 : 32;
-    for (int j = 0; j < n; ++j) {
-      const float p = sc[t0 + j] * inv;
-      if ((t0 + j) & 1) acc_b = fmaf(vs[j * 33 + lane], p, acc_b);
-      else acc_a = fmaf(vs[j * 33 + lane], p, acc_a);
+    const float v = part + __shfl_down_sync(0xffffffffu, part, 8);  // vs0[l] + vs1[l]
+    const float t4 = v + __shfl_down_sync(0xffffffffu, v, 4);
+    const float u = t4 + __shfl_down_sync(0xffffffffu, t4, 1);
+    float sum = u + __shfl_down_sync(0xffffffffu, u, 2);
+    if (lane == 0) {
+      for (int t = L8; t < L; ++t) sum = sum + sc[t];
+      red[4] = 1.0f / sum;
     }
   }
-  a.out[size_t(s) * kHidden + h * 32 + lane] = acc_a + acc_b;
+  __syncthreads();
+  if (tid < 64) {  // accumulator a (even keys, threads 0-31) or b (odd keys, threads 32-63) of dim d
+    const float inv = red[4];
+    const int d = tid & 31;
+    float acc = 0.0f;
+    for (int t = tid >> 5; t < L; t += 2) acc = fmaf(vs[t * 33 + d], sc[t] * inv, acc);
+    accs[tid] = acc;
+  }
+  __syncthreads();
+  if (tid < 32) a.out[size_t(s) * kHidden + h * 32 + tid] = accs[tid] + accs[32 + tid];
 }
 
 constexpr size_t kRowsSmemMax = 220 * 1024;  // dynamic shared memory cap (static smem comes on top)
@@ -1168,7 +1182,7 @@ int attention_prime() {
   r |= smem_attr((const void*)k_attention_rows<32>, rows_smem_cap(g_static_rows));
   r |= smem_attr((const void*)k_attention_wide<ATTN_WIDE_256>, rows_smem_cap(g_static_wide2));
   r |= smem_attr((const void*)k_attention_wide<4, 1>, rows_smem_cap(g_static_wide4));
-  r |= smem_attr((const void*)k_attention_cls, 4 * kClsWarpFloats * 4);
+  r |= smem_attr((const void*)k_attention_cls, cls_smem_floats(kMaxPos) * 4);
   r |= smem_attr((const void*)k_qkv_attention, kQaSmem);
   return r;
 }
@@ -1186,8 +1200,7 @@ int launch_attention_exact(const AttnArgs& a, int n_seqs, cudaStream_t st) {
   if (n_seqs <= 0) return 0;
   if (a.max_len <= 0 || a.max_len > kMaxPos) return -1;
   if (a.cls_mode) {
-    const int items = n_seqs * kHeads;
-    return launch_pdl(k_attention_cls, dim3((items + 3) / 4), dim3(128), size_t(4 * kClsWarpFloats * 4), st, a, n_seqs) ==
+    return launch_pdl(k_attention_cls, dim3(n_seqs * kHeads), dim3(128), cls_smem_floats(a.max_len) * 4, st, a, n_seqs) ==
                    cudaSuccess
                ? 0
                : -3;
