@@ -286,8 +286,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (g.out_tt && !g.res) {  // one 128-byte line per column for the warp's 32 rows
             float* o = g.out_f32 + tt_index(row, n0 + c0, g.ldo);
 #pragma unroll
-            for (int j = 0; j < CW; ++j)
-              o[size_t(j) << 7] = fmaf(float(int(r[j])), as * s_ws[c0 + j], s_bias[c0 + j]);
+            for (int j4 = 0; j4 < CW / 4; ++j4) {  // column parameters as 16-byte broadcast loads
+              const float4 w4 = *reinterpret_cast<const float4*>(s_ws + c0 + 4 * j4);
+              const float4 b4 = *reinterpret_cast<const float4*>(s_bias + c0 + 4 * j4);
+              const float wv[4] = {w4.x, w4.y, w4.z, w4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                o[size_t(4 * j4 + e) << 7] = fmaf(float(int(r[4 * j4 + e])), as * wv[e], bv[e]);
+            }
             continue;
           }
           float* o = g.out_f32 + size_t(row) * g.ldo + n0 + c0;
