@@ -115,6 +115,14 @@ __global__ void __launch_bounds__(256) k_ln_quant_rows(const float* __restrict__
                                                        int hidden_tt, int8_t* __restrict__ q,
                                                        float* __restrict__ scale) {
   pdl_trigger();
+  // the LayerNorm and SmoothQuant vectors are model constants: staged before the dependency wait
+  __shared__ float s_gamma[kHidden], s_beta[kHidden], s_invs[kHidden];
+  for (int i = threadIdx.x; i < kHidden; i += blockDim.x) {
+    s_gamma[i] = gamma[i];
+    s_beta[i] = beta[i];
+    s_invs[i] = inv_s[i];
+  }
+  __syncthreads();
   pdl_wait();
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 4;
   const int l = threadIdx.x & 15;
@@ -142,16 +150,16 @@ __global__ void __launch_bounds__(256) k_ln_quant_rows(const float* __restrict__
 #pragma unroll
   for (int i = 0; i < 24; ++i) {
     const int j = l + 16 * i;
-    h[i] = fmaf((h[i] - mean) * rstd, gamma[j], beta[j]);
+    h[i] = fmaf((h[i] - mean) * rstd, s_gamma[j], s_beta[j]);
     if (active) hidden[hidden_tt ? tt_index(hw, j, kHidden) : size_t(hw) * kHidden + j] = h[i];
-    vmax = fmaxf(vmax, fabsf(h[i] * inv_s[j]));
+    vmax = fmaxf(vmax, fabsf(h[i] * s_invs[j]));
   }
   const float max_abs = halfwarp_max(vmax, mask);
   const float inv_scale = 127.0f / max_abs;
 #pragma unroll
   for (int i = 0; i < 24; ++i) {
     const int j = l + 16 * i;
-    const int8_t qv = int8_t(quant_i8(h[i] * (inv_s[j] * inv_scale)));
+    const int8_t qv = int8_t(quant_i8(h[i] * (s_invs[j] * inv_scale)));
     if (active) q[size_t(hw) * kHidden + j] = qv;
   }
   if (active && l == 0) scale[hw] = max_abs / 127.0f;
@@ -168,6 +176,11 @@ __global__ void __launch_bounds__(128) k_ln_final_rows(const float* __restrict__
                                                        const float* __restrict__ gamma,
                                                        const float* __restrict__ beta, float* __restrict__ out) {
   pdl_trigger();
+  __shared__ float s_gamma[kHidden], s_beta[kHidden];  // model constants, staged before the wait
+  for (int i = threadIdx.x; i < kHidden; i += blockDim.x) {
+    s_gamma[i] = gamma[i];
+    s_beta[i] = beta[i];
+  }
   pdl_wait();
   extern __shared__ float xs[];  // [kLnFinalRows][kLnFinalPitch]
   const int r0 = blockIdx.x * kLnFinalRows;
@@ -191,7 +204,7 @@ __global__ void __launch_bounds__(128) k_ln_final_rows(const float* __restrict__
     const float rstd = 1.0f / sqrtf(var / float(kHidden) + kLnEps);
     float ss = 0.0f;
     for (int j = 0; j < kHidden; ++j) {
-      const float y = (x[j] - mean) * rstd * gamma[j] + beta[j];
+      const float y = (x[j] - mean) * rstd * s_gamma[j] + s_beta[j];
       x[j] = y;
       ss = ss + y * y;
     }
@@ -212,6 +225,9 @@ __global__ void __launch_bounds__(128) k_ln_final_rows(const float* __restrict__
 __global__ void __launch_bounds__(256) k_smooth_quant(const float* __restrict__ x, const float* __restrict__ inv_s,
                                                       int8_t* __restrict__ q, float* __restrict__ scale, int rows) {
   pdl_trigger();
+  __shared__ float s_invs[kHidden];  // model constant, staged before the dependency wait
+  for (int i = threadIdx.x; i < kHidden; i += blockDim.x) s_invs[i] = inv_s[i];
+  __syncthreads();
   pdl_wait();
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -230,7 +246,7 @@ __global__ void __launch_bounds__(256) k_smooth_quant(const float* __restrict__ 
 #pragma unroll
   for (int i = 0; i < 12; ++i) {
     const int j = 4 * (lane + 32 * (i / 4)) + (i % 4);
-    vmax = fmaxf(vmax, fabsf(v[i] * inv_s[j]));
+    vmax = fmaxf(vmax, fabsf(v[i] * s_invs[j]));
   }
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, o));
@@ -242,7 +258,7 @@ __global__ void __launch_bounds__(256) k_smooth_quant(const float* __restrict__ 
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int j = 4 * (lane + 32 * i) + e;
-      w |= (uint32_t(quant_i8(v[4 * i + e] * (inv_s[j] * inv_scale))) & 0xFFu) << (8 * e);
+      w |= (uint32_t(quant_i8(v[4 * i + e] * (s_invs[j] * inv_scale))) & 0xFFu) << (8 * e);
     }
     reinterpret_cast<uint32_t*>(qr)[lane + 32 * i] = w;
   }
