@@ -117,6 +117,10 @@ __global__ void __launch_bounds__(256) k_ln_quant_rows(const float* __restrict__
   pdl_trigger();
   // the LayerNorm and SmoothQuant vectors are model constants: staged before the dependency wait
   __shared__ float s_gamma[kHidden], s_beta[kHidden], s_invs[kHidden];
+  // the block's 16 output rows, staged so that the stores are contiguous: hidden as [column][row]
+  // (a tile-transposed column of the 16 rows is 64 contiguous bytes), int8 rows as [row][column]
+  __shared__ float tile[kHidden][17];
+  __shared__ __align__(16) int8_t qtile[16][kHidden];
   for (int i = threadIdx.x; i < kHidden; i += blockDim.x) {
     s_gamma[i] = gamma[i];
     s_beta[i] = beta[i];
@@ -124,7 +128,9 @@ __global__ void __launch_bounds__(256) k_ln_quant_rows(const float* __restrict__
   }
   __syncthreads();
   pdl_wait();
-  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 4;
+  const int r0 = blockIdx.x * 16;
+  const int lr = threadIdx.x >> 4;  // row within the block
+  const int row = r0 + lr;
   const int l = threadIdx.x & 15;
   const unsigned mask = 0xffffffffu;
   const bool active = row < M;
@@ -151,7 +157,7 @@ __global__ void __launch_bounds__(256) k_ln_quant_rows(const float* __restrict__
   for (int i = 0; i < 24; ++i) {
     const int j = l + 16 * i;
     h[i] = fmaf((h[i] - mean) * rstd, s_gamma[j], s_beta[j]);
-    if (active) hidden[hidden_tt ? tt_index(hw, j, kHidden) : size_t(hw) * kHidden + j] = h[i];
+    tile[j][lr] = h[i];
     vmax = fmaxf(vmax, fabsf(h[i] * s_invs[j]));
   }
   const float max_abs = halfwarp_max(vmax, mask);
@@ -159,10 +165,28 @@ __global__ void __launch_bounds__(256) k_ln_quant_rows(const float* __restrict__
 #pragma unroll
   for (int i = 0; i < 24; ++i) {
     const int j = l + 16 * i;
-    const int8_t qv = int8_t(quant_i8(h[i] * (s_invs[j] * inv_scale)));
-    if (active) q[size_t(hw) * kHidden + j] = qv;
+    qtile[lr][j] = int8_t(quant_i8(h[i] * (s_invs[j] * inv_scale)));
   }
   if (active && l == 0) scale[hw] = max_abs / 127.0f;
+  __syncthreads();
+  const int rows = M - r0 < 16 ? M - r0 : 16;
+  if (hidden_tt) {
+    for (int i = threadIdx.x; i < kHidden * 16; i += blockDim.x) {  // rows fastest
+      const int j = i >> 4, rr = i & 15;
+      if (rr < rows) hidden[tt_index(r0 + rr, j, kHidden)] = tile[j][rr];
+    }
+  } else {
+    for (int i = threadIdx.x; i < kHidden * 16; i += blockDim.x) {  // columns fastest
+      const int rr = i / kHidden, j = i - rr * kHidden;
+      if (rr < rows) hidden[size_t(r0 + rr) * kHidden + j] = tile[j][rr];
+    }
+  }
+  for (int i = threadIdx.x; i < 16 * (kHidden / 16); i += blockDim.x) {  // 16-byte pieces of the int8 rows
+    const int rr = i / (kHidden / 16), c = i - rr * (kHidden / 16);
+    if (rr < rows)
+      *reinterpret_cast<uint4*>(q + size_t(r0 + rr) * kHidden + 16 * c) =
+          *reinterpret_cast<const uint4*>(&qtile[rr][16 * c]);
+  }
 }
 
 // layernorm_inplace_row + l2_normalize_inplace (src/simd_math.rs:481-497, :2892-2903) on rows of
