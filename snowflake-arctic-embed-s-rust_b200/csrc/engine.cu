@@ -111,6 +111,7 @@ struct ae_ctx {
   cudaStream_t own_stream = nullptr;
   cudaStream_t stream = nullptr;
   int* d_err = nullptr;
+  uint32_t* d_cu_single = nullptr;  // [513][2]: {0, L} at 2L, the cu_seqlens of one sequence of L ids
   bool has_model = false;
   DevModel model;
   Workspace ws;
@@ -805,6 +806,15 @@ int ae_ctx_create(int device, ae_ctx** out) {
   // stream preparing the inputs of ae_forward_ragged_device) is ordered with the context's work
   e = cudaStreamCreate(&c->own_stream);
   if (e == cudaSuccess) e = cudaMalloc(&c->d_err, sizeof(int));
+  if (e == cudaSuccess) e = cudaMalloc(&c->d_cu_single, sizeof(uint32_t) * 2 * (kMaxPos + 1));
+  if (e == cudaSuccess) {
+    std::vector<uint32_t> t(2 * (kMaxPos + 1));
+    for (int L = 0; L <= kMaxPos; ++L) {
+      t[2 * L] = 0;
+      t[2 * L + 1] = uint32_t(L);
+    }
+    e = cudaMemcpy(c->d_cu_single, t.data(), t.size() * sizeof(uint32_t), cudaMemcpyHostToDevice);
+  }
   if (e == cudaSuccess) e = cudaMemset(c->d_err, 0, sizeof(int));
   if (e != cudaSuccess) {
     if (c->own_stream) cudaStreamDestroy(c->own_stream);
@@ -837,6 +847,7 @@ int ae_ctx_destroy(ae_ctx* c) {
   }
   for (auto e : c->prof_pool) cudaEventDestroy(e);
   if (c->d_err) cudaFree(c->d_err);
+  if (c->d_cu_single) cudaFree(c->d_cu_single);
   if (c->own_stream) cudaStreamDestroy(c->own_stream);
   delete c;
   return 0;
@@ -1060,19 +1071,17 @@ int ae_forward_cls(ae_ctx* c, const uint16_t* ids, uint32_t len, float* out) {
   Workspace& W = c->ws;
   auto it = c->graphs.find(L);
   if (it == c->graphs.end()) {
-    // capture: H2D ids + cu, forward, D2H out, all at fixed workspace addresses
-    W.h_cu[0] = 0;
-    W.h_cu[1] = L;
+    // capture: H2D ids, forward, D2H out, all at fixed addresses (cu_seqlens {0, L} from the
+    // context's constant table)
     Graph gr;
     CUDA_TRY(c, cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
     int r = 0;
-    if (cudaMemcpyAsync(W.ids, W.h_ids, L * 2, cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
-        cudaMemcpyAsync(W.cu, W.h_cu, 2 * 4, cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
-      r = fail(c, AE_ERR_CUDA, "capture of input copies failed");
+    if (cudaMemcpyAsync(W.ids, W.h_ids, L * 2, cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
+      r = fail(c, AE_ERR_CUDA, "capture of the input copy failed");
     const uint64_t before = c->launches;
     const bool prof = c->prof;
     c->prof = false;  // no event records inside the graph
-    if (!r) r = enqueue_forward(c, W.ids, W.cu, int(L), 1, int(L), W.out);
+    if (!r) r = enqueue_forward(c, W.ids, c->d_cu_single + 2 * L, int(L), 1, int(L), W.out);
     c->prof = prof;
     gr.kernels = c->launches - before;
     c->launches = before;  // captured, not launched
@@ -1092,8 +1101,6 @@ int ae_forward_cls(ae_ctx* c, const uint16_t* ids, uint32_t len, float* out) {
     it = c->graphs.emplace(L, gr).first;
   }
   std::memcpy(W.h_ids, ids, L * 2);
-  W.h_cu[0] = 0;
-  W.h_cu[1] = L;
   CUDA_TRY(c, cudaGraphLaunch(it->second.exec, c->stream));
   c->launches += it->second.kernels;
   CUDA_TRY(c, cudaStreamSynchronize(c->stream));

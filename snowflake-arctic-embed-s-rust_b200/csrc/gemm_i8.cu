@@ -775,7 +775,7 @@ static cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const Ge
 int gemm_i8_prime() {
   int r = 0;
   r |= set_smem<64, EPI_F32, true, 4>();
-  r |= set_smem<64, EPI_F32, false, 4>();
+  r |= set_smem<64, EPI_F32, false, 8>();
   r |= set_smem<128, EPI_F32, true, 4>();
   r |= set_smem<192, EPI_F32, true, 4>();
   r |= set_smem<256, EPI_F32, true, 4>();
@@ -802,7 +802,7 @@ int gemm_i8_launch(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const 
       const int mt = (g.M + BM - 1) / BM;
       const bool few = mt * (g.N / 128) < num_sms();
       if (few && g.N % 64 == 0 && mt * (g.N / 64) <= num_sms())
-        e = res ? launch<64, EPI_F32, true, 4>(ta, tb, g, st) : launch<64, EPI_F32, false, 4>(ta, tb, g, st);
+        e = res ? launch<64, EPI_F32, true, 4>(ta, tb, g, st) : launch<64, EPI_F32, false, 8>(ta, tb, g, st);
       else if (few && g.N % 128 == 0)
         e = res ? launch<128, EPI_F32, true, 4>(ta, tb, g, st) : launch<128, EPI_F32, false, 4>(ta, tb, g, st);
       else if (g.N % 256 == 0)
@@ -812,7 +812,7 @@ int gemm_i8_launch(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const 
       else if (g.N % 128 == 0)
         e = res ? launch<128, EPI_F32, true, 4>(ta, tb, g, st) : launch<128, EPI_F32, false, 4>(ta, tb, g, st);
       else if (g.N % 64 == 0)
-        e = res ? launch<64, EPI_F32, true, 4>(ta, tb, g, st) : launch<64, EPI_F32, false, 4>(ta, tb, g, st);
+        e = res ? launch<64, EPI_F32, true, 4>(ta, tb, g, st) : launch<64, EPI_F32, false, 8>(ta, tb, g, st);
       else
         return -11;
       break;

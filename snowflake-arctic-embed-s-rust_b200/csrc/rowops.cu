@@ -42,6 +42,15 @@ __device__ __forceinline__ float halfwarp_max(float v, unsigned mask) {
 // block's 16 consecutive rows (64 contiguous bytes).
 __global__ void __launch_bounds__(256) k_embed_ln_quant(EmbedArgs a) {
   pdl_trigger();
+  // model constants, staged before the dependency wait
+  __shared__ float s_type0[kHidden], s_gamma[kHidden], s_beta[kHidden], s_invs[kHidden];
+  for (int i = threadIdx.x; i < kHidden; i += blockDim.x) {
+    s_type0[i] = a.type0[i];
+    s_gamma[i] = a.gamma[i];
+    s_beta[i] = a.beta[i];
+    s_invs[i] = a.inv_smooth[i];
+  }
+  __syncthreads();
   pdl_wait();
   __shared__ float tile[kHidden][17];
   const int r0 = blockIdx.x * 16;
@@ -65,7 +74,7 @@ __global__ void __launch_bounds__(256) k_embed_ln_quant(EmbedArgs a) {
 #pragma unroll
   for (int i = 0; i < 24; ++i) {
     const int j = l + 16 * i;
-    h[i] = (float(wq[j]) * ws + float(pq[j]) * ps) + a.type0[j];
+    h[i] = (float(wq[j]) * ws + float(pq[j]) * ps) + s_type0[j];
     p = p + h[i];
   }
   const float mean = halfwarp_tree16(p, mask) / float(kHidden);
@@ -81,9 +90,9 @@ __global__ void __launch_bounds__(256) k_embed_ln_quant(EmbedArgs a) {
 #pragma unroll
   for (int i = 0; i < 24; ++i) {
     const int j = l + 16 * i;
-    h[i] = fmaf((h[i] - mean) * rstd, a.gamma[j], a.beta[j]);
+    h[i] = fmaf((h[i] - mean) * rstd, s_gamma[j], s_beta[j]);
     tile[j][lr] = h[i];
-    vmax = fmaxf(vmax, fabsf(h[i] * a.inv_smooth[j]));
+    vmax = fmaxf(vmax, fabsf(h[i] * s_invs[j]));
   }
   const float max_abs = halfwarp_max(vmax, mask);
   const float inv_scale = 127.0f / max_abs;
@@ -91,7 +100,7 @@ __global__ void __launch_bounds__(256) k_embed_ln_quant(EmbedArgs a) {
 #pragma unroll
   for (int i = 0; i < 24; ++i) {
     const int j = l + 16 * i;
-    const int8_t qv = int8_t(quant_i8(h[i] * (a.inv_smooth[j] * inv_scale)));
+    const int8_t qv = int8_t(quant_i8(h[i] * (s_invs[j] * inv_scale)));
     if (active) qrow[j] = qv;
   }
   if (active && l == 0) a.act_s[hw] = max_abs / 127.0f;
