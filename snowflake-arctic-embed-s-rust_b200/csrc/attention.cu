@@ -842,6 +842,156 @@ __global__ void __launch_bounds__(128, 2)
   if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
+// Attention for few (sequence, head) pairs (single sequences: the latency path). The TMEM kernels
+// hold one query per thread, so a 32-token sequence gives 12 CTAs of one warp and a 512-token one 48
+// CTAs; here four lanes share a query, so each CTA (one sequence, one head, QT queries) has 4 QT
+// threads and no TMEM. Sub-lane sl of a query computes the scores and exponentials of the keys
+// whose softmax-sum slots it owns -- in every full 16-key chunk t0 the keys t0 + 2sl, t0 + 2sl + 1
+// (slots 2sl, 2sl + 1 of the first 8-lane accumulator) and t0 + 8 + 2sl, t0 + 9 + 2sl (the second),
+// in the trailing 8-key chunk L16 + 2sl, L16 + 2sl + 1, and the tail keys L8 + sl + 4k (scalar exp,
+// added after the tree) -- so each of the reference's 16 sum chains stays in one thread, in order;
+// the hsum256 tree of the 8 lanes runs over two shuffles. The weighted sum: sub-lane sl owns dims
+// 8sl .. 8sl + 7, both the even- and odd-key accumulators, over all keys in order. K and V are
+// staged dim-major with an odd-stride pitch P = 4k + 1, so that the four sub-lanes' reads fall in
+// different banks; the scores, then exponentials, of the CTA's queries live in shared memory.
+// Longest sequence the kernel takes: at 96-128 keys the TMEM kernels' one query per thread is faster
+// for a single sequence, at 512 keys much faster (48 CTAs of 16 warps against 192 of 4).
+constexpr int kLatMaxLen = 64;
+__host__ __device__ constexpr int lat_pitch(int L) { return ((L + 3) & ~3) + 1; }
+__host__ __device__ constexpr size_t lat_smem_bytes(int L, int QT) { return size_t(64 + QT) * lat_pitch(L) * 4; }
+
+template <int QT>
+__global__ void __launch_bounds__(4 * QT) k_attention_lat(AttnArgs a) {
+  pdl_trigger();
+  pdl_wait();
+  extern __shared__ float4 smem4[];
+  const int s = blockIdx.x;
+  const int h = blockIdx.y;
+  const int tile = blockIdx.z;
+  const int tid = threadIdx.x;
+  const int s0 = int(a.cu[s]);
+  const int L = int(a.cu[s + 1]) - s0;
+  if (L <= 0 || L > a.max_len) {
+    if (tid == 0 && tile == 0 && h == 0) record_err(a.err, DEV_ERR_BAD_SHAPE);
+    return;
+  }
+  if (tile * QT >= L) return;
+  const int P = lat_pitch(L);
+  float* kd = reinterpret_cast<float*>(smem4);  // [32][P]: dim d of key t at d * P + t
+  float* vd = kd + 32 * P;                      // [32][P]
+  float* es = vd + 32 * P;                      // [QT][P]: scores, then exponentials, of the tile's queries
+  const int kc = a.k_col + 32 * h, vc = a.v_col + 32 * h;
+  for (int i = tid; i < 32 * L; i += 4 * QT) {  // keys fastest: coalesced in the tile-transposed layout
+    const int d = i / L, t = i - d * L;
+    kd[d * P + t] = ld_act(a.kv, a.kv_C, a.kv_tt, s0 + t, kc + d);
+    vd[d * P + t] = ld_act(a.kv, a.kv_C, a.kv_tt, s0 + t, vc + d);
+  }
+  const int ql = tid >> 2, sl = tid & 3;
+  const int qi = tile * QT + ql;
+  const bool active = qi < L;
+  float q[32];
+  load_query(a, s0 + (active ? qi : L - 1), h, q);
+  __syncthreads();
+  float* er = es + ql * P;
+  const int L4 = L & ~3, L8 = L & ~7, L16 = L & ~15;
+  const unsigned full = 0xffffffffu;
+
+  auto score = [&](int t) -> float {  // score_pair's order for one key
+    float s8[8];
+#pragma unroll
+    for (int l = 0; l < 8; ++l)
+      s8[l] = fmaf(q[8 + l], kd[(8 + l) * P + t], q[l] * kd[l * P + t]) +
+              fmaf(q[24 + l], kd[(24 + l) * P + t], q[16 + l] * kd[(16 + l) * P + t]);
+    return (t < L4) ? ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]))
+                    : ((s8[0] + s8[4]) + (s8[1] + s8[5])) + ((s8[2] + s8[6]) + (s8[3] + s8[7]));
+  };
+
+  // pass 1: scores of the owned keys, their max over the query's four sub-lanes
+  float mx = -INFINITY;
+  for (int t0 = 0; t0 < L16; t0 += 16) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int t = t0 + 2 * sl + (k & 1) + 8 * (k >> 1);
+      const float sv = score(t);
+      er[t] = sv;
+      mx = fmaxf(mx, sv);
+    }
+  }
+  for (int t = L16 + 2 * sl; t < L16 + 2 * sl + 2 && t < L8; ++t) {
+    const float sv = score(t);
+    er[t] = sv;
+    mx = fmaxf(mx, sv);
+  }
+  for (int t = L8 + sl; t < L; t += 4) {
+    const float sv = score(t);
+    er[t] = sv;
+    mx = fmaxf(mx, sv);
+  }
+  mx = fmaxf(mx, __shfl_xor_sync(full, mx, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(full, mx, 2));
+
+  // pass 2: exponentials of the owned keys and the owned sum chains (slots 2sl, 2sl + 1 of both
+  // 8-lane accumulators), in chunk order
+  float c0a = 0.0f, c0b = 0.0f, c1a = 0.0f, c1b = 0.0f;
+  for (int t0 = 0; t0 < L16; t0 += 16) {
+    const int t = t0 + 2 * sl;
+    const float e0 = cw_exp(er[t] - mx), e1 = cw_exp(er[t + 1] - mx);
+    const float e2 = cw_exp(er[t + 8] - mx), e3 = cw_exp(er[t + 9] - mx);
+    er[t] = e0;
+    er[t + 1] = e1;
+    er[t + 8] = e2;
+    er[t + 9] = e3;
+    c0a = c0a + e0;
+    c0b = c0b + e1;
+    c1a = c1a + e2;
+    c1b = c1b + e3;
+  }
+  if (L16 + 2 * sl < L8) {  // the trailing 8-key chunk feeds the first accumulator
+    const int t = L16 + 2 * sl;
+    const float e0 = cw_exp(er[t] - mx), e1 = cw_exp(er[t + 1] - mx);
+    er[t] = e0;
+    er[t + 1] = e1;
+    c0a = c0a + e0;
+    c0b = c0b + e1;
+  }
+  for (int t = L8 + sl; t < L; t += 4) er[t] = scalar_expf(er[t] - mx);
+  // hsum256 of v[m] = acc0[m] + acc1[m]: sub-lane sl holds v[2sl], v[2sl + 1]
+  const float vx = c0a + c1a, vy = c0b + c1b;
+  const float ax = vx + __shfl_down_sync(full, vx, 2);  // v0 + v4 | v2 + v6
+  const float ay = vy + __shfl_down_sync(full, vy, 2);  // v1 + v5 | v3 + v7
+  const float tt = ax + ay;
+  float sum = tt + __shfl_down_sync(full, tt, 1);
+  __syncwarp();
+  if (sl == 0)
+    for (int t = L8; t < L; ++t) sum = sum + er[t];  // the tail keys in order, after the tree
+  const float inv = __shfl_sync(full, 1.0f / sum, tid & 31 & ~3);
+
+  // pass 3: weighted sum of V, dims 8sl .. 8sl + 7; even keys to the first accumulator
+  float acc_e[8], acc_o[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) acc_e[k] = acc_o[k] = 0.0f;
+  const float* vrow = vd + 8 * sl * P;
+  int t = 0;
+  for (; t + 1 < L; t += 2) {
+    const float p0 = er[t] * inv, p1 = er[t + 1] * inv;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      acc_e[k] = fmaf(vrow[k * P + t], p0, acc_e[k]);
+      acc_o[k] = fmaf(vrow[k * P + t + 1], p1, acc_o[k]);
+    }
+  }
+  if (t < L) {
+    const float p0 = er[t] * inv;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc_e[k] = fmaf(vrow[k * P + t], p0, acc_e[k]);
+  }
+  if (active) {
+    float4* o = reinterpret_cast<float4*>(a.out + size_t(s0 + qi) * kHidden + h * 32 + 8 * sl);
+    o[0] = make_float4(acc_e[0] + acc_o[0], acc_e[1] + acc_o[1], acc_e[2] + acc_o[2], acc_e[3] + acc_o[3]);
+    o[1] = make_float4(acc_e[4] + acc_o[4], acc_e[5] + acc_o[5], acc_e[6] + acc_o[6], acc_e[7] + acc_o[7]);
+  }
+}
+
 // NWG warpgroups per 128-query tile: warps w, w + 4, ... share TMEM lane quadrant w & 3 (the same
 // queries). Scores and exponentials: group g takes keys t0 + g KPG .. t0 + (g + 1) KPG - 1 of
 // every 16-key chunk (KPG = 16 / NWG), so each of the reference's 16 sum slots is summed in order
@@ -1183,6 +1333,7 @@ int attention_prime() {
   r |= smem_attr((const void*)k_attention_wide<ATTN_WIDE_256>, rows_smem_cap(g_static_wide2));
   r |= smem_attr((const void*)k_attention_wide<4, 1>, rows_smem_cap(g_static_wide4));
   r |= smem_attr((const void*)k_attention_cls, cls_smem_floats(kMaxPos) * 4);
+  r |= smem_attr((const void*)k_attention_lat<32>, lat_smem_bytes(kMaxPos, 32));
   r |= smem_attr((const void*)k_qkv_attention, kQaSmem);
   return r;
 }
@@ -1211,6 +1362,12 @@ int launch_attention_exact(const AttnArgs& a, int n_seqs, cudaStream_t st) {
   // per SM, so one-warp tiles would leave each SM one warp for L x 32 query-key pairs).
   const int cap = a.max_len <= 32 ? 32 : a.max_len <= 64 ? 64 : 128;
   const long heads = long(n_seqs) * kHeads;
+  // few (sequence, head) pairs of short sequences: four lanes per query, 32-query tiles, no TMEM
+  if (a.max_len <= kLatMaxLen && heads * ((a.max_len + 31) / 32) <= 2 * 148)
+    return launch_pdl(k_attention_lat<32>, dim3(n_seqs, kHeads, (a.max_len + 31) / 32), dim3(128),
+                      lat_smem_bytes(a.max_len, 32), st, a) == cudaSuccess
+               ? 0
+               : -3;
   if (a.max_len > 128) return launch_rows<128>(a, n_seqs, st);
 #ifndef ATTN_PAIRS
 #define ATTN_PAIRS 1
