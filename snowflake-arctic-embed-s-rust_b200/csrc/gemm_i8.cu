@@ -69,9 +69,19 @@ struct Layout {
   static constexpr int PARAM_FLOATS = 3 * BN + 2 * kHidden;             // ws, bias, invs | gamma, beta
   static constexpr int XCH_FLOATS_GELU = 2 * 4 * BM + 2 * kGeluCluster * BM;
   static constexpr int STAGING_BYTES = EPI == EPI_GELU_QUANT ? kEpiWarps * 32 * 80 : 0;  // int8 output rows
+  static constexpr int NBARS_ = 2 * STAGES + 1 + 2 * 2 + 2;
+  // EPI_F32 with a row-major output: each epilogue warp transposes its 32 rows x STG_W columns through
+  // shared memory (pitch STG_W + 1) so that the stores are whole row segments; 32 columns where
+  // the memory allows, else 16, else none (per-row stores)
+  static constexpr int BASE_BYTES = 1024 + B_RES + RING + 4 * PARAM_FLOATS + 8 * NBARS_ + 16;
+  static constexpr int STG_W = EPI != EPI_F32 ? 0
+                               : (BASE_BYTES + 4 * kEpiWarps * 32 * 33 <= 232448 && (BN / 4) % 32 == 0)
+                                   ? 32
+                                   : (BASE_BYTES + 4 * kEpiWarps * 32 * 17 <= 232448 ? 16 : 0);
+  static constexpr int STG_FLOATS = STG_W ? kEpiWarps * 32 * (STG_W + 1) : 0;
   static constexpr int XCH_FLOATS =
-      LN ? (2 * BM * 16 + BM * 4) : (EPI == EPI_GELU_QUANT ? XCH_FLOATS_GELU + STAGING_BYTES / 4 : 0);
-  static constexpr int NBARS = 2 * STAGES + 1 + 2 * 2 + 2;
+      LN ? (2 * BM * 16 + BM * 4) : (EPI == EPI_GELU_QUANT ? XCH_FLOATS_GELU + STAGING_BYTES / 4 : STG_FLOATS);
+  static constexpr int NBARS = NBARS_;
   static constexpr int TOTAL = 1024 + B_RES + RING + 4 * (PARAM_FLOATS + XCH_FLOATS) + 8 * NBARS + 16;
   static_assert(TOTAL <= 232448, "shared memory of one CTA exceeds the sm_100 limit");
 };
@@ -276,13 +286,39 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[b]);
-        if (valid) {
-          if (g.acc_dbg) {
-            int4* ad = reinterpret_cast<int4*>(g.acc_dbg + size_t(row) * g.N + n0 + c0);
+        if (valid && g.acc_dbg) {
+          int4* ad = reinterpret_cast<int4*>(g.acc_dbg + size_t(row) * g.N + n0 + c0);
 #pragma unroll
-            for (int q = 0; q < CW / 4; ++q)
-              ad[q] = make_int4(int(r[4 * q]), int(r[4 * q + 1]), int(r[4 * q + 2]), int(r[4 * q + 3]));
+          for (int q = 0; q < CW / 4; ++q)
+            ad[q] = make_int4(int(r[4 * q]), int(r[4 * q + 1]), int(r[4 * q + 2]), int(r[4 * q + 3]));
+        }
+        if constexpr (Ly::STG_W > 0) {
+          if (!g.out_tt && !g.res) {
+            // row-major output through the warp's staging tile: lane = row writes SW values, then
+            // lane = column stores whole row segments (SW = 32: one 128-byte line per row)
+            constexpr int SW = Ly::STG_W, PITCH = SW + 1;
+            float* stg = xch + ew * 32 * PITCH;
+            const int rbase = m0 + Q * 32;
+#pragma unroll
+            for (int c1 = 0; c1 < CW; c1 += SW) {
+#pragma unroll
+              for (int j = 0; j < SW; ++j)
+                stg[lane * PITCH + j] = fmaf(float(int(r[c1 + j])), as * s_ws[c0 + c1 + j], s_bias[c0 + c1 + j]);
+              __syncwarp();
+              constexpr int RPI = 32 / SW;  // rows per store instruction
+              const int cl = lane % SW, rsub = lane / SW;
+              float* ocol = g.out_f32 + n0 + c0 + c1 + cl;
+#pragma unroll 4
+              for (int r0 = 0; r0 < 32; r0 += RPI) {
+                const int rr = r0 + rsub;
+                if (ok && rbase + rr < g.M) ocol[size_t(rbase + rr) * g.ldo] = stg[rr * PITCH + cl];
+              }
+              __syncwarp();
+            }
+            continue;
           }
+        }
+        if (valid) {
           if (g.out_tt && !g.res) {  // one 128-byte line per column for the warp's 32 rows
             float* o = g.out_f32 + tt_index(row, n0 + c0, g.ldo);
 #pragma unroll
