@@ -107,6 +107,29 @@ __device__ __forceinline__ void stage_kv_pairs(const AttnArgs& a, int s0, int L,
     cp_async_wait_all();
     return;
   }
+  if (!a.kv_tt) {
+    // row-major rows: one key's 32 dims of a head are 128 contiguous bytes; an item takes dims
+    // 4g .. 4g + 3 of both keys of a pair as 16-byte loads (eight items cover a key row)
+    for (int i = threadIdx.x; i < pairs * 8; i += blockDim.x) {
+      const int p = i >> 3, g = i & 7;
+      const size_t r0 = size_t(s0 + 2 * p) * a.kv_C;
+      const bool two = 2 * p + 1 < L;
+      const float4 ka = *reinterpret_cast<const float4*>(a.kv + r0 + kc + 4 * g);
+      const float4 va = *reinterpret_cast<const float4*>(a.kv + r0 + vc + 4 * g);
+      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 kb = two ? *reinterpret_cast<const float4*>(a.kv + r0 + a.kv_C + kc + 4 * g) : z;
+      const float4 vb = two ? *reinterpret_cast<const float4*>(a.kv + r0 + a.kv_C + vc + 4 * g) : z;
+      const float k0[4] = {ka.x, ka.y, ka.z, ka.w}, k1[4] = {kb.x, kb.y, kb.z, kb.w};
+      const float v0[4] = {va.x, va.y, va.z, va.w}, v1[4] = {vb.x, vb.y, vb.z, vb.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int d = 4 * g + e;
+        kp[p * KPS + (d & 7) * 4 + (d >> 3)] = f2(k0[e], k1[e]);  // score_pair's order
+        vp[p * KPS + d] = f2(v0[e], v1[e]);
+      }
+    }
+    return;
+  }
   const int groups = (pairs + 7) >> 3;  // 8-pair groups
   for (int i = threadIdx.x; i < groups * 256; i += blockDim.x) {
     const int w = i >> 5, l = i & 31;
@@ -590,6 +613,23 @@ __device__ __forceinline__ void stage_kv_dim_major(const AttnArgs& a, int s0, in
       float* dst = (row < 64 ? kd + row * rs : vd + (row - 64) * rs) + t;
       const int valid = L - t < 4 ? (L - t > 0 ? L - t : 0) : 4;
       cp_async16(dst, a.kv + tt_index(s0 + (valid ? t : 0), col, a.kv_C), uint32_t(valid) * 4u);
+    }
+    return;
+  }
+  if (!a.kv_tt) {
+    // row-major rows: an item takes dims 4g .. 4g + 3 of one key (K or V of one of the two heads)
+    // as one 16-byte load; the columns L .. rs - 1 are zero
+    for (int i = threadIdx.x; i < 32 * rs; i += blockDim.x) {  // keys fastest: conflict-free stores
+      const int g = i / rs, t = i - g * rs;  // g: K dims 4g (g < 16), V dims 4 (g - 16) (g >= 16)
+      const int dd = 4 * (g & 15);
+      const int col = (g < 16 ? kc : vc) + dd;
+      float* dst = (g < 16 ? kd : vd) + dd * rs + t;
+      const float4 x = t < L ? *reinterpret_cast<const float4*>(a.kv + size_t(s0 + t) * a.kv_C + col)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+      dst[0] = x.x;
+      dst[rs] = x.y;
+      dst[2 * rs] = x.z;
+      dst[3 * rs] = x.w;
     }
     return;
   }
