@@ -200,6 +200,11 @@ __global__ void __launch_bounds__(QT, 512 / QT) k_attention_rows(AttnArgs a) {
     tmem_alloc(&tmem_slot, cols);
     tmem_relinquish();
   }
+  const int qi = tile * QT + tid;
+  const bool active = qi < L;
+  const int qrow = s0 + (active ? qi : L - 1);
+  float q[32];
+  load_query(a, qrow, h, q);  // requested before the K / V staging, in flight with it
   const int pairs = (L + 1) >> 1;
   float2* kp = reinterpret_cast<float2*>(smem4);
   float2* vp = kp + pairs * KPS;
@@ -208,12 +213,6 @@ __global__ void __launch_bounds__(QT, 512 / QT) k_attention_rows(AttnArgs a) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tl = tmem_slot + (uint32_t(warp * 32) << 16);  // this warp's 32 lanes
-
-  const int qi = tile * QT + tid;
-  const bool active = qi < L;
-  const int qrow = s0 + (active ? qi : L - 1);
-  float q[32];
-  load_query(a, qrow, h, q);
   const int L4 = L & ~3, L8 = L & ~7, L16 = L & ~15;
   uint32_t r[16];
 
@@ -1066,6 +1065,11 @@ __global__ void __launch_bounds__(128 * NWG, MINB) k_attention_wide(AttnArgs a) 
     tmem_alloc(&tmem_slot, cols);
     tmem_relinquish();
   }
+  const int qi = tile * 128 + qt;
+  const bool active = qi < L;
+  const int qrow = s0 + (active ? qi : L - 1);
+  float q[32];
+  load_query(a, qrow, h, q);  // requested before the K / V staging, in flight with it
   const int pairs = (L + 1) >> 1;
   float2* kp = reinterpret_cast<float2*>(smem4);
   float2* vp = kp + pairs * KPS;
@@ -1074,10 +1078,6 @@ __global__ void __launch_bounds__(128 * NWG, MINB) k_attention_wide(AttnArgs a) 
   __syncthreads();
   tc_fence_after();
   const uint32_t tl = tmem_slot + (uint32_t((warp & 3) * 32) << 16);
-
-  const int qi = tile * 128 + qt;
-  const bool active = qi < L;
-  const int qrow = s0 + (active ? qi : L - 1);
   const int L4 = L & ~3, L8 = L & ~7, L16 = L & ~15;
   const int ko = KPG * grp;  // this group's keys within a 16-key chunk
   uint32_t r[16];
@@ -1085,8 +1085,6 @@ __global__ void __launch_bounds__(128 * NWG, MINB) k_attention_wide(AttnArgs a) 
   // pass 1: scores -> TMEM and their max
   float mx = -INFINITY;
   {
-    float q[32];
-    load_query(a, qrow, h, q);
     for (int t0 = 0; t0 < L; t0 += 16) {
 #pragma unroll
       for (int j = 0; j < KPG / 2; ++j) {
