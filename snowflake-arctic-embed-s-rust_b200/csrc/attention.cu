@@ -1114,7 +1114,29 @@ __global__ void __launch_bounds__(128 * NWG, MINB) k_attention_wide(AttnArgs a) 
   float2 vs[KPG / 2];
 #pragma unroll
   for (int j = 0; j < KPG / 2; ++j) vs[j] = f2(0.0f, 0.0f);
-  for (int t0 = 0; t0 < L; t0 += 16) {
+  int t0 = 0;
+  for (; t0 + 64 <= L16; t0 += 64) {  // four full chunks per TMEM round trip, summed in chunk order
+    uint32_t rq[4][KPG];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      if constexpr (KPG == 8) tmem_ld8(tl + t0 + 16 * c + ko, rq[c]);
+      else tmem_ld4(tl + t0 + 16 * c + ko, rq[c]);
+    }
+    tmem_ld_wait();
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+#pragma unroll
+      for (int j = 0; j < KPG / 2; ++j) {
+        const float2 e = cw_exp2(add2(f2(__uint_as_float(rq[c][2 * j]), __uint_as_float(rq[c][2 * j + 1])), neg_mx));
+        vs[j] = add2(vs[j], e);
+        rq[c][2 * j] = __float_as_uint(e.x);
+        rq[c][2 * j + 1] = __float_as_uint(e.y);
+      }
+      if constexpr (KPG == 8) tmem_st8(tl + t0 + 16 * c + ko, rq[c]);
+      else tmem_st4(tl + t0 + 16 * c + ko, rq[c]);
+    }
+  }
+  for (; t0 < L; t0 += 16) {
     if constexpr (KPG == 8) tmem_ld8(tl + t0 + ko, r);
     else tmem_ld4(tl + t0 + ko, r);
     tmem_ld_wait();
@@ -1176,7 +1198,24 @@ __global__ void __launch_bounds__(128 * NWG, MINB) k_attention_wide(AttnArgs a) 
   float2 acc[DPG];
 #pragma unroll
   for (int d = 0; d < DPG; ++d) acc[d] = f2(0.0f, 0.0f);
-  for (int t0 = 0; t0 < L; t0 += 16) {
+  for (t0 = 0; t0 + 32 <= L; t0 += 32) {  // two full chunks per TMEM round trip, keys in order
+    uint32_t rq[32];
+    tmem_ld16(tl + t0, rq);
+    tmem_ld16(tl + t0 + 16, rq + 16);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float2 p = mul2(f2(__uint_as_float(rq[2 * j]), __uint_as_float(rq[2 * j + 1])), inv2);
+      const float4* v4 = reinterpret_cast<const float4*>(vp + ((t0 >> 1) + j) * KPS + DPG * grp);
+#pragma unroll
+      for (int i = 0; i < DPG / 2; ++i) {
+        const float4 vv = v4[i];
+        acc[2 * i] = fma2(f2(vv.x, vv.y), p, acc[2 * i]);
+        acc[2 * i + 1] = fma2(f2(vv.z, vv.w), p, acc[2 * i + 1]);
+      }
+    }
+  }
+  for (; t0 < L; t0 += 16) {
     tmem_ld16(tl + t0, r);
     tmem_ld_wait();
 #pragma unroll
