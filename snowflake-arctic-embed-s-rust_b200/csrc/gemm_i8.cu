@@ -28,7 +28,8 @@
 //                  combined through shared memory with the reference's hsum256 tree.
 //   EPI_GELU_QUANT g = GELU(h) * inv_smooth, row max over all 1536 columns, row quantization
 //                  (FFN-up; gelu_smooth_quantize_row_avx2, src/simd_math.rs:1371-1435). A cluster
-//                  of 6 CTAs holds the 6 slices of 256 columns of the same 128 rows; each CTA sends
+//                  of 6 CTAs holds the 6 slices of 256 columns of the same 128 rows (12 CTAs of 128
+//                  columns when the batch has at most 12 row tiles); each CTA sends
 //                  its partial row maxima into its peers' shared memory with st.async, which
 //                  completes on the peers' mbarriers. GELU is the reference's rational
 //                  approximation (gelu_ref) or, on request, the exact erf.
@@ -55,7 +56,6 @@ constexpr int kThreads = (2 + kEpiWarps) * 32;
 constexpr int kTmemBar = 8;  // named barrier of the MMA and epilogue warps (the epilogue uses 1..4)
 constexpr int kResK = 384;         // K of the GEMMs whose weight slice stays resident
 constexpr int kResKB = kResK / BK;
-constexpr int kGeluCluster = 6;
 
 template <int BN, int EPI, bool RES, int STAGES>
 struct Layout {
@@ -67,7 +67,9 @@ struct Layout {
   static constexpr int STAGE = A_STAGE + (RES ? 0 : BN * BK);
   static constexpr int RING = STAGES * STAGE;
   static constexpr int PARAM_FLOATS = 3 * BN + 2 * kHidden;             // ws, bias, invs | gamma, beta
-  static constexpr int XCH_FLOATS_GELU = 2 * 4 * BM + 2 * kGeluCluster * BM;
+  // EPI_GELU_QUANT: the cluster holds the 1,536 columns of a tile as kInter / BN slices of BN columns
+  static constexpr int GCL = EPI == EPI_GELU_QUANT ? kInter / BN : 1;
+  static constexpr int XCH_FLOATS_GELU = 2 * 4 * BM + 2 * GCL * BM;
   static constexpr int STAGING_BYTES = EPI == EPI_GELU_QUANT ? kEpiWarps * 32 * 80 : 0;  // int8 output rows
   static constexpr int NBARS_ = 2 * STAGES + 1 + 2 * 2 + 2;
   // EPI_F32 with a row-major output: each epilogue warp transposes its 32 rows x STG_W columns through
@@ -364,7 +366,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int par = it & 1;
         const uint32_t rank = cluster_ctarank();
         float* xg = xch + par * 4 * BM;                           // [4][BM] maxima of the column quarters
-        float* rmx = xch + 2 * 4 * BM + par * kGeluCluster * BM;  // [6][BM] maxima of the cluster CTAs
+        float* rmx = xch + 2 * 4 * BM + par * Ly::GCL * BM;  // [GCL][BM] maxima of the cluster CTAs
         uint32_t r[16];
         float vmax = 1e-8f;
         if (ok) {
@@ -409,20 +411,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         xg[qq * BM + rt] = vmax;
         named_bar(1 + Q, 128);
         const float cta_max = fmaxf(fmaxf(xg[rt], xg[BM + rt]), fmaxf(xg[2 * BM + rt], xg[3 * BM + rt]));
-        if (ew == 0 && lane == 0) mbar_arrive_expect_tx(&rmx_bar[par], kGeluCluster * BM * 4);
+        if (ew == 0 && lane == 0) mbar_arrive_expect_tx(&rmx_bar[par], Ly::GCL * BM * 4);
         if (qq == 0) {
 #pragma unroll
-          for (uint32_t q = 0; q < kGeluCluster; ++q)
+          for (uint32_t q = 0; q < uint32_t(Ly::GCL); ++q)
             st_async_f32(map_peer(&rmx[rank * BM + rt], q), cta_max, map_peer(&rmx_bar[par], q));
         }
         if (ok) ok = mbar_wait(&rmx_bar[par], (it >> 1) & 1, g.err, DEV_ERR_TIMEOUT_EPILOGUE);
         float max_abs = rmx[rt];
 #pragma unroll
-        for (int q = 1; q < kGeluCluster; ++q) max_abs = fmaxf(max_abs, rmx[q * BM + rt]);
+        for (int q = 1; q < Ly::GCL; ++q) max_abs = fmaxf(max_abs, rmx[q * BM + rt]);
         const float inv_scale = 127.0f / max_abs;
         {
-          // quantize into this warp's staging slot (32 rows x 64 bytes, rows padded to 80 bytes),
-          // then write 8 rows x 64 contiguous bytes per store instruction
+          // quantize into this warp's staging slot (32 rows x CW bytes, rows padded to 80 bytes),
+          // then write 32 / (CW / 16) rows x CW contiguous bytes per store instruction
           uint8_t* stg = reinterpret_cast<uint8_t*>(xch + Ly::XCH_FLOATS_GELU) + ew * (32 * 80);
           if (ok) {
 #pragma unroll 1
@@ -442,9 +444,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[b]);
+          constexpr int PPR = CW / 16, RPI = 32 / PPR;  // 16-byte pieces per row, rows per instruction
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int rr = 8 * i + (lane >> 2), q = lane & 3;
+          for (int i = 0; i < 32 / RPI; ++i) {
+            const int rr = RPI * i + lane / PPR, q = lane % PPR;
             const int grow = m0 + Q * 32 + rr;
             const uint4 v = *reinterpret_cast<const uint4*>(stg + rr * 80 + 16 * q);
             if (ok && grow < g.M) *reinterpret_cast<uint4*>(g.out_q + size_t(grow) * g.N + n0 + c0 + 16 * q) = v;
@@ -780,7 +783,7 @@ static cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const Ge
   if constexpr (EPI == EPI_GELU_QUANT) {
     // nt == cluster size: the 6 CTAs of a cluster hold the 6 column slices of one 128-row tile
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = kGeluCluster;
+    attr[0].val.clusterDim.x = Ly::GCL;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.numAttrs = 1;
@@ -788,13 +791,13 @@ static cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const Ge
     int dev = 0;
     cudaGetDevice(&dev);
     if (!max_clusters[dev]) {
-      cfg.gridDim = dim3(kGeluCluster * 8, 1, 1);
+      cfg.gridDim = dim3(Ly::GCL * 8, 1, 1);
       int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, kfn, &cfg) != cudaSuccess || n <= 0) n = num_sms() / kGeluCluster;
+      if (cudaOccupancyMaxActiveClusters(&n, kfn, &cfg) != cudaSuccess || n <= 0) n = num_sms() / Ly::GCL;
       max_clusters[dev] = n;
     }
     const int clusters = mt < max_clusters[dev] ? mt : max_clusters[dev];
-    ctas = kGeluCluster * clusters;
+    ctas = Ly::GCL * clusters;
     cfg.numAttrs = 2;
   } else {
     cfg.attrs = attr + 1;
@@ -823,6 +826,13 @@ int gemm_i8_prime() {
   r |= set_smem<384, EPI_LN_FINAL, true, 3>();
   r |= set_smem<384, EPI_LN_FINAL, false, 3>();
   r |= set_smem<256, EPI_GELU_QUANT, true, 4>();
+  r |= set_smem<128, EPI_GELU_QUANT, true, 4>();
+  r |= set_smem<128, EPI_GELU_QUANT, false, 4>();
+  // 12-CTA clusters (128-column slices, few row tiles) exceed the portable cluster size of 8
+  r |= cudaFuncSetAttribute(k_gemm_i8<128, EPI_GELU_QUANT, true, 4>, cudaFuncAttributeNonPortableClusterSizeAllowed,
+                            1) == cudaSuccess ? 0 : -1;
+  r |= cudaFuncSetAttribute(k_gemm_i8<128, EPI_GELU_QUANT, false, 4>, cudaFuncAttributeNonPortableClusterSizeAllowed,
+                            1) == cudaSuccess ? 0 : -1;
   r |= set_smem<256, EPI_GELU_QUANT, false, 3>();
   return r;
 }
@@ -861,9 +871,17 @@ int gemm_i8_launch(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const 
       if (g.N != kHidden) return -11;
       e = res ? launch<384, EPI_LN_FINAL, true, 3>(ta, tb, g, st) : launch<384, EPI_LN_FINAL, false, 3>(ta, tb, g, st);
       break;
-    case EPI_GELU_QUANT:
-      if (g.N != kGeluCluster * 256) return -11;
-      e = res ? launch<256, EPI_GELU_QUANT, true, 4>(ta, tb, g, st) : launch<256, EPI_GELU_QUANT, false, 3>(ta, tb, g, st);
+    case EPI_GELU_QUANT: {
+      if (g.N != kInter) return -11;
+      // few row tiles: 12 slices of 128 columns (half the epilogue work per SM sub-partition);
+      // otherwise 6 slices of 256
+      const int mt = (g.M + BM - 1) / BM;
+      if (mt * (kInter / 128) <= num_sms())
+        e = res ? launch<128, EPI_GELU_QUANT, true, 4>(ta, tb, g, st) : launch<128, EPI_GELU_QUANT, false, 4>(ta, tb, g, st);
+      else
+        e = res ? launch<256, EPI_GELU_QUANT, true, 4>(ta, tb, g, st) : launch<256, EPI_GELU_QUANT, false, 3>(ta, tb, g, st);
+      break;
+    }
       break;
     default:
       return -12;

@@ -86,12 +86,13 @@ def test_ln_quant_in_place(engine):
     np.testing.assert_array_equal(d_as.cpu().numpy(), s_ref)
 
 
-@pytest.mark.parametrize("M", [1, 77, 128, 390])
+@pytest.mark.parametrize("M", [1, 77, 128, 390, 2000])
 def test_gelu_quant_epilogue(engine, M):
     """GELU + SmoothQuant + row quantization (gelu_smooth_quantize_row_avx2). The GPU restates the
     reference's rational GELU with a correctly rounded reciprocal where the reference uses the
     12-bit rcp_ps estimate, so the two agree to about one ulp: int8 outputs may differ by one
-    level at a rounding boundary (rarely), the row scales by at most a few ulp."""
+    level at a rounding boundary (rarely), the row scales by at most a few ulp. Up to 12 row
+    tiles the 1,536 columns are 12 slices of 128 (a 12-CTA cluster), beyond that 6 of 256."""
     K, N = 384, 1536
     a, w, a_s, w_s, b = make_case(M, K, N, 3 * M)
     inv_s = rng(M).uniform(0.5, 2.0, N).astype(np.float32)
