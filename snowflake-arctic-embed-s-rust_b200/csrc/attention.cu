@@ -899,17 +899,33 @@ constexpr int kLatMaxLen = 64;
 __host__ __device__ constexpr int lat_pitch(int L) { return ((L + 3) & ~3) + 1; }
 __host__ __device__ constexpr size_t lat_smem_bytes(int L, int QT) { return size_t(64 + QT) * lat_pitch(L) * 4; }
 
-template <int QT>
+//
+// QUANT: launched as clusters of the 12 heads of one (sequence, tile); the context rows are also
+// quantized here (smooth_quantize_row, src/simd_math.rs:584-649, as k_smooth_quant does): each
+// CTA sends its heads' partial row maxima max|ctx * inv_s| into every peer's shared memory with
+// st.async, then quantizes its 32 columns with the row's maximum over all 384.
+template <int QT, bool QUANT>
 __global__ void __launch_bounds__(4 * QT) k_attention_lat(AttnArgs a) {
   pdl_trigger();
-  pdl_wait();
   extern __shared__ float4 smem4[];
+  __shared__ float rmx[QUANT ? kHeads : 1][QT];  // QUANT: partial row maxima of the 12 heads
+  __shared__ uint64_t rbar;
   const int s = blockIdx.x;
   const int h = blockIdx.y;
   const int tile = blockIdx.z;
   const int tid = threadIdx.x;
+  if constexpr (QUANT) {  // the peers' barriers exist before any st.async
+    if (tid == 0) {
+      mbar_init(&rbar, 1);
+      fence_mbar_init();
+    }
+    cluster_arrive_release();
+    cluster_wait_acquire();
+  }
+  pdl_wait();
   const int s0 = int(a.cu[s]);
   const int L = int(a.cu[s + 1]) - s0;
+  // the 12 CTAs of a cluster share the sequence and the tile: these exits are cluster-uniform
   if (L <= 0 || L > a.max_len) {
     if (tid == 0 && tile == 0 && h == 0) record_err(a.err, DEV_ERR_BAD_SHAPE);
     return;
@@ -1024,10 +1040,44 @@ __global__ void __launch_bounds__(4 * QT) k_attention_lat(AttnArgs a) {
 #pragma unroll
     for (int k = 0; k < 8; ++k) acc_e[k] = fmaf(vrow[k * P + t], p0, acc_e[k]);
   }
-  if (active) {
-    float4* o = reinterpret_cast<float4*>(a.out + size_t(s0 + qi) * kHidden + h * 32 + 8 * sl);
-    o[0] = make_float4(acc_e[0] + acc_o[0], acc_e[1] + acc_o[1], acc_e[2] + acc_o[2], acc_e[3] + acc_o[3]);
-    o[1] = make_float4(acc_e[4] + acc_o[4], acc_e[5] + acc_o[5], acc_e[6] + acc_o[6], acc_e[7] + acc_o[7]);
+  float cx[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) cx[k] = acc_e[k] + acc_o[k];
+  if constexpr (!QUANT) {
+    if (active) {
+      float4* o = reinterpret_cast<float4*>(a.out + size_t(s0 + qi) * kHidden + h * 32 + 8 * sl);
+      o[0] = make_float4(cx[0], cx[1], cx[2], cx[3]);
+      o[1] = make_float4(cx[4], cx[5], cx[6], cx[7]);
+    }
+  } else {
+    const float* ivs = a.quant_inv_s + h * 32 + 8 * sl;
+    float vmax = 1e-8f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) vmax = fmaxf(vmax, fabsf(cx[k] * ivs[k]));
+    vmax = fmaxf(vmax, __shfl_xor_sync(full, vmax, 1));
+    vmax = fmaxf(vmax, __shfl_xor_sync(full, vmax, 2));
+    if (tid == 0) mbar_arrive_expect_tx(&rbar, kHeads * QT * 4);
+    if (sl == 0)
+      for (uint32_t pr = 0; pr < uint32_t(kHeads); ++pr)
+        st_async_f32(map_peer(&rmx[h][ql], pr), vmax, map_peer(&rbar, pr));
+    const bool got = mbar_wait(&rbar, 0, a.err, DEV_ERR_TIMEOUT_EPILOGUE);
+    float max_abs = rmx[0][ql];
+#pragma unroll
+    for (int g = 1; g < kHeads; ++g) max_abs = fmaxf(max_abs, rmx[g][ql]);
+    const float inv_scale = 127.0f / max_abs;
+    if (active && got) {
+      uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        w0 |= (uint32_t(quant_i8(cx[k] * (ivs[k] * inv_scale))) & 0xFFu) << (8 * k);
+        w1 |= (uint32_t(quant_i8(cx[4 + k] * (ivs[4 + k] * inv_scale))) & 0xFFu) << (8 * k);
+      }
+      *reinterpret_cast<uint2*>(a.quant_q + size_t(s0 + qi) * kHidden + h * 32 + 8 * sl) = make_uint2(w0, w1);
+      if (h == 0 && sl == 0) a.quant_scale[s0 + qi] = max_abs / 127.0f;
+    }
+    // no CTA leaves while a peer may still write into it
+    cluster_arrive_release();
+    cluster_wait_acquire();
   }
 }
 
@@ -1410,7 +1460,11 @@ int attention_prime() {
   r |= smem_attr((const void*)k_attention_wide<ATTN_WIDE_256>, rows_smem_cap(g_static_wide2));
   r |= smem_attr((const void*)k_attention_wide<4, 1>, rows_smem_cap(g_static_wide4));
   r |= smem_attr((const void*)k_attention_cls, cls_smem_floats(kMaxPos) * 4);
-  r |= smem_attr((const void*)k_attention_lat<32>, lat_smem_bytes(kMaxPos, 32));
+  r |= smem_attr((const void*)k_attention_lat<32, false>, lat_smem_bytes(kMaxPos, 32));
+  r |= smem_attr((const void*)k_attention_lat<32, true>, lat_smem_bytes(kMaxPos, 32));
+  // 12-CTA clusters (the heads of one sequence) exceed the portable cluster size of 8
+  r |= cudaFuncSetAttribute((const void*)k_attention_lat<32, true>, cudaFuncAttributeNonPortableClusterSizeAllowed,
+                            1) == cudaSuccess ? 0 : -1;
   r |= smem_attr((const void*)k_qkv_attention, kQaSmem);
   return r;
 }
@@ -1424,7 +1478,8 @@ int launch_qkv_attention(const CUtensorMap& tm_act, const CUtensorMap& tm_w, con
              : -3;
 }
 
-int launch_attention_exact(const AttnArgs& a, int n_seqs, cudaStream_t st) {
+int launch_attention_exact(const AttnArgs& a, int n_seqs, cudaStream_t st, int* quantized) {
+  if (quantized) *quantized = 0;
   if (n_seqs <= 0) return 0;
   if (a.max_len <= 0 || a.max_len > kMaxPos) return -1;
   if (a.cls_mode) {
@@ -1440,11 +1495,31 @@ int launch_attention_exact(const AttnArgs& a, int n_seqs, cudaStream_t st) {
   const int cap = a.max_len <= 32 ? 32 : a.max_len <= 64 ? 64 : 128;
   const long heads = long(n_seqs) * kHeads;
   // few (sequence, head) pairs of short sequences: four lanes per query, 32-query tiles, no TMEM
-  if (a.max_len <= kLatMaxLen && heads * ((a.max_len + 31) / 32) <= 2 * 148)
-    return launch_pdl(k_attention_lat<32>, dim3(n_seqs, kHeads, (a.max_len + 31) / 32), dim3(128),
-                      lat_smem_bytes(a.max_len, 32), st, a) == cudaSuccess
-               ? 0
-               : -3;
+  if (a.max_len <= kLatMaxLen && heads * ((a.max_len + 31) / 32) <= 2 * 148) {
+    const dim3 grid(n_seqs, kHeads, (a.max_len + 31) / 32);
+    if (!(quantized && a.quant_inv_s && a.quant_q && a.quant_scale))
+      return launch_pdl(k_attention_lat<32, false>, grid, dim3(128), lat_smem_bytes(a.max_len, 32), st, a) ==
+                     cudaSuccess
+                 ? 0
+                 : -3;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = lat_smem_bytes(a.max_len, 32);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = kHeads;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    if (cudaLaunchKernelEx(&cfg, k_attention_lat<32, true>, a) != cudaSuccess) return -3;
+    *quantized = 1;
+    return 0;
+  }
   if (a.max_len > 128) return launch_rows<128>(a, n_seqs, st);
 #ifndef ATTN_PAIRS
 #define ATTN_PAIRS 1

@@ -397,9 +397,18 @@ int gemm(ae_ctx* c, int epi, const CUtensorMap& ta, const DevLinear& L, int M, c
   return 0;
 }
 
+// quant (optional): {inverse smoothing factors, int8 rows, row scales} of the context rows; when
+// the launch quantized them itself *quantized is set to 1 and the caller skips k_smooth_quant.
+struct CtxQuant {
+  const float* inv_s;
+  int8_t* q;
+  float* scale;
+};
 int attention(ae_ctx* c, const float* q, int q_C, int q_col, int q_tt, const float* kv, int kv_C, int k_col,
               int v_col, int kv_tt, float* out, const uint32_t* cu, int n, int max_len, int cls,
-              const std::vector<AttnSegment>* segs = nullptr) {
+              const std::vector<AttnSegment>* segs = nullptr, const CtxQuant* quant = nullptr,
+              int* quantized = nullptr) {
+  if (quantized) *quantized = 0;
   AttnArgs a{};
   a.q = q;
   a.q_C = q_C;
@@ -415,6 +424,11 @@ int attention(ae_ctx* c, const float* q, int q_C, int q_col, int q_tt, const flo
   a.max_len = max_len;
   a.cls_mode = cls;
   a.err = c->d_err;
+  if (quant) {
+    a.quant_inv_s = quant->inv_s;
+    a.quant_q = quant->q;
+    a.quant_scale = quant->scale;
+  }
   if (segs && segs->size() > 1) {  // one launch per length class, sized for that class
     for (const AttnSegment& g : *segs) {
       AttnArgs b = a;
@@ -426,7 +440,8 @@ int attention(ae_ctx* c, const float* q, int q_C, int q_col, int q_tt, const flo
     return 0;
   }
   ++c->launches;
-  if (launch_attention_exact(a, n, c->stream)) return fail(c, AE_ERR_CUDA, "attention launch failed");
+  if (launch_attention_exact(a, n, c->stream, quant ? quantized : nullptr))
+    return fail(c, AE_ERR_CUDA, "attention launch failed");
   return 0;
 }
 
@@ -509,6 +524,7 @@ int enqueue_forward(ae_ctx* c, const uint16_t* d_ids, const uint32_t* d_cu, int 
   const bool fused = max_len <= 128 && c->fused_qkv == 1;
   for (int l = 0; l + 1 < kLayers; ++l) {
     const DevLayer& Ly = M.layers[l];
+    int ctx_quantized = 0;  // the attention kernel also wrote act_q / act_s
     if (fused) {
       ProfScope ps(c, AE_KERNEL_ATTENTION);
       QkvAttnArgs qa{};
@@ -530,12 +546,13 @@ int enqueue_forward(ae_ctx* c, const uint16_t* d_ids, const uint32_t* d_cu, int 
       }
       {
         ProfScope ps(c, AE_KERNEL_ATTENTION);
+        const CtxQuant cq{Ly.ao.inv_s, W.act_q, W.act_s};
         AE_TRY(attention(c, W.qkv, 3 * kHidden, 0, 1, W.qkv, 3 * kHidden, kHidden, 2 * kHidden, 1, W.ctx, d_cu, n,
-                         max_len, 0, segs));
+                         max_len, 0, segs, &cq, &ctx_quantized));
       }
     }
-    ++c->launches;
-    {
+    if (!ctx_quantized) {
+      ++c->launches;
       ProfScope ps(c, AE_KERNEL_CTX_QUANT);
       if (launch_smooth_quant(W.ctx, Ly.ao.inv_s, W.act_q, W.act_s, T, st))
         return fail(c, AE_ERR_CUDA, "context quantization launch failed");

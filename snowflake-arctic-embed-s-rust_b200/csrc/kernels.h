@@ -38,6 +38,11 @@ struct AttnArgs {
   int max_len;                // upper bound of any sequence length (<= 512)
   int cls_mode;               // 1: one query per sequence, at row s of q / out
   int* err;
+  // optional: where a launch that can quantize the context rows itself (the SmoothQuant row
+  // quantization of the next GEMM's input) writes them; see launch_attention_exact
+  const float* quant_inv_s;   // [384] inverse smoothing factors, or nullptr
+  int8_t* quant_q;            // [rows, 384]
+  float* quant_scale;         // [rows]
 };
 
 // Launch with programmatic stream serialization (the kernel calls pdl_wait before it touches data
@@ -80,7 +85,9 @@ struct AttnSegment {
 // columns a CTA allocates for its scores).
 constexpr int kAttnClasses = 5;
 inline int attn_class(int len) { return len <= 32 ? 0 : len <= 64 ? 1 : len <= 128 ? 2 : len <= 256 ? 3 : 4; }
-int launch_attention_exact(const AttnArgs& a, int n_seqs, cudaStream_t st);
+// quantized (optional): set to 1 when the launch also wrote the quantized context rows
+// (a.quant_*; the single-sequence path for at most 64 keys), else 0 (the caller quantizes).
+int launch_attention_exact(const AttnArgs& a, int n_seqs, cudaStream_t st, int* quantized = nullptr);
 
 // QKV projection fused with the attention (sequences of at most 128 keys): the int8 GEMM
 // fma(float(acc), a_scale[row] * w_scale[n], bias[n]) of one sequence's 128-row tile against the
