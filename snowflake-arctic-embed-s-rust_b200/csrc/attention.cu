@@ -1086,19 +1086,25 @@ __global__ void __launch_bounds__(4 * QT) k_attention_lat(AttnArgs a) {
 // every 16-key chunk (KPG = 16 / NWG), so each of the reference's 16 sum slots is summed in order
 // by one group; P.V: group g accumulates dims g DPG .. (g + 1) DPG - 1 (DPG = 32 / NWG) over all
 // keys in order.
-template <int NWG, int MINB>
+// DSPLIT > 1 (few (sequence, head) pairs: single sequences): blockIdx.z = tile * DSPLIT + part,
+// and CTA `part` runs the scores and exponentials of its tile (the same work in every part) but the
+// weighted sum only for dims part * 32 / DSPLIT .. + 32 / DSPLIT - 1, so a tile's attention spreads
+// over DSPLIT SMs.
+template <int NWG, int MINB, int DSPLIT = 1>
 __global__ void __launch_bounds__(128 * NWG, MINB) k_attention_wide(AttnArgs a) {
   pdl_trigger();
   pdl_wait();
-  constexpr int KPG = 16 / NWG;  // keys of a 16-key chunk per group (8 or 4)
-  constexpr int DPG = 32 / NWG;  // dims of V per group (16 or 8)
+  constexpr int KPG = 16 / NWG;           // keys of a 16-key chunk per group (8 or 4)
+  constexpr int DPG = 32 / NWG / DSPLIT;  // dims of V per group
+  static_assert(DPG >= 4, "a group's dims are stored as float4");
   extern __shared__ float4 smem4[];
   __shared__ uint32_t tmem_slot;
   __shared__ float xmx[NWG][128];
   __shared__ float xsl[16][128];  // the 16 slot sums of every query
   const int s = blockIdx.x;
   const int h = blockIdx.y;
-  const int tile = blockIdx.z;
+  const int tile = blockIdx.z / DSPLIT;
+  const int dbase = (blockIdx.z % DSPLIT) * (32 / DSPLIT);  // first dim of this CTA's weighted sum
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int grp = warp >> 2;
@@ -1256,7 +1262,7 @@ __global__ void __launch_bounds__(128 * NWG, MINB) k_attention_wide(AttnArgs a) 
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const float2 p = mul2(f2(__uint_as_float(rq[2 * j]), __uint_as_float(rq[2 * j + 1])), inv2);
-      const float4* v4 = reinterpret_cast<const float4*>(vp + ((t0 >> 1) + j) * KPS + DPG * grp);
+      const float4* v4 = reinterpret_cast<const float4*>(vp + ((t0 >> 1) + j) * KPS + dbase + DPG * grp);
 #pragma unroll
       for (int i = 0; i < DPG / 2; ++i) {
         const float4 vv = v4[i];
@@ -1273,7 +1279,7 @@ __global__ void __launch_bounds__(128 * NWG, MINB) k_attention_wide(AttnArgs a) 
       const int t = t0 + 2 * j;
       if (t + 1 < L) {
         const float2 p = mul2(f2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), inv2);
-        const float4* v4 = reinterpret_cast<const float4*>(vp + (t >> 1) * KPS + DPG * grp);
+        const float4* v4 = reinterpret_cast<const float4*>(vp + (t >> 1) * KPS + dbase + DPG * grp);
 #pragma unroll
         for (int i = 0; i < DPG / 2; ++i) {
           const float4 vv = v4[i];
@@ -1282,14 +1288,14 @@ __global__ void __launch_bounds__(128 * NWG, MINB) k_attention_wide(AttnArgs a) 
         }
       } else if (t < L) {  // odd L: the last key goes to the even accumulator
         const float pa = __uint_as_float(r[2 * j]) * inv;
-        const float2* v = vp + (t >> 1) * KPS + DPG * grp;
+        const float2* v = vp + (t >> 1) * KPS + dbase + DPG * grp;
 #pragma unroll
         for (int d = 0; d < DPG; ++d) acc[d].x = fmaf(v[d].x, pa, acc[d].x);
       }
     }
   }
   if (active) {
-    float4* o = reinterpret_cast<float4*>(a.out + size_t(s0 + qi) * kHidden + h * 32 + DPG * grp);
+    float4* o = reinterpret_cast<float4*>(a.out + size_t(s0 + qi) * kHidden + h * 32 + dbase + DPG * grp);
 #pragma unroll
     for (int i = 0; i < DPG / 4; ++i)
       o[i] = make_float4(acc[4 * i].x + acc[4 * i].y, acc[4 * i + 1].x + acc[4 * i + 1].y,
@@ -1414,14 +1420,29 @@ static size_t rows_smem(int max_len, size_t static_bytes) {
 template <int QT>
 static int launch_rows(const AttnArgs& a, int n_seqs, cudaStream_t st) {
   dim3 grid(n_seqs, kHeads, (a.max_len + QT - 1) / QT);
+  // few tiles (single sequences): each tile's weighted sum split by dims over 2 or 4 CTAs
+  const long units = long(grid.x) * grid.y * grid.z;
   if (QT == 128 && tmem_cols_for_len(a.max_len) == 256) {  // 2 CTAs per SM: two warpgroups each
-    return launch_pdl(k_attention_wide<ATTN_WIDE_256>, grid, dim3(128 * ATTN_WIDE_256_NWG),
-                      rows_smem(a.max_len, g_static_wide2), st, a) == cudaSuccess ? 0 : -3;
-  }
-  if (QT == 128 && tmem_cols_for_len(a.max_len) == 512) {  // 1 CTA per SM: four warpgroups
-    return launch_pdl(k_attention_wide<4, 1>, grid, dim3(512), rows_smem(a.max_len, g_static_wide4), st, a) == cudaSuccess
+    const size_t sm = rows_smem(a.max_len, g_static_wide2);
+    if (units * 4 <= 2 * 148) {
+      grid.z *= 4;
+      return launch_pdl(k_attention_wide<2, 2, 4>, grid, dim3(256), sm, st, a) == cudaSuccess ? 0 : -3;
+    }
+    if (units * 2 <= 2 * 148) {
+      grid.z *= 2;
+      return launch_pdl(k_attention_wide<2, 2, 2>, grid, dim3(256), sm, st, a) == cudaSuccess ? 0 : -3;
+    }
+    return launch_pdl(k_attention_wide<ATTN_WIDE_256>, grid, dim3(128 * ATTN_WIDE_256_NWG), sm, st, a) == cudaSuccess
                ? 0
                : -3;
+  }
+  if (QT == 128 && tmem_cols_for_len(a.max_len) == 512) {  // 1 CTA per SM: four warpgroups
+    const size_t sm = rows_smem(a.max_len, g_static_wide4);
+    if (units * 2 <= 148) {
+      grid.z *= 2;
+      return launch_pdl(k_attention_wide<4, 1, 2>, grid, dim3(512), sm, st, a) == cudaSuccess ? 0 : -3;
+    }
+    return launch_pdl(k_attention_wide<4, 1>, grid, dim3(512), sm, st, a) == cudaSuccess ? 0 : -3;
   }
   return launch_pdl(k_attention_rows<QT>, grid, dim3(QT), rows_smem(a.max_len, g_static_rows), st, a) == cudaSuccess ? 0 : -3;
 }
@@ -1459,6 +1480,9 @@ int attention_prime() {
   r |= smem_attr((const void*)k_attention_rows<32>, rows_smem_cap(g_static_rows));
   r |= smem_attr((const void*)k_attention_wide<ATTN_WIDE_256>, rows_smem_cap(g_static_wide2));
   r |= smem_attr((const void*)k_attention_wide<4, 1>, rows_smem_cap(g_static_wide4));
+  r |= smem_attr((const void*)k_attention_wide<4, 1, 2>, rows_smem_cap(g_static_wide4));
+  r |= smem_attr((const void*)k_attention_wide<2, 2, 2>, rows_smem_cap(g_static_wide2));
+  r |= smem_attr((const void*)k_attention_wide<2, 2, 4>, rows_smem_cap(g_static_wide2));
   r |= smem_attr((const void*)k_attention_cls, cls_smem_floats(kMaxPos) * 4);
   r |= smem_attr((const void*)k_attention_lat<32, false>, lat_smem_bytes(kMaxPos, 32));
   r |= smem_attr((const void*)k_attention_lat<32, true>, lat_smem_bytes(kMaxPos, 32));
