@@ -177,15 +177,21 @@ __host__ __device__ constexpr uint32_t tmem_cols_for_len(int L) {
 // the scores, then the exponentials, of its query in its TMEM lane (column t = key t), so shared
 // memory holds only the head's K / V pairs. Threads whose query lies past the sequence still take
 // part in the warp-collective TMEM loads and stores and write nothing.
-template <int QT>
+//
+// DSPLIT > 1 (few tiles: single sequences): blockIdx.z = tile * DSPLIT + part, and CTA `part`
+// repeats the scores and exponentials of its tile but runs the weighted sum only for dims
+// part * 32 / DSPLIT .. + 32 / DSPLIT - 1.
+template <int QT, int DSPLIT = 1>
 __global__ void __launch_bounds__(QT, 512 / QT) k_attention_rows(AttnArgs a) {
   pdl_trigger();
   pdl_wait();
+  constexpr int DN = 32 / DSPLIT;  // dims of this CTA's weighted sum
   extern __shared__ float4 smem4[];
   __shared__ uint32_t tmem_slot;
   const int s = blockIdx.x;
   const int h = blockIdx.y;
-  const int tile = blockIdx.z;
+  const int tile = blockIdx.z / DSPLIT;
+  const int dbase = (blockIdx.z % DSPLIT) * DN;
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int s0 = int(a.cu[s]);
@@ -305,9 +311,9 @@ __global__ void __launch_bounds__(QT, 512 / QT) k_attention_rows(AttnArgs a) {
   const float2 inv2 = f2(inv, inv);
 
   // pass 3: probabilities and the weighted sum of V; lane x = even keys (a), lane y = odd keys (b)
-  float2 acc[32];
+  float2 acc[DN];
 #pragma unroll
-  for (int d = 0; d < 32; ++d) acc[d] = f2(0.0f, 0.0f);
+  for (int d = 0; d < DN; ++d) acc[d] = f2(0.0f, 0.0f);
   for (int t0 = 0; t0 < L; t0 += 16) {
     tmem_ld16(tl + t0, r);
     tmem_ld_wait();
@@ -315,9 +321,9 @@ __global__ void __launch_bounds__(QT, 512 / QT) k_attention_rows(AttnArgs a) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const float2 p = mul2(f2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), inv2);
-        const float4* v4 = reinterpret_cast<const float4*>(vp + ((t0 >> 1) + j) * KPS);
+        const float4* v4 = reinterpret_cast<const float4*>(vp + ((t0 >> 1) + j) * KPS + dbase);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
+        for (int i = 0; i < DN / 2; ++i) {
           const float4 vv = v4[i];
           acc[2 * i] = fma2(f2(vv.x, vv.y), p, acc[2 * i]);
           acc[2 * i + 1] = fma2(f2(vv.z, vv.w), p, acc[2 * i + 1]);
@@ -330,25 +336,25 @@ __global__ void __launch_bounds__(QT, 512 / QT) k_attention_rows(AttnArgs a) {
       const int t = t0 + 2 * j;
       if (t + 1 < L) {
         const float2 p = mul2(f2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1])), inv2);
-        const float4* v4 = reinterpret_cast<const float4*>(vp + (t >> 1) * KPS);
+        const float4* v4 = reinterpret_cast<const float4*>(vp + (t >> 1) * KPS + dbase);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
+        for (int i = 0; i < DN / 2; ++i) {
           const float4 vv = v4[i];
           acc[2 * i] = fma2(f2(vv.x, vv.y), p, acc[2 * i]);
           acc[2 * i + 1] = fma2(f2(vv.z, vv.w), p, acc[2 * i + 1]);
         }
       } else if (t < L) {  // odd L: the last key goes to the even accumulator
         const float pa = __uint_as_float(r[2 * j]) * inv;
-        const float2* v = vp + (t >> 1) * KPS;
+        const float2* v = vp + (t >> 1) * KPS + dbase;
 #pragma unroll
-        for (int d = 0; d < 32; ++d) acc[d].x = fmaf(v[d].x, pa, acc[d].x);
+        for (int d = 0; d < DN; ++d) acc[d].x = fmaf(v[d].x, pa, acc[d].x);
       }
     }
   }
   if (active) {
-    float4* o = reinterpret_cast<float4*>(a.out + size_t(s0 + qi) * kHidden + h * 32);
+    float4* o = reinterpret_cast<float4*>(a.out + size_t(s0 + qi) * kHidden + h * 32 + dbase);
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
+    for (int i = 0; i < DN / 4; ++i)
       o[i] = make_float4(acc[4 * i].x + acc[4 * i].y, acc[4 * i + 1].x + acc[4 * i + 1].y,
                          acc[4 * i + 2].x + acc[4 * i + 2].y, acc[4 * i + 3].x + acc[4 * i + 3].y);
   }
@@ -1444,6 +1450,13 @@ static int launch_rows(const AttnArgs& a, int n_seqs, cudaStream_t st) {
     }
     return launch_pdl(k_attention_wide<4, 1>, grid, dim3(512), sm, st, a) == cudaSuccess ? 0 : -3;
   }
+  if (QT == 32 && units * 2 <= 2 * 148) {  // a 32-query tile holds 1 warp: several CTAs per SM
+    grid.z *= 2;
+    return launch_pdl(k_attention_rows<32, 2>, grid, dim3(32), rows_smem(a.max_len, g_static_rows), st, a) ==
+                   cudaSuccess
+               ? 0
+               : -3;
+  }
   return launch_pdl(k_attention_rows<QT>, grid, dim3(QT), rows_smem(a.max_len, g_static_rows), st, a) == cudaSuccess ? 0 : -3;
 }
 
@@ -1478,6 +1491,7 @@ int attention_prime() {
   r |= smem_attr((const void*)k_attention_rows<128>, rows_smem_cap(g_static_rows));
   r |= smem_attr((const void*)k_attention_rows<64>, rows_smem_cap(g_static_rows));
   r |= smem_attr((const void*)k_attention_rows<32>, rows_smem_cap(g_static_rows));
+  r |= smem_attr((const void*)k_attention_rows<32, 2>, rows_smem_cap(g_static_rows));
   r |= smem_attr((const void*)k_attention_wide<ATTN_WIDE_256>, rows_smem_cap(g_static_wide2));
   r |= smem_attr((const void*)k_attention_wide<4, 1>, rows_smem_cap(g_static_wide4));
   r |= smem_attr((const void*)k_attention_wide<4, 1, 2>, rows_smem_cap(g_static_wide4));
