@@ -19,6 +19,15 @@
 // k_attention_wide: the same with two or four warpgroups on one tile's TMEM lanes, for sequences
 // of more than 128 keys (whose score columns leave room for only 1-2 CTAs per SM).
 //
+// k_attention_rows2: two queries per thread and two heads per CTA for wide batches of 65-128 keys
+// (every staged K / V load feeds both queries).
+//
+// k_attention_lat: single sequences of at most 64 keys: four lanes per query, no TMEM, and
+// optionally the context quantization of the next GEMM's input (clusters of the 12 heads).
+//
+// For few tiles (single sequences) the TMEM kernels split a tile's weighted sum by dims over 2-4
+// CTAs, each repeating the tile's scores and exponentials, to spread the work over more SMs.
+//
 // k_attention_cls: one CTA per (sequence, head) for the single [CLS] query of layer 11: threads
 // split the keys for the scores (all K / V loads of a thread in flight at once), 16 lanes run the
 // 16 exp-sum chains, 64 threads the even / odd weighted-sum accumulators of the 32 dims.
@@ -476,7 +485,32 @@ __device__ __forceinline__ void attend_rows_dm(const float (&q)[NQ][32], const f
     for (int u = 0; u < NQ; ++u)
 #pragma unroll
       for (int j = 0; j < 4; ++j) vs0[u][j] = vs1[u][j] = f2(0.0f, 0.0f);
-    for (int t0 = 0; t0 < L; t0 += 16) {
+    int t0 = 0;
+    for (; t0 + 32 <= L16; t0 += 32) {  // two full chunks per TMEM round trip, summed in chunk order
+      uint32_t rb[NQ][32];
+#pragma unroll
+      for (int u = 0; u < NQ; ++u) {
+        tmem_ld16(tl + u * qcols + t0, rb[u]);
+        tmem_ld16(tl + u * qcols + t0 + 16, rb[u] + 16);
+      }
+      tmem_ld_wait();
+#pragma unroll
+      for (int u = 0; u < NQ; ++u) {
+        const float2 neg_mx = f2(-mx[u], -mx[u]);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float2 e =
+              cw_exp2(add2(f2(__uint_as_float(rb[u][2 * j]), __uint_as_float(rb[u][2 * j + 1])), neg_mx));
+          if ((j & 7) < 4) vs0[u][j & 3] = add2(vs0[u][j & 3], e);
+          else vs1[u][j & 3] = add2(vs1[u][j & 3], e);
+          rb[u][2 * j] = __float_as_uint(e.x);
+          rb[u][2 * j + 1] = __float_as_uint(e.y);
+        }
+        tmem_st16(tl + u * qcols + t0, rb[u]);
+        tmem_st16(tl + u * qcols + t0 + 16, rb[u] + 16);
+      }
+    }
+    for (; t0 < L; t0 += 16) {
 #pragma unroll
       for (int u = 0; u < NQ; ++u) tmem_ld16(tl + u * qcols + t0, r[u]);
       tmem_ld_wait();
