@@ -485,32 +485,7 @@ __device__ __forceinline__ void attend_rows_dm(const float (&q)[NQ][32], const f
     for (int u = 0; u < NQ; ++u)
 #pragma unroll
       for (int j = 0; j < 4; ++j) vs0[u][j] = vs1[u][j] = f2(0.0f, 0.0f);
-    int t0 = 0;
-    for (; t0 + 32 <= L16; t0 += 32) {  // two full chunks per TMEM round trip, summed in chunk order
-      uint32_t rb[NQ][32];
-#pragma unroll
-      for (int u = 0; u < NQ; ++u) {
-        tmem_ld16(tl + u * qcols + t0, rb[u]);
-        tmem_ld16(tl + u * qcols + t0 + 16, rb[u] + 16);
-      }
-      tmem_ld_wait();
-#pragma unroll
-      for (int u = 0; u < NQ; ++u) {
-        const float2 neg_mx = f2(-mx[u], -mx[u]);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float2 e =
-              cw_exp2(add2(f2(__uint_as_float(rb[u][2 * j]), __uint_as_float(rb[u][2 * j + 1])), neg_mx));
-          if ((j & 7) < 4) vs0[u][j & 3] = add2(vs0[u][j & 3], e);
-          else vs1[u][j & 3] = add2(vs1[u][j & 3], e);
-          rb[u][2 * j] = __float_as_uint(e.x);
-          rb[u][2 * j + 1] = __float_as_uint(e.y);
-        }
-        tmem_st16(tl + u * qcols + t0, rb[u]);
-        tmem_st16(tl + u * qcols + t0 + 16, rb[u] + 16);
-      }
-    }
-    for (; t0 < L; t0 += 16) {
+    for (int t0 = 0; t0 < L; t0 += 16) {
 #pragma unroll
       for (int u = 0; u < NQ; ++u) tmem_ld16(tl + u * qcols + t0, r[u]);
       tmem_ld_wait();
