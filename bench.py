@@ -254,7 +254,7 @@ def measure_fp32_peak() -> float:
 def microbench(eng, stream, peaks: dict) -> dict:
     """Config 5: the four int8 GEMM shapes x M in {512, 8192, 65536} (plain dequant epilogue, and the
     fused model epilogue where the shape has one) and the masked attention over 64 x 12 x 512 x 32
-    fp32. CUDA events on the launch stream, median of 5 after warm-up, L2 flushed before each."""
+    (fp32 in the reference's order, and the reference's int8 scheme). CUDA events on the launch stream, median of 5 after warm-up, L2 flushed before each."""
     import torch
 
     hbm = peaks.get("hbm_gbs", 6650.0)
@@ -323,6 +323,9 @@ def microbench(eng, stream, peaks: dict) -> dict:
     fl = n * 12 * 2.0 * 2.0 * L * L * 32
     out["attention"] = {"shape": "64 x 12 heads x 512 x 32, fp32, exact reference order", "ms": ms,
                         "tflops": fl / ms / 1e9}
+    ms8 = timed(lambda: eng.attention_i8(qkv, cu, n, L, ctx))
+    out["attention_int8"] = {"shape": "64 x 12 heads x 512 x 32, the reference's int8 scheme (dp4a Q.K, dp2a P.V)",
+                             "ms": ms8, "int_tops": fl / ms8 / 1e9}
     out["basis"] = (f"roofline_ms = max(ops / int8 peak (2 x measured bf16 = {i8peak:.0f} TOPS), bytes / measured "
                     f"HBM {hbm} GB/s); frac = roofline_ms / ms")
     return out
@@ -365,6 +368,9 @@ def main() -> int:
     ap.add_argument("--no-extras", action="store_true", help="skip latency, kernel breakdown and CPU baseline")
     ap.add_argument("--micro", action="store_true", help="also run the config-5 kernel microbenchmarks")
     ap.add_argument("--ragged", action="store_true", help="also run config 4 (131,072 ragged sequences)")
+    ap.add_argument("--attention", default="exact", choices=["exact", "int8"],
+                    help="attention of layers 0-10: fp32 in the reference's x86 order (default) or the "
+                         "reference's int8 scheme (ae_set_attention_mode)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -398,6 +404,10 @@ def main() -> int:
 
     pack = synth.pack_path(0)
     eng = Engine(local).load_file(pack)
+    if args.attention == "int8":
+        from arctic_embed_s_int8 import ATTENTION_INT8
+
+        eng.set_attention_mode(ATTENTION_INT8)
     stream = torch.cuda.Stream()
     eng.set_stream(stream)
     n_batches = args.warmup + args.steps
@@ -452,12 +462,15 @@ def main() -> int:
     result = {
         "metric": METRIC, "value": value, "unit": "embeddings/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * total_s / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8 GEMM (int32 acc) / fp32 elementwise+attention",
+        "scaling": "weak", "vs_baseline": None,
+        "dtype": ("int8 GEMM (int32 acc) / fp32 elementwise+attention" if args.attention == "exact" else
+                  "int8 GEMM (int32 acc) / fp32 elementwise / int8 attention (the reference's SME scheme)"),
         "data": "synthetic (seeded .ae8 pack, random-init arctic-embed-s weights; token ids [CLS]+U[1000,30521]+[SEP])",
         "config": {"workload": "config 3: batches of 512 sequences x 128 tokens per GPU, one batch per step",
                    "global_batch": world * BATCH_SEQS, "seq_len": SEQ_LEN, "tokens_per_step_per_gpu": T,
                    "parallelism": f"data-parallel shards x{world}, no collective",
-                   "l2": "flushed (256 MB write) between timed steps, outside the step events"},
+                   "l2": "flushed (256 MB write) between timed steps, outside the step events",
+                   "attention": args.attention},
         "e2e": {"value": e2e, "unit": "embeddings/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "api": "ae_forward_ragged (host ids in, host embeddings out; wall clock)"},
         "gpu_launches": int(launches),

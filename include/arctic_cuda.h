@@ -145,6 +145,26 @@ int ae_gemm_i8(ae_ctx* ctx, int epi, uint32_t M, uint32_t N, uint32_t K, const i
 int ae_attention_f32(ae_ctx* ctx, const float* d_qkv, const uint32_t* d_cu_seqlens, uint32_t n_seqs,
                      uint32_t max_len, float* d_ctx);
 
+/* Attention of layers 0-10 (no counterpart in the reference's API: the crate picks its attention by
+ * SIMD backend, src/model.rs:245 and :608):
+ *   AE_ATTENTION_EXACT (default): fp32 in the operation order of the reference's x86 kernels.
+ *   AE_ATTENTION_INT8: the reference's int8 scheme of its SME backend (attention_heads_sme,
+ *     src/simd_math.rs:1933-2186: per-token int8 Q / K, per-column int8 V, 14-bit integer exp2
+ *     probabilities, int32 products) for every sequence of at least 16 tokens, with scales taken
+ *     over each sequence's own keys (what forward_cls computes for it alone); shorter sequences and
+ *     the layer-11 [CLS] row stay fp32, as in the reference. Results differ from the fp32 mode by
+ *     about 4e-5 in cosine.
+ * The environment variable ARCTIC_ATTN=int8 selects the int8 scheme for new contexts.
+ * Changing the mode drops the context's captured single-sequence graphs. */
+enum { AE_ATTENTION_EXACT = 0, AE_ATTENTION_INT8 = 1 };
+int ae_set_attention_mode(ae_ctx* ctx, int mode);
+int ae_get_attention_mode(const ae_ctx* ctx);
+
+/* The int8 scheme on device buffers, every sequence (any length 1..512), same layout as
+ * ae_attention_f32. */
+int ae_attention_i8(ae_ctx* ctx, const float* d_qkv, const uint32_t* d_cu_seqlens, uint32_t n_seqs,
+                    uint32_t max_len, float* d_ctx);
+
 /* Allocation-free variant of the single-sequence forward, for callers that cannot call cudaMalloc
  * when they embed: code recording into a CUDA graph it is capturing, hosts that hand out device
  * memory once at start-up from their own pool, latency paths that must not wait on the allocator.

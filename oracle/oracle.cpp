@@ -9,6 +9,7 @@
 
 #include <immintrin.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdio>
@@ -64,6 +65,7 @@ struct or_model {
   std::vector<float> type0;  // pre-dequantized token_type_embeddings[0], src/model.rs:50-54
   std::vector<float> emb_lnw, emb_lnb;
   Layer layers[NL];
+  int attn_mode = OR_ATTENTION_EXACT;  // or_model_set_attention_mode
 };
 
 namespace {
@@ -608,6 +610,104 @@ void attend(const float* q, const float* k_head, const float* v_head, size_t L, 
   }
 }
 
+// ------------------------------------------------------------------------------------------ int8 attention
+// The reference's int8 attention scheme, attention_heads_sme (src/simd_math.rs:1933-2186), which
+// the crate runs on its SME backend for layers 0-10 (src/model.rs:245, :608):
+//   pack_qkv_head_int8_neon (:2564-2800): Q and K rows of a head quantized per token with
+//     quantize_head32_row_neon (:2482-2527), the K scale carrying 1/sqrt(32) * log2(e) so that the
+//     softmax runs in base 2; V quantized per column (:2598-2640, quantize_v_row_neon :2530-2561);
+//   Q.K^T as int32 dot products, dequantized as (acc * k_scale) * q_scale
+//     (softmax_quantize_i16_from_acc_neon :2291-2336);
+//   softmax_exp2_quantize_pass_i16_neon (:2379-2410): q = round(16383 * 2^(s - max)) through
+//     exp2_q_neon (:2353-2366) for the row's complete 8-key blocks and through exp2 + round for
+//     the last len % 8 keys, p_scale = 1 / sum(q);
+//   P.V as int32 dot products of the 14-bit q with the int8 V, ctx = acc * (v_scale * p_scale).
+// Every step is elementwise or an integer sum, so this scalar restatement gives the NEON lanes'
+// values whatever the order. Scales are taken over one sequence's keys: what forward_cls computes
+// for that sequence on its own.
+inline int8_t sat_i8(int32_t v) { return int8_t(v < -128 ? -128 : v > 127 ? 127 : v); }
+inline int32_t rn_even(float x) { return int32_t(std::nearbyint(x)); }  // vcvtnq_s32_f32
+
+// quantize_head32_row_neon: q = sat(rn(x * (127 / m))), m = max(1e-8, max |x|); returns (m / 127) * mul
+float quant_head_row(const float* x, float mul, int8_t* q) {
+  float m = 0.0f;
+  for (size_t d = 0; d < HD; ++d) m = std::max(m, std::fabs(x[d]));
+  m = std::max(m, 1e-8f);
+  const float inv = 127.0f / m;
+  for (size_t d = 0; d < HD; ++d) q[d] = sat_i8(rn_even(x[d] * inv));
+  return (m / 127.0f) * mul;
+}
+
+// exp2_q_neon(x, 16383, -16): round(16383 * 2^x) for x <= 0, degree-3 polynomial for 2^f on
+// [0, 1) and the integer part added to the exponent field.
+int32_t exp2_q16383(float x) {
+  const float scale = 16383.0f;
+  x = std::max(x, -16.0f);
+  const int32_t n = int32_t(std::floor(x));
+  const float f = x - float(n);
+  float p = std::fma(f, 0.07842169f * scale, 0.22511937f * scale);
+  p = std::fma(f, p, 0.6963853f * scale);
+  p = std::fma(f, p, 0.999857f * scale);
+  uint32_t b;
+  std::memcpy(&b, &p, 4);
+  b += uint32_t(n) << 23;
+  std::memcpy(&p, &b, 4);
+  return rn_even(p);
+}
+
+// One sequence of L keys: qkv rows (stride 3 * 384: Q | K | V) -> ctx rows (stride 384).
+void attention_i8_seq(const float* qkv, size_t L, float* ctx) {
+  const float k_mul = (1.0f / std::sqrt(32.0f)) * 1.44269504088896341f;  // inv_sqrt_d * LOG2_E
+  std::vector<int8_t> qq(L * HD), kq(L * HD), vq(L * HD);
+  std::vector<float> qs(L), ks(L), s(L);
+  std::vector<int32_t> p(L);
+  for (size_t h = 0; h < NH; ++h) {
+    const size_t ho = h * HD;
+    float vm[HD], v_scale[HD], v_inv[HD];
+    for (size_t c = 0; c < HD; ++c) vm[c] = 1e-8f;
+    for (size_t t = 0; t < L; ++t)
+      for (size_t c = 0; c < HD; ++c) vm[c] = std::max(vm[c], std::fabs(qkv[t * 3 * H + 2 * H + ho + c]));
+    for (size_t c = 0; c < HD; ++c) {
+      v_scale[c] = vm[c] * (1.0f / 127.0f);
+      v_inv[c] = 127.0f / vm[c];
+    }
+    for (size_t t = 0; t < L; ++t) {
+      const float* row = qkv + t * 3 * H;
+      for (size_t c = 0; c < HD; ++c) vq[t * HD + c] = sat_i8(rn_even(row[2 * H + ho + c] * v_inv[c]));
+      qs[t] = quant_head_row(row + ho, 1.0f, &qq[t * HD]);
+      ks[t] = quant_head_row(row + H + ho, k_mul, &kq[t * HD]);
+    }
+    const size_t vec_end = L - L % 8;
+    for (size_t i = 0; i < L; ++i) {
+      float mx = -INFINITY;
+      for (size_t j = 0; j < L; ++j) {
+        int32_t acc = 0;
+        for (size_t d = 0; d < HD; ++d) acc += int32_t(qq[i * HD + d]) * int32_t(kq[j * HD + d]);
+        s[j] = (float(acc) * ks[j]) * qs[i];
+        mx = std::max(mx, s[j]);
+      }
+      int32_t isum = 0;
+      for (size_t j = 0; j < L; ++j) {
+        int32_t q;
+        if (j < vec_end) {
+          q = exp2_q16383(s[j] - mx);
+        } else {
+          const int32_t e = int32_t(std::round(std::exp2(s[j] - mx) * 16383.0f));
+          q = e < 0 ? 0 : e > 16383 ? 16383 : e;
+        }
+        p[j] = q;
+        isum += q;
+      }
+      const float p_scale = 1.0f / float(std::max(isum, 1));
+      for (size_t c = 0; c < HD; ++c) {
+        int32_t acc = 0;
+        for (size_t j = 0; j < L; ++j) acc += p[j] * int32_t(vq[j * HD + c]);
+        ctx[i * H + ho + c] = float(acc) * (v_scale[c] * p_scale);
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------------------------------ forward
 // Workspace, src/model.rs:123-173
 struct Workspace {
@@ -666,7 +766,14 @@ void layers_0_10(const or_model& m, Workspace& ws, size_t total, const std::vect
     if (tr && tr->gemm_in_s) std::memcpy(tr->gemm_in_s + l * total, ws.act_scale.data(), total * 4);
     gemm(total, ws.act_q.data(), ws.scratch, ws.act_scale.data(), ly.qkv, nullptr, ws.qkv.data());
     if (tr && tr->qkv_out) std::memcpy(tr->qkv_out + l * total * 3 * H, ws.qkv.data(), total * 3 * H * 4);
-    for (auto& sg : segs) attention_segment(ws, sg.first, sg.second - sg.first);
+    for (auto& sg : segs) {
+      const size_t L = sg.second - sg.first;
+      // int8 mode: the reference's crossover for one sequence (src/model.rs:245), per sequence
+      if (m.attn_mode == OR_ATTENTION_INT8 && L >= 16)
+        attention_i8_seq(ws.qkv.data() + sg.first * 3 * H, L, ws.ctx.data() + sg.first * H);
+      else
+        attention_segment(ws, sg.first, L);
+    }
     if (tr && tr->ctx) std::memcpy(tr->ctx + l * total * H, ws.ctx.data(), total * H * 4);
     for (size_t t = 0; t < total; ++t)
       ws.act_scale[t] = smooth_quant(ws.ctx.data() + t * H, ly.attn_out.inv_s.data(), ws.act_q.data() + t * H, H);
@@ -1052,6 +1159,14 @@ void or_l2_normalize(float* x, uint32_t n) { l2_normalize(x, n); }
 void or_attention_query(const float* q32, const float* k, const float* v, uint32_t L, float* out32) {
   std::vector<float> scores(L > 0 ? L : 1);
   attend(q32, k, v, L, scores.data(), out32);
+}
+int or_model_set_attention_mode(or_model* m, int mode) {
+  if (mode != OR_ATTENTION_EXACT && mode != OR_ATTENTION_INT8) return -1;
+  m->attn_mode = mode;
+  return 0;
+}
+void or_attention_i8(const float* qkv, uint32_t L, float* ctx) {
+  if (L > 0) attention_i8_seq(qkv, L, ctx);
 }
 void or_gelu_ref(const float* x, float* y, uint32_t n) {
   for (uint32_t i = 0; i < n; ++i) y[i] = g_avx2_fma ? gelu_lane(x[i]) : scalar_gelu(x[i]);

@@ -69,6 +69,15 @@ void or_l2_normalize(float* x, uint32_t n);
 /* One attention head for one query: compute_scores_head32 + softmax_inplace + weighted_sum_head32. */
 void or_attention_query(const float* q32, const float* k_head, const float* v_head, uint32_t seq_len,
                         float* out32);
+/* Attention of layers 0-10: the reference's x86 fp32 kernels (OR_ATTENTION_EXACT, the default), or
+ * its int8 scheme (attention_heads_sme, src/simd_math.rs:1933-2186) for every sequence of at least
+ * 16 tokens (OR_ATTENTION_INT8; shorter ones and the layer-11 [CLS] row stay fp32, as in
+ * src/model.rs:245 and :427-450), with scales over each sequence's own keys. Returns -1 for an
+ * unknown mode. */
+enum { OR_ATTENTION_EXACT = 0, OR_ATTENTION_INT8 = 1 };
+int or_model_set_attention_mode(or_model* m, int mode);
+/* The int8 scheme on one sequence: qkv [L][1152] row-major (Q | K | V) -> ctx [L][384]. */
+void or_attention_i8(const float* qkv, uint32_t L, float* ctx);
 /* The AVX2 GELU approximation of the reference (avx2_gelu_f32), elementwise. */
 void or_gelu_ref(const float* x, float* y, uint32_t n);
 

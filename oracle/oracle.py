@@ -18,6 +18,7 @@ BACKEND_AVX_VNNI = 5
 BACKEND_AVX2 = 6
 BACKEND_SCALAR = 7
 H = 384
+ATTENTION_EXACT, ATTENTION_INT8 = 0, 1  # or_model_set_attention_mode
 
 _lib = None
 
@@ -60,6 +61,8 @@ def lib():
     L.or_l2_normalize.argtypes = [f32p, C.c_uint32]
     L.or_attention_query.argtypes = [f32p, f32p, f32p, C.c_uint32, f32p]
     L.or_gelu_ref.argtypes = [f32p, f32p, C.c_uint32]
+    L.or_model_set_attention_mode.argtypes = [P, C.c_int]
+    L.or_attention_i8.argtypes = [f32p, C.c_uint32, f32p]
     _lib = L
     return L
 
@@ -109,6 +112,12 @@ class OracleModel:
         if getattr(self, "_h", None):
             lib().or_model_free(self._h)
             self._h = None
+
+    def set_attention_mode(self, mode: int) -> "OracleModel":
+        """ATTENTION_EXACT (fp32, the default) or ATTENTION_INT8 (the reference's int8 scheme)."""
+        if lib().or_model_set_attention_mode(self._h, int(mode)) != 0:
+            raise ValueError(f"unknown attention mode {mode}")
+        return self
 
     def forward_cls(self, ids) -> np.ndarray:
         ids = np.ascontiguousarray(ids, dtype=np.uint16)
@@ -199,6 +208,14 @@ def attention_query(q32, k_head, v_head):
     q32, k, v = (np.ascontiguousarray(a, np.float32) for a in (q32, k_head, v_head))
     out = np.zeros(32, np.float32)
     lib().or_attention_query(_p(q32, C.c_float), _p(k, C.c_float), _p(v, C.c_float), k.shape[0], _p(out, C.c_float))
+    return out
+
+
+def attention_i8(qkv):
+    """The reference's int8 attention scheme on one sequence: qkv [L, 1152] -> ctx [L, 384]."""
+    qkv = np.ascontiguousarray(qkv, np.float32)
+    out = np.zeros((qkv.shape[0], H), np.float32)
+    lib().or_attention_i8(_p(qkv, C.c_float), qkv.shape[0], _p(out, C.c_float))
     return out
 
 

@@ -21,10 +21,12 @@ MAX_POSITIONS = 512
 MODEL_FILE = "model.ae8"
 VOCAB_FILE = "vocab.txt"
 MODEL_DIR_ENV_VAR = "ARCTIC_EMBED_MODEL_DIR"
+# attention of layers 0-10 (ae_set_attention_mode): fp32 in the reference's x86 order, or its int8 scheme
+ATTENTION_EXACT, ATTENTION_INT8 = 0, 1
 
 __all__ = [
     "AeError", "Engine", "ArcticEmbedS", "Workspace", "ParallelContext", "cosine_similarity", "default_model_dir",
-    "embed_batch_multi", "pack_sequences", "plan_shards", "HIDDEN_SIZE",
+    "embed_batch_multi", "pack_sequences", "plan_shards", "HIDDEN_SIZE", "ATTENTION_EXACT", "ATTENTION_INT8",
 ]
 
 
@@ -171,6 +173,19 @@ class Engine:
 
     def attention_f32(self, qkv, cu, n_seqs: int, max_len: int, ctx) -> None:
         self._check(lib().ae_attention_f32(self._h, _ptr(qkv), _ptr(cu), n_seqs, max_len, _ptr(ctx)))
+
+    def attention_i8(self, qkv, cu, n_seqs: int, max_len: int, ctx) -> None:
+        """ae_attention_i8: the reference's int8 attention scheme on device buffers (every sequence)."""
+        self._check(lib().ae_attention_i8(self._h, _ptr(qkv), _ptr(cu), n_seqs, max_len, _ptr(ctx)))
+
+    def set_attention_mode(self, mode: int) -> "Engine":
+        """ATTENTION_EXACT (fp32, default) or ATTENTION_INT8 (the reference's int8 scheme) for layers 0-10."""
+        self._check(lib().ae_set_attention_mode(self._h, int(mode)))
+        return self
+
+    @property
+    def attention_mode(self) -> int:
+        return int(lib().ae_get_attention_mode(self._h))
 
     def sync(self) -> None:
         self._check(lib().ae_sync(self._h))

@@ -33,7 +33,7 @@ SYMBOLS = [
     "ae_plan_shards", "ae_forward_cls_noalloc", "ae_profile", "ae_profile_read", "ae_sync",
     "ae_tokenizer_create_from_file", "ae_tokenizer_create_from_vocab", "ae_tokenizer_destroy",
     "ae_tokenizer_vocab_size", "ae_tokenizer_last_error", "ae_tokenize", "ae_tokenize_batch",
-    "ae_selftest_wait_timeout",
+    "ae_selftest_wait_timeout", "ae_set_attention_mode", "ae_get_attention_mode", "ae_attention_i8",
 ]
 
 
@@ -102,6 +102,9 @@ def lib():
     L.ae_embed_batch_multi.argtypes = [C.POINTER(P), C.c_int, P, P, u32, u32, P]
     L.ae_gemm_i8.argtypes = [P, C.c_int, u32, u32, u32] + [P] * 13
     L.ae_attention_f32.argtypes = [P, P, P, u32, u32, P]
+    L.ae_attention_i8.argtypes = [P, P, P, u32, u32, P]
+    L.ae_set_attention_mode.argtypes = [P, C.c_int]
+    L.ae_get_attention_mode.argtypes = [P]
     L.ae_sync.argtypes = [P]
     L.ae_kernel_launches.argtypes = [P]
     L.ae_plan_shards.argtypes = [P, u32, C.c_int, P]

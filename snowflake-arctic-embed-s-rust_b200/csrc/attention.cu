@@ -1525,6 +1525,225 @@ int launch_qkv_attention(const CUtensorMap& tm_act, const CUtensorMap& tm_w, con
              : -3;
 }
 
+// ------------------------------------------------------------------------------------------ int8 mode
+// The reference's int8 attention scheme (attention_heads_sme, src/simd_math.rs:1933-2186; run by the
+// crate on its SME backend for layers 0-10 of sequences of at least 16 tokens, src/model.rs:245):
+//   Q and K rows of a head quantized per token (quantize_head32_row_neon :2482-2527), the K scale
+//   carrying 1/sqrt(32) * log2(e); V quantized per column over the sequence's keys (:2598-2640);
+//   scores s = (int32 Q.K * k_scale) * q_scale (softmax_quantize_i16_from_acc_neon :2291-2336);
+//   q = round(16383 * 2^(s - max)) by exp2_q_neon (:2353-2366) for the row's complete 8-key blocks
+//   and by exp2 + round for the last len % 8 keys (softmax_exp2_quantize_pass_i16_neon :2379-2410);
+//   ctx = int32 (q . V) * (v_scale * (1 / sum q)).
+// Every step is elementwise or an integer sum, so any order gives the reference's values: the
+// integer products run as dp4a (Q.K, 4 dims a step) and dp2a (14-bit q times int8 V, 2 keys a step).
+//
+// k_attention_i8: one CTA per (sequence, head, 64 queries), 8 warps. The CTA quantizes the head's
+// K rows, V columns and its queries into shared memory; then each warp takes one query at a time:
+// lanes split the keys for the scores and the exponentials (kept in registers, 16 keys a lane at
+// most), the integer probabilities go to the warp's shared row, and lane c sums column c of P.V.
+constexpr int kI8Queries = 64;
+constexpr int kI8Threads = 256;
+constexpr int kI8VPitch = kMaxPos / 4 + 1;  // words per V column (+1: the 32 lanes hit 32 banks)
+
+struct I8Smem {
+  int4 ka[kMaxPos];             // key j, dims 0-15 as int8
+  int4 kb[kMaxPos];             // dims 16-31
+  float ks[kMaxPos];            // key scales (with 1/sqrt(32) * log2 e)
+  int4 qa[kI8Queries], qb[kI8Queries];
+  float qs[kI8Queries];
+  int vq[kHeadDim * kI8VPitch];  // column c: byte j of word c * pitch + j / 4 = key j
+  float v_scale[kHeadDim], v_inv[kHeadDim];
+  int2 p[kI8Threads / 32][kMaxPos / 4];  // a warp's 14-bit probabilities, 4 keys (int16) an int2
+};
+
+// quantize_head32_row_neon: q = sat(rn(x * (127 / m))), m = max(1e-8, max |x|); returns (m / 127) * mul.
+__device__ __forceinline__ float i8_quant_head_row(const float (&x)[32], float mul, int4& lo, int4& hi) {
+  float m = 0.0f;
+#pragma unroll
+  for (int d = 0; d < 32; ++d) m = fmaxf(m, fabsf(x[d]));
+  m = fmaxf(m, 1e-8f);
+  const float inv = __fdiv_rn(127.0f, m);
+  uint32_t w[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) w[i] = 0u;
+#pragma unroll
+  for (int d = 0; d < 32; ++d) {
+    const int v = max(-128, min(127, __float2int_rn(__fmul_rn(x[d], inv))));
+    w[d >> 2] |= (uint32_t(v) & 0xffu) << (8 * (d & 3));
+  }
+  lo = make_int4(int(w[0]), int(w[1]), int(w[2]), int(w[3]));
+  hi = make_int4(int(w[4]), int(w[5]), int(w[6]), int(w[7]));
+  return __fmul_rn(__fdiv_rn(m, 127.0f), mul);
+}
+
+// The 32 values of row t, columns c0 .. c0+31 (tile-transposed or row-major activations).
+__device__ __forceinline__ void i8_load_head_row(const float* base, int C, int tt, int t, int c0, float (&x)[32]) {
+  if (tt) {
+    const float* p = base + tt_index(t, c0, C);
+#pragma unroll
+    for (int d = 0; d < 32; ++d) x[d] = p[size_t(d) << 7];
+  } else {
+    const float4* p = reinterpret_cast<const float4*>(base + size_t(t) * C + c0);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 v = p[i];
+      x[4 * i] = v.x;
+      x[4 * i + 1] = v.y;
+      x[4 * i + 2] = v.z;
+      x[4 * i + 3] = v.w;
+    }
+  }
+}
+
+// exp2_q_neon(x, 16383, -16): round(16383 * 2^x), x <= 0; c[] = the polynomial's coefficients * 16383.
+__device__ __forceinline__ int i8_exp2_q(float x, const float (&c)[4]) {
+  x = fmaxf(x, -16.0f);
+  const int n = __float2int_rd(x);
+  const float f = __fsub_rn(x, __int2float_rn(n));
+  float p = __fmaf_rn(f, c[3], c[2]);
+  p = __fmaf_rn(f, p, c[1]);
+  p = __fmaf_rn(f, p, c[0]);
+  return __float2int_rn(__int_as_float(__float_as_int(p) + int(uint32_t(n) << 23)));
+}
+
+// min_len: sequences shorter than this are left to the fp32 kernels (their context rows untouched).
+__global__ void __launch_bounds__(kI8Threads, 4) k_attention_i8(AttnArgs a, int min_len) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ I8Smem sm;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int s = blockIdx.x, h = blockIdx.y;
+  const int s0 = int(a.cu[s]);
+  const int L = int(a.cu[s + 1]) - s0;
+  if (L <= 0 || L > a.max_len) {
+    if (tid == 0) record_err(a.err, DEV_ERR_BAD_SHAPE);
+    return;
+  }
+  const int i0 = blockIdx.z * kI8Queries;
+  if (L < min_len || i0 >= L) return;
+  const int nq = min(kI8Queries, L - i0);
+  const int L4 = (L + 3) & ~3, L8 = L & ~7;
+  const int qc = a.q_col + 32 * h, kc = a.k_col + 32 * h, vc = a.v_col + 32 * h;
+
+  // K rows and the tile's query rows, quantized per token
+  const float k_mul = __fmul_rn(__fdiv_rn(1.0f, __fsqrt_rn(32.0f)), 1.44269504088896341f);
+  for (int j = tid; j < L; j += kI8Threads) {
+    float x[32];
+    i8_load_head_row(a.kv, a.kv_C, a.kv_tt, s0 + j, kc, x);
+    sm.ks[j] = i8_quant_head_row(x, k_mul, sm.ka[j], sm.kb[j]);
+  }
+  for (int i = tid; i < nq; i += kI8Threads) {
+    float x[32];
+    i8_load_head_row(a.q, a.q_C, a.q_tt, s0 + i0 + i, qc, x);
+    sm.qs[i] = i8_quant_head_row(x, 1.0f, sm.qa[i], sm.qb[i]);
+  }
+  // V column maxima: warp w takes columns 4w .. 4w+3, lanes split the keys
+  {
+    float cm[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int j = lane; j < L; j += 32) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) cm[e] = fmaxf(cm[e], fabsf(ld_act(a.kv, a.kv_C, a.kv_tt, s0 + j, vc + 4 * warp + e)));
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) cm[e] = fmaxf(cm[e], __shfl_xor_sync(0xffffffffu, cm[e], o));
+    }
+    if (lane < 4) {
+      const float m = fmaxf(lane == 0 ? cm[0] : lane == 1 ? cm[1] : lane == 2 ? cm[2] : cm[3], 1e-8f);
+      sm.v_scale[4 * warp + lane] = __fmul_rn(m, __fdiv_rn(1.0f, 127.0f));
+      sm.v_inv[4 * warp + lane] = __fdiv_rn(127.0f, m);
+    }
+  }
+  __syncthreads();
+  {
+    int8_t* vb = reinterpret_cast<int8_t*>(sm.vq);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int c = 4 * warp + e;
+      const float inv = sm.v_inv[c];
+      for (int j = lane; j < L4; j += 32) {  // keys L .. L4-1 are zero
+        const int v = j < L ? max(-128, min(127, __float2int_rn(__fmul_rn(ld_act(a.kv, a.kv_C, a.kv_tt, s0 + j, vc + c), inv))))
+                            : 0;
+        vb[c * kI8VPitch * 4 + j] = int8_t(v);
+      }
+    }
+  }
+  __syncthreads();
+
+  float cexp[4];
+  cexp[0] = __fmul_rn(0.999857f, 16383.0f);
+  cexp[1] = __fmul_rn(0.6963853f, 16383.0f);
+  cexp[2] = __fmul_rn(0.22511937f, 16383.0f);
+  cexp[3] = __fmul_rn(0.07842169f, 16383.0f);
+  int16_t* prow = reinterpret_cast<int16_t*>(sm.p[warp]);
+  const int* vcol = sm.vq + lane * kI8VPitch;
+  for (int qi = warp; qi < nq; qi += kI8Threads / 32) {
+    const int4 qa = sm.qa[qi], qb = sm.qb[qi];
+    const float qsc = sm.qs[qi];
+    float sv[kMaxPos / 32];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int m = 0; m < kMaxPos / 32; ++m) {
+      const int j = lane + 32 * m;
+      sv[m] = -INFINITY;
+      if (j < L) {
+        const int4 ka = sm.ka[j], kb = sm.kb[j];
+        int acc = __dp4a(qa.x, ka.x, 0);
+        acc = __dp4a(qa.y, ka.y, acc);
+        acc = __dp4a(qa.z, ka.z, acc);
+        acc = __dp4a(qa.w, ka.w, acc);
+        acc = __dp4a(qb.x, kb.x, acc);
+        acc = __dp4a(qb.y, kb.y, acc);
+        acc = __dp4a(qb.z, kb.z, acc);
+        acc = __dp4a(qb.w, kb.w, acc);
+        sv[m] = __fmul_rn(__fmul_rn(__int2float_rn(acc), sm.ks[j]), qsc);
+        mx = fmaxf(mx, sv[m]);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    int isum = 0;
+#pragma unroll
+    for (int m = 0; m < kMaxPos / 32; ++m) {
+      const int j = lane + 32 * m;
+      if (j < L4) {
+        int q = 0;
+        if (j < L8) {
+          q = i8_exp2_q(__fsub_rn(sv[m], mx), cexp);
+        } else if (j < L) {
+          q = int(roundf(__fmul_rn(exp2f(__fsub_rn(sv[m], mx)), 16383.0f)));
+          q = max(0, min(16383, q));
+        }
+        isum += q;
+        prow[j] = int16_t(q);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) isum += __shfl_xor_sync(0xffffffffu, isum, o);
+    const float p_scale = __fdiv_rn(1.0f, __int2float_rn(max(isum, 1)));
+    __syncwarp();
+    int acc = 0;
+    const int2* pw = sm.p[warp];
+    for (int w = 0; w < (L4 >> 2); ++w) {
+      const int2 pp = pw[w];
+      const int b = vcol[w];
+      acc = __dp2a_lo(pp.x, b, acc);
+      acc = __dp2a_hi(pp.y, b, acc);
+    }
+    a.out[size_t(s0 + i0 + qi) * kHidden + h * 32 + lane] =
+        __fmul_rn(__int2float_rn(acc), __fmul_rn(sm.v_scale[lane], p_scale));
+    __syncwarp();
+  }
+}
+
+int launch_attention_i8(const AttnArgs& a, int n_seqs, int min_len, cudaStream_t st) {
+  if (n_seqs <= 0) return 0;
+  if (a.max_len <= 0 || a.max_len > kMaxPos || a.cls_mode) return -1;
+  const dim3 grid(n_seqs, kHeads, (a.max_len + kI8Queries - 1) / kI8Queries);
+  return launch_pdl(k_attention_i8, grid, dim3(kI8Threads), 0, st, a, min_len) == cudaSuccess ? 0 : -3;
+}
+
 int launch_attention_exact(const AttnArgs& a, int n_seqs, cudaStream_t st, int* quantized) {
   if (quantized) *quantized = 0;
   if (n_seqs <= 0) return 0;

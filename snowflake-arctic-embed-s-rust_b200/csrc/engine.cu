@@ -119,6 +119,7 @@ struct ae_ctx {
   std::string err;
   int gelu_erf = 0;       // ARCTIC_GELU=erf selects the exact-erf GELU (outside the parity tolerance)
   int fused_qkv = 0;      // ARCTIC_FUSED_QKV=1: QKV projection fused into the attention (sequences <= 128 keys)
+  int attn_mode = AE_ATTENTION_EXACT;  // ae_set_attention_mode, ARCTIC_ATTN=int8
   bool prof = false;      // record CUDA events around every launch (ae_profile)
   int prof_kind = 0;      // kind of the launches being enqueued
   std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> prof_events;
@@ -445,6 +446,49 @@ int attention(ae_ctx* c, const float* q, int q_C, int q_col, int q_tt, const flo
   return 0;
 }
 
+// Sequences of fewer keys than this keep the fp32 attention in the int8 mode (the reference's
+// crossover for one sequence, src/model.rs:245).
+constexpr int kI8MinLen = 16;
+
+// Attention of layers 0-10 in the int8 mode: per length run (or over the whole batch), the fp32
+// kernels for the sequences below kI8MinLen, when the run may hold some, then the int8 kernel for
+// the others. min_len: the shortest sequence of the batch when known, else 1.
+int attention_i8(ae_ctx* c, const float* qkv, float* out, const uint32_t* cu, int n, int max_len, int min_len,
+                 const std::vector<AttnSegment>* segs) {
+  AttnArgs a{};
+  a.q = qkv;
+  a.q_C = 3 * kHidden;
+  a.q_col = 0;
+  a.q_tt = 1;
+  a.kv = qkv;
+  a.kv_C = 3 * kHidden;
+  a.k_col = kHidden;
+  a.v_col = 2 * kHidden;
+  a.kv_tt = 1;
+  a.out = out;
+  a.err = c->d_err;
+  std::vector<AttnSegment> whole;
+  if (!segs || segs->empty()) {
+    whole.push_back(AttnSegment{0, n, max_len, min_len});
+    segs = &whole;
+  }
+  for (const AttnSegment& g : *segs) {
+    AttnArgs b = a;
+    b.cu = cu + g.first;
+    b.max_len = g.max_len;
+    if (g.min_len < kI8MinLen) {
+      ++c->launches;
+      if (launch_attention_exact(b, g.count, c->stream)) return fail(c, AE_ERR_CUDA, "attention launch failed");
+    }
+    if (g.max_len >= kI8MinLen) {
+      ++c->launches;
+      if (launch_attention_i8(b, g.count, kI8MinLen, c->stream))
+        return fail(c, AE_ERR_CUDA, "int8 attention launch failed");
+    }
+  }
+  return 0;
+}
+
 // Residual GEMM followed by LayerNorm + SmoothQuant quantization (attention-out, FFN-down):
 // fused into the GEMM epilogue when the batch has enough 128-row tiles to fill the GPU; otherwise
 // a plain-epilogue GEMM split over narrow column slices writes h = fma(acc, as*ws, bias + res)
@@ -483,8 +527,10 @@ int gemm_ln(ae_ctx* c, const CUtensorMap& ta, const DevLinear& L, int M, const f
 //
 // segs (optional): the packed sequences as runs of one attention length class each (host packing
 // knows the lengths); the attention of layers 0-10 then launches once per run.
+// min_len: a lower bound of the sequence lengths (the int8 attention mode uses it when segs is
+// not given).
 int enqueue_forward(ae_ctx* c, const uint16_t* d_ids, const uint32_t* d_cu, int T, int n, int max_len, float* d_out,
-                    const std::vector<AttnSegment>* segs = nullptr) {
+                    const std::vector<AttnSegment>* segs = nullptr, int min_len = 1) {
   Workspace& W = c->ws;
   const DevModel& M = c->model;
   cudaStream_t st = c->stream;
@@ -521,7 +567,7 @@ int enqueue_forward(ae_ctx* c, const uint16_t* d_ids, const uint32_t* d_cu, int 
   // kernels (its load / MMA / dequantization prologue runs while the SM's FP32 pipes idle) and
   // 8 % slower for single sequences; by default a QKV GEMM writes the projections to global memory
   // for the attention kernels of every length class.
-  const bool fused = max_len <= 128 && c->fused_qkv == 1;
+  const bool fused = max_len <= 128 && c->fused_qkv == 1 && c->attn_mode == AE_ATTENTION_EXACT;
   for (int l = 0; l + 1 < kLayers; ++l) {
     const DevLayer& Ly = M.layers[l];
     int ctx_quantized = 0;  // the attention kernel also wrote act_q / act_s
@@ -547,8 +593,11 @@ int enqueue_forward(ae_ctx* c, const uint16_t* d_ids, const uint32_t* d_cu, int 
       {
         ProfScope ps(c, AE_KERNEL_ATTENTION);
         const CtxQuant cq{Ly.ao.inv_s, W.act_q, W.act_s};
-        AE_TRY(attention(c, W.qkv, 3 * kHidden, 0, 1, W.qkv, 3 * kHidden, kHidden, 2 * kHidden, 1, W.ctx, d_cu, n,
-                         max_len, 0, segs, &cq, &ctx_quantized));
+        if (c->attn_mode == AE_ATTENTION_INT8)
+          AE_TRY(attention_i8(c, W.qkv, W.ctx, d_cu, n, max_len, min_len, segs));
+        else
+          AE_TRY(attention(c, W.qkv, 3 * kHidden, 0, 1, W.qkv, 3 * kHidden, kHidden, 2 * kHidden, 1, W.ctx, d_cu, n,
+                           max_len, 0, segs, &cq, &ctx_quantized));
       }
     }
     if (!ctx_quantized) {
@@ -639,16 +688,20 @@ int pack_host(ae_ctx* c, const uint16_t* ids, const uint32_t* cu, uint32_t n, in
   c->order.resize(n);
   c->segs.clear();
   uint32_t filled = 0;
-  for (int cls = 0; cls < kAttnClasses; ++cls) {
+  // the int8 attention mode keeps the sequences below its crossover in a class of their own
+  const bool i8 = c->attn_mode == AE_ATTENTION_INT8;
+  auto class_of = [&](int len) { return i8 ? (len < kI8MinLen ? 0 : 1 + attn_class(len)) : attn_class(len); };
+  for (int cls = 0; cls < kAttnClasses + (i8 ? 1 : 0); ++cls) {
     const uint32_t first = filled;
-    int seg_max = 0;
+    int seg_max = 0, seg_min = kMaxPos;
     for (uint32_t i = 0; i < n; ++i) {
       const uint32_t len = len_of(i);
-      if (attn_class(int(len)) != cls) continue;
+      if (class_of(int(len)) != cls) continue;
       c->order[filled++] = i;
       seg_max = std::max<int>(seg_max, int(len));
+      seg_min = std::min<int>(seg_min, int(len));
     }
-    if (filled > first) c->segs.push_back(AttnSegment{int(first), int(filled - first), seg_max});
+    if (filled > first) c->segs.push_back(AttnSegment{int(first), int(filled - first), seg_max, seg_min});
   }
   uint32_t off = 0;
   W.h_cu[0] = 0;
@@ -843,6 +896,8 @@ int ae_ctx_create(int device, ae_ctx** out) {
   c->gelu_erf = (gm && std::strcmp(gm, "erf") == 0) ? 1 : 0;
   const char* fq = std::getenv("ARCTIC_FUSED_QKV");
   c->fused_qkv = (fq && std::strcmp(fq, "1") == 0) ? 1 : 0;
+  const char* am = std::getenv("ARCTIC_ATTN");
+  c->attn_mode = (am && std::strcmp(am, "int8") == 0) ? AE_ATTENTION_INT8 : AE_ATTENTION_EXACT;
   if (gemm_i8_prime() || attention_prime()) {
     ae_ctx_destroy(c);
     return fail(nullptr, AE_ERR_CUDA, "kernel attribute setup failed on device %d", device);
@@ -1098,7 +1153,7 @@ int ae_forward_cls(ae_ctx* c, const uint16_t* ids, uint32_t len, float* out) {
     const uint64_t before = c->launches;
     const bool prof = c->prof;
     c->prof = false;  // no event records inside the graph
-    if (!r) r = enqueue_forward(c, W.ids, c->d_cu_single + 2 * L, int(L), 1, int(L), W.out);
+    if (!r) r = enqueue_forward(c, W.ids, c->d_cu_single + 2 * L, int(L), 1, int(L), W.out, nullptr, int(L));
     c->prof = prof;
     gr.kernels = c->launches - before;
     c->launches = before;  // captured, not launched
@@ -1264,6 +1319,43 @@ int ae_attention_f32(ae_ctx* c, const float* d_qkv, const uint32_t* d_cu, uint32
                    int(max_len), 0);
 }
 
+int ae_attention_i8(ae_ctx* c, const float* d_qkv, const uint32_t* d_cu, uint32_t n, uint32_t max_len, float* d_ctx) {
+  if (!c) return AE_ERR_INVALID_ARG;
+  if (!d_qkv || !d_cu || !d_ctx || max_len == 0 || max_len > uint32_t(kMaxPos))
+    return fail(c, AE_ERR_INVALID_ARG, "ae_attention_i8: bad arguments");
+  if (n == 0) return 0;
+  DeviceGuard g(c->device);
+  AttnArgs a{};
+  a.q = d_qkv;
+  a.q_C = 3 * kHidden;
+  a.kv = d_qkv;
+  a.kv_C = 3 * kHidden;
+  a.k_col = kHidden;
+  a.v_col = 2 * kHidden;
+  a.out = d_ctx;
+  a.cu = d_cu;
+  a.max_len = int(max_len);
+  a.err = c->d_err;
+  ++c->launches;
+  if (launch_attention_i8(a, int(n), 1, c->stream)) return fail(c, AE_ERR_CUDA, "int8 attention launch failed");
+  return 0;
+}
+
+int ae_set_attention_mode(ae_ctx* c, int mode) {
+  if (!c) return AE_ERR_INVALID_ARG;
+  if (mode != AE_ATTENTION_EXACT && mode != AE_ATTENTION_INT8)
+    return fail(c, AE_ERR_INVALID_ARG, "unknown attention mode %d", mode);
+  if (mode != c->attn_mode) {
+    DeviceGuard g(c->device);
+    cudaStreamSynchronize(c->stream);
+    drop_graphs(c);
+    c->attn_mode = mode;
+  }
+  return 0;
+}
+
+int ae_get_attention_mode(const ae_ctx* c) { return c ? c->attn_mode : AE_ERR_INVALID_ARG; }
+
 // ArcticEmbedS::embed_batch (src/lib.rs:138-260) across GPUs: token-weighted greedy shards, one host
 // thread per context; each context packs its shard (longest first) into batches of <= max_tokens.
 int ae_embed_batch_multi(ae_ctx* const* ctxs, int n_ctx, const uint16_t* ids, const uint32_t* cu, uint32_t n,
@@ -1421,7 +1513,7 @@ extern "C" int ae_forward_cls_noalloc(ae_ctx* c, const uint16_t* d_ids, uint32_t
   // run the forward on the static scratch: the context's own workspace is set aside for the call
   Workspace saved = c->ws;
   c->ws = W;
-  const int r = enqueue_forward(c, d_ids, W.cu, int(len), 1, int(len), d_out384);
+  const int r = enqueue_forward(c, d_ids, W.cu, int(len), 1, int(len), d_out384, nullptr, int(len));
   c->ws = saved;
   return r;
 }

@@ -80,6 +80,7 @@ struct AttnSegment {
   int first;
   int count;
   int max_len;
+  int min_len;
 };
 // Length classes of the attention launch: 1-32, 33-64, 65-128, 129-256, 257-512 keys (the TMEM
 // columns a CTA allocates for its scores).
@@ -88,6 +89,9 @@ inline int attn_class(int len) { return len <= 32 ? 0 : len <= 64 ? 1 : len <= 1
 // quantized (optional): set to 1 when the launch also wrote the quantized context rows
 // (a.quant_*; the single-sequence path for at most 64 keys), else 0 (the caller quantizes).
 int launch_attention_exact(const AttnArgs& a, int n_seqs, cudaStream_t st, int* quantized = nullptr);
+// The reference's int8 attention scheme (no cls_mode) for the sequences of at least min_len keys;
+// the context rows of shorter ones are left as they are.
+int launch_attention_i8(const AttnArgs& a, int n_seqs, int min_len, cudaStream_t st);
 
 // QKV projection fused with the attention (sequences of at most 128 keys): the int8 GEMM
 // fma(float(acc), a_scale[row] * w_scale[n], bias[n]) of one sequence's 128-row tile against the

@@ -123,3 +123,94 @@ def test_row_kernels_known_answers():
     assert sc[0] == np.float32(1e-8) / np.float32(127.0) and not q.any()
     y = orc.gelu_ref(np.array([0.0, 10.0, -10.0, 1.0], np.float32))
     assert y[0] == 0.0 and y[1] == 10.0 and y[2] == 0.0 and abs(y[3] - 0.8413447) < 1e-5
+
+
+# ------------------------------------------------------------------------------------ int8 attention
+def bench_qkv(L):
+    """The reference's attention micro-benchmark input (examples/attn_bench.rs:19-21):
+    qkv[i] = ((i * 2654435761) % 1000) / 300 - 1.6, as f32 [L, 1152]."""
+    i = np.arange(L * 1152, dtype=np.uint64)
+    v = ((i * np.uint64(2654435761)) % np.uint64(1000)).astype(np.float32) / np.float32(300.0) - np.float32(1.6)
+    return v.reshape(L, 1152)
+
+
+def np_attention_i8(qkv):
+    """Independent NumPy statement of the reference's int8 attention scheme (attention_heads_sme,
+    src/simd_math.rs:1933-2186) for one sequence: float32 elementwise steps, exact integer sums,
+    the polynomial's fused multiply-adds as float64 products and sums (exact products; a double
+    rounding only at an exact float32 midpoint)."""
+    f32 = np.float32
+    L = qkv.shape[0]
+    out = np.zeros((L, 384), f32)
+    k_mul = (f32(1.0) / np.sqrt(f32(32.0))) * f32(1.4426950408889634)
+
+    def quant_rows(x, mul):
+        m = np.maximum(np.abs(x).max(axis=1), f32(1e-8))
+        q = np.clip(np.rint(x * (f32(127.0) / m)[:, None]), -128, 127).astype(np.int64)
+        return q, (m / f32(127.0)) * f32(mul)
+
+    c = [f32(f32(0.999857) * f32(16383.0)), f32(f32(0.6963853) * f32(16383.0)),
+         f32(f32(0.22511937) * f32(16383.0)), f32(f32(0.07842169) * f32(16383.0))]
+
+    def fma(a, b, d):
+        return (a.astype(np.float64) * b.astype(np.float64) + np.float64(d)).astype(f32)
+
+    L8 = L - L % 8
+    for h in range(12):
+        q, qs = quant_rows(qkv[:, 32 * h:32 * h + 32], 1.0)
+        k, ks = quant_rows(qkv[:, 384 + 32 * h:384 + 32 * h + 32], k_mul)
+        v = qkv[:, 768 + 32 * h:768 + 32 * h + 32]
+        vm = np.maximum(np.abs(v).max(axis=0), f32(1e-8))
+        v_scale = vm * (f32(1.0) / f32(127.0))
+        vq = np.clip(np.rint(v * (f32(127.0) / vm)[None, :]), -128, 127).astype(np.int64)
+        s = ((q @ k.T).astype(f32) * ks[None, :]) * qs[:, None]
+        x = s - s.max(axis=1, keepdims=True)
+        xv = np.maximum(x[:, :L8], f32(-16.0))
+        n = np.floor(xv).astype(np.int32)
+        fr = xv - n.astype(f32)
+        p = fma(fr, c[3] * np.ones_like(fr), c[2])
+        p = fma(fr, p, c[1])
+        p = fma(fr, p, c[0])
+        pv = np.rint((p.view(np.int32) + (n << 23)).view(f32)).astype(np.int64)
+        e = np.exp2(x[:, L8:]) * f32(16383.0)
+        pt = np.clip(np.floor(e.astype(np.float64) + 0.5), 0, 16383).astype(np.int64)
+        P = np.concatenate([pv, pt], axis=1)
+        p_scale = f32(1.0) / np.maximum(P.sum(axis=1), 1).astype(f32)
+        out[:, 32 * h:32 * h + 32] = (P @ vq).astype(f32) * (v_scale[None, :] * p_scale[:, None])
+    return out
+
+
+@pytest.mark.parametrize("L", [1, 4, 16, 33, 128, 512])
+def test_int8_attention_restatements_agree(L):
+    """The oracle's C++ restatement of the int8 scheme vs an independent NumPy statement, on the
+    reference's own benchmark input and on N(0, 1) data."""
+    for qkv in (bench_qkv(L), rng(L).normal(0, 1, (L, 1152)).astype(np.float32)):
+        got = orc.attention_i8(qkv)
+        ref = np_attention_i8(qkv)
+        # the only admitted difference: exp2 of the last L % 8 keys (glibc vs NumPy), which can
+        # move one 14-bit probability by one step
+        assert (got == ref).mean() > 0.99
+        np.testing.assert_allclose(got, ref, rtol=0, atol=1e-3 * float(np.abs(ref).max()))
+        if L % 8 == 0:
+            np.testing.assert_array_equal(got, ref)
+
+
+def test_int8_attention_mode_forward(pack_path, oracle_model):
+    """int8 mode of layers 0-10: sequences under 16 tokens keep the fp32 attention (src/model.rs:245),
+    longer ones stay within the reference's own accuracy bar of its int8 path against fp32
+    (tests/accuracy_test.rs:109-132: cos > 0.9985 per record); scales are per sequence, so a
+    packed batch gives each sequence's single-sequence result."""
+    m8 = orc.OracleModel(pack_path).set_attention_mode(orc.ATTENTION_INT8)
+    r = rng(77)
+    lens = [3, 15, 16, 40, 128, 300]
+    seqs = [synth.token_ids(L, r) for L in lens]
+    for s in seqs:
+        a, b = oracle_model.forward_cls(s), m8.forward_cls(s)
+        if len(s) < 16:
+            np.testing.assert_array_equal(a, b)
+        else:
+            assert float(a @ b) > 0.9985 and not np.array_equal(a, b)
+    packed = m8.forward_ragged(seqs[:4])
+    np.testing.assert_array_equal(packed, np.stack([m8.forward_cls(s) for s in seqs[:4]]))
+    with pytest.raises(ValueError):
+        m8.set_attention_mode(2)
