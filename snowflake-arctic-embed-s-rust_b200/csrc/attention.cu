@@ -33,6 +33,7 @@
 // 16 exp-sum chains, 64 threads the even / odd weighted-sum accumulators of the 32 dims.
 #include <cuda_runtime.h>
 
+#include <cstddef>
 #include <cstdint>
 
 #include "kernels.h"
@@ -205,6 +206,7 @@ __global__ void __launch_bounds__(QT, 512 / QT) k_attention_rows(AttnArgs a) {
   const int warp = tid >> 5;
   const int s0 = int(a.cu[s]);
   const int L = int(a.cu[s + 1]) - s0;
+  if (a.skip_from > 0 && L >= a.skip_from) return;  // another kernel takes these sequences
   if (L <= 0 || L > a.max_len) {
     if (tid == 0 && tile == 0 && h == 0) record_err(a.err, DEV_ERR_BAD_SHAPE);
     return;
@@ -680,6 +682,7 @@ __global__ void __launch_bounds__(128, 2) k_attention_rows2(AttnArgs a) {
   const int h = 2 * y + unit;
   const int s0 = int(a.cu[s]);
   const int L = int(a.cu[s + 1]) - s0;
+  if (a.skip_from > 0 && L >= a.skip_from) return;  // another kernel takes these sequences
   if (L <= 0 || L > a.max_len || L > 128) {
     if (tid == 0 && y == 0) record_err(a.err, DEV_ERR_BAD_SHAPE);
     return;
@@ -941,6 +944,7 @@ __global__ void __launch_bounds__(4 * QT) k_attention_lat(AttnArgs a) {
   const int s0 = int(a.cu[s]);
   const int L = int(a.cu[s + 1]) - s0;
   // the 12 CTAs of a cluster share the sequence and the tile: these exits are cluster-uniform
+  if (a.skip_from > 0 && L >= a.skip_from) return;  // another kernel takes these sequences
   if (L <= 0 || L > a.max_len) {
     if (tid == 0 && tile == 0 && h == 0) record_err(a.err, DEV_ERR_BAD_SHAPE);
     return;
@@ -1126,6 +1130,7 @@ __global__ void __launch_bounds__(128 * NWG, MINB) k_attention_wide(AttnArgs a) 
   const int qt = tid & 127;
   const int s0 = int(a.cu[s]);
   const int L = int(a.cu[s + 1]) - s0;
+  if (a.skip_from > 0 && L >= a.skip_from) return;  // another kernel takes these sequences
   if (L <= 0 || L > a.max_len) {
     if (tid == 0 && tile == 0 && h == 0) record_err(a.err, DEV_ERR_BAD_SHAPE);
     return;
@@ -1555,6 +1560,7 @@ struct I8Smem {
   float v_scale[kHeadDim], v_inv[kHeadDim];
   int2 p[kI8Threads / 32][kMaxPos / 4];  // a warp's 14-bit probabilities, 4 keys (int16) an int2
 };
+static_assert(offsetof(I8Smem, p) % 16 == 0, "probability rows are read as 16-byte words");
 
 // quantize_head32_row_neon: q = sat(rn(x * (127 / m))), m = max(1e-8, max |x|); returns (m / 127) * mul.
 __device__ __forceinline__ float i8_quant_head_row(const float (&x)[32], float mul, int4& lo, int4& hi) {
@@ -1723,14 +1729,27 @@ __global__ void __launch_bounds__(kI8Threads, 4) k_attention_i8(AttnArgs a, int 
     for (int o = 16; o >= 1; o >>= 1) isum += __shfl_xor_sync(0xffffffffu, isum, o);
     const float p_scale = __fdiv_rn(1.0f, __int2float_rn(max(isum, 1)));
     __syncwarp();
-    int acc = 0;
+    // four independent integer sums (exact in any order: |sum| < 512 * 16383 * 127 < 2^31)
+    int acc0 = 0, acc1 = 0, acc2 = 0, acc3 = 0;
     const int2* pw = sm.p[warp];
-    for (int w = 0; w < (L4 >> 2); ++w) {
+    const int nw = L4 >> 2;
+    int w = 0;
+#pragma unroll 4
+    for (; w + 2 <= nw; w += 2) {
+      const int4 pp = *reinterpret_cast<const int4*>(pw + w);  // keys 4w .. 4w+7
+      const int b0 = vcol[w], b1 = vcol[w + 1];
+      acc0 = __dp2a_lo(pp.x, b0, acc0);
+      acc1 = __dp2a_hi(pp.y, b0, acc1);
+      acc2 = __dp2a_lo(pp.z, b1, acc2);
+      acc3 = __dp2a_hi(pp.w, b1, acc3);
+    }
+    if (w < nw) {
       const int2 pp = pw[w];
       const int b = vcol[w];
-      acc = __dp2a_lo(pp.x, b, acc);
-      acc = __dp2a_hi(pp.y, b, acc);
+      acc0 = __dp2a_lo(pp.x, b, acc0);
+      acc1 = __dp2a_hi(pp.y, b, acc1);
     }
+    const int acc = (acc0 + acc1) + (acc2 + acc3);
     a.out[size_t(s0 + i0 + qi) * kHidden + h * 32 + lane] =
         __fmul_rn(__int2float_rn(acc), __fmul_rn(sm.v_scale[lane], p_scale));
     __syncwarp();

@@ -476,9 +476,14 @@ int attention_i8(ae_ctx* c, const float* qkv, float* out, const uint32_t* cu, in
     AttnArgs b = a;
     b.cu = cu + g.first;
     b.max_len = g.max_len;
-    if (g.min_len < kI8MinLen) {
+    if (g.min_len < kI8MinLen) {  // the sequences below the crossover, sized for them
+      AttnArgs x = b;
+      if (g.max_len >= kI8MinLen) {
+        x.max_len = kI8MinLen - 1;
+        x.skip_from = kI8MinLen;
+      }
       ++c->launches;
-      if (launch_attention_exact(b, g.count, c->stream)) return fail(c, AE_ERR_CUDA, "attention launch failed");
+      if (launch_attention_exact(x, g.count, c->stream)) return fail(c, AE_ERR_CUDA, "attention launch failed");
     }
     if (g.max_len >= kI8MinLen) {
       ++c->launches;

@@ -43,6 +43,7 @@ struct AttnArgs {
   const float* quant_inv_s;   // [384] inverse smoothing factors, or nullptr
   int8_t* quant_q;            // [rows, 384]
   float* quant_scale;         // [rows]
+  int skip_from;              // > 0: the exact kernels leave sequences of at least this many keys alone
 };
 
 // Launch with programmatic stream serialization (the kernel calls pdl_wait before it touches data
