@@ -1542,25 +1542,20 @@ int launch_qkv_attention(const CUtensorMap& tm_act, const CUtensorMap& tm_w, con
 // Every step is elementwise or an integer sum, so any order gives the reference's values: the
 // integer products run as dp4a (Q.K, 4 dims a step) and dp2a (14-bit q times int8 V, 2 keys a step).
 //
-// k_attention_i8: one CTA per (sequence, head, 64 queries), 8 warps. The CTA quantizes the head's
-// K rows, V columns and its queries into shared memory; then each warp takes one query at a time:
-// lanes split the keys for the scores and the exponentials (kept in registers, 16 keys a lane at
-// most), the integer probabilities go to the warp's shared row, and lane c sums column c of P.V.
-constexpr int kI8Queries = 64;
-constexpr int kI8Threads = 256;
-constexpr int kI8VPitch = kMaxPos / 4 + 1;  // words per V column (+1: the 32 lanes hit 32 banks)
+// k_attention_i8: one CTA per (sequence, head, 128 queries), one thread per query. The CTA
+// quantizes the head's K rows and V columns into shared memory (K as 32 int8 per key, V as key
+// pairs interleaved per column pair for dp2a), so that every shared load is a broadcast that
+// serves the warp's 32 queries. A thread makes two passes over the keys: the scores and their
+// maximum, then the same scores again (the same operations, so the same values), their 14-bit
+// exponentials, the integer sum and the 32 integer column sums of P.V in registers.
+constexpr int kI8Queries = 128;
 
 struct I8Smem {
-  int4 ka[kMaxPos];             // key j, dims 0-15 as int8
-  int4 kb[kMaxPos];             // dims 16-31
-  float ks[kMaxPos];            // key scales (with 1/sqrt(32) * log2 e)
-  int4 qa[kI8Queries], qb[kI8Queries];
-  float qs[kI8Queries];
-  int vq[kHeadDim * kI8VPitch];  // column c: byte j of word c * pitch + j / 4 = key j
+  int4 k[kMaxPos][2];          // key j: dims 0-15, 16-31 as int8
+  float ks[kMaxPos];           // key scales (with 1/sqrt(32) * log2 e)
+  int v[kMaxPos / 2][16];      // key pair (2p, 2p+1), word w: v[2p][2w], v[2p+1][2w], v[2p][2w+1], v[2p+1][2w+1]
   float v_scale[kHeadDim], v_inv[kHeadDim];
-  int2 p[kI8Threads / 32][kMaxPos / 4];  // a warp's 14-bit probabilities, 4 keys (int16) an int2
 };
-static_assert(offsetof(I8Smem, p) % 16 == 0, "probability rows are read as 16-byte words");
 
 // quantize_head32_row_neon: q = sat(rn(x * (127 / m))), m = max(1e-8, max |x|); returns (m / 127) * mul.
 __device__ __forceinline__ float i8_quant_head_row(const float (&x)[32], float mul, int4& lo, int4& hi) {
@@ -1612,8 +1607,22 @@ __device__ __forceinline__ int i8_exp2_q(float x, const float (&c)[4]) {
   return __float2int_rn(__int_as_float(__float_as_int(p) + int(uint32_t(n) << 23)));
 }
 
+// The score of key j for a query held as (qa, qb, qsc): (int32 q.k * k_scale) * q_scale.
+__device__ __forceinline__ float i8_score(const I8Smem& sm, int j, const int4& qa, const int4& qb, float qsc) {
+  const int4 ka = sm.k[j][0], kb = sm.k[j][1];
+  int acc = __dp4a(qa.x, ka.x, 0);
+  acc = __dp4a(qa.y, ka.y, acc);
+  acc = __dp4a(qa.z, ka.z, acc);
+  acc = __dp4a(qa.w, ka.w, acc);
+  acc = __dp4a(qb.x, kb.x, acc);
+  acc = __dp4a(qb.y, kb.y, acc);
+  acc = __dp4a(qb.z, kb.z, acc);
+  acc = __dp4a(qb.w, kb.w, acc);
+  return __fmul_rn(__fmul_rn(__int2float_rn(acc), sm.ks[j]), qsc);
+}
+
 // min_len: sequences shorter than this are left to the fp32 kernels (their context rows untouched).
-__global__ void __launch_bounds__(kI8Threads, 4) k_attention_i8(AttnArgs a, int min_len) {
+__global__ void __launch_bounds__(kI8Queries, 4) k_attention_i8(AttnArgs a, int min_len) {
   pdl_trigger();
   pdl_wait();
   __shared__ I8Smem sm;
@@ -1627,132 +1636,124 @@ __global__ void __launch_bounds__(kI8Threads, 4) k_attention_i8(AttnArgs a, int 
   }
   const int i0 = blockIdx.z * kI8Queries;
   if (L < min_len || i0 >= L) return;
-  const int nq = min(kI8Queries, L - i0);
-  const int L4 = (L + 3) & ~3, L8 = L & ~7;
+  const int L8 = L & ~7, pairs = (L + 1) >> 1;
   const int qc = a.q_col + 32 * h, kc = a.k_col + 32 * h, vc = a.v_col + 32 * h;
 
-  // K rows and the tile's query rows, quantized per token
+  // K rows, quantized per token
   const float k_mul = __fmul_rn(__fdiv_rn(1.0f, __fsqrt_rn(32.0f)), 1.44269504088896341f);
-  for (int j = tid; j < L; j += kI8Threads) {
+  for (int j = tid; j < L; j += kI8Queries) {
     float x[32];
     i8_load_head_row(a.kv, a.kv_C, a.kv_tt, s0 + j, kc, x);
-    sm.ks[j] = i8_quant_head_row(x, k_mul, sm.ka[j], sm.kb[j]);
+    sm.ks[j] = i8_quant_head_row(x, k_mul, sm.k[j][0], sm.k[j][1]);
   }
-  for (int i = tid; i < nq; i += kI8Threads) {
-    float x[32];
-    i8_load_head_row(a.q, a.q_C, a.q_tt, s0 + i0 + i, qc, x);
-    sm.qs[i] = i8_quant_head_row(x, 1.0f, sm.qa[i], sm.qb[i]);
-  }
-  // V column maxima: warp w takes columns 4w .. 4w+3, lanes split the keys
+  // V column maxima: warp w takes columns 8w .. 8w+7, lanes split the keys
   {
-    float cm[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float cm[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) cm[e] = 0.0f;
     for (int j = lane; j < L; j += 32) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) cm[e] = fmaxf(cm[e], fabsf(ld_act(a.kv, a.kv_C, a.kv_tt, s0 + j, vc + 4 * warp + e)));
+      for (int e = 0; e < 8; ++e) cm[e] = fmaxf(cm[e], fabsf(ld_act(a.kv, a.kv_C, a.kv_tt, s0 + j, vc + 8 * warp + e)));
     }
+    float mine = 0.0f;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
+    for (int e = 0; e < 8; ++e) {
 #pragma unroll
       for (int o = 16; o >= 1; o >>= 1) cm[e] = fmaxf(cm[e], __shfl_xor_sync(0xffffffffu, cm[e], o));
+      if (lane == e) mine = cm[e];
     }
-    if (lane < 4) {
-      const float m = fmaxf(lane == 0 ? cm[0] : lane == 1 ? cm[1] : lane == 2 ? cm[2] : cm[3], 1e-8f);
-      sm.v_scale[4 * warp + lane] = __fmul_rn(m, __fdiv_rn(1.0f, 127.0f));
-      sm.v_inv[4 * warp + lane] = __fdiv_rn(127.0f, m);
+    if (lane < 8) {
+      const float m = fmaxf(mine, 1e-8f);
+      sm.v_scale[8 * warp + lane] = __fmul_rn(m, __fdiv_rn(1.0f, 127.0f));
+      sm.v_inv[8 * warp + lane] = __fdiv_rn(127.0f, m);
     }
   }
   __syncthreads();
-  {
-    int8_t* vb = reinterpret_cast<int8_t*>(sm.vq);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int c = 4 * warp + e;
-      const float inv = sm.v_inv[c];
-      for (int j = lane; j < L4; j += 32) {  // keys L .. L4-1 are zero
-        const int v = j < L ? max(-128, min(127, __float2int_rn(__fmul_rn(ld_act(a.kv, a.kv_C, a.kv_tt, s0 + j, vc + c), inv))))
-                            : 0;
-        vb[c * kI8VPitch * 4 + j] = int8_t(v);
-      }
+  // V as int8 key pairs per column pair (the second key of an odd L's last pair is zero); lanes take
+  // consecutive key pairs of one column pair (tile-transposed rows) or consecutive column pairs of
+  // one key pair (row-major rows), so that their loads are contiguous
+  for (int i = tid; i < pairs * 16; i += kI8Queries) {
+    const int p = a.kv_tt ? i % pairs : i >> 4;
+    const int w = a.kv_tt ? i / pairs : i & 15;
+    const int t0 = 2 * p, c0 = 2 * w;
+    const float i0v = sm.v_inv[c0], i1v = sm.v_inv[c0 + 1];
+    auto q8 = [](float x, float inv) { return uint32_t(max(-128, min(127, __float2int_rn(__fmul_rn(x, inv))))) & 0xffu; };
+    const uint32_t a0 = q8(ld_act(a.kv, a.kv_C, a.kv_tt, s0 + t0, vc + c0), i0v);
+    const uint32_t a1 = q8(ld_act(a.kv, a.kv_C, a.kv_tt, s0 + t0, vc + c0 + 1), i1v);
+    uint32_t b0 = 0u, b1 = 0u;
+    if (t0 + 1 < L) {
+      b0 = q8(ld_act(a.kv, a.kv_C, a.kv_tt, s0 + t0 + 1, vc + c0), i0v);
+      b1 = q8(ld_act(a.kv, a.kv_C, a.kv_tt, s0 + t0 + 1, vc + c0 + 1), i1v);
     }
+    sm.v[p][w] = int(a0 | (b0 << 8) | (a1 << 16) | (b1 << 24));
   }
   __syncthreads();
 
+  const int qi = i0 + tid;
+  if (qi >= L) return;  // no barrier follows
+  int4 qa, qb;
+  float qsc;
+  {
+    float x[32];
+    i8_load_head_row(a.q, a.q_C, a.q_tt, s0 + qi, qc, x);
+    qsc = i8_quant_head_row(x, 1.0f, qa, qb);
+  }
+  // pass 1: the maximum score
+  float mx = -INFINITY;
+  {
+    int j = 0;
+    for (; j + 4 <= L; j += 4) {
+      const float e0 = i8_score(sm, j, qa, qb, qsc), e1 = i8_score(sm, j + 1, qa, qb, qsc);
+      const float e2 = i8_score(sm, j + 2, qa, qb, qsc), e3 = i8_score(sm, j + 3, qa, qb, qsc);
+      mx = fmaxf(mx, fmaxf(fmaxf(e0, e1), fmaxf(e2, e3)));
+    }
+    for (; j < L; ++j) mx = fmaxf(mx, i8_score(sm, j, qa, qb, qsc));
+  }
+  // pass 2: 14-bit exponentials, their sum and P.V (integer sums: exact in any order)
   float cexp[4];
   cexp[0] = __fmul_rn(0.999857f, 16383.0f);
   cexp[1] = __fmul_rn(0.6963853f, 16383.0f);
   cexp[2] = __fmul_rn(0.22511937f, 16383.0f);
   cexp[3] = __fmul_rn(0.07842169f, 16383.0f);
-  int16_t* prow = reinterpret_cast<int16_t*>(sm.p[warp]);
-  const int* vcol = sm.vq + lane * kI8VPitch;
-  for (int qi = warp; qi < nq; qi += kI8Threads / 32) {
-    const int4 qa = sm.qa[qi], qb = sm.qb[qi];
-    const float qsc = sm.qs[qi];
-    float sv[kMaxPos / 32];
-    float mx = -INFINITY;
+  auto prob = [&](int j) -> int {
+    if (j >= L) return 0;
+    const float x = __fsub_rn(i8_score(sm, j, qa, qb, qsc), mx);
+    if (j < L8) return i8_exp2_q(x, cexp);
+    return max(0, min(16383, int(roundf(__fmul_rn(exp2f(x), 16383.0f)))));
+  };
+  int acc[32];
 #pragma unroll
-    for (int m = 0; m < kMaxPos / 32; ++m) {
-      const int j = lane + 32 * m;
-      sv[m] = -INFINITY;
-      if (j < L) {
-        const int4 ka = sm.ka[j], kb = sm.kb[j];
-        int acc = __dp4a(qa.x, ka.x, 0);
-        acc = __dp4a(qa.y, ka.y, acc);
-        acc = __dp4a(qa.z, ka.z, acc);
-        acc = __dp4a(qa.w, ka.w, acc);
-        acc = __dp4a(qb.x, kb.x, acc);
-        acc = __dp4a(qb.y, kb.y, acc);
-        acc = __dp4a(qb.z, kb.z, acc);
-        acc = __dp4a(qb.w, kb.w, acc);
-        sv[m] = __fmul_rn(__fmul_rn(__int2float_rn(acc), sm.ks[j]), qsc);
-        mx = fmaxf(mx, sv[m]);
-      }
-    }
+  for (int c = 0; c < 32; ++c) acc[c] = 0;
+  int isum = 0;
+  for (int p = 0; p < pairs; ++p) {
+    const int p0 = prob(2 * p), p1 = prob(2 * p + 1);
+    isum += p0 + p1;
+    const int pp = int(uint32_t(p0) | (uint32_t(p1) << 16));
+    const int4* vr = reinterpret_cast<const int4*>(sm.v[p]);
 #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    int isum = 0;
+    for (int g = 0; g < 4; ++g) {
+      const int4 wv = vr[g];
+      acc[8 * g + 0] = __dp2a_lo(pp, wv.x, acc[8 * g + 0]);
+      acc[8 * g + 1] = __dp2a_hi(pp, wv.x, acc[8 * g + 1]);
+      acc[8 * g + 2] = __dp2a_lo(pp, wv.y, acc[8 * g + 2]);
+      acc[8 * g + 3] = __dp2a_hi(pp, wv.y, acc[8 * g + 3]);
+      acc[8 * g + 4] = __dp2a_lo(pp, wv.z, acc[8 * g + 4]);
+      acc[8 * g + 5] = __dp2a_hi(pp, wv.z, acc[8 * g + 5]);
+      acc[8 * g + 6] = __dp2a_lo(pp, wv.w, acc[8 * g + 6]);
+      acc[8 * g + 7] = __dp2a_hi(pp, wv.w, acc[8 * g + 7]);
+    }
+  }
+  const float p_scale = __fdiv_rn(1.0f, __int2float_rn(max(isum, 1)));
+  float4* o = reinterpret_cast<float4*>(a.out + size_t(s0 + qi) * kHidden + h * 32);
 #pragma unroll
-    for (int m = 0; m < kMaxPos / 32; ++m) {
-      const int j = lane + 32 * m;
-      if (j < L4) {
-        int q = 0;
-        if (j < L8) {
-          q = i8_exp2_q(__fsub_rn(sv[m], mx), cexp);
-        } else if (j < L) {
-          q = int(roundf(__fmul_rn(exp2f(__fsub_rn(sv[m], mx)), 16383.0f)));
-          q = max(0, min(16383, q));
-        }
-        isum += q;
-        prow[j] = int16_t(q);
-      }
-    }
+  for (int g = 0; g < 8; ++g) {
+    float r[4];
 #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) isum += __shfl_xor_sync(0xffffffffu, isum, o);
-    const float p_scale = __fdiv_rn(1.0f, __int2float_rn(max(isum, 1)));
-    __syncwarp();
-    // four independent integer sums (exact in any order: |sum| < 512 * 16383 * 127 < 2^31)
-    int acc0 = 0, acc1 = 0, acc2 = 0, acc3 = 0;
-    const int2* pw = sm.p[warp];
-    const int nw = L4 >> 2;
-    int w = 0;
-#pragma unroll 4
-    for (; w + 2 <= nw; w += 2) {
-      const int4 pp = *reinterpret_cast<const int4*>(pw + w);  // keys 4w .. 4w+7
-      const int b0 = vcol[w], b1 = vcol[w + 1];
-      acc0 = __dp2a_lo(pp.x, b0, acc0);
-      acc1 = __dp2a_hi(pp.y, b0, acc1);
-      acc2 = __dp2a_lo(pp.z, b1, acc2);
-      acc3 = __dp2a_hi(pp.w, b1, acc3);
+    for (int e = 0; e < 4; ++e) {
+      const int c = 4 * g + e;
+      r[e] = __fmul_rn(__int2float_rn(acc[c]), __fmul_rn(sm.v_scale[c], p_scale));
     }
-    if (w < nw) {
-      const int2 pp = pw[w];
-      const int b = vcol[w];
-      acc0 = __dp2a_lo(pp.x, b, acc0);
-      acc1 = __dp2a_hi(pp.y, b, acc1);
-    }
-    const int acc = (acc0 + acc1) + (acc2 + acc3);
-    a.out[size_t(s0 + i0 + qi) * kHidden + h * 32 + lane] =
-        __fmul_rn(__int2float_rn(acc), __fmul_rn(sm.v_scale[lane], p_scale));
-    __syncwarp();
+    o[g] = make_float4(r[0], r[1], r[2], r[3]);
   }
 }
 
@@ -1760,7 +1761,7 @@ int launch_attention_i8(const AttnArgs& a, int n_seqs, int min_len, cudaStream_t
   if (n_seqs <= 0) return 0;
   if (a.max_len <= 0 || a.max_len > kMaxPos || a.cls_mode) return -1;
   const dim3 grid(n_seqs, kHeads, (a.max_len + kI8Queries - 1) / kI8Queries);
-  return launch_pdl(k_attention_i8, grid, dim3(kI8Threads), 0, st, a, min_len) == cudaSuccess ? 0 : -3;
+  return launch_pdl(k_attention_i8, grid, dim3(kI8Queries), 0, st, a, min_len) == cudaSuccess ? 0 : -3;
 }
 
 int launch_attention_exact(const AttnArgs& a, int n_seqs, cudaStream_t st, int* quantized) {
