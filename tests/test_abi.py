@@ -52,6 +52,9 @@ def test_errors_are_codes_not_crashes():
     assert lib.ae_ctx_create(0, None) == -1
     assert lib.ae_sync(None) == -1
     assert lib.ae_forward_cls(None, None, 0, None) == -1
+    assert lib.ae_set_attention_mode(None, 1) == -1
+    assert lib.ae_get_attention_mode(None) == -1
+    assert lib.ae_attention_i8(None, None, None, 1, 16, None) == -1
 
 
 def test_plan_shards_balances_cost():

@@ -87,12 +87,15 @@ def test_truncation(oracle_model):
 
 
 def test_golden_fixture(pack_path, oracle_model):
-    """Committed fixture: the seeded pack's digest and the oracle's embeddings of a few sequences."""
+    """Committed fixture: the seeded pack's digest and the oracle's embeddings of a few sequences,
+    with the fp32 attention and in the int8 attention mode."""
     g = np.load(GOLDEN)
     assert synth.file_sha256(pack_path) == str(g["pack_sha256"])
+    m8 = orc.OracleModel(pack_path).set_attention_mode(orc.ATTENTION_INT8)
     for i in range(int(g["n"])):
         ids = g[f"ids_{i}"]
         np.testing.assert_allclose(oracle_model.forward_cls(ids), g[f"emb_{i}"], rtol=0, atol=1e-6)
+        np.testing.assert_allclose(m8.forward_cls(ids), g[f"emb_i8_{i}"], rtol=0, atol=1e-6)
 
 
 def test_pack_round_trip_and_errors(pack_path, tmp_path):
