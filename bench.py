@@ -10,10 +10,17 @@ torchrun, no collective on the data path: weak scaling). Synthetic seeded model 
             total = max over ranks
   e2e       the same metric through the public host API (ae_forward_ragged): every step copies the
             ids from host memory to the GPU and the embeddings back, host wall clock, max over ranks
-  latency   p50 / p99 of ae_forward_cls (batch 1, CUDA-graph replay, host buffers) at 32 and 512 tokens
-  roofline  the dominant kernel of a step, timed alone with CUDA events at the step's shapes
+  latency   p50 / p99 of ae_forward_cls (batch 1, CUDA-graph replay, host buffers) at 8, 32, 128 and
+            512 tokens (config 2), with latency_roofline (int8 ops / p50 against the measured int8
+            peak; weight bytes / p50 against HBM)
+  roofline  the dominant kernel of a step, timed with CUDA events around its launches in the step
   cpu_baseline  the CPU oracle (C++ restatement of the reference's x86 path) on a bounded sample,
-            all host threads
+            all host threads; cpu_latency: its single-threaded forward_cls at 8/32/128/512 tokens
+  int8_peak the library's own tcgen05 kind::i8 loop (one CTA per SM, resident operands)
+  micro     config 5: the GEMM shapes and the 64 x 12 x 512 attention (N = 1)
+  ragged    config 4: 131,072 log-uniform sequences through ae_embed_batch_multi (N = 1)
+  multi_api at N > 1, rank 0 alone drives all N GPUs through ae_embed_batch_multi (the product's
+            multi-GPU entry point: planner, host threads, pinned staging, host gather)
 
 `--impl reference` times the reference's CPU path (the oracle; the Rust crate cannot be built
 here) on the same metric and prints its own JSON line.
@@ -166,6 +173,43 @@ def cpu_baseline(seconds: float = 10.0, L: int = SEQ_LEN, threads: int | None = 
             "cpu": _cpu_name()}
 
 
+def cpu_latency(runs: int = 100) -> dict:
+    """Config 2 on the CPU: the oracle's single-threaded forward_cls (the reference's x86 path) at 8,
+    32, 128 and 512 tokens, p50 / p99 over `runs` calls after 3 warm-up calls, on the same ids as
+    the GPU latency (the reference's own sweep: src/bin/arctic_embed.rs:99-138)."""
+    from arctic_embed_s_int8 import synth
+    from oracle import oracle as orc
+
+    orc.build()
+    m = orc.OracleModel(synth.pack_path(0))
+    r = np.random.Generator(np.random.PCG64(42))
+    out = {"cores": 1, "kind": "port", "runs": runs, "cpu": _cpu_name(),
+           "api": "oracle forward_cls, one thread (the backend SimdBackend::detect picks on this host)"}
+    for L in (8, 32, 128, 512):
+        ids = synth.token_ids(L, r)
+        for _ in range(3):
+            m.forward_cls(ids)
+        ts = []
+        for _ in range(runs):
+            t0 = time.perf_counter()
+            m.forward_cls(ids)
+            ts.append((time.perf_counter() - t0) * 1e3)
+        out[f"p50_ms@{L}"] = float(np.percentile(ts, 50))
+        out[f"p99_ms@{L}"] = float(np.percentile(ts, 99))
+    return out
+
+
+def weight_bytes_per_forward() -> int:
+    """Model bytes one forward pass must read: the int8 weights of layers 0-10 (QKV, attention-out,
+    FFN-up, FFN-down) and of layer 11's KV / Q / attention-out / FFN, with their f32 scales and
+    biases, plus the LayerNorm vectors (the embedding rows of the tokens are counted apart)."""
+    H, I = 384, 1536
+    lin = lambda n, k: n * k + 8 * n + 4 * k  # int8 weights + w_scale, bias + inv_smooth
+    per_layer = lin(3 * H, H) + lin(H, H) + lin(I, H) + lin(H, I) + 4 * 4 * H
+    last = lin(2 * H, H) + lin(H, H) + lin(H, H) + lin(I, H) + lin(H, I) + 4 * 4 * H
+    return 11 * per_layer + last + 2 * 4 * H
+
+
 def _cpu_name():
     try:
         with open("/proc/cpuinfo") as f:
@@ -251,14 +295,13 @@ def measure_fp32_peak() -> float:
     return 2.0 * 8192 ** 3 / best / 1e9
 
 
-def microbench(eng, stream, peaks: dict) -> dict:
+def microbench(eng, stream, peaks: dict, i8peak: float) -> dict:
     """Config 5: the four int8 GEMM shapes x M in {512, 8192, 65536} (plain dequant epilogue, and the
     fused model epilogue where the shape has one) and the masked attention over 64 x 12 x 512 x 32
     (fp32 in the reference's order, and the reference's int8 scheme). CUDA events on the launch stream, median of 5 after warm-up, L2 flushed before each."""
     import torch
 
     hbm = peaks.get("hbm_gbs", 6650.0)
-    i8peak = 2.0 * peaks.get("bf16_tflops", 1590.0)
     g = torch.Generator(device="cpu").manual_seed(5)
     flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device="cuda")
 
@@ -326,8 +369,8 @@ def microbench(eng, stream, peaks: dict) -> dict:
     ms8 = timed(lambda: eng.attention_i8(qkv, cu, n, L, ctx))
     out["attention_int8"] = {"shape": "64 x 12 heads x 512 x 32, the reference's int8 scheme (dp4a Q.K, dp2a P.V)",
                              "ms": ms8, "int_tops": fl / ms8 / 1e9}
-    out["basis"] = (f"roofline_ms = max(ops / int8 peak (2 x measured bf16 = {i8peak:.0f} TOPS), bytes / measured "
-                    f"HBM {hbm} GB/s); frac = roofline_ms / ms")
+    out["basis"] = (f"roofline_ms = max(ops / int8 peak ({i8peak:.0f} TOPS, measured by ae_measure_int8_peak), "
+                    f"bytes / HBM {hbm} GB/s of measured); frac = roofline_ms / ms")
     return out
 
 
@@ -356,6 +399,45 @@ def ragged_throughput(eng) -> dict:
             "api": "ae_embed_batch_multi, host buffers (wall clock, includes packing and copies)"}
 
 
+def multi_api(world: int, pack: str, steps: int) -> dict:
+    """The product's multi-GPU entry point, driven by one process over all `world` GPUs:
+    ae_embed_batch_multi (token-weighted shard plan, one host thread and context per GPU, pinned
+    staging, host gather of the 384-d outputs; no collective) on (a) the config-3 set of this run
+    (world x 512 x steps sequences of 128 tokens) and (b) config 4 (131,072 log-uniform sequences).
+    Wall clock around the call (host ids in, host embeddings out), after a warm-up call; then a
+    profiled pass gives each GPU's busy time (sum of its kernels' CUDA-event times)."""
+    from arctic_embed_s_int8 import Engine, embed_batch_multi, pack_sequences, synth
+
+    engines = [Engine(d).load_file(pack) for d in range(world)]
+    r = np.random.Generator(np.random.PCG64(2024))
+    sets = {
+        "config3": [synth.token_ids(SEQ_LEN, r) for _ in range(world * BATCH_SEQS * steps)],
+        "config4": [synth.token_ids(int(L), r)
+                    for L in np.exp(r.uniform(np.log(8), np.log(512), 131072)).astype(np.int64)],
+    }
+    out = {"gpus": world, "api": "ae_embed_batch_multi (one process, one context and host thread per GPU)"}
+    for name, seqs in sets.items():
+        ids, cu = pack_sequences(seqs)
+        embed_batch_multi(engines, ids=ids[: int(cu[world * 256])], cu=cu[: world * 256 + 1])  # warm-up
+        t0 = time.perf_counter()
+        embed_batch_multi(engines, ids=ids, cu=cu)
+        dt = time.perf_counter() - t0
+        for e in engines:
+            e.profile(True)
+        embed_batch_multi(engines, ids=ids, cu=cu)
+        busy = []
+        for e in engines:
+            e.sync()
+            busy.append(round(sum(v[0] for v in e.profile_read().values()) / 1e3, 4))
+            e.profile(False)
+        out[name] = {"sequences": len(seqs), "tokens": int(cu[-1]), "seconds": dt,
+                     "embeddings_per_s": len(seqs) / dt, "device_busy_s": busy,
+                     "busy_over_wall": round(max(busy) / dt, 3)}
+    for e in engines:
+        e.close()
+    return out
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -365,9 +447,17 @@ def main() -> int:
     ap.add_argument("--latency-runs", type=int, default=1000)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seqs-per-step", type=int, default=64)
-    ap.add_argument("--no-extras", action="store_true", help="skip latency, kernel breakdown and CPU baseline")
-    ap.add_argument("--micro", action="store_true", help="also run the config-5 kernel microbenchmarks")
-    ap.add_argument("--ragged", action="store_true", help="also run config 4 (131,072 ragged sequences)")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip latency, kernel breakdown, CPU baselines, configs 4 and 5, multi_api")
+    ap.add_argument("--cpu-latency-runs", type=int, default=100)
+    ap.add_argument("--no-cpu-latency", action="store_true", help="skip the CPU latency baseline")
+    ap.add_argument("--no-micro", action="store_true", help="skip the config-5 kernel microbenchmarks")
+    ap.add_argument("--no-ragged", action="store_true", help="skip config 4 (131,072 ragged sequences)")
+    ap.add_argument("--latency-only", type=int, default=0, metavar="L",
+                    help="only replay ae_forward_cls at L tokens (--latency-runs times) and print its p50 "
+                         "(a small case for profilers)")
+    ap.add_argument("--micro-only", action="store_true",
+                    help="only run the config-5 kernel microbenchmarks (a small case for profilers)")
     ap.add_argument("--attention", default="exact", choices=["exact", "int8"],
                     help="attention of layers 0-10: fp32 in the reference's x86 order (default) or the "
                          "reference's int8 scheme (ae_set_attention_mode)")
@@ -409,7 +499,33 @@ def main() -> int:
 
         eng.set_attention_mode(ATTENTION_INT8)
     stream = torch.cuda.Stream()
+    if args.latency_only:
+        # one length of config 2 alone (ae_forward_cls, CUDA-graph replay): a small case for profilers
+        ids = synth.token_ids(args.latency_only, np.random.Generator(np.random.PCG64(42)))
+        for _ in range(args.warmup):
+            eng.forward_cls(ids)
+        ts = []
+        for _ in range(args.latency_runs):
+            t0 = time.perf_counter()
+            eng.forward_cls(ids)
+            ts.append((time.perf_counter() - t0) * 1e3)
+        print(json.dumps({"latency_only": args.latency_only, "runs": args.latency_runs,
+                          "p50_ms": float(np.percentile(ts, 50)), "warmup": args.warmup}), flush=True)
+        eng.close()
+        return 0
     eng.set_stream(stream)
+    if args.micro_only:
+        # config 5 alone: a small case for profilers
+        peaks = {}
+        try:
+            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+                peaks = json.load(f)
+        except OSError:
+            pass
+        _, i8peak = eng.measure_int8_peak(100000)
+        print(json.dumps({"micro": microbench(eng, stream, peaks, i8peak), "int8_peak_tops": i8peak}), flush=True)
+        eng.close()
+        return 0
     n_batches = args.warmup + args.steps
     batches = make_batches(n_batches, seed=1000 + rank)
     T = BATCH_SEQS * SEQ_LEN
@@ -477,8 +593,20 @@ def main() -> int:
         "clocks": clk.summary(),
     }
 
-    if not args.no_extras and rank == 0:
-        # latency (config 2 subset): p50/p99 of forward_cls, host buffers, CUDA-graph replay
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    src = "of measured" if peaks else "of fallback"
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    if not args.no_extras and rank == 0 and world == 1:
+        # int8 tensor-pipe peak of this GPU: the library's own resident-operand tcgen05 kind::i8 loop
+        pk_ms, i8peak = eng.measure_int8_peak(100000)
+        result["int8_peak"] = {"tops": i8peak, "ms": pk_ms, "spec_dense_tops": 4500.0,
+                               "api": "ae_measure_int8_peak (148 CTAs x 100,000 rounds of M128 N256 K128)"}
+        # latency (config 2): p50/p99 of forward_cls, host buffers, CUDA-graph replay
         lat = {}
         r = np.random.Generator(np.random.PCG64(42))
         for L, runs in ((8, args.latency_runs), (32, args.latency_runs), (128, args.latency_runs),
@@ -495,15 +623,26 @@ def main() -> int:
             lat[f"p99_ms@{L}"] = float(np.percentile(ts, 99))
             lat[f"runs@{L}"] = runs
         result["latency"] = lat
+        wb = weight_bytes_per_forward()
+        result["latency_roofline"] = {
+            f"@{L}": {"int8_tops": int8_ops_per_seq(L) / (lat[f"p50_ms@{L}"] * 1e-3) / 1e12,
+                      "frac_int8_peak": int8_ops_per_seq(L) / (lat[f"p50_ms@{L}"] * 1e-3) / 1e12 / i8peak,
+                      "weight_gbs": (wb + L * (H + 4) * 2) / (lat[f"p50_ms@{L}"] * 1e-3) / 1e9,
+                      "frac_hbm": (wb + L * (H + 4) * 2) / (lat[f"p50_ms@{L}"] * 1e-3) / 1e9 / hbm}
+            for L in (8, 32, 128, 512)}
+        result["latency_roofline"]["basis"] = (
+            f"int8 ops of one sequence (2 x (19,759,104 L + 1,474,560)) / p50 against the measured int8 peak "
+            f"({i8peak:.0f} TOPS); model bytes one forward reads ({wb} B of weights, scales, biases and "
+            f"LayerNorm vectors + the L embedding rows) / p50 against HBM {hbm} GB/s {src}")
         # model start-up (config 2's companion, the reference's ~10 ms .ae8 load): ae_model_load_file
         # of the 33.8 MB pack into a context that already exists, median of 5 after one warm-up
         lt = []
         for i in range(6):
             t0 = time.perf_counter()
-            eng.load_file(synth.pack_path(0))
+            eng.load_file(pack)
             lt.append((time.perf_counter() - t0) * 1e3)
         result["model_load_ms"] = {"median": float(np.median(lt[1:])), "first": lt[0],
-                                   "api": "ae_model_load_file (mmap, one upload, device-side placement)"}
+                                   "api": "ae_model_load_file (mmap, pinned host image, one DMA, arena reused)"}
         # per-kernel times of the forward itself: CUDA events around every launch on the launch
         # stream, over K more steps of the same workload (profiling is off in the timed region)
         eng.profile(True)
@@ -520,22 +659,15 @@ def main() -> int:
         result["kernels_ms_per_step"] = {k: round(v, 4) for k, v in per_step_ms.items()}
         result["kernels_launches_per_step"] = {k: v[1] // args.steps for k, v in prof.items() if v[1]}
         dom = max(per_step_ms, key=per_step_ms.get)
-        peaks = {}
-        try:
-            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-                peaks = json.load(f)
-        except OSError:
-            pass
         bf16 = peaks.get("bf16_tflops", 1590.0)
-        src = "of measured" if peaks else "of fallback"
         launches = prof[dom][1] // args.steps
         ms_launch = per_step_ms[dom] / max(launches, 1)
         if dom in ("qkv", "attn_out", "ffn_up", "ffn_down"):
             ach = work[dom] / (per_step_ms[dom] * 1e-3) / 1e12
-            peak = 2.0 * bf16
-            result["roofline"] = {"kernel": dom, "bound": "tensor", "achieved": ach, "peak": peak, "unit": "TOPS (int8)",
-                                  "frac": ach / peak, "traffic": None, "ms_per_launch": ms_launch,
-                                  "peak_basis": f"int8 dense = 2 x bf16 dense {src} ({bf16} TFLOP/s)"}
+            result["roofline"] = {"kernel": dom, "bound": "tensor", "achieved": ach, "peak": i8peak,
+                                  "unit": "TOPS (int8)", "frac": ach / i8peak, "traffic": None,
+                                  "ms_per_launch": ms_launch,
+                                  "peak_basis": "int8 dense, measured by ae_measure_int8_peak in this run"}
         elif dom == "attention":
             ach = work[dom] / (per_step_ms[dom] * 1e-3) / 1e12
             fp32 = measure_fp32_peak()
@@ -546,28 +678,40 @@ def main() -> int:
                                   "ms_per_launch": ms_launch,
                                   "peak_basis": "measured here: cuBLAS SGEMM 8192^3, TF32 off (the attention keeps "
                                                 "the reference's fp32 operation order, so it runs on the CUDA cores)",
+                                  "fp32_issue_peak_at_max_clock": 148 * 128 * 2 * 1.965e9 / 1e12,
                                   "bf16_tensor_peak_of_measured": bf16}
         else:
-            hbm = peaks.get("hbm_gbs", 6650.0)
             ach = work.get(dom, 0.0) / (per_step_ms[dom] * 1e-3) / 1e9
             result["roofline"] = {"kernel": dom, "bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
                                   "frac": ach / hbm, "traffic": None, "ms_per_launch": ms_launch,
                                   "peak_basis": f"HBM copy bandwidth {src}"}
         result["int8_tops_whole_step"] = BATCH_SEQS * int8_ops_per_seq(SEQ_LEN) / (total_s / args.steps) / 1e12
+        if not args.no_micro:
+            result["micro"] = microbench(eng, stream, peaks, i8peak)
+        if not args.no_ragged:
+            result["ragged"] = ragged_throughput(eng)
         try:
             result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
         except Exception as e:  # reported, not fatal
             result["cpu_baseline"] = {"error": str(e)}
-    if rank == 0 and args.micro:
-        peaks = {}
-        try:
-            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-                peaks = json.load(f)
-        except OSError:
-            pass
-        result["micro"] = microbench(eng, stream, peaks)
-    if rank == 0 and args.ragged:
-        result["ragged"] = ragged_throughput(eng)
+        if not args.no_cpu_latency:
+            try:
+                result["cpu_latency"] = cpu_latency(args.cpu_latency_runs)
+            except Exception as e:  # reported, not fatal
+                result["cpu_latency"] = {"error": str(e)}
+    if world > 1 and not args.no_extras:
+        # the product's multi-GPU entry point: rank 0 alone drives every GPU of the box while the
+        # other ranks wait on a host-side (gloo) barrier, which leaves their GPUs idle
+        from datetime import timedelta
+
+        host = dist.new_group(backend="gloo", timeout=timedelta(seconds=900))
+        dist.barrier(group=host)
+        if rank == 0:
+            try:
+                result["multi_api"] = multi_api(world, pack, args.steps)
+            except Exception as e:  # reported, not fatal
+                result["multi_api"] = {"error": str(e)}
+        dist.barrier(group=host)
     if rank == 0:
         print(json.dumps(result), flush=True)
     eng.close()

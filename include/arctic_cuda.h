@@ -166,19 +166,39 @@ int ae_attention_i8(ae_ctx* ctx, const float* d_qkv, const uint32_t* d_cu_seqlen
                     uint32_t max_len, float* d_ctx);
 
 /* Allocation-free variant of the single-sequence forward, for callers that cannot call cudaMalloc
- * when they embed: code recording into a CUDA graph it is capturing, hosts that hand out device
- * memory once at start-up from their own pool, latency paths that must not wait on the allocator.
- * No counterpart in the reference (the CPU crate gets the same effect from a reusable Workspace).
+ * when they embed: hosts that hand out device memory once at start-up from their own pool (a
+ * service with a fixed memory budget), and latency paths that must not block on the allocator
+ * (cudaMalloc / cudaFree can synchronise the device). No counterpart in the reference (the CPU
+ * crate gets the same effect from a reusable Workspace).
  * d_ids: 1..512 token ids in device memory of ctx's GPU (longer inputs are rejected with
  * AE_ERR_CAPACITY: truncate to the first 512 first); d_out384: device float[384]. Asynchronous on
  * the context's stream. The model must already be loaded (ae_model_load allocates; this call
  * does not). Scratch: a file-scope 8 MiB device array in the library, which every GPU that loads
- * the library holds until the process exits. The first call on a device looks up that array's
- * device address (cudaGetSymbolAddress) and builds its tensor maps; make that first call before
- * any stream capture. Every call shares the one array and nothing in it has to start at zero (the
- * call writes every row it reads); calls that overlap on the GPU, from any context on the same
- * device, race on it. */
+ * the library holds until the process exits. The first call on a device (and the first call after
+ * a device reset, which moves the array) looks up that array's device address
+ * (cudaGetSymbolAddress) and builds its tensor maps; make that first call before any stream
+ * capture. Every call shares the one array, which keeps the last call's contents: nothing in it
+ * has to start at zero, because every row a kernel's result depends on is written by this call
+ * first (the GEMMs load whole 128-row tiles, so rows past len still hold an earlier call's data;
+ * rows are independent and those rows' results are never stored). Calls that overlap on the GPU,
+ * from any context on the same device, race on the array. Per-kernel profiling (ae_profile) does
+ * not record this call. */
 int ae_forward_cls_noalloc(ae_ctx* ctx, const uint16_t* d_ids, uint32_t len, float* d_out384);
+
+/* Test hook (no counterpart in the reference's API; it exposes what the reference computes inside
+ * forward_ragged_cls, src/model.rs:521-914): runs the forward pass of a packed batch of host
+ * sequences, as ae_forward_ragged does, up to `stage` and copies rows of the device workspace back,
+ * in the caller's order (T = the sum of the sequences' lengths, each truncated to 512):
+ *   AE_TRACE_EMBED: f32 [T, 384] = the hidden state after the embedding LayerNorm; q [T, 384] and
+ *     scale [T] = its quantization for layer 0's QKV GEMM (dequant_add_embeddings_row,
+ *     src/simd_math.rs:1827-1881, + layernorm_smooth_quantize_row, src/model.rs:196-219);
+ *   AE_TRACE_ATTN0: f32 = layer 0's attention context; q / scale = its SmoothQuant row quantization
+ *     with attn_out.inv_smooth (smooth_quantize_row, src/simd_math.rs:584-649), the attention-out
+ *     GEMM's input, from whichever kernel the forward pass used for it (a separate kernel, or the
+ *     attention kernel itself for short single sequences). */
+enum { AE_TRACE_EMBED = 0, AE_TRACE_ATTN0 = 1 };
+int ae_trace_forward(ae_ctx* ctx, const uint16_t* ids, const uint32_t* cu_seqlens, uint32_t n_seqs, int stage,
+                     float* f32, int8_t* q, float* scale);
 
 /* Per-kernel timing of the forward pass (CUDA events around every launch on the context's stream).
  * Kinds, in the order of the forward pass: */
@@ -204,6 +224,13 @@ uint64_t ae_kernel_launches(const ae_ctx* ctx);
 
 /* Waits for the context's stream; reports a device-side error (AE_ERR_DEVICE) if one was raised. */
 int ae_sync(ae_ctx* ctx);
+
+/* Measured int8 tensor-core throughput of this GPU (no counterpart in the reference; the roofline
+ * denominator of the GEMMs): one CTA per SM issues `iters` (1..1,000,000) rounds of tcgen05.mma
+ * kind::i8 (M = 128, N = 256, K = 128 per round) on operands resident in shared memory, after one
+ * shorter warm-up launch. *ms = CUDA-event time of the timed launch, *tops = its int8 ops / time
+ * in 10^12 ops/s. */
+int ae_measure_int8_peak(ae_ctx* ctx, uint32_t iters, float* ms, double* tops);
 
 /* Self-test of failure detection (no reference counterpart): launches a kernel whose bounded wait
  * on an mbarrier can never complete, with a limit of limit_us microseconds (1..1,000,000) instead

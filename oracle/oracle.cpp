@@ -1066,6 +1066,17 @@ void or_forward_trace(const or_model* m, const uint16_t* ids, uint32_t len, int8
   forward_cls(*m, ids, len, ws, out, &tr);
 }
 
+// The embedding rows of one sequence (dequant_add_embeddings_row, src/simd_math.rs:1827-1881, then
+// the first layernorm_smooth_quantize_row with layers[0].qkv.inv_smooth, src/model.rs:196-219).
+void or_embed_rows(const or_model* m, const uint16_t* ids, uint32_t len, float* hidden, int8_t* q, float* scale) {
+  Workspace ws;
+  const size_t L = len < MAXPOS ? len : MAXPOS;
+  embed_rows(*m, ids, L, 0, ws);
+  std::memcpy(hidden, ws.hidden.data(), L * H * 4);
+  std::memcpy(q, ws.act_q.data(), L * H);
+  std::memcpy(scale, ws.act_scale.data(), L * 4);
+}
+
 void or_forward_ragged(const or_model* m, const uint16_t* ids, const uint32_t* cu, uint32_t n, float* out) {
   thread_local Workspace ws;
   std::vector<const uint16_t*> seqs(n);

@@ -53,6 +53,11 @@ void or_embed_batch(const or_model* m, const uint16_t* ids, const uint32_t* cu, 
 void or_forward_trace(const or_model* m, const uint16_t* ids, uint32_t len, int8_t* gemm_in_q, float* gemm_in_s,
                       float* qkv_out, float* ctx, float* hidden, int8_t* down_in_q, float* down_in_s);
 
+/* The embedding rows of one sequence of L = min(len, 512) ids: hidden [L][384] after the embedding
+ * LayerNorm, q [L][384] / scale [L] its quantization with layers[0].qkv.inv_smooth
+ * (src/simd_math.rs:1827-1881, src/model.rs:196-219). */
+void or_embed_rows(const or_model* m, const uint16_t* ids, uint32_t len, float* hidden, int8_t* q, float* scale);
+
 /* gemm_int8_fused (src/gemm.rs:630-671) with a row-major [N,K] weight packed for `backend`;
  * acc_out (nullable) receives the int32 accumulators. */
 void or_gemm(int backend, uint32_t M, uint32_t K, uint32_t N, const int8_t* a_q, const float* a_scale,

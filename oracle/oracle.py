@@ -50,6 +50,7 @@ def lib():
     L.or_forward_ragged.argtypes = [P, u16p, u32p, C.c_uint32, f32p]
     L.or_embed_batch.argtypes = [P, u16p, u32p, C.c_uint32, C.c_uint32, f32p]
     L.or_forward_trace.argtypes = [P, u16p, C.c_uint32, i8p, f32p, f32p, f32p, f32p, i8p, f32p]
+    L.or_embed_rows.argtypes = [P, u16p, C.c_uint32, f32p, i8p, f32p]
     L.or_gemm.argtypes = [C.c_int, C.c_uint32, C.c_uint32, C.c_uint32, i8p, f32p, i8p, f32p, f32p, f32p, f32p, i32p]
     L.or_layernorm_smooth_quantize_row.restype = C.c_float
     L.or_layernorm_smooth_quantize_row.argtypes = [f32p, f32p, f32p, f32p, i8p, C.c_uint32]
@@ -140,6 +141,17 @@ class OracleModel:
         out = np.zeros((n, H), np.float32)
         lib().or_embed_batch(self._h, _p(ids, C.c_uint16), _p(cu, C.c_uint32), n, threads, _p(out, C.c_float))
         return out
+
+    def embed_rows(self, ids):
+        """(hidden [L,384], q [L,384], scale [L]): the embedding LayerNorm rows of one sequence and their
+        quantization for layer 0's QKV GEMM."""
+        ids = np.ascontiguousarray(ids, dtype=np.uint16)
+        L = min(len(ids), 512)
+        hid = np.zeros((L, H), np.float32)
+        q = np.zeros((L, H), np.int8)
+        sc = np.zeros(L, np.float32)
+        lib().or_embed_rows(self._h, _p(ids, C.c_uint16), len(ids), _p(hid, C.c_float), _p(q, C.c_int8), _p(sc, C.c_float))
+        return hid, q, sc
 
     def trace(self, ids) -> dict:
         ids = np.ascontiguousarray(ids, dtype=np.uint16)

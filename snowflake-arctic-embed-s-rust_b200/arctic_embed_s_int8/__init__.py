@@ -163,6 +163,21 @@ class Engine:
         self._check(lib().ae_forward_ragged_device(self._h, _ptr(d_ids), _ptr(d_cu), n_seqs, total_tokens, max_len,
                                                    _ptr(d_out)))
 
+    TRACE_EMBED, TRACE_ATTN0 = 0, 1
+
+    def trace(self, seqs, stage: int):
+        """ae_trace_forward (a test hook): (f32 [T,384], q [T,384], scale [T]) of the forward pass of
+        `seqs` stopped at TRACE_EMBED (embedding LayerNorm rows and their quantization) or
+        TRACE_ATTN0 (layer 0's attention context and its quantization), rows in the caller's order."""
+        ids, cu = pack_sequences(seqs)
+        T = int(sum(min(len(s), MAX_POSITIONS) for s in seqs))
+        f32 = np.zeros((T, HIDDEN_SIZE), np.float32)
+        q = np.zeros((T, HIDDEN_SIZE), np.int8)
+        sc = np.zeros(T, np.float32)
+        self._check(lib().ae_trace_forward(self._h, _ptr(ids), _ptr(cu), len(seqs), stage, _ptr(f32), _ptr(q),
+                                           _ptr(sc)))
+        return f32, q, sc
+
     def gemm_i8(self, epi, a, a_scale, w, w_scale, bias, res=None, gamma=None, beta=None, inv_smooth=None, out=None,
                 out_q=None, out_scale=None, acc=None) -> None:
         M, K = a.shape
@@ -186,6 +201,12 @@ class Engine:
     @property
     def attention_mode(self) -> int:
         return int(lib().ae_get_attention_mode(self._h))
+
+    def measure_int8_peak(self, iters: int = 100000) -> tuple[float, float]:
+        """ae_measure_int8_peak: (ms, int8 TOPS) of the resident-operand tcgen05 kind::i8 loop."""
+        ms, tops = C.c_float(), C.c_double()
+        self._check(lib().ae_measure_int8_peak(self._h, iters, C.byref(ms), C.byref(tops)))
+        return float(ms.value), float(tops.value)
 
     def sync(self) -> None:
         self._check(lib().ae_sync(self._h))

@@ -34,6 +34,7 @@ SYMBOLS = [
     "ae_tokenizer_create_from_file", "ae_tokenizer_create_from_vocab", "ae_tokenizer_destroy",
     "ae_tokenizer_vocab_size", "ae_tokenizer_last_error", "ae_tokenize", "ae_tokenize_batch",
     "ae_selftest_wait_timeout", "ae_set_attention_mode", "ae_get_attention_mode", "ae_attention_i8",
+    "ae_trace_forward", "ae_measure_int8_peak",
 ]
 
 
@@ -112,6 +113,8 @@ def lib():
     L.ae_profile.argtypes = [P, C.c_int]
     L.ae_profile_read.argtypes = [P, P, P]
     L.ae_selftest_wait_timeout.argtypes = [P, u32]
+    L.ae_trace_forward.argtypes = [P, P, P, u32, C.c_int, P, P, P]
+    L.ae_measure_int8_peak.argtypes = [P, u32, C.POINTER(C.c_float), C.POINTER(C.c_double)]
     L.ae_tokenizer_create_from_file.argtypes = [C.c_char_p, C.POINTER(P)]
     L.ae_tokenizer_create_from_vocab.argtypes = [C.c_char_p, C.c_size_t, C.POINTER(P)]
     L.ae_tokenizer_destroy.argtypes = [P]

@@ -114,6 +114,8 @@ struct ae_ctx {
   uint32_t* d_cu_single = nullptr;  // [513][2]: {0, L} at 2L, the cu_seqlens of one sequence of L ids
   bool has_model = false;
   DevModel model;
+  void* h_model = nullptr;  // pinned host image of the model arena (reused across loads)
+  size_t h_model_bytes = 0;
   Workspace ws;
   std::map<uint32_t, Graph> graphs;  // forward_cls graph per sequence length
   std::string err;
@@ -195,33 +197,44 @@ bool check_linear(const ae_linear_desc& d, uint64_t n, uint64_t k, bool allow_pr
   return d.n_out == n && d.k_in == k && d.w_q && d.w_scale && d.bias && d.inv_smooth;
 }
 
-// Model upload. From a descriptor of host arrays: every tensor is copied to its offset in a host
-// image of the device arena, and one cudaMemcpy moves the image. From a mapped .ae8 file: the file
-// is copied to the GPU as it is, and each tensor moves to its aligned arena slot with a
-// device-to-device copy (no host-side copy of the 34 MB at all).
+// Model upload: every tensor is copied (memcpy on host threads) to its offset in a host image of
+// the device arena, held in pinned memory that the context keeps across loads, and one DMA moves
+// the image to the arena. A reload of the same model shape reuses the arena (no cudaFree /
+// cudaMalloc); when every tensor lands at its old address, the captured single-sequence graphs stay
+// valid, since they hold device addresses, not data.
 struct Uploader {
   const uint8_t* dev_base = nullptr;  // the model arena
-  uint8_t* host = nullptr;            // host image of the arena (descriptor loads), or
-  const uint8_t* file = nullptr;      // the mapped .ae8 file (file loads)
-  size_t file_size = 0;
-  const uint8_t* dev_file = nullptr;  // its copy on the device
+  uint8_t* host = nullptr;            // pinned host image of the arena
   struct Copy {
-    void* dst;
+    size_t off;
     const void* src;
     size_t n;
   };
-  std::vector<Copy> d2d, h2d;
+  std::vector<Copy> copies;
+  size_t bytes = 0;
   template <class T>
   void put(T* dst, const void* src, size_t n) {
-    const size_t bytes = n * sizeof(T);
-    const auto* sp = static_cast<const uint8_t*>(src);
-    if (host) {
-      std::memcpy(host + (reinterpret_cast<const uint8_t*>(dst) - dev_base), src, bytes);
-    } else if (sp >= file && sp + bytes <= file + file_size) {
-      d2d.push_back(Copy{dst, dev_file + (sp - file), bytes});
-    } else {
-      h2d.push_back(Copy{dst, src, bytes});  // host-side values built during the load
-    }
+    const size_t b = n * sizeof(T);
+    copies.push_back(Copy{size_t(reinterpret_cast<const uint8_t*>(dst) - dev_base), src, b});
+    bytes += b;
+  }
+  // Runs the copies, split into byte ranges of about equal size over a few host threads.
+  void run() {
+    const int nt = bytes >= (size_t(8) << 20) ? 4 : 1;
+    auto part = [&](int t) {
+      const size_t lo = bytes * size_t(t) / size_t(nt), hi = bytes * size_t(t + 1) / size_t(nt);
+      size_t at = 0;
+      for (const Copy& cp : copies) {
+        const size_t a = std::max(lo, at), b = std::min(hi, at + cp.n);
+        if (a < b) std::memcpy(host + cp.off + (a - at), static_cast<const uint8_t*>(cp.src) + (a - at), b - a);
+        at += cp.n;
+        if (at >= hi) break;
+      }
+    };
+    std::vector<std::thread> th;
+    for (int t = 1; t < nt; ++t) th.emplace_back(part, t);
+    part(0);
+    for (auto& x : th) x.join();
   }
 };
 
@@ -239,6 +252,25 @@ int upload_linear(ae_ctx* c, Carve& cv, Uploader& img, const ae_linear_desc& d, 
   img.put(o.bias, d.bias, d.n_out);
   if (make_tmap_i8(&o.tmap, o.w, o.n, o.k, kBoxB) != 0) return fail(c, AE_ERR_CUDA, "cuTensorMapEncodeTiled failed for weights");
   return 0;
+}
+
+// True when every tensor of a and b sits at the same device address with the same shape (a tensor
+// map is a function of its address and shape, so those agree too).
+bool same_placement(const DevModel& a, const DevModel& b) {
+  auto lin = [](const DevLinear& x, const DevLinear& y) {
+    return x.n == y.n && x.k == y.k && x.w == y.w && x.ws == y.ws && x.bias == y.bias && x.inv_s == y.inv_s;
+  };
+  if (a.arena != b.arena || a.word_q != b.word_q || a.word_s != b.word_s || a.pos_q != b.pos_q || a.pos_s != b.pos_s ||
+      a.type0 != b.type0 || a.emb_lnw != b.emb_lnw || a.emb_lnb != b.emb_lnb)
+    return false;
+  for (int l = 0; l < kLayers; ++l) {
+    const DevLayer &x = a.layers[l], &y = b.layers[l];
+    if (!lin(x.qkv, y.qkv) || !lin(x.q_only, y.q_only) || !lin(x.kv_only, y.kv_only) || !lin(x.ao, y.ao) ||
+        !lin(x.fi, y.fi) || !lin(x.fo, y.fo) || x.ln1w != y.ln1w || x.ln1b != y.ln1b || x.ln2w != y.ln2w ||
+        x.ln2b != y.ln2b)
+      return false;
+  }
+  return true;
 }
 
 void free_model(ae_ctx* c) {
@@ -534,8 +566,10 @@ int gemm_ln(ae_ctx* c, const CUtensorMap& ta, const DevLinear& L, int M, const f
 // knows the lengths); the attention of layers 0-10 then launches once per run.
 // min_len: a lower bound of the sequence lengths (the int8 attention mode uses it when segs is
 // not given).
+// stop (ae_trace_forward): AE_TRACE_EMBED returns after the embedding kernel, AE_TRACE_ATTN0 after
+// layer 0's attention and context quantization; -1 runs the whole pass.
 int enqueue_forward(ae_ctx* c, const uint16_t* d_ids, const uint32_t* d_cu, int T, int n, int max_len, float* d_out,
-                    const std::vector<AttnSegment>* segs = nullptr, int min_len = 1) {
+                    const std::vector<AttnSegment>* segs = nullptr, int min_len = 1, int stop = -1) {
   Workspace& W = c->ws;
   const DevModel& M = c->model;
   cudaStream_t st = c->stream;
@@ -566,6 +600,7 @@ int enqueue_forward(ae_ctx* c, const uint16_t* d_ids, const uint32_t* d_cu, int 
     ProfScope ps(c, AE_KERNEL_EMBED);
     if (launch_embed(e, st)) return fail(c, AE_ERR_CUDA, "embedding launch failed");
   }
+  if (stop == AE_TRACE_EMBED) return 0;
 
   // QKV projection fused with the attention (sequences of at most 128 keys) only on request
   // (ARCTIC_FUSED_QKV=1): measured on config 3 it is 2 % slower than the QKV GEMM + attention
@@ -611,6 +646,7 @@ int enqueue_forward(ae_ctx* c, const uint16_t* d_ids, const uint32_t* d_cu, int 
       if (launch_smooth_quant(W.ctx, Ly.ao.inv_s, W.act_q, W.act_s, T, st))
         return fail(c, AE_ERR_CUDA, "context quantization launch failed");
     }
+    if (stop == AE_TRACE_ATTN0) return 0;
     {
       ProfScope ps(c, AE_KERNEL_ATTN_OUT);
       AE_TRY(gemm_ln(c, W.tm_act_q, Ly.ao, T, W.act_s, W.hidden, 1, Ly.ln1w, Ly.ln1b, Ly.fi.inv_s, W.act_q, W.act_s,
@@ -918,6 +954,7 @@ int ae_ctx_destroy(ae_ctx* c) {
   drop_graphs(c);
   free_ws(c);
   free_model(c);
+  if (c->h_model) cudaFreeHost(c->h_model);
   for (auto& e : c->prof_events) {
     cudaEventDestroy(e.second.first);
     cudaEventDestroy(e.second.second);
@@ -943,9 +980,9 @@ int ae_ctx_device(const ae_ctx* c) { return c ? c->device : AE_ERR_INVALID_ARG; 
 
 namespace {
 
-// ae_model_load with an optional source file: file / file_size is the mapped .ae8 pack that the
-// descriptor's pointers point into (then uploaded as is and sorted on the device).
-int load_model(ae_ctx* c, const ae_model_desc* d, const uint8_t* file, size_t file_size) {
+// ae_model_load: validates the descriptor, builds the arena image in the context's pinned staging
+// buffer and moves it with one DMA (see Uploader).
+int load_model(ae_ctx* c, const ae_model_desc* d) {
   // validation (the sizes src/quantize.rs:9-18 fix; the reference asserts them while packing)
   if (!d->word_emb_q || !d->word_emb_scale || !d->pos_emb_q || !d->pos_emb_scale || !d->type_emb_q ||
       !d->type_emb_scale || !d->emb_ln_weight || !d->emb_ln_bias)
@@ -963,13 +1000,12 @@ int load_model(ae_ctx* c, const ae_model_desc* d, const uint8_t* file, size_t fi
         return fail(c, AE_ERR_BAD_PACK, "layer %d: qkv must be 1152x384", l);
     } else {
       if (L.has_split != 1 || !check_linear(L.q_only, kHidden, kHidden, false) ||
-          !check_linear(L.kv_only, 2 * kHidden, kHidden, false) || L.qkv.k_in != kHidden || !L.qkv.inv_smooth)
+          !check_linear(L.kv_only, 2 * kHidden, kHidden, false) || L.qkv.k_in != kHidden || !L.qkv.inv_smooth ||
+          (L.qkv.n_out != 0 && !check_linear(L.qkv, 3 * kHidden, kHidden, false)))
         return fail(c, AE_ERR_BAD_PACK, "layer 11 must carry the [CLS]-pruned split (q_only 384x384, kv_only 768x384)");
     }
   }
   cudaStreamSynchronize(c->stream);
-  drop_graphs(c);
-  free_model(c);
   size_t bytes = size_t(kVocab) * kHidden + kVocab * 4 + kMaxPos * kHidden + kMaxPos * 4 + 3 * kHidden * 4 + 64 * 1024;
   for (int l = 0; l < kLayers; ++l) {
     const ae_layer_desc& L = d->layers[l];
@@ -977,34 +1013,29 @@ int load_model(ae_ctx* c, const ae_model_desc* d, const uint8_t* file, size_t fi
              4 * kHidden * 4 + 4096;
     if (L.has_split) bytes += linear_bytes(L.q_only) + linear_bytes(L.kv_only);
   }
-  void* arena = nullptr;
-  CUDA_TRY(c, cudaMalloc(&arena, bytes));
-  DevModel& M = c->model;
-  M.arena = arena;
-  M.arena_bytes = bytes;
-  Carve cv{static_cast<uint8_t*>(arena)};
-  Uploader img;
-  img.dev_base = static_cast<const uint8_t*>(arena);
-  std::unique_ptr<uint8_t[]> host;
-  void* dev_file = nullptr;
-  if (file) {
-    if (cudaMalloc(&dev_file, file_size) != cudaSuccess ||
-        cudaMemcpy(dev_file, file, file_size, cudaMemcpyHostToDevice) != cudaSuccess) {
-      if (dev_file) cudaFree(dev_file);
-      free_model(c);
-      return fail(c, AE_ERR_CUDA, "model upload failed");
-    }
-    img.file = file;
-    img.file_size = file_size;
-    img.dev_file = static_cast<const uint8_t*>(dev_file);
-  } else {
-    host.reset(new (std::nothrow) uint8_t[bytes]);
-    if (!host) {
-      free_model(c);
-      return fail(c, AE_ERR_CAPACITY, "host memory for the model image");
-    }
-    img.host = host.get();
+  // the arena of the previous model is reused when it is large enough
+  if (!c->model.arena || c->model.arena_bytes < bytes) {
+    drop_graphs(c);
+    free_model(c);
+    void* arena = nullptr;
+    CUDA_TRY(c, cudaMalloc(&arena, bytes));
+    c->model.arena = arena;
+    c->model.arena_bytes = bytes;
   }
+  if (c->h_model_bytes < bytes) {
+    if (c->h_model) cudaFreeHost(c->h_model);
+    c->h_model = nullptr;
+    c->h_model_bytes = 0;
+    CUDA_TRY(c, cudaMallocHost(&c->h_model, bytes));
+    c->h_model_bytes = bytes;
+  }
+  DevModel M = DevModel();
+  M.arena = c->model.arena;
+  M.arena_bytes = c->model.arena_bytes;
+  Carve cv{static_cast<uint8_t*>(M.arena)};
+  Uploader img;
+  img.dev_base = static_cast<const uint8_t*>(M.arena);
+  img.host = static_cast<uint8_t*>(c->h_model);
   M.word_q = cv.take<int8_t>(size_t(kVocab) * kHidden);
   M.word_s = cv.take<float>(kVocab);
   M.pos_q = cv.take<int8_t>(size_t(kMaxPos) * kHidden);
@@ -1045,22 +1076,23 @@ int load_model(ae_ctx* c, const ae_model_desc* d, const uint8_t* file, size_t fi
     }
   }
   if (!r && cv.off > bytes) r = fail(c, AE_ERR_BAD_PACK, "internal: model arena overflow");
-  if (!r && host && cudaMemcpy(arena, host.get(), cv.off, cudaMemcpyHostToDevice) != cudaSuccess)
-    r = fail(c, AE_ERR_CUDA, "model upload failed");
-  for (size_t i = 0; !r && i < img.d2d.size(); ++i)
-    if (cudaMemcpyAsync(img.d2d[i].dst, img.d2d[i].src, img.d2d[i].n, cudaMemcpyDeviceToDevice, c->stream) !=
-        cudaSuccess)
+  if (!r) {
+    // from here on the arena's contents change: a failure leaves no model
+    c->has_model = false;
+    img.run();
+    if (cudaMemcpyAsync(M.arena, c->h_model, cv.off, cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
+        cudaStreamSynchronize(c->stream) != cudaSuccess)
       r = fail(c, AE_ERR_CUDA, "model upload failed");
-  for (size_t i = 0; !r && i < img.h2d.size(); ++i)
-    if (cudaMemcpyAsync(img.h2d[i].dst, img.h2d[i].src, img.h2d[i].n, cudaMemcpyHostToDevice, c->stream) !=
-        cudaSuccess)
-      r = fail(c, AE_ERR_CUDA, "model upload failed");
-  if (cudaStreamSynchronize(c->stream) != cudaSuccess && !r) r = fail(c, AE_ERR_CUDA, "model upload failed");
-  if (dev_file) cudaFree(dev_file);
+  }
   if (r) {
+    drop_graphs(c);
     free_model(c);
     return r;
   }
+  // graphs captured against the previous model stay valid only if every tensor (and so every
+  // tensor map) is where it was
+  if (!same_placement(M, c->model)) drop_graphs(c);
+  c->model = M;
   c->has_model = true;
   return 0;
 }
@@ -1070,7 +1102,7 @@ int load_model(ae_ctx* c, const ae_model_desc* d, const uint8_t* file, size_t fi
 int ae_model_load(ae_ctx* c, const ae_model_desc* d) {
   if (!c || !d) return fail(c, AE_ERR_INVALID_ARG, "null argument");
   DeviceGuard g(c->device);
-  return load_model(c, d, nullptr, 0);
+  return load_model(c, d);
 }
 
 int ae_model_load_file(ae_ctx* c, const char* path) {
@@ -1120,7 +1152,7 @@ int ae_model_load_file(ae_ctx* c, const char* path) {
       return fail(c, AE_ERR_BAD_PACK, "layer %d: LayerNorm vectors must have 384 entries", l);
   }
   if (!p.ok) return fail(c, AE_ERR_BAD_PACK, "truncated or inconsistent .ae8 pack");
-  return load_model(c, &d, mf.data, mf.size);
+  return load_model(c, &d);
 }
 
 int ae_reserve(ae_ctx* c, uint32_t max_tokens, uint32_t max_seqs) {
@@ -1306,6 +1338,33 @@ int ae_gemm_i8(ae_ctx* c, int epi, uint32_t M, uint32_t N, uint32_t K, const int
   return 0;
 }
 
+int ae_measure_int8_peak(ae_ctx* c, uint32_t iters, float* ms, double* tops) {
+  if (!c || !ms || !tops || iters == 0 || iters > 1000000)
+    return fail(c, AE_ERR_INVALID_ARG, "ae_measure_int8_peak: iters must be 1..1000000 and outputs non-null");
+  DeviceGuard g(c->device);
+  int ctas = 0;
+  if (i8_peak_launch(int(std::min<uint32_t>(iters, 1000)), c->d_err, c->stream, &ctas))  // warm-up
+    return fail(c, AE_ERR_CUDA, "peak probe launch failed");
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  CUDA_TRY(c, cudaEventCreate(&e0));
+  CUDA_TRY(c, cudaEventCreate(&e1));
+  cudaEventRecord(e0, c->stream);
+  const int r = i8_peak_launch(int(iters), c->d_err, c->stream, &ctas);
+  cudaEventRecord(e1, c->stream);
+  const cudaError_t e = cudaEventSynchronize(e1);
+  float t = 0.0f;
+  if (e == cudaSuccess) cudaEventElapsedTime(&t, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  c->launches += 2;
+  if (r) return fail(c, AE_ERR_CUDA, "peak probe launch failed");
+  if (e != cudaSuccess) return fail(c, AE_ERR_CUDA, "peak probe: %s", cudaGetErrorString(e));
+  AE_TRY(check_dev_err(c));
+  *ms = t;
+  *tops = t > 0.0f ? i8_peak_ops(int(iters), ctas) / (double(t) * 1e-3) / 1e12 : 0.0;
+  return 0;
+}
+
 int ae_selftest_wait_timeout(ae_ctx* c, uint32_t limit_us) {
   if (!c || limit_us == 0 || limit_us > 1000000) return fail(c, AE_ERR_INVALID_ARG, "limit_us must be 1..1000000");
   DeviceGuard g(c->device);
@@ -1360,6 +1419,63 @@ int ae_set_attention_mode(ae_ctx* c, int mode) {
 }
 
 int ae_get_attention_mode(const ae_ctx* c) { return c ? c->attn_mode : AE_ERR_INVALID_ARG; }
+
+int ae_trace_forward(ae_ctx* c, const uint16_t* ids, const uint32_t* cu, uint32_t n, int stage, float* f32, int8_t* q,
+                     float* scale) {
+  if (!c) return AE_ERR_INVALID_ARG;
+  if (!c->has_model) return fail(c, AE_ERR_NO_MODEL, "no model loaded");
+  if (stage != AE_TRACE_EMBED && stage != AE_TRACE_ATTN0) return fail(c, AE_ERR_INVALID_ARG, "unknown stage %d", stage);
+  if (!ids || !cu || !f32 || !q || !scale || n == 0) return fail(c, AE_ERR_INVALID_ARG, "null pointer or no sequence");
+  DeviceGuard g(c->device);
+  int T = 0, max_len = 0;
+  AE_TRY(pack_host(c, ids, cu, n, &T, &max_len));
+  Workspace& W = c->ws;
+  CUDA_TRY(c, cudaMemcpyAsync(W.ids, W.h_ids, size_t(T) * 2, cudaMemcpyHostToDevice, c->stream));
+  CUDA_TRY(c, cudaMemcpyAsync(W.cu, W.h_cu, size_t(n + 1) * 4, cudaMemcpyHostToDevice, c->stream));
+  const bool prof = c->prof;
+  c->prof = false;
+  int r = enqueue_forward(c, W.ids, W.cu, T, int(n), max_len, W.out, &c->segs, 1, stage);
+  // an attention kernel that quantized the context rows itself did not store them in fp32: run the
+  // same attention once more without the quantization (the rows it computes are the same bits)
+  if (!r && stage == AE_TRACE_ATTN0 && c->attn_mode == AE_ATTENTION_EXACT)
+    r = attention(c, W.qkv, 3 * kHidden, 0, 1, W.qkv, 3 * kHidden, kHidden, 2 * kHidden, 1, W.ctx, W.cu, int(n), max_len,
+                  0, &c->segs);
+  c->prof = prof;
+  AE_TRY(r);
+  const size_t Tp = align_up(size_t(T), 128);
+  std::vector<float> rows(Tp * kHidden);
+  std::vector<int8_t> qr(size_t(T) * kHidden);
+  std::vector<float> sr(T);
+  CUDA_TRY(c, cudaMemcpyAsync(rows.data(), stage == AE_TRACE_EMBED ? W.hidden : W.ctx,
+                              (stage == AE_TRACE_EMBED ? Tp : size_t(T)) * kHidden * 4, cudaMemcpyDeviceToHost,
+                              c->stream));
+  CUDA_TRY(c, cudaMemcpyAsync(qr.data(), W.act_q, qr.size(), cudaMemcpyDeviceToHost, c->stream));
+  CUDA_TRY(c, cudaMemcpyAsync(sr.data(), W.act_s, sr.size() * 4, cudaMemcpyDeviceToHost, c->stream));
+  CUDA_TRY(c, cudaStreamSynchronize(c->stream));
+  AE_TRY(check_dev_err(c));
+  // packed rows -> the caller's order; the hidden state is tile-transposed: (t, j) at
+  // ((t >> 7) * 384 + j) * 128 + (t & 127)
+  std::vector<uint32_t> dst0(n);
+  uint32_t off = 0;
+  for (uint32_t i = 0; i < n; ++i) {
+    dst0[i] = off;
+    off += std::min<uint32_t>(cu[i + 1] - cu[i], kMaxPos);
+  }
+  for (uint32_t k = 0; k < n; ++k) {
+    const uint32_t i = c->order[k];
+    for (uint32_t t = W.h_cu[k]; t < W.h_cu[k + 1]; ++t) {
+      const size_t d = dst0[i] + (t - W.h_cu[k]);
+      if (stage == AE_TRACE_EMBED) {
+        for (int j = 0; j < kHidden; ++j) f32[d * kHidden + j] = rows[((size_t(t) >> 7) * kHidden + j) * 128 + (t & 127)];
+      } else {
+        std::memcpy(f32 + d * kHidden, &rows[size_t(t) * kHidden], kHidden * 4);
+      }
+      std::memcpy(q + d * kHidden, &qr[size_t(t) * kHidden], kHidden);
+      scale[d] = sr[t];
+    }
+  }
+  return 0;
+}
 
 // ArcticEmbedS::embed_batch (src/lib.rs:138-260) across GPUs: token-weighted greedy shards, one host
 // thread per context; each context packs its shard (longest first) into batches of <= max_tokens.
@@ -1434,34 +1550,65 @@ int ae_embed_batch_multi(ae_ctx* const* ctxs, int n_ctx, const uint16_t* ids, co
 // ============================================================================================
 // Allocation-free single-sequence forward.
 //
-// Some callers cannot call cudaMalloc at the time they embed: code that records the call into a
-// CUDA graph it is capturing (allocation breaks the capture), hosts whose device memory is handed
-// out once at start-up by their own pool, and real-time paths that must not block on the
-// allocator. ae_forward_cls_noalloc serves them: its scratch (the activations of one <= 512-token
-// sequence, about 6 MB) lives in the file-scope device array below instead of the context's
-// cudaMalloc'd workspace, so the call itself allocates nothing.
+// Some callers cannot call cudaMalloc at the time they embed: hosts whose device memory is handed
+// out once at start-up by their own pool (a service with a fixed memory budget), and real-time
+// paths that must not block on the allocator (cudaMalloc / cudaFree can synchronise the device).
+// ae_forward_cls_noalloc serves them: its scratch (the activations of one <= 512-token sequence,
+// about 6 MB) lives in the file-scope device array below instead of the context's cudaMalloc'd
+// workspace, so the call itself allocates nothing.
 namespace {
 
 constexpr size_t kNoAllocBytes = size_t(8) << 20;  // 8 MiB: holds the workspace of one 512-token sequence
 __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
 
 // Per-device view of g_noalloc_scratch: its device address (from cudaGetSymbolAddress, not the
-// host-side name) carved into a Workspace, with tensor maps for the GEMM A operands.
+// host-side name) carved into a Workspace, with tensor maps for the GEMM A operands. The address
+// belongs to the CUDA context the module was loaded in: after a device reset (or any teardown of
+// the primary context) the array can move, so the view records its context's id and is rebuilt
+// when the current context differs.
 struct NoAllocState {
   bool ready = false;
+  unsigned long long ctx_id = 0;
   Workspace ws;
 };
 NoAllocState g_noalloc[kMaxDevices];
 std::mutex g_noalloc_mu;
+
+// Unique id of the calling thread's current CUDA context (cuCtxGetId: ids are never reused within
+// a process), or 0 when the driver cannot report it.
+unsigned long long current_ctx_id() {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrent>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetId>(p);
+  });
+  CUcontext cx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&cx) != CUDA_SUCCESS || !cx || get_id(cx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
 
 __global__ void k_noalloc_cu(uint32_t* cu, uint32_t len) {
   cu[0] = 0;
   cu[1] = len;
 }
 
-int noalloc_setup(ae_ctx* c, NoAllocState& st) {
+int noalloc_setup(ae_ctx* c, NoAllocState& st, unsigned long long ctx_id) {
+  st.ready = false;
   void* base = nullptr;
   CUDA_TRY(c, cudaGetSymbolAddress(&base, g_noalloc_scratch));
+  st.ws = Workspace();
   Workspace& w = st.ws;
   const size_t T = kMaxPos, B = 128;  // one sequence; [CLS] buffers keep the 128-row tile height
   Carve cv{static_cast<uint8_t*>(base)};
@@ -1490,6 +1637,7 @@ int noalloc_setup(ae_ctx* c, NoAllocState& st) {
   if (make_tmap_i8(&w.tm_act_q, w.act_q, int(T), kHidden, kBoxA) || make_tmap_i8(&w.tm_inter_q, w.inter_q, int(T), kInter, kBoxA) ||
       make_tmap_i8(&w.tm_cq, w.cq, int(B), kHidden, kBoxA) || make_tmap_i8(&w.tm_cinter_q, w.cinter_q, int(B), kInter, kBoxA))
     return fail(c, AE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the static scratch");
+  st.ctx_id = ctx_id;
   st.ready = true;
   return 0;
 }
@@ -1507,18 +1655,24 @@ extern "C" int ae_forward_cls_noalloc(ae_ctx* c, const uint16_t* d_ids, uint32_t
                 len);
   DeviceGuard g(c->device);
   NoAllocState& st = g_noalloc[c->device];
+  Workspace W;
   {
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
-    if (!st.ready) AE_TRY(noalloc_setup(c, st));
+    const unsigned long long id = current_ctx_id();
+    if (!st.ready || (id != 0 && id != st.ctx_id)) AE_TRY(noalloc_setup(c, st, id));
+    W = st.ws;
   }
-  Workspace& W = st.ws;
   k_noalloc_cu<<<1, 1, 0, c->stream>>>(W.cu, len);
   CUDA_TRY(c, cudaGetLastError());
   ++c->launches;
-  // run the forward on the static scratch: the context's own workspace is set aside for the call
+  // run the forward on the static scratch: the context's own workspace is set aside for the call,
+  // and so is per-kernel profiling (its host-side events are not part of this call's contract)
   Workspace saved = c->ws;
+  const bool prof = c->prof;
   c->ws = W;
+  c->prof = false;
   const int r = enqueue_forward(c, d_ids, W.cu, int(len), 1, int(len), d_out384, nullptr, int(len));
   c->ws = saved;
+  c->prof = prof;
   return r;
 }

@@ -809,6 +809,72 @@ static cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const Ge
   return cudaLaunchKernelEx(&cfg, kfn, ta, tb, g, nt, mt);
 }
 
+// ------------------------------------------------------------------------ int8 tensor-pipe peak
+// Throughput of tcgen05.mma kind::i8 with its operands resident in shared memory: one CTA per SM,
+// A (128 rows x 128 bytes) and B (256 rows x 128 bytes) filled with a fixed pseudo-random pattern,
+// one thread issuing `iters` rounds of 4 MMAs (M = 128, N = 256, K = 32 each, the whole 128-byte K
+// block) into two TMEM accumulators taken in turn. The roofline denominator of the GEMMs.
+constexpr int kPeakN = 256;
+// 160 KB of dynamic shared memory (48 KB used) keeps the launch at one CTA per SM
+constexpr int kPeakSmem = 160 * 1024;
+static_assert(BM * BK + kPeakN * BK + 1024 <= kPeakSmem, "peak probe operands");
+
+__global__ void __launch_bounds__(128, 1) k_i8_peak(int iters, int* err) {
+  extern __shared__ uint8_t peak_raw[];
+  __shared__ uint64_t done;
+  __shared__ uint32_t tmem_base;
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(peak_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x;
+  for (int i = tid; i < (BM + kPeakN) * BK / 4; i += blockDim.x)
+    reinterpret_cast<uint32_t*>(sm)[i] = (uint32_t(i) * 2654435761u) ^ 0x5bd1e995u;
+  fence_proxy_async();  // the MMA (async proxy) reads what these generic stores wrote
+  if (tid < 32) {
+    tmem_alloc(&tmem_base, 2 * kPeakN);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    mbar_init(&done, 1);
+    fence_mbar_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t d = tmem_base;
+  if (tid == 0) {
+    constexpr uint32_t idesc = idesc_i8(BM, kPeakN);
+    const uint32_t a = smem_u32(sm), b = a + BM * BK;
+    for (int it = 0; it < iters; ++it) {
+#pragma unroll
+      for (int ks = 0; ks < BK / 32; ++ks)
+        mma_i8(d + uint32_t(it & 1) * kPeakN, sdesc_sw128(a + ks * 32), sdesc_sw128(b + ks * 32), idesc,
+               (it > 1 || ks > 0) ? 1u : 0u);
+    }
+    mma_commit(&done);
+    mbar_wait(&done, 0, err, DEV_ERR_TIMEOUT_MMA);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (tid < 32) tmem_dealloc(d, 2 * kPeakN);
+}
+
+int i8_peak_launch(int iters, int* err, cudaStream_t st, int* ctas_out) {
+  static bool attr_set[kMaxDevices] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < kMaxDevices && !attr_set[dev]) {
+    if (cudaFuncSetAttribute(k_i8_peak, cudaFuncAttributeMaxDynamicSharedMemorySize, kPeakSmem) != cudaSuccess)
+      return -1;
+    attr_set[dev] = true;
+  }
+  const int ctas = num_sms();
+  if (ctas_out) *ctas_out = ctas;
+  k_i8_peak<<<ctas, 128, kPeakSmem, st>>>(iters, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -2;
+}
+
+double i8_peak_ops(int iters, int ctas) { return 2.0 * BM * kPeakN * BK * double(iters) * double(ctas); }
+
 // Sets the dynamic shared-memory limit of every GEMM variant on the current device (called once per
 // device before any launch can be captured into a CUDA graph).
 int gemm_i8_prime() {

@@ -42,4 +42,9 @@ constexpr int kBoxA = 128;
 constexpr int kBoxB = 64;
 int gemm_i8_launch(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& g, cudaStream_t st);
 
+// int8 tensor-pipe throughput probe: one CTA per SM issuing `iters` rounds of resident-operand
+// tcgen05.mma kind::i8 (M = 128, N = 256, K = 128 per round); i8_peak_ops gives its int8 ops.
+int i8_peak_launch(int iters, int* err, cudaStream_t st, int* ctas_out);
+double i8_peak_ops(int iters, int ctas);
+
 }  // namespace ae

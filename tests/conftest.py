@@ -11,8 +11,9 @@ for p in (ROOT, PKG):
     if p not in sys.path:
         sys.path.insert(0, p)
 
-# sequence lengths of the reference's parallel test (tests/parallel_test.rs:21)
-REF_LENGTHS = [1, 2, 5, 8, 15, 16, 17, 31, 33, 64, 100, 128, 257, 512]
+# sequence lengths of the reference's parallel test (tests/parallel_test.rs:21), plus 32: the parity
+# configuration (one 32-token sequence)
+REF_LENGTHS = [1, 2, 5, 8, 15, 16, 17, 31, 32, 33, 64, 100, 128, 257, 512]
 COS_MIN = 0.9999     # north-star tolerance on the final embeddings
 MAXABS_MAX = 2e-3
 

@@ -125,6 +125,31 @@ def test_fresh_engines_deterministic(pack_path):
     e2.close()
 
 
+def test_model_reload(pack_path):
+    """QuantizedModelRaw::load_ae8 + PackedModel::from_raw (src/quantize.rs:76-137, src/model.rs:49-84)
+    run again on a live context: a reload of the same model shape reuses the device arena, and the
+    single-sequence graphs captured before it then compute with the new weights; the host-array
+    descriptor path (ae_model_load) gives the same bits as the file path."""
+    from arctic_embed_s_int8 import ae8
+
+    other = synth.pack_path(1)
+    ids = synth.token_ids(40, rng(13))
+    e = Engine(0).load_file(pack_path)
+    a0 = e.forward_cls(ids)
+    e.load_file(other)
+    b = e.forward_cls(ids)
+    fresh = Engine(0).load_file(other)
+    np.testing.assert_array_equal(b, fresh.forward_cls(ids))
+    assert not np.array_equal(a0, b)
+    e.load(ae8.read_ae8(pack_path))
+    np.testing.assert_array_equal(e.forward_cls(ids), a0)
+    np.testing.assert_array_equal(e.forward_ragged([ids, ids[:7]])[0], a0)
+    e.load_file(pack_path)
+    np.testing.assert_array_equal(e.forward_cls(ids), a0)
+    fresh.close()
+    e.close()
+
+
 def test_truncation_to_512(engine):
     ids = synth.token_ids(700, rng(6))
     np.testing.assert_array_equal(engine.forward_cls(ids), engine.forward_cls(ids[:512]))
