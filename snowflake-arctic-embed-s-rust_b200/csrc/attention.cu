@@ -36,6 +36,7 @@
 #include <cstddef>
 #include <cstdint>
 
+#include "attn_lanes4.cuh"
 #include "kernels.h"
 #include "ptx.cuh"
 #include "rowmath.cuh"
@@ -967,101 +968,9 @@ __global__ void __launch_bounds__(4 * QT) k_attention_lat(AttnArgs a) {
   load_query(a, s0 + (active ? qi : L - 1), h, q);
   __syncthreads();
   float* er = es + ql * P;
-  const int L4 = L & ~3, L8 = L & ~7, L16 = L & ~15;
   const unsigned full = 0xffffffffu;
-
-  auto score = [&](int t) -> float {  // score_pair's order for one key
-    float s8[8];
-#pragma unroll
-    for (int l = 0; l < 8; ++l)
-      s8[l] = fmaf(q[8 + l], kd[(8 + l) * P + t], q[l] * kd[l * P + t]) +
-              fmaf(q[24 + l], kd[(24 + l) * P + t], q[16 + l] * kd[(16 + l) * P + t]);
-    return (t < L4) ? ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]))
-                    : ((s8[0] + s8[4]) + (s8[1] + s8[5])) + ((s8[2] + s8[6]) + (s8[3] + s8[7]));
-  };
-
-  // pass 1: scores of the owned keys, their max over the query's four sub-lanes
-  float mx = -INFINITY;
-  for (int t0 = 0; t0 < L16; t0 += 16) {
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int t = t0 + 2 * sl + (k & 1) + 8 * (k >> 1);
-      const float sv = score(t);
-      er[t] = sv;
-      mx = fmaxf(mx, sv);
-    }
-  }
-  for (int t = L16 + 2 * sl; t < L16 + 2 * sl + 2 && t < L8; ++t) {
-    const float sv = score(t);
-    er[t] = sv;
-    mx = fmaxf(mx, sv);
-  }
-  for (int t = L8 + sl; t < L; t += 4) {
-    const float sv = score(t);
-    er[t] = sv;
-    mx = fmaxf(mx, sv);
-  }
-  mx = fmaxf(mx, __shfl_xor_sync(full, mx, 1));
-  mx = fmaxf(mx, __shfl_xor_sync(full, mx, 2));
-
-  // pass 2: exponentials of the owned keys and the owned sum chains (slots 2sl, 2sl + 1 of both
-  // 8-lane accumulators), in chunk order
-  float c0a = 0.0f, c0b = 0.0f, c1a = 0.0f, c1b = 0.0f;
-  for (int t0 = 0; t0 < L16; t0 += 16) {
-    const int t = t0 + 2 * sl;
-    const float e0 = cw_exp(er[t] - mx), e1 = cw_exp(er[t + 1] - mx);
-    const float e2 = cw_exp(er[t + 8] - mx), e3 = cw_exp(er[t + 9] - mx);
-    er[t] = e0;
-    er[t + 1] = e1;
-    er[t + 8] = e2;
-    er[t + 9] = e3;
-    c0a = c0a + e0;
-    c0b = c0b + e1;
-    c1a = c1a + e2;
-    c1b = c1b + e3;
-  }
-  if (L16 + 2 * sl < L8) {  // the trailing 8-key chunk feeds the first accumulator
-    const int t = L16 + 2 * sl;
-    const float e0 = cw_exp(er[t] - mx), e1 = cw_exp(er[t + 1] - mx);
-    er[t] = e0;
-    er[t + 1] = e1;
-    c0a = c0a + e0;
-    c0b = c0b + e1;
-  }
-  for (int t = L8 + sl; t < L; t += 4) er[t] = scalar_expf(er[t] - mx);
-  // hsum256 of v[m] = acc0[m] + acc1[m]: sub-lane sl holds v[2sl], v[2sl + 1]
-  const float vx = c0a + c1a, vy = c0b + c1b;
-  const float ax = vx + __shfl_down_sync(full, vx, 2);  // v0 + v4 | v2 + v6
-  const float ay = vy + __shfl_down_sync(full, vy, 2);  // v1 + v5 | v3 + v7
-  const float tt = ax + ay;
-  float sum = tt + __shfl_down_sync(full, tt, 1);
-  __syncwarp();
-  if (sl == 0)
-    for (int t = L8; t < L; ++t) sum = sum + er[t];  // the tail keys in order, after the tree
-  const float inv = __shfl_sync(full, 1.0f / sum, tid & 31 & ~3);
-
-  // pass 3: weighted sum of V, dims 8sl .. 8sl + 7; even keys to the first accumulator
-  float acc_e[8], acc_o[8];
-#pragma unroll
-  for (int k = 0; k < 8; ++k) acc_e[k] = acc_o[k] = 0.0f;
-  const float* vrow = vd + 8 * sl * P;
-  int t = 0;
-  for (; t + 1 < L; t += 2) {
-    const float p0 = er[t] * inv, p1 = er[t + 1] * inv;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      acc_e[k] = fmaf(vrow[k * P + t], p0, acc_e[k]);
-      acc_o[k] = fmaf(vrow[k * P + t + 1], p1, acc_o[k]);
-    }
-  }
-  if (t < L) {
-    const float p0 = er[t] * inv;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) acc_e[k] = fmaf(vrow[k * P + t], p0, acc_e[k]);
-  }
   float cx[8];
-#pragma unroll
-  for (int k = 0; k < 8; ++k) cx[k] = acc_e[k] + acc_o[k];
+  attend_query_lanes4(q, kd, vd, P, er, L, sl, cx);
   if constexpr (!QUANT) {
     if (active) {
       float4* o = reinterpret_cast<float4*>(a.out + size_t(s0 + qi) * kHidden + h * 32 + 8 * sl);

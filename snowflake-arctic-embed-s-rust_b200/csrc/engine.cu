@@ -36,6 +36,7 @@
 #include "../../include/arctic_cuda.h"
 #include "gemm_i8.h"
 #include "kernels.h"
+#include "latency.h"
 #include "ptx.cuh"
 #include "rowmath.cuh"
 
@@ -49,7 +50,8 @@ struct DevLinear {
   float* ws = nullptr;
   float* bias = nullptr;
   float* inv_s = nullptr;
-  CUtensorMap tmap;
+  CUtensorMap tmap;    // 64-row boxes (the GEMM kernels)
+  CUtensorMap tmap32;  // 32-row boxes (the single-sequence cluster forward)
 };
 
 struct DevLayer {
@@ -67,6 +69,7 @@ struct DevModel {
   float* type0 = nullptr;
   float *emb_lnw = nullptr, *emb_lnb = nullptr;
   DevLayer layers[kLayers];
+  LatModel* lat = nullptr;  // what the single-sequence cluster forward reads (in the arena)
 };
 
 struct Workspace {
@@ -122,6 +125,7 @@ struct ae_ctx {
   int gelu_erf = 0;       // ARCTIC_GELU=erf selects the exact-erf GELU (outside the parity tolerance)
   int fused_qkv = 0;      // ARCTIC_FUSED_QKV=1: QKV projection fused into the attention (sequences <= 128 keys)
   int attn_mode = AE_ATTENTION_EXACT;  // ae_set_attention_mode, ARCTIC_ATTN=int8
+  bool lat_cluster = false;  // single sequences of <= 32 tokens as one cluster kernel (ARCTIC_LAT_CLUSTER=0: off)
   bool prof = false;      // record CUDA events around every launch (ae_profile)
   int prof_kind = 0;      // kind of the launches being enqueued
   std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> prof_events;
@@ -250,7 +254,8 @@ int upload_linear(ae_ctx* c, Carve& cv, Uploader& img, const ae_linear_desc& d, 
   img.put(o.w, d.w_q, d.n_out * d.k_in);
   img.put(o.ws, d.w_scale, d.n_out);
   img.put(o.bias, d.bias, d.n_out);
-  if (make_tmap_i8(&o.tmap, o.w, o.n, o.k, kBoxB) != 0) return fail(c, AE_ERR_CUDA, "cuTensorMapEncodeTiled failed for weights");
+  if (make_tmap_i8(&o.tmap, o.w, o.n, o.k, kBoxB) != 0 || make_tmap_i8(&o.tmap32, o.w, o.n, o.k, 32) != 0)
+    return fail(c, AE_ERR_CUDA, "cuTensorMapEncodeTiled failed for weights");
   return 0;
 }
 
@@ -261,7 +266,7 @@ bool same_placement(const DevModel& a, const DevModel& b) {
     return x.n == y.n && x.k == y.k && x.w == y.w && x.ws == y.ws && x.bias == y.bias && x.inv_s == y.inv_s;
   };
   if (a.arena != b.arena || a.word_q != b.word_q || a.word_s != b.word_s || a.pos_q != b.pos_q || a.pos_s != b.pos_s ||
-      a.type0 != b.type0 || a.emb_lnw != b.emb_lnw || a.emb_lnb != b.emb_lnb)
+      a.type0 != b.type0 || a.emb_lnw != b.emb_lnw || a.emb_lnb != b.emb_lnb || a.lat != b.lat)
     return false;
   for (int l = 0; l < kLayers; ++l) {
     const DevLayer &x = a.layers[l], &y = b.layers[l];
@@ -939,6 +944,8 @@ int ae_ctx_create(int device, ae_ctx** out) {
   c->fused_qkv = (fq && std::strcmp(fq, "1") == 0) ? 1 : 0;
   const char* am = std::getenv("ARCTIC_ATTN");
   c->attn_mode = (am && std::strcmp(am, "int8") == 0) ? AE_ATTENTION_INT8 : AE_ATTENTION_EXACT;
+  const char* lc = std::getenv("ARCTIC_LAT_CLUSTER");
+  c->lat_cluster = !(lc && std::strcmp(lc, "0") == 0) && lat_prime();
   if (gemm_i8_prime() || attention_prime()) {
     ae_ctx_destroy(c);
     return fail(nullptr, AE_ERR_CUDA, "kernel attribute setup failed on device %d", device);
@@ -1006,7 +1013,8 @@ int load_model(ae_ctx* c, const ae_model_desc* d) {
     }
   }
   cudaStreamSynchronize(c->stream);
-  size_t bytes = size_t(kVocab) * kHidden + kVocab * 4 + kMaxPos * kHidden + kMaxPos * 4 + 3 * kHidden * 4 + 64 * 1024;
+  size_t bytes = size_t(kVocab) * kHidden + kVocab * 4 + kMaxPos * kHidden + kMaxPos * 4 + 3 * kHidden * 4 + 64 * 1024 +
+                 align_up(sizeof(LatModel), 256);
   for (int l = 0; l < kLayers; ++l) {
     const ae_layer_desc& L = d->layers[l];
     bytes += linear_bytes(L.qkv) + linear_bytes(L.attn_out) + linear_bytes(L.ffn_inter) + linear_bytes(L.ffn_out) +
@@ -1074,6 +1082,38 @@ int load_model(ae_ctx* c, const ae_model_desc* d) {
       img.put(D.ln2w, L.ln2_weight, kHidden);
       img.put(D.ln2b, L.ln2_bias, kHidden);
     }
+  }
+  // the single-sequence cluster forward's view of the model: device pointers and 32-row tensor maps
+  std::unique_ptr<LatModel> lat(new LatModel());
+  if (!r) {
+    std::memset(lat.get(), 0, sizeof(LatModel));
+    auto lin = [](const DevLinear& x) { return LatLinear{x.ws, x.bias, x.inv_s}; };
+    for (int l = 0; l < kLayers; ++l) {
+      const DevLayer& D = M.layers[l];
+      LatLayer& T = lat->layer[l];
+      T.qkv = lin(D.qkv);
+      T.q_only = lin(D.q_only);
+      T.kv_only = lin(D.kv_only);
+      T.ao = lin(D.ao);
+      T.fi = lin(D.fi);
+      T.fo = lin(D.fo);
+      T.ln1w = D.ln1w;
+      T.ln1b = D.ln1b;
+      T.ln2w = D.ln2w;
+      T.ln2b = D.ln2b;
+      const DevLinear* src[LAT_MAPS] = {&D.qkv, &D.q_only, &D.kv_only, &D.ao, &D.fi, &D.fo};
+      for (int k = 0; k < LAT_MAPS; ++k)
+        if (src[k]->w) lat->tm[l][k] = src[k]->tmap32;
+    }
+    lat->word_q = M.word_q;
+    lat->word_s = M.word_s;
+    lat->pos_q = M.pos_q;
+    lat->pos_s = M.pos_s;
+    lat->type0 = M.type0;
+    lat->emb_lnw = M.emb_lnw;
+    lat->emb_lnb = M.emb_lnb;
+    M.lat = cv.take<LatModel>(1);
+    img.put(M.lat, lat.get(), 1);
   }
   if (!r && cv.off > bytes) r = fail(c, AE_ERR_BAD_PACK, "internal: model arena overflow");
   if (!r) {
@@ -1190,7 +1230,17 @@ int ae_forward_cls(ae_ctx* c, const uint16_t* ids, uint32_t len, float* out) {
     const uint64_t before = c->launches;
     const bool prof = c->prof;
     c->prof = false;  // no event records inside the graph
-    if (!r) r = enqueue_forward(c, W.ids, c->d_cu_single + 2 * L, int(L), 1, int(L), W.out, nullptr, int(L));
+    // at most 32 tokens: the whole forward as one 12-CTA cluster kernel (the same arithmetic; the
+    // int8 attention mode keeps the multi-kernel path for the sequences it covers)
+    const bool one_kernel = c->lat_cluster && c->model.lat && L <= uint32_t(kLatMaxTokens) &&
+                            (c->attn_mode == AE_ATTENTION_EXACT || L < uint32_t(kI8MinLen));
+    if (!r && one_kernel) {
+      ++c->launches;
+      if (launch_forward_lat(c->model.lat, W.ids, int(L), W.out, c->d_err, c->gelu_erf, c->stream))
+        r = fail(c, AE_ERR_CUDA, "cluster forward launch failed");
+    } else if (!r) {
+      r = enqueue_forward(c, W.ids, c->d_cu_single + 2 * L, int(L), 1, int(L), W.out, nullptr, int(L));
+    }
     c->prof = prof;
     gr.kernels = c->launches - before;
     c->launches = before;  // captured, not launched

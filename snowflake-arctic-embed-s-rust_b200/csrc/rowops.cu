@@ -35,7 +35,7 @@ __device__ __forceinline__ float halfwarp_max(float v, unsigned mask) {
   return v;
 }
 
-// One half-warp per token row, 16 rows per block: dequant_add_embeddings_row
+// One half-warp per token row, 16 rows per block and step (grid-stride): dequant_add_embeddings_row
 // (src/simd_math.rs:1827-1881, generic path) + layernorm_smooth_quantize_row (src/simd_math.rs:369-477)
 // with the embedding LayerNorm and layers[0].qkv.inv_smooth (src/model.rs:196-219). The hidden
 // rows go through a shared-memory tile so that the tile-transposed store of a column covers the
@@ -53,7 +53,7 @@ __global__ void __launch_bounds__(256) k_embed_ln_quant(EmbedArgs a) {
   __syncthreads();
   pdl_wait();
   __shared__ float tile[kHidden][17];
-  const int r0 = blockIdx.x * 16;
+  for (int r0 = blockIdx.x * 16; r0 < a.T; r0 += gridDim.x * 16) {
   const int lr = threadIdx.x >> 4;  // row within the block
   const int row = r0 + lr;
   const int l = threadIdx.x & 15;
@@ -109,6 +109,8 @@ __global__ void __launch_bounds__(256) k_embed_ln_quant(EmbedArgs a) {
   for (int i = threadIdx.x; i < kHidden * 16; i += blockDim.x) {
     const int j = i >> 4, rr = i & 15;
     if (r0 + rr < a.T) a.hidden[tt_index(r0 + rr, j, kHidden)] = tile[j][rr];
+  }
+  __syncthreads();  // the tile is reused by the next row group
   }
 }
 
@@ -255,47 +257,60 @@ __global__ void __launch_bounds__(128) k_ln_final_rows(const float* __restrict__
 
 // One warp per row: smooth_quantize_row_avx2 (src/simd_math.rs:584-649), the quantization of the
 // attention context with attn_out.inv_smooth (src/model.rs:324-328).
+// Grid-stride over the rows: a block's warps keep the lane's 12 inverse smoothing factors in
+// registers (loaded once, before the dependency wait) and take rows two at a time, the loads of
+// both rows in flight together.
 __global__ void __launch_bounds__(256) k_smooth_quant(const float* __restrict__ x, const float* __restrict__ inv_s,
                                                       int8_t* __restrict__ q, float* __restrict__ scale, int rows) {
   pdl_trigger();
-  __shared__ float s_invs[kHidden];  // model constant, staged before the dependency wait
-  for (int i = threadIdx.x; i < kHidden; i += blockDim.x) s_invs[i] = inv_s[i];
-  __syncthreads();
-  pdl_wait();
-  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
-  const float* xr = x + size_t(row) * kHidden;
-  float v[12];
-  float vmax = 1e-8f;
+  float s[12];  // element 4 (lane + 32 i) + e of the row
 #pragma unroll
   for (int i = 0; i < 3; ++i) {
-    const float4 t = reinterpret_cast<const float4*>(xr)[lane + 32 * i];
-    v[4 * i] = t.x;
-    v[4 * i + 1] = t.y;
-    v[4 * i + 2] = t.z;
-    v[4 * i + 3] = t.w;
+    const float4 t = reinterpret_cast<const float4*>(inv_s)[lane + 32 * i];
+    s[4 * i] = t.x;
+    s[4 * i + 1] = t.y;
+    s[4 * i + 2] = t.z;
+    s[4 * i + 3] = t.w;
   }
+  pdl_wait();
+  const int nwarps = gridDim.x * (blockDim.x >> 5);
+  for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += 2 * nwarps) {
+    const int rr[2] = {r, r + nwarps < rows ? r + nwarps : -1};
+    float v[2][12];
 #pragma unroll
-  for (int i = 0; i < 12; ++i) {
-    const int j = 4 * (lane + 32 * (i / 4)) + (i % 4);
-    vmax = fmaxf(vmax, fabsf(v[i] * s_invs[j]));
-  }
+    for (int u = 0; u < 2; ++u) {
+      const float4* xr = reinterpret_cast<const float4*>(x + size_t(rr[u] < 0 ? r : rr[u]) * kHidden);
 #pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, o));
-  const float inv_scale = 127.0f / vmax;
-  int8_t* qr = q + size_t(row) * kHidden;
-#pragma unroll
-  for (int i = 0; i < 3; ++i) {
-    uint32_t w = 0;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int j = 4 * (lane + 32 * i) + e;
-      w |= (uint32_t(quant_i8(v[4 * i + e] * (s_invs[j] * inv_scale))) & 0xFFu) << (8 * e);
+      for (int i = 0; i < 3; ++i) {
+        const float4 t = xr[lane + 32 * i];
+        v[u][4 * i] = t.x;
+        v[u][4 * i + 1] = t.y;
+        v[u][4 * i + 2] = t.z;
+        v[u][4 * i + 3] = t.w;
+      }
     }
-    reinterpret_cast<uint32_t*>(qr)[lane + 32 * i] = w;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      if (rr[u] < 0) continue;
+      float vmax = 1e-8f;
+#pragma unroll
+      for (int i = 0; i < 12; ++i) vmax = fmaxf(vmax, fabsf(v[u][i] * s[i]));
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, o));
+      const float inv_scale = 127.0f / vmax;
+      int8_t* qr = q + size_t(rr[u]) * kHidden;
+#pragma unroll
+      for (int i = 0; i < 3; ++i) {
+        uint32_t w = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          w |= (uint32_t(quant_i8(v[u][4 * i + e] * (s[4 * i + e] * inv_scale))) & 0xFFu) << (8 * e);
+        reinterpret_cast<uint32_t*>(qr)[lane + 32 * i] = w;
+      }
+      if (lane == 0) scale[rr[u]] = vmax / 127.0f;
+    }
   }
-  if (lane == 0) scale[row] = vmax / 127.0f;
 }
 
 // Per-row metadata of a packed batch: position of each row inside its sequence (positions restart
@@ -356,7 +371,9 @@ int launch_wait_selftest(int* err, uint64_t limit_ns, cudaStream_t st) {
 int launch_embed(const EmbedArgs& a, cudaStream_t st) {
   if (a.T <= 0) return 0;
   const int rows_per_block = 16;
-  const dim3 grid((a.T + rows_per_block - 1) / rows_per_block);
+  // grid-stride over 16-row groups: at most 4 blocks per SM, the model constants staged once each
+  const int groups = (a.T + rows_per_block - 1) / rows_per_block;
+  const dim3 grid(groups < 148 * 4 ? groups : 148 * 4);
   return launch_pdl(k_embed_ln_quant, grid, dim3(256), 0, st, a) == cudaSuccess ? 0 : -1;
 }
 
@@ -376,7 +393,9 @@ int launch_ln_final_rows(const float* h_in, int M, const float* gamma, const flo
 
 int launch_smooth_quant(const float* x, const float* inv_s, int8_t* q, float* scale, int rows, cudaStream_t st) {
   if (rows <= 0) return 0;
-  return launch_pdl(k_smooth_quant, dim3((rows + 7) / 8), dim3(256), 0, st, x, inv_s, q, scale, rows) == cudaSuccess ? 0 : -1;
+  // enough warps for every row of a small batch, at most 8 blocks of 8 warps per SM
+  const int blocks = (rows + 7) / 8 < 148 * 8 ? (rows + 7) / 8 : 148 * 8;
+  return launch_pdl(k_smooth_quant, dim3(blocks), dim3(256), 0, st, x, inv_s, q, scale, rows) == cudaSuccess ? 0 : -1;
 }
 
 int launch_row_meta(const uint32_t* cu, int n_seqs, uint16_t* pos, int32_t* cls_row, int* err, cudaStream_t st) {

@@ -146,8 +146,45 @@ def test_model_reload(pack_path):
     np.testing.assert_array_equal(e.forward_ragged([ids, ids[:7]])[0], a0)
     e.load_file(pack_path)
     np.testing.assert_array_equal(e.forward_cls(ids), a0)
+    # a short sequence (the single-kernel cluster forward) across a reload of other weights
+    short = synth.token_ids(20, rng(14))
+    s0 = e.forward_cls(short)
+    e.load_file(other)
+    np.testing.assert_array_equal(e.forward_cls(short), fresh.forward_cls(short))
+    e.load_file(pack_path)
+    np.testing.assert_array_equal(e.forward_cls(short), s0)
     fresh.close()
     e.close()
+
+
+def test_cluster_forward_matches_multi_kernel_path(pack_path, oracle_model, monkeypatch):
+    """Single sequences of at most 32 tokens run as one 12-CTA cluster kernel (latency.cu); it
+    computes every value with the multi-kernel path's arithmetic in the same order, so every
+    embedding is the same bits (ARCTIC_LAT_CLUSTER=0 selects the multi-kernel path), one launch per
+    forward instead of about 90, and within the tolerance of the oracle."""
+    monkeypatch.setenv("ARCTIC_LAT_CLUSTER", "0")
+    multi = Engine(0).load_file(pack_path)
+    monkeypatch.delenv("ARCTIC_LAT_CLUSTER")
+    one = Engine(0).load_file(pack_path)
+    r = rng(77)
+    for L in range(1, 33):
+        for _ in range(2 if L in (1, 8, 16, 17, 31, 32) else 1):
+            ids = synth.token_ids(L, r)
+            n0 = one.kernel_launches()
+            got = one.forward_cls(ids)
+            assert one.kernel_launches() - n0 == 1, L
+            np.testing.assert_array_equal(got, multi.forward_cls(ids), err_msg=f"L={L}")
+    for L in (3, 32):  # against the oracle as well
+        ids = synth.token_ids(L, r)
+        cos, mx = close(one.forward_cls(ids), oracle_model.forward_cls(ids))
+        assert cos >= COS_MIN and mx <= MAXABS_MAX, (L, cos, mx)
+    # longer sequences keep the multi-kernel path
+    ids = synth.token_ids(33, r)
+    n0 = one.kernel_launches()
+    np.testing.assert_array_equal(one.forward_cls(ids), multi.forward_cls(ids))
+    assert one.kernel_launches() - n0 > 1
+    multi.close()
+    one.close()
 
 
 def test_truncation_to_512(engine):
