@@ -36,7 +36,7 @@
 #include <cstddef>
 #include <cstdint>
 
-#include "attn_lanes4.cuh"
+#include "attn_lanes.cuh"
 #include "kernels.h"
 #include "ptx.cuh"
 #include "rowmath.cuh"

@@ -1,8 +1,8 @@
-// The attention of one query over at most 64 keys with four lanes per query, in the reference's
-// exact operation order (compute_scores_head32_avx2 + softmax_inplace_avx2 +
+// The attention of one query over at most 64 keys with four (or eight) lanes per query, in the
+// reference's exact operation order (compute_scores_head32_avx2 + softmax_inplace_avx2 +
 // weighted_sum_head32_avx2, src/simd_math.rs:2953-3070). Shared by the short-sequence attention
-// kernel (attention.cu, k_attention_lat) and the single-sequence cluster forward (latency.cu), so
-// both compute the same bits.
+// kernel (attention.cu, k_attention_lat) and the single-sequence cluster forward (latency.cu, eight
+// lanes), so both compute the same bits.
 //
 // Sub-lane sl (0..3) of a query computes the scores and exponentials of the keys whose softmax-sum
 // slots it owns -- in every full 16-key chunk t0 the keys t0 + 2sl, t0 + 2sl + 1 (slots 2sl, 2sl + 1
@@ -119,6 +119,99 @@ __device__ __forceinline__ void attend_query_lanes4(const float (&q)[32], const 
   }
 #pragma unroll
   for (int k = 0; k < 8; ++k) cx[k] = acc_e[k] + acc_o[k];
+}
+
+// The same with eight lanes per query (consecutive lanes 8k .. 8k + 7 of a warp; every lane of the
+// warp calls it): sub-lane s owns slot s of both 8-lane sum accumulators -- in every full 16-key
+// chunk t0 the keys t0 + s (first accumulator) and t0 + 8 + s (second), key L16 + s of the trailing
+// 8-key chunk (first), and tail key L8 + s (scalar exp, added in order after the tree by sub-lane 0)
+// -- and dims 4s .. 4s + 3 of the even / odd weighted-sum accumulators. Every chain the reference
+// keeps runs in one thread in the reference's order, so the result is the same bits as
+// attend_query_lanes4. cx: dims 4s .. 4s + 3 of the context row.
+__device__ __forceinline__ void attend_query_lanes8(const float (&q)[32], const float* __restrict__ kd,
+                                                    const float* __restrict__ vd, int P, float* er, int L, int s,
+                                                    float (&cx)[4]) {
+  const int L4 = L & ~3, L8 = L & ~7, L16 = L & ~15;
+  const unsigned full = 0xffffffffu;
+
+  auto score = [&](int t) -> float {  // score_pair's order for one key
+    float s8[8];
+#pragma unroll
+    for (int l = 0; l < 8; ++l)
+      s8[l] = fmaf(q[8 + l], kd[(8 + l) * P + t], q[l] * kd[l * P + t]) +
+              fmaf(q[24 + l], kd[(24 + l) * P + t], q[16 + l] * kd[(16 + l) * P + t]);
+    return (t < L4) ? ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]))
+                    : ((s8[0] + s8[4]) + (s8[1] + s8[5])) + ((s8[2] + s8[6]) + (s8[3] + s8[7]));
+  };
+
+  // pass 1: scores of the owned keys, their max over the query's eight sub-lanes
+  float mx = -INFINITY;
+  for (int t0 = 0; t0 < L16; t0 += 16) {
+    const float a = score(t0 + s), b = score(t0 + 8 + s);
+    er[t0 + s] = a;
+    er[t0 + 8 + s] = b;
+    mx = fmaxf(mx, fmaxf(a, b));
+  }
+  if (L16 + s < L8) {
+    const float a = score(L16 + s);
+    er[L16 + s] = a;
+    mx = fmaxf(mx, a);
+  }
+  if (L8 + s < L) {
+    const float a = score(L8 + s);
+    er[L8 + s] = a;
+    mx = fmaxf(mx, a);
+  }
+  mx = fmaxf(mx, __shfl_xor_sync(full, mx, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(full, mx, 2));
+  mx = fmaxf(mx, __shfl_xor_sync(full, mx, 4));
+
+  // pass 2: exponentials of the owned keys and the owned sum chains (slot s of both accumulators)
+  float c0 = 0.0f, c1 = 0.0f;
+  for (int t0 = 0; t0 < L16; t0 += 16) {
+    const float e0 = cw_exp(er[t0 + s] - mx), e1 = cw_exp(er[t0 + 8 + s] - mx);
+    er[t0 + s] = e0;
+    er[t0 + 8 + s] = e1;
+    c0 = c0 + e0;
+    c1 = c1 + e1;
+  }
+  if (L16 + s < L8) {  // the trailing 8-key chunk feeds the first accumulator
+    const float e0 = cw_exp(er[L16 + s] - mx);
+    er[L16 + s] = e0;
+    c0 = c0 + e0;
+  }
+  if (L8 + s < L) er[L8 + s] = scalar_expf(er[L8 + s] - mx);
+  // hsum256 of v[m] = acc0[m] + acc1[m]: sub-lane s holds v[s]
+  const float v = c0 + c1;
+  const float a = v + __shfl_down_sync(full, v, 4);  // v0 + v4 | v1 + v5 | v2 + v6 | v3 + v7
+  const float b = a + __shfl_down_sync(full, a, 1);  // (v0 + v4) + (v1 + v5) | ... (sub-lanes 0, 2)
+  float sum = b + __shfl_down_sync(full, b, 2);      // sub-lane 0
+  __syncwarp();
+  if (s == 0)
+    for (int t = L8; t < L; ++t) sum = sum + er[t];  // the tail keys in order, after the tree
+  const float inv = __shfl_sync(full, 1.0f / sum, (threadIdx.x & 31) & ~7);
+
+  // pass 3: weighted sum of V, dims 4s .. 4s + 3; even keys to the first accumulator
+  float acc_e[4], acc_o[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) acc_e[k] = acc_o[k] = 0.0f;
+  const float* vrow = vd + 4 * s * P;
+  int t = 0;
+  for (; t + 1 < L; t += 2) {
+    const float p0 = er[t] * inv, p1 = er[t + 1] * inv;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      acc_e[k] = fmaf(vrow[k * P + t], p0, acc_e[k]);
+      acc_o[k] = fmaf(vrow[k * P + t + 1], p1, acc_o[k]);
+    }
+  }
+  if (t < L) {
+    const float p0 = er[t] * inv;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc_e[k] = fmaf(vrow[k * P + t], p0, acc_e[k]);
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) cx[k] = acc_e[k] + acc_o[k];
 }
 
 }  // namespace ae

@@ -13,7 +13,7 @@
 // Per layer (L <= 32 rows, one 128-row tcgen05 tile whose rows L..127 are ignored):
 //   QKV    MMA of the layer input (int8, shared memory) with the 96 weight rows of head c's Q | K |
 //          V (N = 96, K = 384), dequantized as the QKV GEMM's plain epilogue does
-//   attn   the head's attention in the reference's order (attend_query_lanes4); partial row maxima
+//   attn   the head's attention in the reference's order (attend_query_lanes8); partial row maxima
 //          of the context slice -> every CTA                                   | cluster barrier
 //   ctx q  each CTA quantizes its own 32 context columns with the row maxima (smooth_quantize_row,
 //          as the short-sequence attention kernel does) -> every CTA's A operand | cluster barrier
@@ -40,7 +40,7 @@
 
 #include <cstdint>
 
-#include "attn_lanes4.cuh"
+#include "attn_lanes.cuh"
 #include "latency.h"
 #include "ptx.cuh"
 #include "rowmath.cuh"
@@ -353,6 +353,52 @@ __device__ __forceinline__ void ln_quant_owned(const Smem& S, const float* gamma
   }
 }
 
+// FFN-up epilogue of slice c: g = GELU(fma(acc, a_s * w_s, bias)) * inv_smooth (the GEMM's GELU
+// epilogue arithmetic) back into S.acc as floats, and each row's partial maximum over the slice's 128
+// columns -> every CTA. G threads per row (128 / G columns each), so short sequences spread their
+// rows over all threads.
+template <int G>
+__device__ __forceinline__ void gelu_slice(const Smem& S, int c, int rows, int tid, int use_erf) {
+  constexpr int CW = 128 / G;
+  const int r = tid / G, cb = (tid % G) * CW;
+  float vmax = 1e-8f;
+  if (r < rows) {
+    const float as = S.as[r];
+    int32_t* arow = S.acc + r * 129;
+    float* grow = reinterpret_cast<float*>(arow);
+    const float* fws = S.vec + V_FIW + cb;
+    const float* fb = S.vec + V_FIB + cb;
+    const float* finv = S.vec + V_FOINV + cb;
+    if (use_erf) {
+#pragma unroll
+      for (int j = 0; j < CW; ++j) {
+        const float gv = gelu_erf(fmaf(float(arow[cb + j]), as * fws[j], fb[j])) * finv[j];
+        vmax = fmaxf(vmax, fabsf(gv));
+        grow[cb + j] = gv;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < CW; j += 2) {
+        const float2 ws2 = make_float2(fws[j], fws[j + 1]);
+        const float2 b2 = make_float2(fb[j], fb[j + 1]);
+        const float2 iv2 = make_float2(finv[j], finv[j + 1]);
+        const float2 h = __ffma2_rn(make_float2(float(arow[cb + j]), float(arow[cb + j + 1])),
+                                    __fmul2_rn(make_float2(as, as), ws2), b2);
+        const float2 gv = __fmul2_rn(gelu_ref2(h), iv2);
+        vmax = fmaxf(vmax, fmaxf(fabsf(gv.x), fabsf(gv.y)));
+        grow[cb + j] = gv.x;
+        grow[cb + j + 1] = gv.y;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 1; o < G; o <<= 1) vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, o));
+  const int t = tid % G;
+  if (r < rows && t < kLatCtas) st_cluster_f32(map_peer(S.xgm + c * kR + r, uint32_t(t)), vmax);
+  if (G == 8 && r < rows && t < 4)  // 8 threads per row: the first 4 take the remaining CTAs
+    for (int p = t + 8; p < kLatCtas; p += 4) st_cluster_f32(map_peer(S.xgm + c * kR + r, uint32_t(p)), vmax);
+}
+
 __global__ void __launch_bounds__(kLatThreads, 1)
     k_forward_lat(const LatModel* __restrict__ m, const uint16_t* __restrict__ ids, int L, float* __restrict__ out,
                   int* err, int use_erf) {
@@ -451,26 +497,29 @@ __global__ void __launch_bounds__(kLatThreads, 1)
     }
     __syncthreads();
 
-    // ---- attention of head c (threads 0..127: four lanes per query; the [CLS] query alone in the
-    // last layer); the partial row maxima of the context slice -> every CTA
-    float cx[8];
-    const int ql = tid >> 2, sl = tid & 3;
-    const bool att = warp < (last ? 1 : 4);  // warp-uniform
+    // ---- attention of head c (eight lanes per query, all 256 threads; the [CLS] query alone in
+    // the last layer); the partial row maxima of the context slice -> every CTA
+    float cx[4];
+    const int ql = tid >> 3, sl = tid & 7;
+    const bool att = warp < (last ? 1 : 8);  // warp-uniform
     const bool qactive = att && ql < rows;
     const int qi = qactive ? ql : rows - 1;
-    const float* ivs = S.vec + V_AOINV + 32 * c + 8 * sl;
+    const float* ivs = S.vec + V_AOINV + 32 * c + 4 * sl;
     if (att) {
       float q[32];
 #pragma unroll
       for (int d = 0; d < 32; ++d) q[d] = S.qd[qi * 32 + d] * qscale;
-      attend_query_lanes4(q, S.kd, S.vd, kP, S.es + ql * kP, L, sl, cx);
+      attend_query_lanes8(q, S.kd, S.vd, kP, S.es + ql * kP, L, sl, cx);
       float vmax = 1e-8f;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) vmax = fmaxf(vmax, fabsf(cx[k] * ivs[k]));
+      for (int k = 0; k < 4; ++k) vmax = fmaxf(vmax, fabsf(cx[k] * ivs[k]));
       vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
       vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
-      if (qactive && sl < 4)
-        for (int p = sl; p < kLatCtas; p += 4) st_cluster_f32(map_peer(S.xcm + c * kR + qi, uint32_t(p)), vmax);
+      vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 4));
+      if (qactive) {
+        st_cluster_f32(map_peer(S.xcm + c * kR + qi, uint32_t(sl)), vmax);
+        if (sl < kLatCtas - 8) st_cluster_f32(map_peer(S.xcm + c * kR + qi, uint32_t(sl + 8)), vmax);
+      }
     }
     cluster_sync_all();
 
@@ -480,15 +529,12 @@ __global__ void __launch_bounds__(kLatThreads, 1)
 #pragma unroll
       for (int p = 1; p < kLatCtas; ++p) max_abs = fmaxf(max_abs, S.xcm[p * kR + qi]);
       const float inv_scale = 127.0f / max_abs;
-      uint32_t w0 = 0, w1 = 0;
+      uint32_t w = 0;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        w0 |= (uint32_t(quant_i8(cx[k] * (ivs[k] * inv_scale))) & 0xFFu) << (8 * k);
-        w1 |= (uint32_t(quant_i8(cx[4 + k] * (ivs[4 + k] * inv_scale))) & 0xFFu) << (8 * k);
-      }
-      const int off = a_off(qi, 32 * c + 8 * sl);
+      for (int k = 0; k < 4; ++k) w |= (uint32_t(quant_i8(cx[k] * (ivs[k] * inv_scale))) & 0xFFu) << (8 * k);
+      const int off = a_off(qi, 32 * c + 4 * sl);
 #pragma unroll
-      for (int p = 0; p < kLatCtas; ++p) st_cluster_u32x2(map_peer(S.A + off, uint32_t(p)), w0, w1);
+      for (int p = 0; p < kLatCtas; ++p) st_cluster_u32(map_peer(S.A + off, uint32_t(p)), w);
       if (sl == 0) S.as[qi] = max_abs / 127.0f;
     }
     fence_proxy_async_all();
@@ -506,42 +552,9 @@ __global__ void __launch_bounds__(kLatThreads, 1)
 
     // ---- FFN-up slice c (N = 128): g = GELU(h) * inv_smooth; partial row maxima -> every CTA
     ok = run_gemm<128>(m, S, s0 + 2, 3, tmem, c, err, ok, tid, warp, lane);
-    {
-      const int r = tid >> 3, cb = (tid & 7) * 16;  // 32 rows x 8 groups of 16 columns
-      const float as = S.as[r];
-      int32_t* arow = S.acc + r * 129;
-      float* grow = reinterpret_cast<float*>(arow);
-      const float* fws = S.vec + V_FIW + cb;
-      const float* fb = S.vec + V_FIB + cb;
-      const float* finv = S.vec + V_FOINV + cb;
-      float vmax = 1e-8f;
-      if (use_erf) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float gv = gelu_erf(fmaf(float(arow[cb + j]), as * fws[j], fb[j])) * finv[j];
-          vmax = fmaxf(vmax, fabsf(gv));
-          grow[cb + j] = gv;
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 16; j += 2) {
-          const float2 ws2 = make_float2(fws[j], fws[j + 1]);
-          const float2 b2 = make_float2(fb[j], fb[j + 1]);
-          const float2 iv2 = make_float2(finv[j], finv[j + 1]);
-          const float2 h = __ffma2_rn(make_float2(float(arow[cb + j]), float(arow[cb + j + 1])),
-                                      __fmul2_rn(make_float2(as, as), ws2), b2);
-          const float2 gv = __fmul2_rn(gelu_ref2(h), iv2);
-          vmax = fmaxf(vmax, fmaxf(fabsf(gv.x), fabsf(gv.y)));
-          grow[cb + j] = gv.x;
-          grow[cb + j + 1] = gv.y;
-        }
-      }
-      vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 1));
-      vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 2));
-      vmax = fmaxf(vmax, __shfl_xor_sync(0xffffffffu, vmax, 4));
-      if (r < rows && (tid & 7) < 4)
-        for (int p = tid & 7; p < kLatCtas; p += 4) st_cluster_f32(map_peer(S.xgm + c * kR + r, uint32_t(p)), vmax);
-    }
+    if (rows <= 8) gelu_slice<32>(S, c, rows, tid, use_erf);
+    else if (rows <= 16) gelu_slice<16>(S, c, rows, tid, use_erf);
+    else gelu_slice<8>(S, c, rows, tid, use_erf);
     cluster_sync_all();
     {  // the slice quantized with the row maximum over all 1,536 columns -> k-block c of every A
       const int r = tid >> 3, ch = tid & 7;
