@@ -19,8 +19,9 @@ torchrun, no collective on the data path: weak scaling). Synthetic seeded model 
   int8_peak the library's own tcgen05 kind::i8 loop (one CTA per SM, resident operands)
   micro     config 5: the GEMM shapes and the 64 x 12 x 512 attention (N = 1)
   ragged    config 4: 131,072 log-uniform sequences through ae_embed_batch_multi (N = 1)
-  multi_api at N > 1, rank 0 alone drives all N GPUs through ae_embed_batch_multi (the product's
-            multi-GPU entry point: planner, host threads, pinned staging, host gather)
+  multi_api rank 0 alone drives all N GPUs through ae_embed_batch_multi (the product's multi-GPU
+            entry point: planner, host threads, pipelined pinned staging, host gather); at N = 1 the
+            same call on one GPU, the base of its scaling
 
 `--impl reference` times the reference's CPU path (the oracle; the Rust crate cannot be built
 here) on the same metric and prints its own JSON line.
@@ -409,6 +410,8 @@ def multi_api(world: int, pack: str, steps: int) -> dict:
     from arctic_embed_s_int8 import Engine, embed_batch_multi, pack_sequences, synth
 
     engines = [Engine(d).load_file(pack) for d in range(world)]
+    for e in engines:  # the workspace of the largest batch (65,536 rows of 8-token sequences)
+        e.reserve(65536, 8192)
     r = np.random.Generator(np.random.PCG64(2024))
     sets = {
         "config3": [synth.token_ids(SEQ_LEN, r) for _ in range(world * BATCH_SEQS * steps)],
@@ -418,7 +421,7 @@ def multi_api(world: int, pack: str, steps: int) -> dict:
     out = {"gpus": world, "api": "ae_embed_batch_multi (one process, one context and host thread per GPU)"}
     for name, seqs in sets.items():
         ids, cu = pack_sequences(seqs)
-        embed_batch_multi(engines, ids=ids[: int(cu[world * 256])], cu=cu[: world * 256 + 1])  # warm-up
+        embed_batch_multi(engines, ids=ids, cu=cu)  # warm-up: sizes the staging buffers
         t0 = time.perf_counter()
         embed_batch_multi(engines, ids=ids, cu=cu)
         dt = time.perf_counter() - t0
@@ -699,6 +702,10 @@ def main() -> int:
                 result["cpu_latency"] = cpu_latency(args.cpu_latency_runs)
             except Exception as e:  # reported, not fatal
                 result["cpu_latency"] = {"error": str(e)}
+        try:
+            result["multi_api"] = multi_api(1, pack, args.steps)
+        except Exception as e:  # reported, not fatal
+            result["multi_api"] = {"error": str(e)}
     if world > 1 and not args.no_extras:
         # the product's multi-GPU entry point: rank 0 alone drives every GPU of the box while the
         # other ranks wait on a host-side (gloo) barrier, which leaves their GPUs idle

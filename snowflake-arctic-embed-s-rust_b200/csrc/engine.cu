@@ -135,6 +135,21 @@ struct ae_ctx {
   // host packing of the last ragged batch: sequences grouped by attention length class
   std::vector<uint32_t> order;       // packed position -> caller's sequence index
   std::vector<ae::AttnSegment> segs;  // consecutive packed sequences of one class
+  // ae_embed_batch_multi's two staging slots (kept across calls, grown as needed)
+  struct PipeSlot {
+    uint32_t cap_tok = 0, cap_seqs = 0;
+    uint16_t* h_ids = nullptr;
+    uint32_t* h_cu = nullptr;
+    float* h_out = nullptr;
+    uint16_t* d_ids = nullptr;
+    uint32_t* d_cu = nullptr;
+    float* d_out = nullptr;
+    cudaEvent_t done = nullptr;
+    std::vector<uint32_t> order, idx;
+    std::vector<ae::AttnSegment> segs;
+    uint32_t n = 0;
+    bool busy = false;
+  } pipe[2];
 };
 
 namespace {
@@ -713,58 +728,65 @@ int check_dev_err(ae_ctx* c) {
   return 0;
 }
 
-// Packs host sequences (truncating each to 512) into the pinned staging buffers.
-int pack_host(ae_ctx* c, const uint16_t* ids, const uint32_t* cu, uint32_t n, int* T_out, int* maxlen_out) {
-  uint64_t T = 0;
-  int max_len = 0;
-  for (uint32_t i = 0; i < n; ++i) {
-    if (cu[i + 1] < cu[i]) return fail(c, AE_ERR_INVALID_ARG, "cu_seqlens must be non-decreasing");
-    const uint32_t len = std::min<uint32_t>(cu[i + 1] - cu[i], kMaxPos);
-    if (len == 0) return fail(c, AE_ERR_INVALID_ARG, "sequence %u is empty (input_ids must not be empty)", i);
-    T += len;
-    max_len = std::max<int>(max_len, int(len));
-  }
-  if (T > 0x7fffffffu) return fail(c, AE_ERR_CAPACITY, "batch too large");
-  AE_TRY(reserve(c, uint32_t(T), n));
-  Workspace& W = c->ws;
-  // Sequences are packed grouped by attention length class (stable inside a class), so that each
-  // class's attention launch is sized for its own longest sequence; rows are independent, so the
-  // order changes no result, and the output is written back in the caller's order.
+// Packs host sequences (truncating each to 512) into h_ids / h_cu, grouped by attention length
+// class (stable inside a class), so that each class's attention launch is sized for its own longest
+// sequence; rows are independent, so the order changes no result. order[k] = the caller's index of
+// packed sequence k; segs = the runs of one class. Validates lengths and token ids.
+int pack_into(ae_ctx* c, const uint16_t* ids, const uint32_t* cu, uint32_t n, uint16_t* h_ids, uint32_t* h_cu,
+              std::vector<uint32_t>& order, std::vector<AttnSegment>& segs, int* T_out, int* maxlen_out) {
   auto len_of = [&](uint32_t i) { return std::min<uint32_t>(cu[i + 1] - cu[i], kMaxPos); };
-  c->order.resize(n);
-  c->segs.clear();
+  order.resize(n);
+  segs.clear();
   uint32_t filled = 0;
   // the int8 attention mode keeps the sequences below its crossover in a class of their own
   const bool i8 = c->attn_mode == AE_ATTENTION_INT8;
   auto class_of = [&](int len) { return i8 ? (len < kI8MinLen ? 0 : 1 + attn_class(len)) : attn_class(len); };
+  int max_len = 0;
   for (int cls = 0; cls < kAttnClasses + (i8 ? 1 : 0); ++cls) {
     const uint32_t first = filled;
     int seg_max = 0, seg_min = kMaxPos;
     for (uint32_t i = 0; i < n; ++i) {
       const uint32_t len = len_of(i);
       if (class_of(int(len)) != cls) continue;
-      c->order[filled++] = i;
+      order[filled++] = i;
       seg_max = std::max<int>(seg_max, int(len));
       seg_min = std::min<int>(seg_min, int(len));
     }
-    if (filled > first) c->segs.push_back(AttnSegment{int(first), int(filled - first), seg_max, seg_min});
+    if (filled > first) segs.push_back(AttnSegment{int(first), int(filled - first), seg_max, seg_min});
+    max_len = std::max(max_len, seg_max);
   }
   uint32_t off = 0;
-  W.h_cu[0] = 0;
+  h_cu[0] = 0;
   for (uint32_t k = 0; k < n; ++k) {
-    const uint32_t i = c->order[k];
+    const uint32_t i = order[k];
     const uint32_t len = len_of(i);
     const uint16_t* src = ids + cu[i];
     for (uint32_t j = 0; j < len; ++j) {
       if (src[j] >= kVocab) return fail(c, AE_ERR_TOKEN_RANGE, "token id %u at sequence %u is >= 30522", src[j], i);
     }
-    std::memcpy(W.h_ids + off, src, len * 2);
+    std::memcpy(h_ids + off, src, len * 2);
     off += len;
-    W.h_cu[k + 1] = off;
+    h_cu[k + 1] = off;
   }
-  *T_out = int(T);
+  *T_out = int(off);
   *maxlen_out = max_len;
   return 0;
+}
+
+// Checks a host batch (non-decreasing cu_seqlens, no empty sequence), reserves the workspace for it
+// and packs it into the context's pinned staging buffers.
+int pack_host(ae_ctx* c, const uint16_t* ids, const uint32_t* cu, uint32_t n, int* T_out, int* maxlen_out) {
+  uint64_t T = 0;
+  for (uint32_t i = 0; i < n; ++i) {
+    if (cu[i + 1] < cu[i]) return fail(c, AE_ERR_INVALID_ARG, "cu_seqlens must be non-decreasing");
+    const uint32_t len = std::min<uint32_t>(cu[i + 1] - cu[i], kMaxPos);
+    if (len == 0) return fail(c, AE_ERR_INVALID_ARG, "sequence %u is empty (input_ids must not be empty)", i);
+    T += len;
+  }
+  if (T > 0x7fffffffu) return fail(c, AE_ERR_CAPACITY, "batch too large");
+  AE_TRY(reserve(c, uint32_t(T), n));
+  Workspace& W = c->ws;
+  return pack_into(c, ids, cu, n, W.h_ids, W.h_cu, c->order, c->segs, T_out, maxlen_out);
 }
 
 int forward_ragged_host(ae_ctx* c, const uint16_t* ids, const uint32_t* cu, uint32_t n, float* out) {
@@ -896,6 +918,96 @@ std::vector<std::vector<uint32_t>> plan_shards(const uint32_t* cu, uint32_t n, i
   return shard;
 }
 
+// The device batches of one context's shard (sequence indices s, batch b = s[ends[b - 1] ..
+// ends[b])), pipelined over two staging slots: while batch b runs on the GPU, the host packs batch
+// b + 1 into the other slot, then waits for batch b - 1 and copies its embeddings out by index.
+int run_batches(ae_ctx* c, const std::vector<uint32_t>& s, const std::vector<size_t>& ends, const uint16_t* ids,
+                const uint32_t* cu, uint32_t max_tok, uint32_t max_seqs, float* out) {
+  auto len_of = [&](uint32_t i) { return std::min<uint32_t>(cu[i + 1] - cu[i], kMaxPos); };
+  for (auto& sl : c->pipe) {
+    sl.busy = false;
+    if (sl.cap_tok >= max_tok && sl.cap_seqs >= max_seqs) continue;
+    const uint32_t t = std::max(max_tok, sl.cap_tok), q = std::max(max_seqs, sl.cap_seqs);
+    if (sl.h_ids) cudaFreeHost(sl.h_ids);
+    if (sl.h_cu) cudaFreeHost(sl.h_cu);
+    if (sl.h_out) cudaFreeHost(sl.h_out);
+    if (sl.d_ids) cudaFree(sl.d_ids);
+    if (sl.d_cu) cudaFree(sl.d_cu);
+    if (sl.d_out) cudaFree(sl.d_out);
+    sl.h_ids = nullptr;
+    sl.h_cu = nullptr;
+    sl.h_out = nullptr;
+    sl.d_ids = nullptr;
+    sl.d_cu = nullptr;
+    sl.d_out = nullptr;
+    sl.cap_tok = sl.cap_seqs = 0;
+    CUDA_TRY(c, cudaMallocHost(&sl.h_ids, size_t(t) * 2));
+    CUDA_TRY(c, cudaMallocHost(&sl.h_cu, size_t(q + 1) * 4));
+    CUDA_TRY(c, cudaMallocHost(&sl.h_out, size_t(q) * kHidden * 4));
+    CUDA_TRY(c, cudaMalloc(&sl.d_ids, size_t(t) * 2));
+    CUDA_TRY(c, cudaMalloc(&sl.d_cu, size_t(q + 1) * 4));
+    CUDA_TRY(c, cudaMalloc(&sl.d_out, size_t(q) * kHidden * 4));
+    if (!sl.done) CUDA_TRY(c, cudaEventCreateWithFlags(&sl.done, cudaEventDisableTiming));
+    sl.cap_tok = t;
+    sl.cap_seqs = q;
+  }
+  auto drain = [&](ae_ctx::PipeSlot& sl) -> int {
+    if (!sl.busy) return 0;
+    sl.busy = false;
+    CUDA_TRY(c, cudaEventSynchronize(sl.done));
+    for (uint32_t k = 0; k < sl.n; ++k)
+      std::memcpy(out + size_t(sl.idx[sl.order[k]]) * kHidden, sl.h_out + size_t(k) * kHidden, kHidden * 4);
+    return 0;
+  };
+  std::vector<uint16_t> bids;
+  std::vector<uint32_t> bcu;
+  int r = 0;
+  size_t i = 0;
+  for (size_t bi = 0; bi < ends.size() && !r; ++bi) {
+    ae_ctx::PipeSlot& sl = c->pipe[bi & 1];
+    if ((r = drain(sl))) break;  // batch bi - 2
+    const size_t j = ends[bi];
+    bids.clear();
+    bcu.assign(1, 0);
+    sl.idx.clear();
+    uint32_t tok = 0;
+    for (size_t k = i; k < j; ++k) {
+      const uint32_t L = len_of(s[k]);
+      bids.insert(bids.end(), ids + cu[s[k]], ids + cu[s[k]] + L);
+      tok += L;
+      bcu.push_back(tok);
+      sl.idx.push_back(s[k]);
+    }
+    const uint32_t nb = uint32_t(j - i);
+    int T = 0, max_len = 0;
+    if ((r = pack_into(c, bids.data(), bcu.data(), nb, sl.h_ids, sl.h_cu, sl.order, sl.segs, &T, &max_len))) break;
+    if (cudaMemcpyAsync(sl.d_ids, sl.h_ids, size_t(T) * 2, cudaMemcpyHostToDevice, c->stream) != cudaSuccess ||
+        cudaMemcpyAsync(sl.d_cu, sl.h_cu, size_t(nb + 1) * 4, cudaMemcpyHostToDevice, c->stream) != cudaSuccess) {
+      r = fail(c, AE_ERR_CUDA, "batch input copy failed");
+      break;
+    }
+    if ((r = enqueue_forward(c, sl.d_ids, sl.d_cu, T, int(nb), max_len, sl.d_out, &sl.segs))) break;
+    if (cudaMemcpyAsync(sl.h_out, sl.d_out, size_t(nb) * kHidden * 4, cudaMemcpyDeviceToHost, c->stream) !=
+            cudaSuccess ||
+        cudaEventRecord(sl.done, c->stream) != cudaSuccess) {
+      r = fail(c, AE_ERR_CUDA, "batch output copy failed");
+      break;
+    }
+    sl.n = nb;
+    sl.busy = true;
+    i = j;
+  }
+  const size_t nbat = ends.size();
+  for (size_t k = 0; k < 2; ++k) {  // the last two batches, oldest first
+    ae_ctx::PipeSlot& sl = c->pipe[(nbat + k) & 1];
+    const int rd = drain(sl);
+    if (!r) r = rd;
+  }
+  if (cudaStreamSynchronize(c->stream) != cudaSuccess && !r) r = fail(c, AE_ERR_CUDA, "stream synchronisation failed");
+  if (!r) r = check_dev_err(c);
+  return r;
+}
+
 }  // namespace
 
 // ============================================================================================ C ABI
@@ -962,6 +1074,15 @@ int ae_ctx_destroy(ae_ctx* c) {
   free_ws(c);
   free_model(c);
   if (c->h_model) cudaFreeHost(c->h_model);
+  for (auto& sl : c->pipe) {
+    if (sl.h_ids) cudaFreeHost(sl.h_ids);
+    if (sl.h_cu) cudaFreeHost(sl.h_cu);
+    if (sl.h_out) cudaFreeHost(sl.h_out);
+    if (sl.d_ids) cudaFree(sl.d_ids);
+    if (sl.d_cu) cudaFree(sl.d_cu);
+    if (sl.d_out) cudaFree(sl.d_out);
+    if (sl.done) cudaEventDestroy(sl.done);
+  }
   for (auto& e : c->prof_events) {
     cudaEventDestroy(e.second.first);
     cudaEventDestroy(e.second.second);
@@ -1536,17 +1657,16 @@ int ae_embed_batch_multi(ae_ctx* const* ctxs, int n_ctx, const uint16_t* ids, co
   if (!ids || !cu || !out) return fail(ctxs[0], AE_ERR_INVALID_ARG, "null pointer");
   if (max_tokens == 0) max_tokens = 65536;
   max_tokens = std::max<uint32_t>(max_tokens, kMaxPos);
-  for (uint32_t i = 0; i < n; ++i)
+  for (uint32_t i = 0; i < n; ++i) {
     if (cu[i + 1] < cu[i]) return fail(ctxs[0], AE_ERR_INVALID_ARG, "cu_seqlens must be non-decreasing");
+    if (cu[i + 1] == cu[i]) return fail(ctxs[0], AE_ERR_INVALID_ARG, "sequence %u is empty (input_ids must not be empty)", i);
+  }
   auto len_of = [&](uint32_t i) { return std::min<uint32_t>(cu[i + 1] - cu[i], kMaxPos); };
   std::vector<std::vector<uint32_t>> shard = plan_shards(cu, n, n_ctx);
   std::vector<int> rc(n_ctx, 0);
   auto worker = [&](int d) {
     ae_ctx* c = ctxs[d];
     DeviceGuard g(c->device);
-    std::vector<uint16_t> bids;
-    std::vector<uint32_t> bcu;
-    std::vector<float> bout;
     // longest first: each batch then holds sequences of similar length (tight attention launches)
     std::vector<uint32_t> s = shard[d];
     std::stable_sort(s.begin(), s.end(), [&](uint32_t x, uint32_t y) { return len_of(x) > len_of(y); });
@@ -1562,26 +1682,9 @@ int ae_embed_batch_multi(ae_ctx* const* ctxs, int n_ctx, const uint16_t* ids, co
       most_seqs = std::max<uint32_t>(most_seqs, uint32_t(j - i));
       i = j;
     }
-    if (!s.empty()) rc[d] = reserve(c, most_tok, most_seqs);
-    size_t i = 0;
-    for (size_t bi = 0; bi < ends.size() && rc[d] == 0; ++bi) {
-      bids.clear();
-      bcu.assign(1, 0);
-      const size_t j = ends[bi];
-      uint32_t tok = 0;
-      for (size_t k = i; k < j; ++k) {
-        const uint32_t L = len_of(s[k]);
-        bids.insert(bids.end(), ids + cu[s[k]], ids + cu[s[k]] + L);
-        tok += L;
-        bcu.push_back(tok);
-      }
-      const uint32_t nb = uint32_t(j - i);
-      bout.resize(size_t(nb) * kHidden);
-      rc[d] = forward_ragged_host(c, bids.data(), bcu.data(), nb, bout.data());
-      if (rc[d]) break;
-      for (uint32_t k = 0; k < nb; ++k) std::memcpy(out + size_t(s[i + k]) * kHidden, &bout[size_t(k) * kHidden], kHidden * 4);
-      i = j;
-    }
+    if (s.empty()) return;
+    rc[d] = reserve(c, most_tok, most_seqs);
+    if (!rc[d]) rc[d] = run_batches(c, s, ends, ids, cu, most_tok, most_seqs, out);
   };
   std::vector<std::thread> th;
   for (int d = 1; d < n_ctx; ++d) th.emplace_back(worker, d);
