@@ -35,7 +35,7 @@ __device__ __forceinline__ float halfwarp_max(float v, unsigned mask) {
   return v;
 }
 
-// One half-warp per token row, 16 rows per block and step (grid-stride): dequant_add_embeddings_row
+// One half-warp per token row, 16 rows per block: dequant_add_embeddings_row
 // (src/simd_math.rs:1827-1881, generic path) + layernorm_smooth_quantize_row (src/simd_math.rs:369-477)
 // with the embedding LayerNorm and layers[0].qkv.inv_smooth (src/model.rs:196-219). The hidden
 // rows go through a shared-memory tile so that the tile-transposed store of a column covers the
@@ -53,7 +53,7 @@ __global__ void __launch_bounds__(256) k_embed_ln_quant(EmbedArgs a) {
   __syncthreads();
   pdl_wait();
   __shared__ float tile[kHidden][17];
-  for (int r0 = blockIdx.x * 16; r0 < a.T; r0 += gridDim.x * 16) {
+  const int r0 = blockIdx.x * 16;
   const int lr = threadIdx.x >> 4;  // row within the block
   const int row = r0 + lr;
   const int l = threadIdx.x & 15;
@@ -109,8 +109,6 @@ __global__ void __launch_bounds__(256) k_embed_ln_quant(EmbedArgs a) {
   for (int i = threadIdx.x; i < kHidden * 16; i += blockDim.x) {
     const int j = i >> 4, rr = i & 15;
     if (r0 + rr < a.T) a.hidden[tt_index(r0 + rr, j, kHidden)] = tile[j][rr];
-  }
-  __syncthreads();  // the tile is reused by the next row group
   }
 }
 
@@ -371,9 +369,7 @@ int launch_wait_selftest(int* err, uint64_t limit_ns, cudaStream_t st) {
 int launch_embed(const EmbedArgs& a, cudaStream_t st) {
   if (a.T <= 0) return 0;
   const int rows_per_block = 16;
-  // grid-stride over 16-row groups: at most 4 blocks per SM, the model constants staged once each
-  const int groups = (a.T + rows_per_block - 1) / rows_per_block;
-  const dim3 grid(groups < 148 * 4 ? groups : 148 * 4);
+  const dim3 grid((a.T + rows_per_block - 1) / rows_per_block);
   return launch_pdl(k_embed_ln_quant, grid, dim3(256), 0, st, a) == cudaSuccess ? 0 : -1;
 }
 
