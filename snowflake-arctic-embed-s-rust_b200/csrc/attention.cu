@@ -1009,6 +1009,176 @@ __global__ void __launch_bounds__(4 * QT) k_attention_lat(AttnArgs a) {
   }
 }
 
+// Few (sequence, head) pairs of more than 64 keys (single sequences of 65-512 tokens and small
+// batches on the latency path): eight lanes per query, one CTA per (sequence, head, tile of qt
+// queries), qt chosen by the launch so that the tiles of all pairs fill the SMs about once. The
+// TMEM kernels keep one query per thread and so give a 512-token sequence 48 tiles of 128 queries;
+// here 12 tiles of 44 queries per head are 144 CTAs of 11 warps.
+//
+// The chains are attend_query_lanes8's (so the same bits as every other exact kernel): sub-lane s
+// owns slot s of both 8-lane sum accumulators (keys t0 + s and t0 + 8 + s of every full 16-key
+// chunk, L16 + s of the trailing 8-key chunk, tail key L8 + s) and dims 4s .. 4s + 3 of the even /
+// odd weighted-sum accumulators. K and V are staged key-major (32 dims of a key in a row of 128
+// bytes) with the row's 16-byte chunks XOR-swizzled by the key's low 3 bits, so that a lane reads 4
+// dims in one 16-byte load: the 8 sub-lanes reading 8 consecutive keys at one dim chunk, or one key's
+// 8 chunks, touch 8 different bank groups. The scores, then exponentials, of the CTA's queries use a
+// pitch of 8 mod 32 floats (the 4 queries of a warp read 4 different banks).
+__host__ __device__ constexpr int lat8_er_pitch(int L) { return ((L + 31) & ~31) + 8; }
+__host__ __device__ constexpr size_t lat8_smem_bytes(int L, int qt) {
+  return (size_t(64) * ((L + 7) & ~7) + size_t(qt) * lat8_er_pitch(L)) * 4;
+}
+// float index of dims 4j .. 4j + 3 of key t in a key-major swizzled K / V block
+__device__ __forceinline__ int km_index(int t, int j) { return t * 32 + ((j ^ (t & 7)) << 2); }
+
+__device__ __forceinline__ void attend_query_lanes8_km(const float (&q)[32], const float* __restrict__ kk,
+                                                       const float* __restrict__ vv, float* er, int L, int s,
+                                                       float (&cx)[4]) {
+  const int L4 = L & ~3, L8 = L & ~7, L16 = L & ~15;
+  const unsigned full = 0xffffffffu;
+
+  auto score = [&](int t) -> float {  // score_pair's order for one key
+    float k[32];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4 c = *reinterpret_cast<const float4*>(kk + km_index(t, j));
+      k[4 * j] = c.x;
+      k[4 * j + 1] = c.y;
+      k[4 * j + 2] = c.z;
+      k[4 * j + 3] = c.w;
+    }
+    float s8[8];
+#pragma unroll
+    for (int l = 0; l < 8; ++l)
+      s8[l] = fmaf(q[8 + l], k[8 + l], q[l] * k[l]) + fmaf(q[24 + l], k[24 + l], q[16 + l] * k[16 + l]);
+    return (t < L4) ? ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]))
+                    : ((s8[0] + s8[4]) + (s8[1] + s8[5])) + ((s8[2] + s8[6]) + (s8[3] + s8[7]));
+  };
+
+  // pass 1: scores of the owned keys, their max over the query's eight sub-lanes
+  float mx = -INFINITY;
+  for (int t0 = 0; t0 < L16; t0 += 16) {
+    const float a = score(t0 + s), b = score(t0 + 8 + s);
+    er[t0 + s] = a;
+    er[t0 + 8 + s] = b;
+    mx = fmaxf(mx, fmaxf(a, b));
+  }
+  if (L16 + s < L8) {
+    const float a = score(L16 + s);
+    er[L16 + s] = a;
+    mx = fmaxf(mx, a);
+  }
+  if (L8 + s < L) {
+    const float a = score(L8 + s);
+    er[L8 + s] = a;
+    mx = fmaxf(mx, a);
+  }
+  mx = fmaxf(mx, __shfl_xor_sync(full, mx, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(full, mx, 2));
+  mx = fmaxf(mx, __shfl_xor_sync(full, mx, 4));
+
+  // pass 2: exponentials of the owned keys and the owned sum chains (slot s of both accumulators)
+  float c0 = 0.0f, c1 = 0.0f;
+  for (int t0 = 0; t0 < L16; t0 += 16) {
+    const float e0 = cw_exp(er[t0 + s] - mx), e1 = cw_exp(er[t0 + 8 + s] - mx);
+    er[t0 + s] = e0;
+    er[t0 + 8 + s] = e1;
+    c0 = c0 + e0;
+    c1 = c1 + e1;
+  }
+  if (L16 + s < L8) {  // the trailing 8-key chunk feeds the first accumulator
+    const float e0 = cw_exp(er[L16 + s] - mx);
+    er[L16 + s] = e0;
+    c0 = c0 + e0;
+  }
+  if (L8 + s < L) er[L8 + s] = scalar_expf(er[L8 + s] - mx);
+  const float v = c0 + c1;  // hsum256 of v[m] = acc0[m] + acc1[m]: sub-lane s holds v[s]
+  const float a = v + __shfl_down_sync(full, v, 4);
+  const float b = a + __shfl_down_sync(full, a, 1);
+  float sum = b + __shfl_down_sync(full, b, 2);
+  __syncwarp();
+  if (s == 0)
+    for (int t = L8; t < L; ++t) sum = sum + er[t];  // the tail keys in order, after the tree
+  const float inv = __shfl_sync(full, 1.0f / sum, (threadIdx.x & 31) & ~7);
+
+  // pass 3: weighted sum of V, dims 4s .. 4s + 3; even keys to the first accumulator
+  float acc_e[4], acc_o[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) acc_e[k] = acc_o[k] = 0.0f;
+  int t = 0;
+  for (; t + 1 < L; t += 2) {
+    const float2 e2 = *reinterpret_cast<const float2*>(er + t);
+    const float p0 = e2.x * inv, p1 = e2.y * inv;
+    const float4 v0 = *reinterpret_cast<const float4*>(vv + km_index(t, s));
+    const float4 v1 = *reinterpret_cast<const float4*>(vv + km_index(t + 1, s));
+    acc_e[0] = fmaf(v0.x, p0, acc_e[0]);
+    acc_e[1] = fmaf(v0.y, p0, acc_e[1]);
+    acc_e[2] = fmaf(v0.z, p0, acc_e[2]);
+    acc_e[3] = fmaf(v0.w, p0, acc_e[3]);
+    acc_o[0] = fmaf(v1.x, p1, acc_o[0]);
+    acc_o[1] = fmaf(v1.y, p1, acc_o[1]);
+    acc_o[2] = fmaf(v1.z, p1, acc_o[2]);
+    acc_o[3] = fmaf(v1.w, p1, acc_o[3]);
+  }
+  if (t < L) {
+    const float p0 = er[t] * inv;
+    const float4 v0 = *reinterpret_cast<const float4*>(vv + km_index(t, s));
+    acc_e[0] = fmaf(v0.x, p0, acc_e[0]);
+    acc_e[1] = fmaf(v0.y, p0, acc_e[1]);
+    acc_e[2] = fmaf(v0.z, p0, acc_e[2]);
+    acc_e[3] = fmaf(v0.w, p0, acc_e[3]);
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) cx[k] = acc_e[k] + acc_o[k];
+}
+
+__global__ void __launch_bounds__(512) k_attention_lat8(AttnArgs a, int qt) {
+  pdl_trigger();
+  extern __shared__ float4 smem4[];
+  const int s = blockIdx.x;
+  const int h = blockIdx.y;
+  const int tile = blockIdx.z;
+  const int tid = threadIdx.x;
+  pdl_wait();
+  const int s0 = int(a.cu[s]);
+  const int L = int(a.cu[s + 1]) - s0;
+  if (a.skip_from > 0 && L >= a.skip_from) return;  // another kernel takes these sequences
+  if (L <= 0 || L > a.max_len) {
+    if (tid == 0 && tile == 0 && h == 0) record_err(a.err, DEV_ERR_BAD_SHAPE);
+    return;
+  }
+  if (tile * qt >= L) return;
+  const int rows = (L + 7) & ~7;
+  float* kk = reinterpret_cast<float*>(smem4);  // [rows][32] key-major, swizzled
+  float* vv = kk + rows * 32;                   // [rows][32]
+  float* es = vv + rows * 32;                   // [qt][Pe]: scores, then exponentials
+  const int Pe = lat8_er_pitch(L);
+  const int kc = a.k_col + 32 * h, vc = a.v_col + 32 * h;
+  // warp w copies columns w, w + nwarps, ... (K dims 0-31, then V dims), its lanes consecutive keys
+  // (coalesced in the tile-transposed layout): 4-byte asynchronous copies, all in flight at once
+  const int nwarps = blockDim.x >> 5, lane = tid & 31;
+  for (int c = tid >> 5; c < 64; c += nwarps) {
+    const int d = c & 31;
+    float* dst = (c < 32 ? kk : vv) + (d & 3);
+    const int col = (c < 32 ? kc : vc) + d;
+    for (int t = lane; t < L; t += 32) {
+      const float* src = a.kv_tt ? a.kv + tt_index(s0 + t, col, a.kv_C) : a.kv + size_t(s0 + t) * a.kv_C + col;
+      cp_async4(dst + km_index(t, d >> 2), src, 4u);
+    }
+  }
+  cp_async_wait_all();
+  const int ql = tid >> 3, sl = tid & 7;
+  const int qi = tile * qt + ql;
+  const bool active = qi < L;
+  float q[32];
+  load_query(a, s0 + (active ? qi : L - 1), h, q);
+  __syncthreads();
+  float cx[4];
+  attend_query_lanes8_km(q, kk, vv, es + ql * Pe, L, sl, cx);
+  if (active)
+    *reinterpret_cast<float4*>(a.out + size_t(s0 + qi) * kHidden + h * 32 + 4 * sl) =
+        make_float4(cx[0], cx[1], cx[2], cx[3]);
+}
+
 // NWG warpgroups per 128-query tile: warps w, w + 4, ... share TMEM lane quadrant w & 3 (the same
 // queries). Scores and exponentials: group g takes keys t0 + g KPG .. t0 + (g + 1) KPG - 1 of
 // every 16-key chunk (KPG = 16 / NWG), so each of the reference's 16 sum slots is summed in order
@@ -1244,6 +1414,146 @@ __global__ void __launch_bounds__(128 * NWG, MINB) k_attention_wide(AttnArgs a) 
 // Shared memory: q (32), scores / exponentials (max_len), V rows (max_len x 33), two reduction slots.
 __host__ __device__ constexpr size_t cls_smem_floats(int max_len) { return 32 + 8 + size_t(max_len) * 34 + 64; }
 
+// Few (sequence, head) pairs of long sequences: k_attention_wide's passes on tiles of 32 queries
+// (thread = query, so every K / V load is a warp-wide broadcast), with the scores, then
+// exponentials, in shared memory instead of TMEM: a 512-token sequence gives 12 x 16 CTAs
+// instead of 48. Warp g of the 8 takes keys t0 + 2g, t0 + 2g + 1 of every 16-key chunk in the
+// scores pass and in the exponentials pass -- the sum slots 2g, 2g + 1, in chunk order, as
+// k_attention_wide's groups do -- and dims 4g .. 4g + 3 of the weighted sum, over all keys in
+// order; so the same bits. Score rows use a pitch of 2 mod 32 floats (a warp's 32 float2 accesses
+// take the minimum two wavefronts).
+constexpr int kNarrowWarps = 8;
+__host__ __device__ constexpr int narrow_er_pitch(int L) { return ((L + 31) & ~31) + 2; }
+__host__ __device__ constexpr size_t narrow_smem_bytes(int L) {
+  return size_t((L + 1) >> 1) * KPS * 8 * 2 + size_t(32) * narrow_er_pitch(L) * 4;
+}
+
+__global__ void __launch_bounds__(32 * kNarrowWarps) k_attention_narrow(AttnArgs a) {
+  pdl_trigger();
+  pdl_wait();
+  extern __shared__ float4 smem4[];
+  __shared__ float xmx[kNarrowWarps][32];
+  __shared__ float xsl[16][32];  // the 16 slot sums of every query
+  const int s = blockIdx.x;
+  const int h = blockIdx.y;
+  const int tile = blockIdx.z;
+  const int tid = threadIdx.x;
+  const int g = tid >> 5;
+  const int lane = tid & 31;
+  const int s0 = int(a.cu[s]);
+  const int L = int(a.cu[s + 1]) - s0;
+  if (a.skip_from > 0 && L >= a.skip_from) return;  // another kernel takes these sequences
+  if (L <= 0 || L > a.max_len) {
+    if (tid == 0 && tile == 0 && h == 0) record_err(a.err, DEV_ERR_BAD_SHAPE);
+    return;
+  }
+  if (tile * 32 >= L) return;
+  const int qi = tile * 32 + lane;
+  const bool active = qi < L;
+  float q[32];
+  load_query(a, s0 + (active ? qi : L - 1), h, q);  // in flight with the K / V staging
+  const int pairs = (L + 1) >> 1;
+  float2* kp = reinterpret_cast<float2*>(smem4);
+  float2* vp = kp + pairs * KPS;
+  float* er = reinterpret_cast<float*>(vp + pairs * KPS) + lane * narrow_er_pitch(L);
+  stage_kv_pairs(a, s0, L, h, kp, vp);
+  __syncthreads();
+  const int L4 = L & ~3, L8 = L & ~7, L16 = L & ~15;
+  const int ko = 2 * g;  // this warp's keys within a 16-key chunk
+
+  // pass 1: scores and their max
+  float mx = -INFINITY;
+  int t0 = 0;
+#pragma unroll 4
+  for (; t0 + 16 <= L4; t0 += 16) {  // both keys inside complete groups of 4
+    const float2 sp = score_pair(q, kp + ((t0 + ko) >> 1) * KPS, true);
+    mx = fmaxf(mx, fmaxf(sp.x, sp.y));
+    *reinterpret_cast<float2*>(er + t0 + ko) = sp;
+  }
+  for (; t0 < L; t0 += 16) {
+    const int t = t0 + ko;
+    if (t < L) {
+      const float2 sp = score_pair(q, kp + (t >> 1) * KPS, t < L4);
+      mx = fmaxf(mx, sp.x);
+      if (t + 1 < L) mx = fmaxf(mx, sp.y);
+      *reinterpret_cast<float2*>(er + t) = sp;
+    }
+  }
+  xmx[g][lane] = mx;
+  __syncthreads();
+#pragma unroll
+  for (int w = 0; w < kNarrowWarps; ++w) mx = fmaxf(mx, xmx[w][lane]);
+  const float2 neg_mx = f2(-mx, -mx);
+
+  // pass 2: exponentials; this warp's sum slots (and, for slots 0-7, the trailing 8-key chunk)
+  // accumulated in chunk order
+  float2 vs = f2(0.0f, 0.0f);
+#pragma unroll 4
+  for (t0 = 0; t0 + 16 <= L16; t0 += 16) {
+    float2* ep = reinterpret_cast<float2*>(er + t0 + ko);
+    const float2 e = cw_exp2(add2(*ep, neg_mx));
+    vs = add2(vs, e);
+    *ep = e;
+  }
+  for (; t0 < L; t0 += 16) {
+    const int t = t0 + ko;
+    if (t >= L) break;
+    float2* ep = reinterpret_cast<float2*>(er + t);
+    const float2 x = add2(*ep, neg_mx);
+    float2 e;
+    if (t0 + 16 <= L16) {
+      e = cw_exp2(x);
+      vs = add2(vs, e);
+    } else if (ko < 8 && t + 1 < L8) {  // the trailing 8-key chunk (keys L16 .. L16 + 7): slots 0-7
+      e = cw_exp2(x);
+      vs = add2(vs, e);
+    } else {  // the last L % 8 keys: scalar exp, summed after the tree
+      e = f2(scalar_expf(x.x), t + 1 < L ? scalar_expf(x.y) : 0.0f);
+    }
+    *ep = e;
+  }
+  xsl[ko][lane] = vs.x;
+  xsl[ko + 1][lane] = vs.y;
+  __syncthreads();
+  if (g == 0) {
+    float v8[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v8[j] = xsl[j][lane] + xsl[8 + j][lane];  // acc0 + acc1
+    float sum = tree8(v8);
+    for (int t = L8; t < L; ++t) sum = sum + er[t];  // the tail keys in order, after the tree
+    xmx[0][lane] = 1.0f / sum;
+  }
+  __syncthreads();
+  const float inv = xmx[0][lane];
+  const float2 inv2 = f2(inv, inv);
+
+  // pass 3: probabilities and the weighted sum of dims 4g .. 4g + 3; lane x = even keys
+  float2 acc[4];
+#pragma unroll
+  for (int d = 0; d < 4; ++d) acc[d] = f2(0.0f, 0.0f);
+  const int dg = 4 * g;
+  int t = 0;
+#pragma unroll 4
+  for (; t + 1 < L; t += 2) {
+    const float2 p = mul2(*reinterpret_cast<const float2*>(er + t), inv2);
+    const float4* v4 = reinterpret_cast<const float4*>(vp + (t >> 1) * KPS + dg);
+    const float4 va = v4[0], vb = v4[1];
+    acc[0] = fma2(f2(va.x, va.y), p, acc[0]);
+    acc[1] = fma2(f2(va.z, va.w), p, acc[1]);
+    acc[2] = fma2(f2(vb.x, vb.y), p, acc[2]);
+    acc[3] = fma2(f2(vb.z, vb.w), p, acc[3]);
+  }
+  if (t < L) {  // odd L: the last key goes to the even accumulator
+    const float pa = er[t] * inv;
+    const float2* v = vp + (t >> 1) * KPS + dg;
+#pragma unroll
+    for (int d = 0; d < 4; ++d) acc[d].x = fmaf(v[d].x, pa, acc[d].x);
+  }
+  if (active)
+    *reinterpret_cast<float4*>(a.out + size_t(s0 + qi) * kHidden + h * 32 + dg) =
+        make_float4(acc[0].x + acc[0].y, acc[1].x + acc[1].y, acc[2].x + acc[2].y, acc[3].x + acc[3].y);
+}
+
 __global__ void __launch_bounds__(128) k_attention_cls(AttnArgs a, int n_seqs) {
   pdl_trigger();
   pdl_wait();
@@ -1392,6 +1702,34 @@ static int launch_rows2(const AttnArgs& a, int n_seqs, cudaStream_t st) {
   return launch_pdl(k_attention_rows2, dim3(n_seqs, kHeads / 2), dim3(128), bytes, st, a) == cudaSuccess ? 0 : -3;
 }
 
+// k_attention_lat8: the query tiles of all (sequence, head) pairs fill the SMs about once; qt a
+// multiple of 4 (whole warps), capped by shared memory.
+static size_t g_static_lat8 = 0;
+static int launch_lat8(const AttnArgs& a, int n_seqs, cudaStream_t st) {
+  const int L = a.max_len;
+  const long pairs = long(n_seqs) * kHeads;
+  int tiles = int(148 / pairs);
+  if (tiles < 1) tiles = 1;
+  int qt = (L + tiles - 1) / tiles;
+  qt = qt > 64 ? 64 : (qt + 3) & ~3;  // at most 512 threads
+  const size_t cap = 227 * 1024 - g_static_lat8;
+  while (qt > 4 && lat8_smem_bytes(L, qt) > cap) qt -= 4;
+  tiles = (L + qt - 1) / qt;
+  return launch_pdl(k_attention_lat8, dim3(n_seqs, kHeads, tiles), dim3(8 * qt), lat8_smem_bytes(L, qt), st, a, qt) ==
+                 cudaSuccess
+             ? 0
+             : -3;
+}
+
+static size_t g_static_narrow = 0;
+static int launch_narrow(const AttnArgs& a, int n_seqs, cudaStream_t st) {
+  const dim3 grid(n_seqs, kHeads, (a.max_len + 31) / 32);
+  return launch_pdl(k_attention_narrow, grid, dim3(32 * kNarrowWarps), narrow_smem_bytes(a.max_len), st, a) ==
+                 cudaSuccess
+             ? 0
+             : -3;
+}
+
 static int smem_attr(const void* fn, size_t bytes) {
   return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes)) == cudaSuccess ? 0 : -1;
 }
@@ -1409,7 +1747,11 @@ int attention_prime() {
   r |= static_smem((const void*)k_attention_wide<ATTN_WIDE_256>, &g_static_wide2);
   r |= static_smem((const void*)k_attention_wide<4, 1>, &g_static_wide4);
   r |= static_smem((const void*)k_attention_rows2, &g_static_rows2);
+  r |= static_smem((const void*)k_attention_lat8, &g_static_lat8);
+  r |= static_smem((const void*)k_attention_narrow, &g_static_narrow);
   if (r) return r;
+  r |= smem_attr((const void*)k_attention_narrow, 227 * 1024 - g_static_narrow);
+  r |= smem_attr((const void*)k_attention_lat8, 227 * 1024 - g_static_lat8);
   r |= smem_attr((const void*)k_attention_rows2, rows_smem_cap(g_static_rows2));
   r |= smem_attr((const void*)k_attention_rows<128>, rows_smem_cap(g_static_rows));
   r |= smem_attr((const void*)k_attention_rows<64>, rows_smem_cap(g_static_rows));
@@ -1714,6 +2056,15 @@ int launch_attention_exact(const AttnArgs& a, int n_seqs, cudaStream_t st, int* 
     if (cudaLaunchKernelEx(&cfg, k_attention_lat<32, true>, a) != cudaSuccess) return -3;
     *quantized = 1;
     return 0;
+  }
+  // few pairs of longer sequences: eight lanes per query, the tiles sized to fill the SMs once
+  // few pairs of longer sequences: 32-query tiles with the scores in shared memory when those
+  // tiles fill the SMs in one wave, else eight lanes per query in tiles sized to fill them once
+  if (a.few_mode != 1 && heads * ((a.max_len + 127) / 128) <= 148) {
+    const size_t per_cta = narrow_smem_bytes(a.max_len) + g_static_narrow + 1024;
+    const long fit = long(227 * 1024 / per_cta);
+    const bool narrow = a.few_mode == 2 ? fit >= 1 : (a.few_mode == 0 && fit >= 1 && heads * ((a.max_len + 31) / 32) <= 148 * fit);
+    return narrow ? launch_narrow(a, n_seqs, st) : launch_lat8(a, n_seqs, st);
   }
   if (a.max_len > 128) return launch_rows<128>(a, n_seqs, st);
 #ifndef ATTN_PAIRS

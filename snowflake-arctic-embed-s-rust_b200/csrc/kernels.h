@@ -44,6 +44,8 @@ struct AttnArgs {
   int8_t* quant_q;            // [rows, 384]
   float* quant_scale;         // [rows]
   int skip_from;              // > 0: the exact kernels leave sequences of at least this many keys alone
+  int few_mode;               // few long sequences: 0 the faster kernel, 1 the TMEM kernels, 2 32-query
+                              // tiles, 3 eight lanes per query (all the same results; for tests)
 };
 
 // Launch with programmatic stream serialization (the kernel calls pdl_wait before it touches data

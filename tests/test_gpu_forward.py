@@ -282,3 +282,38 @@ def test_fused_qkv_attention_matches_split(pack_path, oracle_model, monkeypatch)
         assert cos >= COS_MIN and mx <= MAXABS_MAX, (L, cos, mx)
     for e in engines.values():
         e.close()
+
+
+def test_few_long_sequence_attention_matches_tmem_kernels(pack_path, oracle_model, monkeypatch):
+    """Few (sequence, head) pairs of more than 64 keys (single sequences of 65-512 tokens, small
+    batches) run the attention either on 32-query tiles with the scores in shared memory or with
+    eight lanes per query, whichever fills the SMs in one wave. Both keep every chain of the
+    reference's order in one thread, so every embedding is the same bits as with the TMEM kernels
+    (ARCTIC_ATTN_FEW=tmem; =narrow and =lanes8 force the other two at every length), and within
+    the tolerance of the oracle."""
+    engines = {}
+    for mode in ("tmem", "narrow", "lanes8", None):
+        if mode:
+            monkeypatch.setenv("ARCTIC_ATTN_FEW", mode)
+        else:
+            monkeypatch.delenv("ARCTIC_ATTN_FEW")
+        engines[mode] = Engine(0).load_file(pack_path)
+    tmem = engines.pop("tmem")
+    r = rng(88)
+    for L in (65, 66, 97, 100, 127, 128, 129, 130, 200, 255, 256, 257, 300, 383, 384, 385, 500, 511, 512):
+        ids = synth.token_ids(L, r)
+        ref = tmem.forward_cls(ids)
+        for mode, e in engines.items():
+            np.testing.assert_array_equal(e.forward_cls(ids), ref, err_msg=f"{mode} L={L}")
+    for lens in ([70, 128], [512, 129, 300], [100] * 12, [90, 3, 65, 128, 77]):
+        seqs = [synth.token_ids(L, r) for L in lens]
+        ref = tmem.forward_ragged(seqs)
+        for mode, e in engines.items():
+            np.testing.assert_array_equal(e.forward_ragged(seqs), ref, err_msg=f"{mode} {lens}")
+    for L in (65, 512):
+        ids = synth.token_ids(L, r)
+        cos, mx = close(engines[None].forward_cls(ids), oracle_model.forward_cls(ids))
+        assert cos >= COS_MIN and mx <= MAXABS_MAX, (L, cos, mx)
+    tmem.close()
+    for e in engines.values():
+        e.close()
