@@ -255,18 +255,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       // epilogue, the first 16 residual values of the row
       float as_pre = 0.0f;
       if constexpr (EPI != EPI_GELU_QUANT) as_pre = row < g.M ? g.a_scale[row] : 0.0f;
-      [[maybe_unused]] float rv0[16];
-      if constexpr (EPI == EPI_LN_QUANT) {
+      [[maybe_unused]] float rv0[16], rv1[16];
+      if constexpr (EPI == EPI_LN_QUANT) {  // residual chunks 0 and 1 (column blocks 0-7)
         if (row < g.M) {
           const float* rr = g.res_tt ? g.res + tt_index(row, 0, g.ldr) : g.res + size_t(row) * g.ldr;
           const size_t rs = g.res_tt ? 128 : 1;
 #pragma unroll
           for (int k = 0; k < 4; ++k)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) rv0[4 * k + e] = rr[size_t(16 * k + 4 * qq + e) * rs];
+            for (int e = 0; e < 4; ++e) {
+              rv0[4 * k + e] = rr[size_t(16 * k + 4 * qq + e) * rs];
+              rv1[4 * k + e] = rr[size_t(16 * (k + 4) + 4 * qq + e) * rs];
+            }
         } else {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) rv0[i] = 0.0f;
+          for (int i = 0; i < 16; ++i) rv0[i] = rv1[i] = 0.0f;
         }
       }
       if (ok) ok = mbar_wait(&acc_full[b], u & 1, g.err, DEV_ERR_TIMEOUT_EPILOGUE);
@@ -471,27 +474,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           rstep = g.res_tt ? 128 : 1;
         }
         if (ok) {
-          // residual chunks double-buffered: chunk i + 1 (16 values) is requested before chunk i is
-          // used; chunk 0 was requested before the accumulator wait
-          float rv1[16];
+          // residual chunks triple-buffered: chunk i + 2 (16 values) is requested before chunk i is
+          // used; chunks 0 and 1 were requested before the accumulator wait
+          float rv2[16];
 #pragma unroll
           for (int i = 0; i < 6; ++i) {
             const int k0 = 4 * i;
-            float* rv = (i & 1) ? rv1 : rv0;
-            float* nx = (i & 1) ? rv0 : rv1;
-            if (i + 1 < 6) {
+            float* rv = (i % 3 == 0) ? rv0 : (i % 3 == 1) ? rv1 : rv2;
+            float* nx = (i % 3 == 0) ? rv2 : (i % 3 == 1) ? rv0 : rv1;
+            if (i + 2 < 6) {
 #pragma unroll
               for (int k = 0; k < 4; ++k)
 #pragma unroll
                 for (int e = 0; e < 4; ++e)
-                  nx[4 * k + e] = valid ? res_row[size_t(16 * (k0 + 4 + k) + cq + e) * rstep] : 0.0f;
+                  nx[4 * k + e] = valid ? res_row[size_t(16 * (k0 + 8 + k) + cq + e) * rstep] : 0.0f;
             }
-#pragma unroll
-            for (int k = 0; k < 4; ++k) tmem_ld4(tb + 16 * (k0 + k) + cq, r + 4 * k);
-            tmem_ld_wait();
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
               const int c = 16 * (k0 + k) + cq;
+              tmem_ld4(tb + c, r + 4 * k);
+              tmem_ld_wait();
               if (valid && g.acc_dbg)
                 *reinterpret_cast<int4*>(g.acc_dbg + size_t(row) * g.N + c) =
                     make_int4(int(r[4 * k]), int(r[4 * k + 1]), int(r[4 * k + 2]), int(r[4 * k + 3]));
