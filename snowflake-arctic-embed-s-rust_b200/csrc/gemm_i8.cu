@@ -53,7 +53,7 @@ constexpr int BK = 128;            // K bytes per block (one 128-byte swizzle at
 constexpr int A_STAGE = BM * BK;   // 16 KB
 constexpr int kEpiWarps = 16;
 constexpr int kThreads = (2 + kEpiWarps) * 32;
-constexpr int kTmemBar = 8;  // named barrier of the MMA and epilogue warps (the epilogue uses 1..4)
+constexpr int kTmemBar = 15;  // named barrier of the MMA and epilogue warps (the epilogues use 1..8)
 constexpr int kResK = 384;         // K of the GEMMs whose weight slice stays resident
 constexpr int kResKB = kResK / BK;
 
@@ -136,7 +136,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bfull, 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], kEpiWarps);
+      // EPI_GELU_QUANT: the epilogue warps form two groups of 8 that take alternate tiles
+      mbar_init(&acc_empty[b], EPI == EPI_GELU_QUANT ? kEpiWarps / 2 : kEpiWarps);
       mbar_init(&rmx_bar[b], 1);
     }
     fence_mbar_init();
@@ -245,8 +246,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int qq = ew >> 2;        // column quarter (F32, GELU) / reduction-lane group (LN)
     const int rt = Q * 32 + lane;  // row within the tile
     const uint32_t tq = tmem + (uint32_t(Q * 32) << 16);
+    // EPI_GELU_QUANT: warps 0-7 of the epilogue take the even tiles (TMEM accumulator 0), warps
+    // 8-15 the odd ones (accumulator 1), two warps per lane quadrant each with half the columns, so
+    // that one group's row-maximum exchange and quantization overlap the other group's GELU
+    const int grp = EPI == EPI_GELU_QUANT ? ew >> 3 : 0;
+    const int it_step = EPI == EPI_GELU_QUANT ? 2 : 1;
     bool ok = true;
-    for (int it = 0; it < my_tiles; ++it) {
+    for (int it = grp; it < my_tiles; it += it_step) {
       const int b = it % NB, u = it / NB;
       const int m0 = (m_first + it * m_stride) * BM;
       const int row = m0 + rt;
@@ -361,14 +367,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       } else if constexpr (EPI == EPI_GELU_QUANT) {
+        static_assert(NB == 2, "the two epilogue groups alternate between the two accumulators");
         // 16 columns at a time: accumulators -> g = GELU(h) * inv_smooth -> back into the same TMEM
         // columns (few registers live, no spills); the accumulator buffer is released after the
         // quantization pass has read g back
-        constexpr int CW = BN / 4;  // 64
-        const int c0 = qq * CW;
-        const int par = it & 1;
+        constexpr int CW = BN / 2;      // columns of this warp: half of the slice
+        const int gq = (ew >> 2) & 1;   // which half
+        const int c0 = gq * CW;
+        const int par = it & 1;         // == grp
         const uint32_t rank = cluster_ctarank();
-        float* xg = xch + par * 4 * BM;                           // [4][BM] maxima of the column quarters
+        // [2][BM] maxima of the column halves, alternating between two slots of the group's [4][BM],
+        // so that no warp can write a slot its partner may still read
+        float* xg = xch + par * 4 * BM + ((it >> 1) & 1) * 2 * BM;
         float* rmx = xch + 2 * 4 * BM + par * Ly::GCL * BM;  // [GCL][BM] maxima of the cluster CTAs
         uint32_t r[16];
         float vmax = 1e-8f;
@@ -411,11 +421,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tmem_st_wait();
         }
-        xg[qq * BM + rt] = vmax;
-        named_bar(1 + Q, 128);
-        const float cta_max = fmaxf(fmaxf(xg[rt], xg[BM + rt]), fmaxf(xg[2 * BM + rt], xg[3 * BM + rt]));
-        if (ew == 0 && lane == 0) mbar_arrive_expect_tx(&rmx_bar[par], Ly::GCL * BM * 4);
-        if (qq == 0) {
+        xg[gq * BM + rt] = vmax;
+        named_bar(1 + Q + 4 * grp, 64);  // the group's two warps of this lane quadrant
+        const float cta_max = fmaxf(xg[rt], xg[BM + rt]);
+        if ((ew & 7) == 0 && lane == 0) mbar_arrive_expect_tx(&rmx_bar[par], Ly::GCL * BM * 4);
+        if (gq == 0) {
 #pragma unroll
           for (uint32_t q = 0; q < uint32_t(Ly::GCL); ++q)
             st_async_f32(map_peer(&rmx[rank * BM + rt], q), cta_max, map_peer(&rmx_bar[par], q));
@@ -426,37 +436,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int q = 1; q < Ly::GCL; ++q) max_abs = fmaxf(max_abs, rmx[q * BM + rt]);
         const float inv_scale = 127.0f / max_abs;
         {
-          // quantize into this warp's staging slot (32 rows x CW bytes, rows padded to 80 bytes),
-          // then write 32 / (CW / 16) rows x CW contiguous bytes per store instruction
+          // quantize 64 columns at a time into this warp's staging slot (32 rows x 64 bytes, rows
+          // padded to 80 bytes), then write 8 rows x 64 contiguous bytes per store instruction
           uint8_t* stg = reinterpret_cast<uint8_t*>(xch + Ly::XCH_FLOATS_GELU) + ew * (32 * 80);
-          if (ok) {
 #pragma unroll 1
-            for (int ch = 0; ch < CW / 16; ++ch) {
-              tmem_ld16(tb + c0 + 16 * ch, r);
-              tmem_ld_wait();
-              uint32_t pk[4];
+          for (int hc = 0; hc < CW / 64; ++hc) {
+            const int cb = c0 + 64 * hc;
+            if (ok) {
+#pragma unroll 1
+              for (int ch = 0; ch < 4; ++ch) {
+                tmem_ld16(tb + cb + 16 * ch, r);
+                tmem_ld_wait();
+                uint32_t pk[4];
 #pragma unroll
-              for (int q = 0; q < 4; ++q)
-                pk[q] = pack_i8x4(quant_bits_scaled(__uint_as_float(r[4 * q]) * inv_scale),
-                                  quant_bits_scaled(__uint_as_float(r[4 * q + 1]) * inv_scale),
-                                  quant_bits_scaled(__uint_as_float(r[4 * q + 2]) * inv_scale),
-                                  quant_bits_scaled(__uint_as_float(r[4 * q + 3]) * inv_scale));
-              *reinterpret_cast<uint4*>(stg + lane * 80 + 16 * ch) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                for (int q = 0; q < 4; ++q)
+                  pk[q] = pack_i8x4(quant_bits_scaled(__uint_as_float(r[4 * q]) * inv_scale),
+                                    quant_bits_scaled(__uint_as_float(r[4 * q + 1]) * inv_scale),
+                                    quant_bits_scaled(__uint_as_float(r[4 * q + 2]) * inv_scale),
+                                    quant_bits_scaled(__uint_as_float(r[4 * q + 3]) * inv_scale));
+                *reinterpret_cast<uint4*>(stg + lane * 80 + 16 * ch) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+              }
             }
-          }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_empty[b]);
-          constexpr int PPR = CW / 16, RPI = 32 / PPR;  // 16-byte pieces per row, rows per instruction
+            if (hc + 1 == CW / 64) {  // the last read of this accumulator
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&acc_empty[b]);
+            }
+            __syncwarp();
 #pragma unroll
-          for (int i = 0; i < 32 / RPI; ++i) {
-            const int rr = RPI * i + lane / PPR, q = lane % PPR;
-            const int grow = m0 + Q * 32 + rr;
-            const uint4 v = *reinterpret_cast<const uint4*>(stg + rr * 80 + 16 * q);
-            if (ok && grow < g.M) *reinterpret_cast<uint4*>(g.out_q + size_t(grow) * g.N + n0 + c0 + 16 * q) = v;
+            for (int i = 0; i < 4; ++i) {
+              const int rr = 8 * i + lane / 4, q = lane % 4;
+              const int grow = m0 + Q * 32 + rr;
+              const uint4 v = *reinterpret_cast<const uint4*>(stg + rr * 80 + 16 * q);
+              if (ok && grow < g.M) *reinterpret_cast<uint4*>(g.out_q + size_t(grow) * g.N + n0 + cb + 16 * q) = v;
+            }
+            __syncwarp();
           }
-          __syncwarp();
-          if (valid && rank == 0 && qq == 0) g.out_scale[row] = max_abs / 127.0f;
+          if (valid && rank == 0 && gq == 0) g.out_scale[row] = max_abs / 127.0f;
         }
       } else if constexpr (EPI == EPI_LN_QUANT) {
         static_assert(BN == kHidden, "row-LayerNorm epilogue needs the full 384-wide row");
