@@ -270,8 +270,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < 4; ++k)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              rv0[4 * k + e] = rr[size_t(16 * k + 4 * qq + e) * rs];
-              rv1[4 * k + e] = rr[size_t(16 * (k + 4) + 4 * qq + e) * rs];
+              rv0[4 * k + e] = __ldcs(rr + size_t(16 * k + 4 * qq + e) * rs);
+              rv1[4 * k + e] = __ldcs(rr + size_t(16 * (k + 4) + 4 * qq + e) * rs);
             }
         } else {
 #pragma unroll
@@ -503,7 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int k = 0; k < 4; ++k)
 #pragma unroll
                 for (int e = 0; e < 4; ++e)
-                  nx[4 * k + e] = valid ? res_row[size_t(16 * (k0 + 8 + k) + cq + e) * rstep] : 0.0f;
+                  nx[4 * k + e] = valid ? __ldcs(res_row + size_t(16 * (k0 + 8 + k) + cq + e) * rstep) : 0.0f;
             }
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
