@@ -1417,22 +1417,27 @@ __host__ __device__ constexpr size_t cls_smem_floats(int max_len) { return 32 + 
 // Few (sequence, head) pairs of long sequences: k_attention_wide's passes on tiles of 32 queries
 // (thread = query, so every K / V load is a warp-wide broadcast), with the scores, then
 // exponentials, in shared memory instead of TMEM: a 512-token sequence gives 12 x 16 CTAs
-// instead of 48. Warp g of the 8 takes keys t0 + 2g, t0 + 2g + 1 of every 16-key chunk in the
-// scores pass and in the exponentials pass -- the sum slots 2g, 2g + 1, in chunk order, as
-// k_attention_wide's groups do -- and dims 4g .. 4g + 3 of the weighted sum, over all keys in
-// order; so the same bits. Score rows use a pitch of 2 mod 32 floats (a warp's 32 float2 accesses
-// take the minimum two wavefronts).
-constexpr int kNarrowWarps = 8;
+// instead of 48. NW = 8 warps: warp g takes the key pair t0 + 2g, t0 + 2g + 1 of every 16-key
+// chunk in the scores pass and in the exponentials pass -- the sum slots 2g, 2g + 1, in chunk
+// order, as k_attention_wide's groups do -- and dims 4g .. 4g + 3 of the weighted sum, over all
+// keys in order. NW = 16 (twice the warps to hide shared-memory latency): warps g and g + 8 take
+// key pair g of alternate chunks for the scores, warp g alone sum slot g (key t0 + g of every
+// chunk) for the exponentials, and dims 2g, 2g + 1 of the weighted sum. Either way every chain the
+// reference keeps runs in one thread in its order, so the same bits. Score rows use a pitch of
+// 2 mod 32 floats (a warp's 32 float2 accesses take the minimum two wavefronts).
 __host__ __device__ constexpr int narrow_er_pitch(int L) { return ((L + 31) & ~31) + 2; }
 __host__ __device__ constexpr size_t narrow_smem_bytes(int L) {
   return size_t((L + 1) >> 1) * KPS * 8 * 2 + size_t(32) * narrow_er_pitch(L) * 4;
 }
 
-__global__ void __launch_bounds__(32 * kNarrowWarps) k_attention_narrow(AttnArgs a) {
+template <int NW>
+__global__ void __launch_bounds__(32 * NW) k_attention_narrow(AttnArgs a) {
+  static_assert(NW == 8 || NW == 16, "8 or 16 warps");
+  constexpr int DPG = 32 / NW;  // dims of the weighted sum per warp
   pdl_trigger();
   pdl_wait();
   extern __shared__ float4 smem4[];
-  __shared__ float xmx[kNarrowWarps][32];
+  __shared__ float xmx[NW][32];
   __shared__ float xsl[16][32];  // the 16 slot sums of every query
   const int s = blockIdx.x;
   const int h = blockIdx.y;
@@ -1459,18 +1464,19 @@ __global__ void __launch_bounds__(32 * kNarrowWarps) k_attention_narrow(AttnArgs
   stage_kv_pairs(a, s0, L, h, kp, vp);
   __syncthreads();
   const int L4 = L & ~3, L8 = L & ~7, L16 = L & ~15;
-  const int ko = 2 * g;  // this warp's keys within a 16-key chunk
 
-  // pass 1: scores and their max
+  // pass 1: scores and their max (key pair ko of the chunks this warp takes)
+  const int ko = 2 * (g & 7);
+  const int c_first = 16 * (g >> 3), c_step = 16 * (NW / 8);
   float mx = -INFINITY;
-  int t0 = 0;
+  int t0 = c_first;
 #pragma unroll 4
-  for (; t0 + 16 <= L4; t0 += 16) {  // both keys inside complete groups of 4
+  for (; t0 + 16 <= L4; t0 += c_step) {  // both keys inside complete groups of 4
     const float2 sp = score_pair(q, kp + ((t0 + ko) >> 1) * KPS, true);
     mx = fmaxf(mx, fmaxf(sp.x, sp.y));
     *reinterpret_cast<float2*>(er + t0 + ko) = sp;
   }
-  for (; t0 < L; t0 += 16) {
+  for (; t0 < L; t0 += c_step) {
     const int t = t0 + ko;
     if (t < L) {
       const float2 sp = score_pair(q, kp + (t >> 1) * KPS, t < L4);
@@ -1482,38 +1488,57 @@ __global__ void __launch_bounds__(32 * kNarrowWarps) k_attention_narrow(AttnArgs
   xmx[g][lane] = mx;
   __syncthreads();
 #pragma unroll
-  for (int w = 0; w < kNarrowWarps; ++w) mx = fmaxf(mx, xmx[w][lane]);
-  const float2 neg_mx = f2(-mx, -mx);
+  for (int w = 0; w < NW; ++w) mx = fmaxf(mx, xmx[w][lane]);
 
   // pass 2: exponentials; this warp's sum slots (and, for slots 0-7, the trailing 8-key chunk)
-  // accumulated in chunk order
-  float2 vs = f2(0.0f, 0.0f);
+  // accumulated in chunk order; the last L % 8 keys by scalar exp, summed after the tree
+  if constexpr (NW == 8) {
+    const float2 neg_mx = f2(-mx, -mx);
+    float2 vs = f2(0.0f, 0.0f);
 #pragma unroll 4
-  for (t0 = 0; t0 + 16 <= L16; t0 += 16) {
-    float2* ep = reinterpret_cast<float2*>(er + t0 + ko);
-    const float2 e = cw_exp2(add2(*ep, neg_mx));
-    vs = add2(vs, e);
-    *ep = e;
-  }
-  for (; t0 < L; t0 += 16) {
-    const int t = t0 + ko;
-    if (t >= L) break;
-    float2* ep = reinterpret_cast<float2*>(er + t);
-    const float2 x = add2(*ep, neg_mx);
-    float2 e;
-    if (t0 + 16 <= L16) {
-      e = cw_exp2(x);
+    for (t0 = 0; t0 + 16 <= L16; t0 += 16) {
+      float2* ep = reinterpret_cast<float2*>(er + t0 + ko);
+      const float2 e = cw_exp2(add2(*ep, neg_mx));
       vs = add2(vs, e);
-    } else if (ko < 8 && t + 1 < L8) {  // the trailing 8-key chunk (keys L16 .. L16 + 7): slots 0-7
-      e = cw_exp2(x);
-      vs = add2(vs, e);
-    } else {  // the last L % 8 keys: scalar exp, summed after the tree
-      e = f2(scalar_expf(x.x), t + 1 < L ? scalar_expf(x.y) : 0.0f);
+      *ep = e;
     }
-    *ep = e;
+    const int t = t0 + ko;  // t0 == L16: the partial chunk
+    if (t < L) {
+      float2* ep = reinterpret_cast<float2*>(er + t);
+      const float2 x = add2(*ep, neg_mx);
+      float2 e;
+      if (ko < 8 && t + 1 < L8) {  // the trailing 8-key chunk (keys L16 .. L16 + 7): slots 0-7
+        e = cw_exp2(x);
+        vs = add2(vs, e);
+      } else {
+        e = f2(scalar_expf(x.x), t + 1 < L ? scalar_expf(x.y) : 0.0f);
+      }
+      *ep = e;
+    }
+    xsl[ko][lane] = vs.x;
+    xsl[ko + 1][lane] = vs.y;
+  } else {
+    float vs = 0.0f;
+#pragma unroll 4
+    for (t0 = 0; t0 + 16 <= L16; t0 += 16) {
+      const float e = cw_exp(er[t0 + g] - mx);
+      vs = vs + e;
+      er[t0 + g] = e;
+    }
+    const int t = t0 + g;  // t0 == L16: the partial chunk
+    if (t < L) {
+      const float x = er[t] - mx;
+      float e;
+      if (g < 8 && t < L8) {  // the trailing 8-key chunk: slots 0-7
+        e = cw_exp(x);
+        vs = vs + e;
+      } else {
+        e = scalar_expf(x);
+      }
+      er[t] = e;
+    }
+    xsl[g][lane] = vs;
   }
-  xsl[ko][lane] = vs.x;
-  xsl[ko + 1][lane] = vs.y;
   __syncthreads();
   if (g == 0) {
     float v8[8];
@@ -1527,31 +1552,37 @@ __global__ void __launch_bounds__(32 * kNarrowWarps) k_attention_narrow(AttnArgs
   const float inv = xmx[0][lane];
   const float2 inv2 = f2(inv, inv);
 
-  // pass 3: probabilities and the weighted sum of dims 4g .. 4g + 3; lane x = even keys
-  float2 acc[4];
+  // pass 3: probabilities and the weighted sum of this warp's dims; lane x = even keys
+  float2 acc[DPG];
 #pragma unroll
-  for (int d = 0; d < 4; ++d) acc[d] = f2(0.0f, 0.0f);
-  const int dg = 4 * g;
+  for (int d = 0; d < DPG; ++d) acc[d] = f2(0.0f, 0.0f);
+  const int dg = DPG * g;
   int t = 0;
 #pragma unroll 4
   for (; t + 1 < L; t += 2) {
     const float2 p = mul2(*reinterpret_cast<const float2*>(er + t), inv2);
     const float4* v4 = reinterpret_cast<const float4*>(vp + (t >> 1) * KPS + dg);
-    const float4 va = v4[0], vb = v4[1];
-    acc[0] = fma2(f2(va.x, va.y), p, acc[0]);
-    acc[1] = fma2(f2(va.z, va.w), p, acc[1]);
-    acc[2] = fma2(f2(vb.x, vb.y), p, acc[2]);
-    acc[3] = fma2(f2(vb.z, vb.w), p, acc[3]);
+#pragma unroll
+    for (int i = 0; i < DPG / 2; ++i) {
+      const float4 va = v4[i];
+      acc[2 * i] = fma2(f2(va.x, va.y), p, acc[2 * i]);
+      acc[2 * i + 1] = fma2(f2(va.z, va.w), p, acc[2 * i + 1]);
+    }
   }
   if (t < L) {  // odd L: the last key goes to the even accumulator
     const float pa = er[t] * inv;
     const float2* v = vp + (t >> 1) * KPS + dg;
 #pragma unroll
-    for (int d = 0; d < 4; ++d) acc[d].x = fmaf(v[d].x, pa, acc[d].x);
+    for (int d = 0; d < DPG; ++d) acc[d].x = fmaf(v[d].x, pa, acc[d].x);
   }
-  if (active)
-    *reinterpret_cast<float4*>(a.out + size_t(s0 + qi) * kHidden + h * 32 + dg) =
-        make_float4(acc[0].x + acc[0].y, acc[1].x + acc[1].y, acc[2].x + acc[2].y, acc[3].x + acc[3].y);
+  if (active) {
+    float* o = a.out + size_t(s0 + qi) * kHidden + h * 32 + dg;
+    if constexpr (DPG == 4)
+      *reinterpret_cast<float4*>(o) =
+          make_float4(acc[0].x + acc[0].y, acc[1].x + acc[1].y, acc[2].x + acc[2].y, acc[3].x + acc[3].y);
+    else
+      *reinterpret_cast<float2*>(o) = make_float2(acc[0].x + acc[0].y, acc[1].x + acc[1].y);
+  }
 }
 
 __global__ void __launch_bounds__(128) k_attention_cls(AttnArgs a, int n_seqs) {
@@ -1722,9 +1753,13 @@ static int launch_lat8(const AttnArgs& a, int n_seqs, cudaStream_t st) {
 }
 
 static size_t g_static_narrow = 0;
+#ifndef ATTN_NARROW_WARPS
+#define ATTN_NARROW_WARPS 16
+#endif
+constexpr int kNarrowWarps = ATTN_NARROW_WARPS;
 static int launch_narrow(const AttnArgs& a, int n_seqs, cudaStream_t st) {
   const dim3 grid(n_seqs, kHeads, (a.max_len + 31) / 32);
-  return launch_pdl(k_attention_narrow, grid, dim3(32 * kNarrowWarps), narrow_smem_bytes(a.max_len), st, a) ==
+  return launch_pdl(k_attention_narrow<kNarrowWarps>, grid, dim3(32 * kNarrowWarps), narrow_smem_bytes(a.max_len), st, a) ==
                  cudaSuccess
              ? 0
              : -3;
@@ -1748,9 +1783,9 @@ int attention_prime() {
   r |= static_smem((const void*)k_attention_wide<4, 1>, &g_static_wide4);
   r |= static_smem((const void*)k_attention_rows2, &g_static_rows2);
   r |= static_smem((const void*)k_attention_lat8, &g_static_lat8);
-  r |= static_smem((const void*)k_attention_narrow, &g_static_narrow);
+  r |= static_smem((const void*)k_attention_narrow<kNarrowWarps>, &g_static_narrow);
   if (r) return r;
-  r |= smem_attr((const void*)k_attention_narrow, 227 * 1024 - g_static_narrow);
+  r |= smem_attr((const void*)k_attention_narrow<kNarrowWarps>, 227 * 1024 - g_static_narrow);
   r |= smem_attr((const void*)k_attention_lat8, 227 * 1024 - g_static_lat8);
   r |= smem_attr((const void*)k_attention_rows2, rows_smem_cap(g_static_rows2));
   r |= smem_attr((const void*)k_attention_rows<128>, rows_smem_cap(g_static_rows));
