@@ -1585,6 +1585,210 @@ __global__ void __launch_bounds__(32 * NW) k_attention_narrow(AttnArgs a) {
   }
 }
 
+// k_attention_narrow for one sequence that starts a 128-row tile of the tile-transposed Q | K | V
+// (the latency path's single sequence): K and V are staged dim-major, exactly as they lie in the
+// tile-transposed layout -- dims 32h .. 32h + 31 of a 128-row tile are 16 KB in a row -- by two
+// bulk copies per tile (no multicast) instead of the key-pair layout's per-thread copies, whose issue
+// dominated the kernel at 257-512 keys. A 16-byte load is one dim of four keys (score_quad), so the
+// scores pass takes quads: warp g the quad g % 4 of the chunks it owns; the exponentials and the
+// weighted sum keep k_attention_narrow's chain ownership, so the same bits.
+__host__ __device__ constexpr int narrow_dm_er_pitch(int L) { return ((L + 31) & ~31) + 4; }
+__host__ __device__ constexpr size_t narrow_dm_smem_bytes(int L) {
+  return size_t((L + 127) >> 7) * 2 * 32 * 128 * 4 + size_t(32) * narrow_dm_er_pitch(L) * 4;
+}
+__device__ __forceinline__ int dm_index(int d, int t) { return ((t >> 7) << 12) + (d << 7) + (t & 127); }
+
+template <int NW>
+__global__ void __launch_bounds__(32 * NW) k_attention_narrow_dm(AttnArgs a) {
+  static_assert(NW == 8 || NW == 16, "8 or 16 warps");
+  constexpr int DPG = 32 / NW;
+  pdl_trigger();
+  pdl_wait();
+  extern __shared__ float4 smem4[];
+  __shared__ float xmx[NW][32];
+  __shared__ float xsl[16][32];
+  __shared__ uint64_t kv_bar;
+  const int h = blockIdx.y;
+  const int tile = blockIdx.z;
+  const int tid = threadIdx.x;
+  const int g = tid >> 5;
+  const int lane = tid & 31;
+  const int s0 = int(a.cu[blockIdx.x]);
+  const int L = int(a.cu[blockIdx.x + 1]) - s0;
+  if (a.skip_from > 0 && L >= a.skip_from) return;
+  if (L <= 0 || L > a.max_len) {
+    if (tid == 0 && tile == 0 && h == 0) record_err(a.err, DEV_ERR_BAD_SHAPE);
+    return;
+  }
+  if (tile * 32 >= L) return;
+  const bool bulk = a.kv_tt && !(s0 & 127);
+  const int ntile = (L + 127) >> 7;
+  float* kd = reinterpret_cast<float*>(smem4);  // [ntile][32][128]
+  float* vd = kd + ntile * 4096;
+  const int Pe = narrow_dm_er_pitch(L);
+  float* er = vd + ntile * 4096 + lane * Pe;
+  if (bulk && tid == 0) {
+    mbar_init(&kv_bar, 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(&kv_bar, uint32_t(ntile) * 2 * 16384);
+    for (int j = 0; j < ntile; ++j) {
+      const float* blk = a.kv + size_t((s0 >> 7) + j) * a.kv_C * 128;
+      bulk_load(kd + j * 4096, blk + size_t(a.k_col + 32 * h) * 128, 16384, &kv_bar);
+      bulk_load(vd + j * 4096, blk + size_t(a.v_col + 32 * h) * 128, 16384, &kv_bar);
+    }
+  }
+  const int qi = tile * 32 + lane;
+  const bool active = qi < L;
+  float q[1][32];
+  load_query(a, s0 + (active ? qi : L - 1), h, q[0]);
+  if (!bulk) {  // a sequence inside a tile: 4-byte asynchronous copies of its rows, all in flight
+    const int nwarps = blockDim.x >> 5;
+    for (int c = g; c < 64; c += nwarps) {
+      const int d = c & 31;
+      const int col = (c < 32 ? a.k_col : a.v_col) + 32 * h + d;
+      float* dst = c < 32 ? kd : vd;
+      for (int t = lane; t < L; t += 32)
+        cp_async4(dst + dm_index(d, t),
+                  a.kv_tt ? a.kv + tt_index(s0 + t, col, a.kv_C) : a.kv + size_t(s0 + t) * a.kv_C + col, 4u);
+    }
+    cp_async_wait_all();
+  }
+  __syncthreads();  // kv_bar initialised; per-thread copies complete
+  const bool ok = !bulk || __syncthreads_and(mbar_wait(&kv_bar, 0, a.err, DEV_ERR_TIMEOUT_PRODUCER));
+  if (!ok) {
+    // the copies' bytes have not all landed: wait once more (bounded) before the CTA's shared
+    // memory is released; nothing of this tile is written
+    mbar_wait(&kv_bar, 0, a.err, DEV_ERR_TIMEOUT_PRODUCER);
+    return;
+  }
+  const int L4 = L & ~3, L8 = L & ~7, L16 = L & ~15;
+
+  // pass 1: scores (quad g % 4 of the chunks this warp owns) and their max
+  const int qo = 4 * (g & 3);
+  const int c_first = 16 * (g >> 2), c_step = 16 * (NW / 4);
+  float mx = -INFINITY;
+  for (int t0 = c_first; t0 < L; t0 += c_step) {
+    const int t = t0 + qo;
+    if (t >= L) continue;
+    float2 sp[1][2];
+    score_quad<1>(q, kd + dm_index(0, t), 128, t < L4, sp);
+    float4 v = make_float4(sp[0][0].x, sp[0][0].y, sp[0][1].x, sp[0][1].y);
+    if (t + 4 <= L) {
+      mx = fmaxf(mx, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+    } else {  // keys past the sequence: 0, outside the max
+      mx = fmaxf(mx, v.x);
+      if (t + 1 < L) mx = fmaxf(mx, v.y); else v.y = 0.0f;
+      if (t + 2 < L) mx = fmaxf(mx, v.z); else v.z = 0.0f;
+      v.w = 0.0f;
+    }
+    *reinterpret_cast<float4*>(er + t) = v;
+  }
+  xmx[g][lane] = mx;
+  __syncthreads();
+#pragma unroll
+  for (int w = 0; w < NW; ++w) mx = fmaxf(mx, xmx[w][lane]);
+
+  // pass 2: as k_attention_narrow
+  int t0;
+  if constexpr (NW == 8) {
+    const int ko = 2 * g;
+    const float2 neg_mx = f2(-mx, -mx);
+    float2 vs = f2(0.0f, 0.0f);
+#pragma unroll 4
+    for (t0 = 0; t0 + 16 <= L16; t0 += 16) {
+      float2* ep = reinterpret_cast<float2*>(er + t0 + ko);
+      const float2 e = cw_exp2(add2(*ep, neg_mx));
+      vs = add2(vs, e);
+      *ep = e;
+    }
+    const int t = t0 + ko;
+    if (t < L) {
+      float2* ep = reinterpret_cast<float2*>(er + t);
+      const float2 x = add2(*ep, neg_mx);
+      float2 e;
+      if (ko < 8 && t + 1 < L8) {
+        e = cw_exp2(x);
+        vs = add2(vs, e);
+      } else {
+        e = f2(scalar_expf(x.x), t + 1 < L ? scalar_expf(x.y) : 0.0f);
+      }
+      *ep = e;
+    }
+    xsl[ko][lane] = vs.x;
+    xsl[ko + 1][lane] = vs.y;
+  } else {
+    float vs = 0.0f;
+#pragma unroll 4
+    for (t0 = 0; t0 + 16 <= L16; t0 += 16) {
+      const float e = cw_exp(er[t0 + g] - mx);
+      vs = vs + e;
+      er[t0 + g] = e;
+    }
+    const int t = t0 + g;
+    if (t < L) {
+      const float x = er[t] - mx;
+      float e;
+      if (g < 8 && t < L8) {
+        e = cw_exp(x);
+        vs = vs + e;
+      } else {
+        e = scalar_expf(x);
+      }
+      er[t] = e;
+    }
+    xsl[g][lane] = vs;
+  }
+  __syncthreads();
+  if (g == 0) {
+    float v8[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v8[j] = xsl[j][lane] + xsl[8 + j][lane];
+    float sum = tree8(v8);
+    for (int t = L8; t < L; ++t) sum = sum + er[t];
+    xmx[0][lane] = 1.0f / sum;
+  }
+  __syncthreads();
+  const float inv = xmx[0][lane];
+  const float2 inv2 = f2(inv, inv);
+
+  // pass 3: the weighted sum of dims DPG g .. DPG g + DPG - 1, four keys per 16-byte load
+  float2 acc[DPG];
+#pragma unroll
+  for (int d = 0; d < DPG; ++d) acc[d] = f2(0.0f, 0.0f);
+  const int dg = DPG * g;
+  int t = 0;
+#pragma unroll 2
+  for (; t + 4 <= L; t += 4) {
+    const float4 e4 = *reinterpret_cast<const float4*>(er + t);
+    const float2 p01 = mul2(f2(e4.x, e4.y), inv2), p23 = mul2(f2(e4.z, e4.w), inv2);
+#pragma unroll
+    for (int d = 0; d < DPG; ++d) {
+      const float4 vv = *reinterpret_cast<const float4*>(vd + dm_index(dg + d, t));
+      acc[d] = fma2(f2(vv.x, vv.y), p01, acc[d]);
+      acc[d] = fma2(f2(vv.z, vv.w), p23, acc[d]);
+    }
+  }
+  for (; t + 1 < L; t += 2) {
+    const float2 p = mul2(f2(er[t], er[t + 1]), inv2);
+#pragma unroll
+    for (int d = 0; d < DPG; ++d)
+      acc[d] = fma2(f2(vd[dm_index(dg + d, t)], vd[dm_index(dg + d, t + 1)]), p, acc[d]);
+  }
+  if (t < L) {  // odd L: the last key goes to the even accumulator
+    const float pa = er[t] * inv;
+#pragma unroll
+    for (int d = 0; d < DPG; ++d) acc[d].x = fmaf(vd[dm_index(dg + d, t)], pa, acc[d].x);
+  }
+  if (active) {
+    float* o = a.out + size_t(s0 + qi) * kHidden + h * 32 + dg;
+    if constexpr (DPG == 4)
+      *reinterpret_cast<float4*>(o) =
+          make_float4(acc[0].x + acc[0].y, acc[1].x + acc[1].y, acc[2].x + acc[2].y, acc[3].x + acc[3].y);
+    else
+      *reinterpret_cast<float2*>(o) = make_float2(acc[0].x + acc[0].y, acc[1].x + acc[1].y);
+  }
+}
+
 __global__ void __launch_bounds__(128) k_attention_cls(AttnArgs a, int n_seqs) {
   pdl_trigger();
   pdl_wait();
@@ -1765,6 +1969,15 @@ static int launch_narrow(const AttnArgs& a, int n_seqs, cudaStream_t st) {
              : -3;
 }
 
+static size_t g_static_narrow_dm = 0;
+static int launch_narrow_dm(const AttnArgs& a, int n_seqs, cudaStream_t st) {
+  const dim3 grid(n_seqs, kHeads, (a.max_len + 31) / 32);
+  return launch_pdl(k_attention_narrow_dm<kNarrowWarps>, grid, dim3(32 * kNarrowWarps), narrow_dm_smem_bytes(a.max_len),
+                    st, a) == cudaSuccess
+             ? 0
+             : -3;
+}
+
 static int smem_attr(const void* fn, size_t bytes) {
   return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes)) == cudaSuccess ? 0 : -1;
 }
@@ -1784,8 +1997,10 @@ int attention_prime() {
   r |= static_smem((const void*)k_attention_rows2, &g_static_rows2);
   r |= static_smem((const void*)k_attention_lat8, &g_static_lat8);
   r |= static_smem((const void*)k_attention_narrow<kNarrowWarps>, &g_static_narrow);
+  r |= static_smem((const void*)k_attention_narrow_dm<kNarrowWarps>, &g_static_narrow_dm);
   if (r) return r;
   r |= smem_attr((const void*)k_attention_narrow<kNarrowWarps>, 227 * 1024 - g_static_narrow);
+  r |= smem_attr((const void*)k_attention_narrow_dm<kNarrowWarps>, 227 * 1024 - g_static_narrow_dm);
   r |= smem_attr((const void*)k_attention_lat8, 227 * 1024 - g_static_lat8);
   r |= smem_attr((const void*)k_attention_rows2, rows_smem_cap(g_static_rows2));
   r |= smem_attr((const void*)k_attention_rows<128>, rows_smem_cap(g_static_rows));
@@ -2098,6 +2313,9 @@ int launch_attention_exact(const AttnArgs& a, int n_seqs, cudaStream_t st, int* 
   if (a.few_mode != 1 && heads * ((a.max_len + 127) / 128) <= 148) {
     const size_t per_cta = narrow_smem_bytes(a.max_len) + g_static_narrow + 1024;
     const long fit = long(227 * 1024 / per_cta);
+    const bool dm_fits = narrow_dm_smem_bytes(a.max_len) + g_static_narrow_dm + 1024 <= 227 * 1024;
+    const bool one_wave = heads * ((a.max_len + 31) / 32) <= 148;
+    if (a.few_mode == 4 || (a.few_mode == 0 && n_seqs == 1 && dm_fits && one_wave)) return launch_narrow_dm(a, n_seqs, st);
     const bool narrow = a.few_mode == 2 ? fit >= 1 : (a.few_mode == 0 && fit >= 1 && heads * ((a.max_len + 31) / 32) <= 148 * fit);
     return narrow ? launch_narrow(a, n_seqs, st) : launch_lat8(a, n_seqs, st);
   }

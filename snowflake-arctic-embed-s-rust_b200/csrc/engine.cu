@@ -125,7 +125,7 @@ struct ae_ctx {
   int gelu_erf = 0;       // ARCTIC_GELU=erf selects the exact-erf GELU (outside the parity tolerance)
   int fused_qkv = 0;      // ARCTIC_FUSED_QKV=1: QKV projection fused into the attention (sequences <= 128 keys)
   int attn_mode = AE_ATTENTION_EXACT;  // ae_set_attention_mode, ARCTIC_ATTN=int8
-  int few_mode = 0;         // ARCTIC_ATTN_FEW=tmem|narrow|lanes8: the attention kernel of few long sequences
+  int few_mode = 0;         // ARCTIC_ATTN_FEW=tmem|narrow|lanes8|dm: the attention kernel of few long sequences
   bool lat_cluster = false;  // single sequences of <= 32 tokens as one cluster kernel (ARCTIC_LAT_CLUSTER=0: off)
   bool prof = false;      // record CUDA events around every launch (ae_profile)
   int prof_kind = 0;      // kind of the launches being enqueued
@@ -1059,7 +1059,7 @@ int ae_ctx_create(int device, ae_ctx** out) {
   const char* am = std::getenv("ARCTIC_ATTN");
   c->attn_mode = (am && std::strcmp(am, "int8") == 0) ? AE_ATTENTION_INT8 : AE_ATTENTION_EXACT;
   const char* fw = std::getenv("ARCTIC_ATTN_FEW");
-  c->few_mode = !fw ? 0 : std::strcmp(fw, "tmem") == 0 ? 1 : std::strcmp(fw, "narrow") == 0 ? 2 : std::strcmp(fw, "lanes8") == 0 ? 3 : 0;
+  c->few_mode = !fw ? 0 : std::strcmp(fw, "tmem") == 0 ? 1 : std::strcmp(fw, "narrow") == 0 ? 2 : std::strcmp(fw, "lanes8") == 0 ? 3 : std::strcmp(fw, "dm") == 0 ? 4 : 0;
   const char* lc = std::getenv("ARCTIC_LAT_CLUSTER");
   c->lat_cluster = !(lc && std::strcmp(lc, "0") == 0) && lat_prime();
   if (gemm_i8_prime() || attention_prime()) {

@@ -45,7 +45,8 @@ struct AttnArgs {
   float* quant_scale;         // [rows]
   int skip_from;              // > 0: the exact kernels leave sequences of at least this many keys alone
   int few_mode;               // few long sequences: 0 the faster kernel, 1 the TMEM kernels, 2 32-query
-                              // tiles, 3 eight lanes per query (all the same results; for tests)
+                              // tiles, 3 eight lanes per query, 4 32-query tiles with dim-major K / V
+                              // (all the same results; for tests)
 };
 
 // Launch with programmatic stream serialization (the kernel calls pdl_wait before it touches data

@@ -289,10 +289,11 @@ def test_few_long_sequence_attention_matches_tmem_kernels(pack_path, oracle_mode
     batches) run the attention either on 32-query tiles with the scores in shared memory or with
     eight lanes per query, whichever fills the SMs in one wave. Both keep every chain of the
     reference's order in one thread, so every embedding is the same bits as with the TMEM kernels
-    (ARCTIC_ATTN_FEW=tmem; =narrow and =lanes8 force the other two at every length), and within
-    the tolerance of the oracle."""
+    (ARCTIC_ATTN_FEW=tmem; =narrow, =lanes8 and =dm force the others at every length; dm is the
+    32-query-tile kernel with K / V staged dim-major, by bulk copies when the sequence starts a
+    128-row tile, the single-sequence default), and within the tolerance of the oracle."""
     engines = {}
-    for mode in ("tmem", "narrow", "lanes8", None):
+    for mode in ("tmem", "narrow", "lanes8", "dm", None):
         if mode:
             monkeypatch.setenv("ARCTIC_ATTN_FEW", mode)
         else:
