@@ -250,6 +250,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // 8-15 the odd ones (accumulator 1), two warps per lane quadrant each with half the columns, so
     // that one group's row-maximum exchange and quantization overlap the other group's GELU
     const int grp = EPI == EPI_GELU_QUANT ? ew >> 3 : 0;
+    // EPI_LN_QUANT: a row-major residual whose rows are 16-byte aligned is read 16 bytes at a time
+    [[maybe_unused]] const bool res_v4 =
+        g.res && !g.res_tt && (reinterpret_cast<uintptr_t>(g.res) & 15) == 0 && (g.ldr & 3) == 0;
     const int it_step = EPI == EPI_GELU_QUANT ? 2 : 1;
     bool ok = true;
     for (int it = grp; it < my_tiles; it += it_step) {
@@ -264,15 +267,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       [[maybe_unused]] float rv0[16], rv1[16];
       if constexpr (EPI == EPI_LN_QUANT) {  // residual chunks 0 and 1 (column blocks 0-7)
         if (row < g.M) {
-          const float* rr = g.res_tt ? g.res + tt_index(row, 0, g.ldr) : g.res + size_t(row) * g.ldr;
-          const size_t rs = g.res_tt ? 128 : 1;
+          if (g.res_tt) {
+            const float* rr = g.res + tt_index(row, 0, g.ldr);
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
+            for (int k = 0; k < 4; ++k)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              rv0[4 * k + e] = __ldcs(rr + size_t(16 * k + 4 * qq + e) * rs);
-              rv1[4 * k + e] = __ldcs(rr + size_t(16 * (k + 4) + 4 * qq + e) * rs);
+              for (int e = 0; e < 4; ++e) {
+                rv0[4 * k + e] = __ldcs(rr + size_t(16 * k + 4 * qq + e) * 128);
+                rv1[4 * k + e] = __ldcs(rr + size_t(16 * (k + 4) + 4 * qq + e) * 128);
+              }
+          } else if (res_v4) {  // row-major: the thread's four columns of a block are one 16-byte load
+            const float4* rr = reinterpret_cast<const float4*>(g.res + size_t(row) * g.ldr + 4 * qq);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float4 x0 = __ldcs(rr + 4 * k), x1 = __ldcs(rr + 4 * (k + 4));
+              rv0[4 * k] = x0.x; rv0[4 * k + 1] = x0.y; rv0[4 * k + 2] = x0.z; rv0[4 * k + 3] = x0.w;
+              rv1[4 * k] = x1.x; rv1[4 * k + 1] = x1.y; rv1[4 * k + 2] = x1.z; rv1[4 * k + 3] = x1.w;
             }
+          } else {
+            const float* rr = g.res + size_t(row) * g.ldr;
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                rv0[4 * k + e] = __ldcs(rr + 16 * k + 4 * qq + e);
+                rv1[4 * k + e] = __ldcs(rr + 16 * (k + 4) + 4 * qq + e);
+              }
+          }
         } else {
 #pragma unroll
           for (int i = 0; i < 16; ++i) rv0[i] = rv1[i] = 0.0f;
@@ -499,11 +520,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             float* rv = (i % 3 == 0) ? rv0 : (i % 3 == 1) ? rv1 : rv2;
             float* nx = (i % 3 == 0) ? rv2 : (i % 3 == 1) ? rv0 : rv1;
             if (i + 2 < 6) {
+              if (res_v4) {  // row-major, 16-byte aligned rows: one 16-byte load per block
 #pragma unroll
-              for (int k = 0; k < 4; ++k)
+                for (int k = 0; k < 4; ++k) {
+                  const float4 x = valid ? __ldcs(reinterpret_cast<const float4*>(res_row + 16 * (k0 + 8 + k) + cq))
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+                  nx[4 * k] = x.x; nx[4 * k + 1] = x.y; nx[4 * k + 2] = x.z; nx[4 * k + 3] = x.w;
+                }
+              } else {
 #pragma unroll
-                for (int e = 0; e < 4; ++e)
-                  nx[4 * k + e] = valid ? __ldcs(res_row + size_t(16 * (k0 + 8 + k) + cq + e) * rstep) : 0.0f;
+                for (int k = 0; k < 4; ++k)
+#pragma unroll
+                  for (int e = 0; e < 4; ++e)
+                    nx[4 * k + e] = valid ? __ldcs(res_row + size_t(16 * (k0 + 8 + k) + cq + e) * rstep) : 0.0f;
+              }
             }
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
