@@ -425,17 +425,24 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             } else {
 #pragma unroll
-              for (int j = 0; j < 16; j += 2) {
+              for (int j = 0; j < 16; j += 4) {  // column parameters as 16-byte broadcast loads
                 const int c = cc + j;
-                const float2 ws2 = *reinterpret_cast<const float2*>(s_ws + c);
-                const float2 b2 = *reinterpret_cast<const float2*>(s_bias + c);
-                const float2 iv2 = *reinterpret_cast<const float2*>(s_invs + c);
-                const float2 h = __ffma2_rn(make_float2(float(int(r[j])), float(int(r[j + 1]))),
-                                            __fmul2_rn(make_float2(as, as), ws2), b2);
-                const float2 gv = __fmul2_rn(gelu_ref2(h), iv2);
-                vmax = fmaxf(vmax, fmaxf(fabsf(gv.x), fabsf(gv.y)));
-                r[j] = __float_as_uint(gv.x);
-                r[j + 1] = __float_as_uint(gv.y);
+                const float4 ws4 = *reinterpret_cast<const float4*>(s_ws + c);
+                const float4 b4 = *reinterpret_cast<const float4*>(s_bias + c);
+                const float4 iv4 = *reinterpret_cast<const float4*>(s_invs + c);
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                  const float2 ws2 = hf ? make_float2(ws4.z, ws4.w) : make_float2(ws4.x, ws4.y);
+                  const float2 b2 = hf ? make_float2(b4.z, b4.w) : make_float2(b4.x, b4.y);
+                  const float2 iv2 = hf ? make_float2(iv4.z, iv4.w) : make_float2(iv4.x, iv4.y);
+                  const int jj = j + 2 * hf;
+                  const float2 h = __ffma2_rn(make_float2(float(int(r[jj])), float(int(r[jj + 1]))),
+                                              __fmul2_rn(make_float2(as, as), ws2), b2);
+                  const float2 gv = __fmul2_rn(gelu_ref2(h), iv2);
+                  vmax = fmaxf(vmax, fmaxf(fabsf(gv.x), fabsf(gv.y)));
+                  r[jj] = __float_as_uint(gv.x);
+                  r[jj + 1] = __float_as_uint(gv.y);
+                }
               }
             }
             tmem_st16(tb + cc, r);
