@@ -1593,26 +1593,30 @@ __global__ void __launch_bounds__(32 * NW) k_attention_narrow(AttnArgs a) {
 // scores pass takes quads: warp g the quad g % 4 of the chunks it owns; the exponentials and the
 // weighted sum keep k_attention_narrow's chain ownership, so the same bits.
 __host__ __device__ constexpr int narrow_dm_er_pitch(int L) { return ((L + 31) & ~31) + 4; }
-__host__ __device__ constexpr size_t narrow_dm_smem_bytes(int L) {
-  return size_t((L + 127) >> 7) * 2 * 32 * 128 * 4 + size_t(32) * narrow_dm_er_pitch(L) * 4;
+__host__ __device__ constexpr size_t narrow_dm_smem_bytes(int L, int qt = 32) {
+  return size_t((L + 127) >> 7) * 2 * 32 * 128 * 4 + size_t(qt) * narrow_dm_er_pitch(L) * 4;
 }
 __device__ __forceinline__ int dm_index(int d, int t) { return ((t >> 7) << 12) + (d << 7) + (t & 127); }
 
-template <int NW>
-__global__ void __launch_bounds__(32 * NW) k_attention_narrow_dm(AttnArgs a) {
-  static_assert(NW == 8 || NW == 16, "8 or 16 warps");
+template <int NW, int ROWS>
+__global__ void __launch_bounds__(32 * NW * ROWS) k_attention_narrow_dm(AttnArgs a, int qt) {
+  static_assert(NW == 8 || NW == 16, "8 or 16 warps per row of queries");
   constexpr int DPG = 32 / NW;
   pdl_trigger();
   pdl_wait();
   extern __shared__ float4 smem4[];
-  __shared__ float xmx[NW][32];
-  __shared__ float xsl[16][32];
+  __shared__ float xmx[ROWS][NW][32];
+  __shared__ float xsl[ROWS][16][32];
   __shared__ uint64_t kv_bar;
   const int h = blockIdx.y;
   const int tile = blockIdx.z;
   const int tid = threadIdx.x;
-  const int g = tid >> 5;
+  const int wid = tid >> 5;
+  const int g = wid % NW;   // warp within its row of queries
+  const int rw = wid / NW;  // row of queries: slots 32 rw .. 32 rw + 31 of the tile
   const int lane = tid & 31;
+  const int slot = 32 * rw + lane;
+  const bool has_row = slot < qt;  // the tile's last row of queries may be partial
   const int s0 = int(a.cu[blockIdx.x]);
   const int L = int(a.cu[blockIdx.x + 1]) - s0;
   if (a.skip_from > 0 && L >= a.skip_from) return;
@@ -1620,13 +1624,13 @@ __global__ void __launch_bounds__(32 * NW) k_attention_narrow_dm(AttnArgs a) {
     if (tid == 0 && tile == 0 && h == 0) record_err(a.err, DEV_ERR_BAD_SHAPE);
     return;
   }
-  if (tile * 32 >= L) return;
+  if (tile * qt >= L) return;
   const bool bulk = a.kv_tt && !(s0 & 127);
   const int ntile = (L + 127) >> 7;
   float* kd = reinterpret_cast<float*>(smem4);  // [ntile][32][128]
   float* vd = kd + ntile * 4096;
   const int Pe = narrow_dm_er_pitch(L);
-  float* er = vd + ntile * 4096 + lane * Pe;
+  float* er = vd + ntile * 4096 + (has_row ? slot : 0) * Pe;
   if (bulk && tid == 0) {
     mbar_init(&kv_bar, 1);
     fence_mbar_init();
@@ -1637,13 +1641,13 @@ __global__ void __launch_bounds__(32 * NW) k_attention_narrow_dm(AttnArgs a) {
       bulk_load(vd + j * 4096, blk + size_t(a.v_col + 32 * h) * 128, 16384, &kv_bar);
     }
   }
-  const int qi = tile * 32 + lane;
-  const bool active = qi < L;
+  const int qi = tile * qt + slot;
+  const bool active = has_row && qi < L;
   float q[1][32];
   load_query(a, s0 + (active ? qi : L - 1), h, q[0]);
   if (!bulk) {  // a sequence inside a tile: 4-byte asynchronous copies of its rows, all in flight
     const int nwarps = blockDim.x >> 5;
-    for (int c = g; c < 64; c += nwarps) {
+    for (int c = wid; c < 64; c += nwarps) {
       const int d = c & 31;
       const int col = (c < 32 ? a.k_col : a.v_col) + 32 * h + d;
       float* dst = c < 32 ? kd : vd;
@@ -1667,7 +1671,7 @@ __global__ void __launch_bounds__(32 * NW) k_attention_narrow_dm(AttnArgs a) {
   const int qo = 4 * (g & 3);
   const int c_first = 16 * (g >> 2), c_step = 16 * (NW / 4);
   float mx = -INFINITY;
-  for (int t0 = c_first; t0 < L; t0 += c_step) {
+  for (int t0 = c_first; has_row && t0 < L; t0 += c_step) {
     const int t = t0 + qo;
     if (t >= L) continue;
     float2 sp[1][2];
@@ -1683,10 +1687,10 @@ __global__ void __launch_bounds__(32 * NW) k_attention_narrow_dm(AttnArgs a) {
     }
     *reinterpret_cast<float4*>(er + t) = v;
   }
-  xmx[g][lane] = mx;
+  xmx[rw][g][lane] = mx;
   __syncthreads();
 #pragma unroll
-  for (int w = 0; w < NW; ++w) mx = fmaxf(mx, xmx[w][lane]);
+  for (int w = 0; w < NW; ++w) mx = fmaxf(mx, xmx[rw][w][lane]);
 
   // pass 2: as k_attention_narrow
   int t0;
@@ -1694,15 +1698,16 @@ __global__ void __launch_bounds__(32 * NW) k_attention_narrow_dm(AttnArgs a) {
     const int ko = 2 * g;
     const float2 neg_mx = f2(-mx, -mx);
     float2 vs = f2(0.0f, 0.0f);
+    const int L16r = has_row ? L16 : 0, Lr = has_row ? L : 0;
 #pragma unroll 4
-    for (t0 = 0; t0 + 16 <= L16; t0 += 16) {
+    for (t0 = 0; t0 + 16 <= L16r; t0 += 16) {
       float2* ep = reinterpret_cast<float2*>(er + t0 + ko);
       const float2 e = cw_exp2(add2(*ep, neg_mx));
       vs = add2(vs, e);
       *ep = e;
     }
     const int t = t0 + ko;
-    if (t < L) {
+    if (t < Lr) {
       float2* ep = reinterpret_cast<float2*>(er + t);
       const float2 x = add2(*ep, neg_mx);
       float2 e;
@@ -1714,18 +1719,19 @@ __global__ void __launch_bounds__(32 * NW) k_attention_narrow_dm(AttnArgs a) {
       }
       *ep = e;
     }
-    xsl[ko][lane] = vs.x;
-    xsl[ko + 1][lane] = vs.y;
+    xsl[rw][ko][lane] = vs.x;
+    xsl[rw][ko + 1][lane] = vs.y;
   } else {
     float vs = 0.0f;
+    const int L16r = has_row ? L16 : 0, Lr = has_row ? L : 0;
 #pragma unroll 4
-    for (t0 = 0; t0 + 16 <= L16; t0 += 16) {
+    for (t0 = 0; t0 + 16 <= L16r; t0 += 16) {
       const float e = cw_exp(er[t0 + g] - mx);
       vs = vs + e;
       er[t0 + g] = e;
     }
     const int t = t0 + g;
-    if (t < L) {
+    if (t < Lr) {
       const float x = er[t] - mx;
       float e;
       if (g < 8 && t < L8) {
@@ -1736,19 +1742,19 @@ __global__ void __launch_bounds__(32 * NW) k_attention_narrow_dm(AttnArgs a) {
       }
       er[t] = e;
     }
-    xsl[g][lane] = vs;
+    xsl[rw][g][lane] = vs;
   }
   __syncthreads();
-  if (g == 0) {
+  if (g == 0 && has_row) {
     float v8[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v8[j] = xsl[j][lane] + xsl[8 + j][lane];
+    for (int j = 0; j < 8; ++j) v8[j] = xsl[rw][j][lane] + xsl[rw][8 + j][lane];
     float sum = tree8(v8);
     for (int t = L8; t < L; ++t) sum = sum + er[t];
-    xmx[0][lane] = 1.0f / sum;
+    xmx[rw][0][lane] = 1.0f / sum;
   }
   __syncthreads();
-  const float inv = xmx[0][lane];
+  const float inv = xmx[rw][0][lane];
   const float2 inv2 = f2(inv, inv);
 
   // pass 3: the weighted sum of dims DPG g .. DPG g + DPG - 1, four keys per 16-byte load
@@ -1757,8 +1763,9 @@ __global__ void __launch_bounds__(32 * NW) k_attention_narrow_dm(AttnArgs a) {
   for (int d = 0; d < DPG; ++d) acc[d] = f2(0.0f, 0.0f);
   const int dg = DPG * g;
   int t = 0;
+  const int L3 = has_row ? L : 0;
 #pragma unroll 2
-  for (; t + 4 <= L; t += 4) {
+  for (; t + 4 <= L3; t += 4) {
     const float4 e4 = *reinterpret_cast<const float4*>(er + t);
     const float2 p01 = mul2(f2(e4.x, e4.y), inv2), p23 = mul2(f2(e4.z, e4.w), inv2);
 #pragma unroll
@@ -1768,13 +1775,13 @@ __global__ void __launch_bounds__(32 * NW) k_attention_narrow_dm(AttnArgs a) {
       acc[d] = fma2(f2(vv.z, vv.w), p23, acc[d]);
     }
   }
-  for (; t + 1 < L; t += 2) {
+  for (; t + 1 < L3; t += 2) {
     const float2 p = mul2(f2(er[t], er[t + 1]), inv2);
 #pragma unroll
     for (int d = 0; d < DPG; ++d)
       acc[d] = fma2(f2(vd[dm_index(dg + d, t)], vd[dm_index(dg + d, t + 1)]), p, acc[d]);
   }
-  if (t < L) {  // odd L: the last key goes to the even accumulator
+  if (t < L3) {  // odd L: the last key goes to the even accumulator
     const float pa = er[t] * inv;
 #pragma unroll
     for (int d = 0; d < DPG; ++d) acc[d].x = fmaf(vd[dm_index(dg + d, t)], pa, acc[d].x);
@@ -1970,10 +1977,26 @@ static int launch_narrow(const AttnArgs& a, int n_seqs, cudaStream_t st) {
 }
 
 static size_t g_static_narrow_dm = 0;
+// one wave of 32-query tiles (16 warps each), or, where that takes two waves, tiles of up to 64
+// queries sized to fill the SMs once (two rows of 8 warps, the second row partial)
+static size_t g_static_narrow_dm2 = 0;
 static int launch_narrow_dm(const AttnArgs& a, int n_seqs, cudaStream_t st) {
-  const dim3 grid(n_seqs, kHeads, (a.max_len + 31) / 32);
-  return launch_pdl(k_attention_narrow_dm<kNarrowWarps>, grid, dim3(32 * kNarrowWarps), narrow_dm_smem_bytes(a.max_len),
-                    st, a) == cudaSuccess
+  const long heads = long(n_seqs) * kHeads;
+  if (heads * ((a.max_len + 31) / 32) <= 148) {
+    const dim3 grid(n_seqs, kHeads, (a.max_len + 31) / 32);
+    return launch_pdl(k_attention_narrow_dm<kNarrowWarps, 1>, grid, dim3(32 * kNarrowWarps),
+                      narrow_dm_smem_bytes(a.max_len), st, a, 32) == cudaSuccess
+               ? 0
+               : -3;
+  }
+  int tiles = int(148 / heads);
+  if (tiles < 1) tiles = 1;
+  int qt = (a.max_len + tiles - 1) / tiles;
+  if (qt > 64) qt = 64;
+  while (qt > 32 && narrow_dm_smem_bytes(a.max_len, qt) + g_static_narrow_dm2 > 227 * 1024) --qt;
+  const dim3 grid(n_seqs, kHeads, (a.max_len + qt - 1) / qt);
+  return launch_pdl(k_attention_narrow_dm<8, 2>, grid, dim3(512), narrow_dm_smem_bytes(a.max_len, qt), st, a, qt) ==
+                 cudaSuccess
              ? 0
              : -3;
 }
@@ -1997,10 +2020,12 @@ int attention_prime() {
   r |= static_smem((const void*)k_attention_rows2, &g_static_rows2);
   r |= static_smem((const void*)k_attention_lat8, &g_static_lat8);
   r |= static_smem((const void*)k_attention_narrow<kNarrowWarps>, &g_static_narrow);
-  r |= static_smem((const void*)k_attention_narrow_dm<kNarrowWarps>, &g_static_narrow_dm);
+  r |= static_smem((const void*)k_attention_narrow_dm<kNarrowWarps, 1>, &g_static_narrow_dm);
+  r |= static_smem((const void*)k_attention_narrow_dm<8, 2>, &g_static_narrow_dm2);
   if (r) return r;
   r |= smem_attr((const void*)k_attention_narrow<kNarrowWarps>, 227 * 1024 - g_static_narrow);
-  r |= smem_attr((const void*)k_attention_narrow_dm<kNarrowWarps>, 227 * 1024 - g_static_narrow_dm);
+  r |= smem_attr((const void*)k_attention_narrow_dm<kNarrowWarps, 1>, 227 * 1024 - g_static_narrow_dm);
+  r |= smem_attr((const void*)k_attention_narrow_dm<8, 2>, 227 * 1024 - g_static_narrow_dm2);
   r |= smem_attr((const void*)k_attention_lat8, 227 * 1024 - g_static_lat8);
   r |= smem_attr((const void*)k_attention_rows2, rows_smem_cap(g_static_rows2));
   r |= smem_attr((const void*)k_attention_rows<128>, rows_smem_cap(g_static_rows));
@@ -2314,8 +2339,7 @@ int launch_attention_exact(const AttnArgs& a, int n_seqs, cudaStream_t st, int* 
     const size_t per_cta = narrow_smem_bytes(a.max_len) + g_static_narrow + 1024;
     const long fit = long(227 * 1024 / per_cta);
     const bool dm_fits = narrow_dm_smem_bytes(a.max_len) + g_static_narrow_dm + 1024 <= 227 * 1024;
-    const bool one_wave = heads * ((a.max_len + 31) / 32) <= 148;
-    if (a.few_mode == 4 || (a.few_mode == 0 && n_seqs == 1 && dm_fits && one_wave)) return launch_narrow_dm(a, n_seqs, st);
+    if (a.few_mode == 4 || (a.few_mode == 0 && n_seqs == 1 && dm_fits)) return launch_narrow_dm(a, n_seqs, st);
     const bool narrow = a.few_mode == 2 ? fit >= 1 : (a.few_mode == 0 && fit >= 1 && heads * ((a.max_len + 31) / 32) <= 148 * fit);
     return narrow ? launch_narrow(a, n_seqs, st) : launch_lat8(a, n_seqs, st);
   }
