@@ -82,7 +82,7 @@ struct Layout {
                                    : (BASE_BYTES + 4 * kEpiWarps * 32 * 17 <= 232448 ? 16 : 0);
   static constexpr int STG_FLOATS = STG_W ? kEpiWarps * 32 * (STG_W + 1) : 0;
   static constexpr int XCH_FLOATS =
-      LN ? (2 * BM * 16 + BM * 4) : (EPI == EPI_GELU_QUANT ? XCH_FLOATS_GELU + STAGING_BYTES / 4 : STG_FLOATS);
+      LN ? (2 * BM * 17 + BM * 5) : (EPI == EPI_GELU_QUANT ? XCH_FLOATS_GELU + STAGING_BYTES / 4 : STG_FLOATS);
   static constexpr int NBARS = NBARS_;
   static constexpr int TOTAL = 1024 + B_RES + RING + 4 * (PARAM_FLOATS + XCH_FLOATS) + 8 * NBARS + 16;
   static_assert(TOTAL <= 232448, "shared memory of one CTA exceeds the sm_100 limit");
@@ -504,9 +504,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else if constexpr (EPI == EPI_LN_QUANT) {
         static_assert(BN == kHidden, "row-LayerNorm epilogue needs the full 384-wide row");
-        float* xs = xch;                 // [BM][16] partial sums
-        float* xv = xch + BM * 16;       // [BM][16] partial sums of squares
-        float* xm = xch + 2 * BM * 16;   // [BM][4]  partial maxima
+        // rows padded to 17 and 5 floats: the 32 rows of a warp fall in 32 different banks
+        float* xs = xch;                 // [BM][17] partial sums
+        float* xv = xch + BM * 17;       // [BM][17] partial sums of squares
+        float* xm = xch + 2 * BM * 17;   // [BM][5]  partial maxima
         const int cq = 4 * qq;           // first owned column of every 16-column block
         uint32_t r[32];
         float p[4] = {0.f, 0.f, 0.f, 0.f};
@@ -566,11 +567,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st_wait();
         }
 #pragma unroll
-        for (int e = 0; e < 4; ++e) xs[rt * 16 + cq + e] = p[e];
+        for (int e = 0; e < 4; ++e) xs[rt * 17 + cq + e] = p[e];
         named_bar(1 + Q, 128);
         float pp[16];
 #pragma unroll
-        for (int l = 0; l < 16; ++l) pp[l] = xs[rt * 16 + l];
+        for (int l = 0; l < 16; ++l) pp[l] = xs[rt * 17 + l];
         const float mean = tree16(pp) / float(kHidden);
         // pass 2: variance
 #pragma unroll
@@ -590,10 +591,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
 #pragma unroll
-        for (int e = 0; e < 4; ++e) xv[rt * 16 + cq + e] = p[e];
+        for (int e = 0; e < 4; ++e) xv[rt * 17 + cq + e] = p[e];
         named_bar(1 + Q, 128);
 #pragma unroll
-        for (int l = 0; l < 16; ++l) pp[l] = xv[rt * 16 + l];
+        for (int l = 0; l < 16; ++l) pp[l] = xv[rt * 17 + l];
         const float var = tree16(pp) / float(kHidden);
         const float rstd = 1.0f / sqrtf(var + kLnEps);
         // pass 3: y = LN(h) -> residual out and TMEM; max |y * inv_smooth|
@@ -635,11 +636,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tmem_st_wait();
         }
-        xm[rt * 4 + qq] = vmax;
+        xm[rt * 5 + qq] = vmax;
         tc_fence_before();
         named_bar(1 + Q, 128);
         tc_fence_after();
-        const float max_abs = fmaxf(fmaxf(xm[rt * 4], xm[rt * 4 + 1]), fmaxf(xm[rt * 4 + 2], xm[rt * 4 + 3]));
+        const float max_abs = fmaxf(fmaxf(xm[rt * 5], xm[rt * 5 + 1]), fmaxf(xm[rt * 5 + 2], xm[rt * 5 + 3]));
         const float inv_scale = 127.0f / max_abs;
         // pass 4: quantize. Elementwise, so this warp takes the 96 contiguous columns
         // 96 qq .. 96 qq + 95 of its rows (written to TMEM by the quadrant's four warps in pass 3)
