@@ -114,6 +114,10 @@ struct ae_ctx {
   cudaStream_t own_stream = nullptr;
   cudaStream_t stream = nullptr;
   int* d_err = nullptr;
+  // ae_forward_cls's graphs: the embedding (384 floats) followed by the graph's own error word, so
+  // that one device-to-host copy inside the graph brings both (no separate read of d_err per call)
+  float* d_lat = nullptr;
+  float* h_lat = nullptr;  // pinned
   uint32_t* d_cu_single = nullptr;  // [513][2]: {0, L} at 2L, the cu_seqlens of one sequence of L ids
   bool has_model = false;
   DevModel model;
@@ -717,15 +721,19 @@ int enqueue_forward(ae_ctx* c, const uint16_t* d_ids, const uint32_t* d_cu, int 
   return 0;
 }
 
+int dev_err_fail(ae_ctx* c, int h) {
+  static const char* names[] = {"ok", "producer wait timed out", "MMA wait timed out", "epilogue wait timed out",
+                                "sequence length outside 1..512", "token id out of range"};
+  return fail(c, AE_ERR_DEVICE, "device error %d (%s)", h, (h >= 0 && h <= 5) ? names[h] : "?");
+}
+
 int check_dev_err(ae_ctx* c) {
   int h = 0;
   CUDA_TRY(c, cudaMemcpy(&h, c->d_err, sizeof(int), cudaMemcpyDeviceToHost));
   if (h != 0) {
     int z = 0;
     cudaMemcpy(c->d_err, &z, sizeof(int), cudaMemcpyHostToDevice);
-    static const char* names[] = {"ok", "producer wait timed out", "MMA wait timed out", "epilogue wait timed out",
-                                  "sequence length outside 1..512", "token id out of range"};
-    return fail(c, AE_ERR_DEVICE, "device error %d (%s)", h, (h >= 0 && h <= 5) ? names[h] : "?");
+    return dev_err_fail(c, h);
   }
   return 0;
 }
@@ -1036,6 +1044,9 @@ int ae_ctx_create(int device, ae_ctx** out) {
   // stream preparing the inputs of ae_forward_ragged_device) is ordered with the context's work
   e = cudaStreamCreate(&c->own_stream);
   if (e == cudaSuccess) e = cudaMalloc(&c->d_err, sizeof(int));
+  if (e == cudaSuccess) e = cudaMalloc(&c->d_lat, (kHidden + 1) * sizeof(float));
+  if (e == cudaSuccess) e = cudaMallocHost(&c->h_lat, (kHidden + 1) * sizeof(float));
+  if (e == cudaSuccess) e = cudaMemset(c->d_lat, 0, (kHidden + 1) * sizeof(float));
   if (e == cudaSuccess) e = cudaMalloc(&c->d_cu_single, sizeof(uint32_t) * 2 * (kMaxPos + 1));
   if (e == cudaSuccess) {
     std::vector<uint32_t> t(2 * (kMaxPos + 1));
@@ -1047,6 +1058,10 @@ int ae_ctx_create(int device, ae_ctx** out) {
   }
   if (e == cudaSuccess) e = cudaMemset(c->d_err, 0, sizeof(int));
   if (e != cudaSuccess) {
+    if (c->d_err) cudaFree(c->d_err);
+    if (c->d_lat) cudaFree(c->d_lat);
+    if (c->h_lat) cudaFreeHost(c->h_lat);
+    if (c->d_cu_single) cudaFree(c->d_cu_single);
     if (c->own_stream) cudaStreamDestroy(c->own_stream);
     delete c;
     return fail(nullptr, AE_ERR_CUDA, "context setup: %s", cudaGetErrorString(e));
@@ -1093,6 +1108,8 @@ int ae_ctx_destroy(ae_ctx* c) {
   }
   for (auto e : c->prof_pool) cudaEventDestroy(e);
   if (c->d_err) cudaFree(c->d_err);
+  if (c->d_lat) cudaFree(c->d_lat);
+  if (c->h_lat) cudaFreeHost(c->h_lat);
   if (c->d_cu_single) cudaFree(c->d_cu_single);
   if (c->own_stream) cudaStreamDestroy(c->own_stream);
   delete c;
@@ -1355,21 +1372,24 @@ int ae_forward_cls(ae_ctx* c, const uint16_t* ids, uint32_t len, float* out) {
     const uint64_t before = c->launches;
     const bool prof = c->prof;
     c->prof = false;  // no event records inside the graph
+    int* const d_err = c->d_err;
+    c->d_err = reinterpret_cast<int*>(c->d_lat + kHidden);  // the graph's kernels report here
     // at most 32 tokens: the whole forward as one 12-CTA cluster kernel (the same arithmetic; the
     // int8 attention mode keeps the multi-kernel path for the sequences it covers)
     const bool one_kernel = c->lat_cluster && c->model.lat && L <= uint32_t(kLatMaxTokens) &&
                             (c->attn_mode == AE_ATTENTION_EXACT || L < uint32_t(kI8MinLen));
     if (!r && one_kernel) {
       ++c->launches;
-      if (launch_forward_lat(c->model.lat, W.ids, int(L), W.out, c->d_err, c->gelu_erf, c->stream))
+      if (launch_forward_lat(c->model.lat, W.ids, int(L), c->d_lat, c->d_err, c->gelu_erf, c->stream))
         r = fail(c, AE_ERR_CUDA, "cluster forward launch failed");
     } else if (!r) {
-      r = enqueue_forward(c, W.ids, c->d_cu_single + 2 * L, int(L), 1, int(L), W.out, nullptr, int(L));
+      r = enqueue_forward(c, W.ids, c->d_cu_single + 2 * L, int(L), 1, int(L), c->d_lat, nullptr, int(L));
     }
     c->prof = prof;
+    c->d_err = d_err;
     gr.kernels = c->launches - before;
     c->launches = before;  // captured, not launched
-    if (!r && cudaMemcpyAsync(W.h_out, W.out, kHidden * 4, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
+    if (!r && cudaMemcpyAsync(c->h_lat, c->d_lat, (kHidden + 1) * 4, cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
       r = fail(c, AE_ERR_CUDA, "capture of output copy failed");
     cudaError_t e = cudaStreamEndCapture(c->stream, &gr.g);
     if (r) {
@@ -1388,8 +1408,14 @@ int ae_forward_cls(ae_ctx* c, const uint16_t* ids, uint32_t len, float* out) {
   CUDA_TRY(c, cudaGraphLaunch(it->second.exec, c->stream));
   c->launches += it->second.kernels;
   CUDA_TRY(c, cudaStreamSynchronize(c->stream));
-  AE_TRY(check_dev_err(c));
-  std::memcpy(out, W.h_out, kHidden * 4);
+  int h_err = 0;
+  std::memcpy(&h_err, c->h_lat + kHidden, sizeof(int));  // the graph's error word, copied with the output
+  if (h_err != 0) {
+    cudaMemsetAsync(c->d_lat + kHidden, 0, sizeof(int), c->stream);
+    cudaStreamSynchronize(c->stream);
+    return dev_err_fail(c, h_err);
+  }
+  std::memcpy(out, c->h_lat, kHidden * 4);
   return 0;
 }
 
