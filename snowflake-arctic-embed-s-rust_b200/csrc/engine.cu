@@ -118,6 +118,7 @@ struct ae_ctx {
   // that one device-to-host copy inside the graph brings both (no separate read of d_err per call)
   float* d_lat = nullptr;
   float* h_lat = nullptr;  // pinned
+  int* h_err = nullptr;    // pinned copy of d_err, taken on the stream before a synchronisation
   uint32_t* d_cu_single = nullptr;  // [513][2]: {0, L} at 2L, the cu_seqlens of one sequence of L ids
   bool has_model = false;
   DevModel model;
@@ -727,6 +728,22 @@ int dev_err_fail(ae_ctx* c, int h) {
   return fail(c, AE_ERR_DEVICE, "device error %d (%s)", h, (h >= 0 && h <= 5) ? names[h] : "?");
 }
 
+// The error word read back on the stream (enqueue before the synchronisation, check after it):
+// saves the synchronous copy of check_dev_err on the hot host paths.
+int enqueue_err_copy(ae_ctx* c) {
+  CUDA_TRY(c, cudaMemcpyAsync(c->h_err, c->d_err, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+  return 0;
+}
+int check_err_copied(ae_ctx* c) {
+  const int h = *c->h_err;
+  if (h != 0) {
+    int z = 0;
+    cudaMemcpy(c->d_err, &z, sizeof(int), cudaMemcpyHostToDevice);
+    return dev_err_fail(c, h);
+  }
+  return 0;
+}
+
 int check_dev_err(ae_ctx* c) {
   int h = 0;
   CUDA_TRY(c, cudaMemcpy(&h, c->d_err, sizeof(int), cudaMemcpyDeviceToHost));
@@ -810,8 +827,9 @@ int forward_ragged_host(ae_ctx* c, const uint16_t* ids, const uint32_t* cu, uint
   CUDA_TRY(c, cudaMemcpyAsync(W.cu, W.h_cu, size_t(n + 1) * 4, cudaMemcpyHostToDevice, c->stream));
   AE_TRY(enqueue_forward(c, W.ids, W.cu, T, int(n), max_len, W.out, &c->segs));
   CUDA_TRY(c, cudaMemcpyAsync(W.h_out, W.out, size_t(n) * kHidden * 4, cudaMemcpyDeviceToHost, c->stream));
+  AE_TRY(enqueue_err_copy(c));
   CUDA_TRY(c, cudaStreamSynchronize(c->stream));
-  AE_TRY(check_dev_err(c));
+  AE_TRY(check_err_copied(c));
   for (uint32_t k = 0; k < n; ++k)
     std::memcpy(out + size_t(c->order[k]) * kHidden, W.h_out + size_t(k) * kHidden, kHidden * 4);
   return 0;
@@ -1046,6 +1064,7 @@ int ae_ctx_create(int device, ae_ctx** out) {
   if (e == cudaSuccess) e = cudaMalloc(&c->d_err, sizeof(int));
   if (e == cudaSuccess) e = cudaMalloc(&c->d_lat, (kHidden + 1) * sizeof(float));
   if (e == cudaSuccess) e = cudaMallocHost(&c->h_lat, (kHidden + 1) * sizeof(float));
+  if (e == cudaSuccess) e = cudaMallocHost(&c->h_err, sizeof(int));
   if (e == cudaSuccess) e = cudaMemset(c->d_lat, 0, (kHidden + 1) * sizeof(float));
   if (e == cudaSuccess) e = cudaMalloc(&c->d_cu_single, sizeof(uint32_t) * 2 * (kMaxPos + 1));
   if (e == cudaSuccess) {
@@ -1061,6 +1080,7 @@ int ae_ctx_create(int device, ae_ctx** out) {
     if (c->d_err) cudaFree(c->d_err);
     if (c->d_lat) cudaFree(c->d_lat);
     if (c->h_lat) cudaFreeHost(c->h_lat);
+    if (c->h_err) cudaFreeHost(c->h_err);
     if (c->d_cu_single) cudaFree(c->d_cu_single);
     if (c->own_stream) cudaStreamDestroy(c->own_stream);
     delete c;
@@ -1110,6 +1130,7 @@ int ae_ctx_destroy(ae_ctx* c) {
   if (c->d_err) cudaFree(c->d_err);
   if (c->d_lat) cudaFree(c->d_lat);
   if (c->h_lat) cudaFreeHost(c->h_lat);
+  if (c->h_err) cudaFreeHost(c->h_err);
   if (c->d_cu_single) cudaFree(c->d_cu_single);
   if (c->own_stream) cudaStreamDestroy(c->own_stream);
   delete c;
