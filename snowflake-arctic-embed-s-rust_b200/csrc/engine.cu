@@ -788,8 +788,11 @@ int pack_into(ae_ctx* c, const uint16_t* ids, const uint32_t* cu, uint32_t n, ui
     const uint32_t i = order[k];
     const uint32_t len = len_of(i);
     const uint16_t* src = ids + cu[i];
-    for (uint32_t j = 0; j < len; ++j) {
-      if (src[j] >= kVocab) return fail(c, AE_ERR_TOKEN_RANGE, "token id %u at sequence %u is >= 30522", src[j], i);
+    uint16_t mx = 0;  // the range check as a (vectorisable) maximum; the offending id only on failure
+    for (uint32_t j = 0; j < len; ++j) mx = src[j] > mx ? src[j] : mx;
+    if (mx >= kVocab) {
+      for (uint32_t j = 0; j < len; ++j)
+        if (src[j] >= kVocab) return fail(c, AE_ERR_TOKEN_RANGE, "token id %u at sequence %u is >= 30522", src[j], i);
     }
     std::memcpy(h_ids + off, src, len * 2);
     off += len;
