@@ -769,19 +769,26 @@ int pack_into(ae_ctx* c, const uint16_t* ids, const uint32_t* cu, uint32_t n, ui
   const bool i8 = c->attn_mode == AE_ATTENTION_INT8;
   auto class_of = [&](int len) { return i8 ? (len < kI8MinLen ? 0 : 1 + attn_class(len)) : attn_class(len); };
   int max_len = 0;
-  for (int cls = 0; cls < kAttnClasses + (i8 ? 1 : 0); ++cls) {
-    const uint32_t first = filled;
-    int seg_max = 0, seg_min = kMaxPos;
-    for (uint32_t i = 0; i < n; ++i) {
-      const uint32_t len = len_of(i);
-      if (class_of(int(len)) != cls) continue;
-      order[filled++] = i;
-      seg_max = std::max<int>(seg_max, int(len));
-      seg_min = std::min<int>(seg_min, int(len));
-    }
-    if (filled > first) segs.push_back(AttnSegment{int(first), int(filled - first), seg_max, seg_min});
-    max_len = std::max(max_len, seg_max);
+  // a stable counting sort of the sequences by class: counts, extremes, then placement
+  constexpr int kMaxClasses = kAttnClasses + 1;
+  const int n_classes = kAttnClasses + (i8 ? 1 : 0);
+  uint32_t count[kMaxClasses] = {}, next[kMaxClasses] = {};
+  int cmax[kMaxClasses] = {}, cmin[kMaxClasses];
+  for (int k = 0; k < kMaxClasses; ++k) cmin[k] = kMaxPos;
+  for (uint32_t i = 0; i < n; ++i) {
+    const int len = int(len_of(i));
+    const int k = class_of(len);
+    ++count[k];
+    cmax[k] = std::max(cmax[k], len);
+    cmin[k] = std::min(cmin[k], len);
   }
+  for (int k = 0; k < n_classes; ++k) {
+    next[k] = filled;
+    if (count[k]) segs.push_back(AttnSegment{int(filled), int(count[k]), cmax[k], cmin[k]});
+    filled += count[k];
+    max_len = std::max(max_len, cmax[k]);
+  }
+  for (uint32_t i = 0; i < n; ++i) order[next[class_of(int(len_of(i)))]++] = i;
   uint32_t off = 0;
   h_cu[0] = 0;
   for (uint32_t k = 0; k < n; ++k) {
@@ -833,8 +840,14 @@ int forward_ragged_host(ae_ctx* c, const uint16_t* ids, const uint32_t* cu, uint
   AE_TRY(enqueue_err_copy(c));
   CUDA_TRY(c, cudaStreamSynchronize(c->stream));
   AE_TRY(check_err_copied(c));
-  for (uint32_t k = 0; k < n; ++k)
-    std::memcpy(out + size_t(c->order[k]) * kHidden, W.h_out + size_t(k) * kHidden, kHidden * 4);
+  bool identity = true;  // a batch of one length class keeps the caller's order: one copy
+  for (uint32_t k = 0; k < n && identity; ++k) identity = c->order[k] == k;
+  if (identity) {
+    std::memcpy(out, W.h_out, size_t(n) * kHidden * 4);
+  } else {
+    for (uint32_t k = 0; k < n; ++k)
+      std::memcpy(out + size_t(c->order[k]) * kHidden, W.h_out + size_t(k) * kHidden, kHidden * 4);
+  }
   return 0;
 }
 
