@@ -413,6 +413,53 @@ __device__ __forceinline__ void score_quad(const float (&q)[NQ][32], const float
     }
 }
 
+// score_quad (grouped order) for the eight keys 8i .. 8i+7 (two quads): dims outer, so that every
+// step of the loop has eight independent key-pair chains per query, and the dot32x4 + hadd tree
+// ((x0 + x1) + (x2 + x3)) + ((x4 + x5) + (x6 + x7)) built as its terms arrive (the same additions in
+// the same order). sp[u][k]: keys (8i + 2k, 8i + 2k + 1).
+template <int NQ>
+__device__ __forceinline__ void score_oct(const float (&q)[NQ][32], const float* __restrict__ kq, int rs,
+                                          float2 (&sp)[NQ][4]) {
+  float2 h[NQ][4], a[NQ][4], b[NQ][4];
+#pragma unroll
+  for (int l = 0; l < 8; ++l) {
+    float4 A[2], B[2], C[2], D[2];
+#pragma unroll
+    for (int o = 0; o < 2; ++o) {
+      A[o] = *reinterpret_cast<const float4*>(kq + 4 * o + l * rs);
+      B[o] = *reinterpret_cast<const float4*>(kq + 4 * o + (l + 8) * rs);
+      C[o] = *reinterpret_cast<const float4*>(kq + 4 * o + (l + 16) * rs);
+      D[o] = *reinterpret_cast<const float4*>(kq + 4 * o + (l + 24) * rs);
+    }
+#pragma unroll
+    for (int u = 0; u < NQ; ++u) {
+      const float2 ql = f2(q[u][l], q[u][l]), ql8 = f2(q[u][l + 8], q[u][l + 8]);
+      const float2 ql16 = f2(q[u][l + 16], q[u][l + 16]), ql24 = f2(q[u][l + 24], q[u][l + 24]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int o = k >> 1;
+        const float2 av = (k & 1) ? f2(A[o].z, A[o].w) : f2(A[o].x, A[o].y);
+        const float2 bv = (k & 1) ? f2(B[o].z, B[o].w) : f2(B[o].x, B[o].y);
+        const float2 cv = (k & 1) ? f2(C[o].z, C[o].w) : f2(C[o].x, C[o].y);
+        const float2 dv = (k & 1) ? f2(D[o].z, D[o].w) : f2(D[o].x, D[o].y);
+        const float2 x = add2(fma2(ql8, bv, mul2(ql, av)), fma2(ql24, dv, mul2(ql16, cv)));
+        // ((x0 + x1) + (x2 + x3)) + ((x4 + x5) + (x6 + x7))
+        if ((l & 1) == 0) {
+          if (l & 2) b[u][k] = x; else a[u][k] = x;
+        } else {
+          if (l & 2) {
+            b[u][k] = add2(b[u][k], x);
+            const float2 t = add2(a[u][k], b[u][k]);
+            if (l == 3) h[u][k] = t; else sp[u][k] = add2(h[u][k], t);
+          } else {
+            a[u][k] = add2(a[u][k], x);
+          }
+        }
+      }
+    }
+  }
+}
+
 // k_attention_rows' three passes for NQ queries per thread over one head's dim-major K / V
 // (row stride rs): every shared-memory load of K or V feeds NQ queries. Query u keeps its scores,
 // then exponentials, in TMEM columns tl + u * qcols .. + L - 1 of the thread's lane. q: pre-scaled
@@ -433,17 +480,17 @@ __device__ __forceinline__ void attend_rows_dm(const float (&q)[NQ][32], const f
   for (int t0 = 0; t0 < L; t0 += 16) {
     if (t0 + 16 <= L4) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float2 sp[NQ][2];
-        score_quad<NQ>(q, kd + t0 + 4 * c, rs, true, sp);
+      for (int c = 0; c < 2; ++c) {
+        float2 sp[NQ][4];
+        score_oct<NQ>(q, kd + t0 + 8 * c, rs, sp);
 #pragma unroll
-        for (int u = 0; u < NQ; ++u) {
-          mx[u] = fmaxf(mx[u], fmaxf(fmaxf(sp[u][0].x, sp[u][0].y), fmaxf(sp[u][1].x, sp[u][1].y)));
-          r[u][4 * c] = __float_as_uint(sp[u][0].x);
-          r[u][4 * c + 1] = __float_as_uint(sp[u][0].y);
-          r[u][4 * c + 2] = __float_as_uint(sp[u][1].x);
-          r[u][4 * c + 3] = __float_as_uint(sp[u][1].y);
-        }
+        for (int u = 0; u < NQ; ++u)
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            mx[u] = fmaxf(mx[u], fmaxf(sp[u][k].x, sp[u][k].y));
+            r[u][8 * c + 2 * k] = __float_as_uint(sp[u][k].x);
+            r[u][8 * c + 2 * k + 1] = __float_as_uint(sp[u][k].y);
+          }
       }
     } else {
 #pragma unroll
@@ -1598,25 +1645,29 @@ __host__ __device__ constexpr size_t narrow_dm_smem_bytes(int L, int qt = 32) {
 }
 __device__ __forceinline__ int dm_index(int d, int t) { return ((t >> 7) << 12) + (d << 7) + (t & 127); }
 
-template <int NW, int ROWS>
+// QPT = 2 (one row of warps): each thread takes the queries of slots lane and 32 + lane, so every
+// staged K / V load feeds two queries (half the shared-memory loads per product of QPT = 1, whose
+// passes are bound by them at 385-512 keys); a thread whose second slot lies past the tile computes
+// that query's scores from a copy of its first query and discards them.
+template <int NW, int ROWS, int QPT = 1>
 __global__ void __launch_bounds__(32 * NW * ROWS) k_attention_narrow_dm(AttnArgs a, int qt) {
   static_assert(NW == 8 || NW == 16, "8 or 16 warps per row of queries");
+  static_assert(QPT == 1 || (QPT == 2 && ROWS == 1), "two queries per thread take one row of warps");
   constexpr int DPG = 32 / NW;
+  constexpr int NR = ROWS * QPT;  // rows of 32 query slots per tile
   pdl_trigger();
   pdl_wait();
   extern __shared__ float4 smem4[];
-  __shared__ float xmx[ROWS][NW][32];
-  __shared__ float xsl[ROWS][16][32];
+  __shared__ float xmx[NR][NW][32];
+  __shared__ float xsl[NR][16][32];
   __shared__ uint64_t kv_bar;
   const int h = blockIdx.y;
   const int tile = blockIdx.z;
   const int tid = threadIdx.x;
   const int wid = tid >> 5;
   const int g = wid % NW;   // warp within its row of queries
-  const int rw = wid / NW;  // row of queries: slots 32 rw .. 32 rw + 31 of the tile
+  const int rw = wid / NW;  // row of warps (QPT = 1): slots 32 rw .. 32 rw + 31 of the tile
   const int lane = tid & 31;
-  const int slot = 32 * rw + lane;
-  const bool has_row = slot < qt;  // the tile's last row of queries may be partial
   const int s0 = int(a.cu[blockIdx.x]);
   const int L = int(a.cu[blockIdx.x + 1]) - s0;
   if (a.skip_from > 0 && L >= a.skip_from) return;
@@ -1630,7 +1681,18 @@ __global__ void __launch_bounds__(32 * NW * ROWS) k_attention_narrow_dm(AttnArgs
   float* kd = reinterpret_cast<float*>(smem4);  // [ntile][32][128]
   float* vd = kd + ntile * 4096;
   const int Pe = narrow_dm_er_pitch(L);
-  float* er = vd + ntile * 4096 + (has_row ? slot : 0) * Pe;
+  // query u of this thread: slot 32 (rw + u) + lane of the tile, row R = rw + u of xmx / xsl
+  bool has[QPT], active[QPT];
+  int qi[QPT];
+  float* er[QPT];
+#pragma unroll
+  for (int u = 0; u < QPT; ++u) {
+    const int slot = 32 * (rw + u) + lane;
+    has[u] = slot < qt;  // the tile's last row of queries may be partial
+    qi[u] = tile * qt + slot;
+    active[u] = has[u] && qi[u] < L;
+    er[u] = vd + ntile * 4096 + (has[u] ? slot : 0) * Pe;
+  }
   if (bulk && tid == 0) {
     mbar_init(&kv_bar, 1);
     fence_mbar_init();
@@ -1641,10 +1703,13 @@ __global__ void __launch_bounds__(32 * NW * ROWS) k_attention_narrow_dm(AttnArgs
       bulk_load(vd + j * 4096, blk + size_t(a.v_col + 32 * h) * 128, 16384, &kv_bar);
     }
   }
-  const int qi = tile * qt + slot;
-  const bool active = has_row && qi < L;
-  float q[1][32];
-  load_query(a, s0 + (active ? qi : L - 1), h, q[0]);
+  float q[QPT][32];
+#pragma unroll
+  for (int u = 0; u < QPT; ++u) {
+    // a slot past the tile takes the first query's row (its results are discarded)
+    const int qr = active[u] ? qi[u] : (active[0] ? qi[0] : L - 1);
+    load_query(a, s0 + qr, h, q[u]);
+  }
   if (!bulk) {  // a sequence inside a tile: 4-byte asynchronous copies of its rows, all in flight
     const int nwarps = blockDim.x >> 5;
     for (int c = wid; c < 64; c += nwarps) {
@@ -1670,129 +1735,166 @@ __global__ void __launch_bounds__(32 * NW * ROWS) k_attention_narrow_dm(AttnArgs
   // pass 1: scores (quad g % 4 of the chunks this warp owns) and their max
   const int qo = 4 * (g & 3);
   const int c_first = 16 * (g >> 2), c_step = 16 * (NW / 4);
-  float mx = -INFINITY;
-  for (int t0 = c_first; has_row && t0 < L; t0 += c_step) {
+  float mx[QPT];
+#pragma unroll
+  for (int u = 0; u < QPT; ++u) mx[u] = -INFINITY;
+  for (int t0 = c_first; has[0] && t0 < L; t0 += c_step) {
     const int t = t0 + qo;
     if (t >= L) continue;
-    float2 sp[1][2];
-    score_quad<1>(q, kd + dm_index(0, t), 128, t < L4, sp);
-    float4 v = make_float4(sp[0][0].x, sp[0][0].y, sp[0][1].x, sp[0][1].y);
-    if (t + 4 <= L) {
-      mx = fmaxf(mx, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
-    } else {  // keys past the sequence: 0, outside the max
-      mx = fmaxf(mx, v.x);
-      if (t + 1 < L) mx = fmaxf(mx, v.y); else v.y = 0.0f;
-      if (t + 2 < L) mx = fmaxf(mx, v.z); else v.z = 0.0f;
-      v.w = 0.0f;
+    float2 sp[QPT][2];
+    score_quad<QPT>(q, kd + dm_index(0, t), 128, t < L4, sp);
+#pragma unroll
+    for (int u = 0; u < QPT; ++u) {
+      float4 v = make_float4(sp[u][0].x, sp[u][0].y, sp[u][1].x, sp[u][1].y);
+      if (t + 4 <= L) {
+        mx[u] = fmaxf(mx[u], fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+      } else {  // keys past the sequence: 0, outside the max
+        mx[u] = fmaxf(mx[u], v.x);
+        if (t + 1 < L) mx[u] = fmaxf(mx[u], v.y); else v.y = 0.0f;
+        if (t + 2 < L) mx[u] = fmaxf(mx[u], v.z); else v.z = 0.0f;
+        v.w = 0.0f;
+      }
+      if (u == 0 || has[u]) *reinterpret_cast<float4*>(er[u] + t) = v;
     }
-    *reinterpret_cast<float4*>(er + t) = v;
   }
-  xmx[rw][g][lane] = mx;
+#pragma unroll
+  for (int u = 0; u < QPT; ++u) xmx[rw + u][g][lane] = mx[u];
   __syncthreads();
 #pragma unroll
-  for (int w = 0; w < NW; ++w) mx = fmaxf(mx, xmx[rw][w][lane]);
+  for (int u = 0; u < QPT; ++u)
+#pragma unroll
+    for (int w = 0; w < NW; ++w) mx[u] = fmaxf(mx[u], xmx[rw + u][w][lane]);
 
   // pass 2: as k_attention_narrow
   int t0;
-  if constexpr (NW == 8) {
-    const int ko = 2 * g;
-    const float2 neg_mx = f2(-mx, -mx);
-    float2 vs = f2(0.0f, 0.0f);
-    const int L16r = has_row ? L16 : 0, Lr = has_row ? L : 0;
+#pragma unroll
+  for (int u = 0; u < QPT; ++u) {
+    const int L16r = has[u] ? L16 : 0, Lr = has[u] ? L : 0;
+    if constexpr (NW == 8) {
+      const int ko = 2 * g;
+      const float2 neg_mx = f2(-mx[u], -mx[u]);
+      float2 vs = f2(0.0f, 0.0f);
 #pragma unroll 4
-    for (t0 = 0; t0 + 16 <= L16r; t0 += 16) {
-      float2* ep = reinterpret_cast<float2*>(er + t0 + ko);
-      const float2 e = cw_exp2(add2(*ep, neg_mx));
-      vs = add2(vs, e);
-      *ep = e;
-    }
-    const int t = t0 + ko;
-    if (t < Lr) {
-      float2* ep = reinterpret_cast<float2*>(er + t);
-      const float2 x = add2(*ep, neg_mx);
-      float2 e;
-      if (ko < 8 && t + 1 < L8) {
-        e = cw_exp2(x);
+      for (t0 = 0; t0 + 16 <= L16r; t0 += 16) {
+        float2* ep = reinterpret_cast<float2*>(er[u] + t0 + ko);
+        const float2 e = cw_exp2(add2(*ep, neg_mx));
         vs = add2(vs, e);
-      } else {
-        e = f2(scalar_expf(x.x), t + 1 < L ? scalar_expf(x.y) : 0.0f);
+        *ep = e;
       }
-      *ep = e;
-    }
-    xsl[rw][ko][lane] = vs.x;
-    xsl[rw][ko + 1][lane] = vs.y;
-  } else {
-    float vs = 0.0f;
-    const int L16r = has_row ? L16 : 0, Lr = has_row ? L : 0;
+      const int t = t0 + ko;
+      if (t < Lr) {
+        float2* ep = reinterpret_cast<float2*>(er[u] + t);
+        const float2 x = add2(*ep, neg_mx);
+        float2 e;
+        if (ko < 8 && t + 1 < L8) {
+          e = cw_exp2(x);
+          vs = add2(vs, e);
+        } else {
+          e = f2(scalar_expf(x.x), t + 1 < L ? scalar_expf(x.y) : 0.0f);
+        }
+        *ep = e;
+      }
+      xsl[rw + u][ko][lane] = vs.x;
+      xsl[rw + u][ko + 1][lane] = vs.y;
+    } else {
+      float vs = 0.0f;
 #pragma unroll 4
-    for (t0 = 0; t0 + 16 <= L16r; t0 += 16) {
-      const float e = cw_exp(er[t0 + g] - mx);
-      vs = vs + e;
-      er[t0 + g] = e;
-    }
-    const int t = t0 + g;
-    if (t < Lr) {
-      const float x = er[t] - mx;
-      float e;
-      if (g < 8 && t < L8) {
-        e = cw_exp(x);
+      for (t0 = 0; t0 + 16 <= L16r; t0 += 16) {
+        const float e = cw_exp(er[u][t0 + g] - mx[u]);
         vs = vs + e;
-      } else {
-        e = scalar_expf(x);
+        er[u][t0 + g] = e;
       }
-      er[t] = e;
+      const int t = t0 + g;
+      if (t < Lr) {
+        const float x = er[u][t] - mx[u];
+        float e;
+        if (g < 8 && t < L8) {
+          e = cw_exp(x);
+          vs = vs + e;
+        } else {
+          e = scalar_expf(x);
+        }
+        er[u][t] = e;
+      }
+      xsl[rw + u][g][lane] = vs;
     }
-    xsl[rw][g][lane] = vs;
   }
   __syncthreads();
-  if (g == 0 && has_row) {
-    float v8[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v8[j] = xsl[rw][j][lane] + xsl[rw][8 + j][lane];
-    float sum = tree8(v8);
-    for (int t = L8; t < L; ++t) sum = sum + er[t];
-    xmx[rw][0][lane] = 1.0f / sum;
+  for (int u = 0; u < QPT; ++u) {
+    if (g == u && has[u]) {
+      float v8[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v8[j] = xsl[rw + u][j][lane] + xsl[rw + u][8 + j][lane];
+      float sum = tree8(v8);
+      for (int t = L8; t < L; ++t) sum = sum + er[u][t];
+      xmx[rw + u][0][lane] = 1.0f / sum;
+    }
   }
   __syncthreads();
-  const float inv = xmx[rw][0][lane];
-  const float2 inv2 = f2(inv, inv);
+  float2 inv2[QPT];
+#pragma unroll
+  for (int u = 0; u < QPT; ++u) {
+    const float inv = xmx[rw + u][0][lane];
+    inv2[u] = f2(inv, inv);
+  }
 
-  // pass 3: the weighted sum of dims DPG g .. DPG g + DPG - 1, four keys per 16-byte load
-  float2 acc[DPG];
+  // pass 3: the weighted sum of dims DPG g .. DPG g + DPG - 1, four keys per 16-byte load; each
+  // V load feeds the thread's QPT queries
+  float2 acc[QPT][DPG];
 #pragma unroll
-  for (int d = 0; d < DPG; ++d) acc[d] = f2(0.0f, 0.0f);
+  for (int u = 0; u < QPT; ++u)
+#pragma unroll
+    for (int d = 0; d < DPG; ++d) acc[u][d] = f2(0.0f, 0.0f);
   const int dg = DPG * g;
   int t = 0;
-  const int L3 = has_row ? L : 0;
+  const int L3 = has[0] ? L : 0;
 #pragma unroll 2
   for (; t + 4 <= L3; t += 4) {
-    const float4 e4 = *reinterpret_cast<const float4*>(er + t);
-    const float2 p01 = mul2(f2(e4.x, e4.y), inv2), p23 = mul2(f2(e4.z, e4.w), inv2);
+    float2 p01[QPT], p23[QPT];
+#pragma unroll
+    for (int u = 0; u < QPT; ++u) {
+      const float4 e4 = (u == 0 || has[u]) ? *reinterpret_cast<const float4*>(er[u] + t) : make_float4(0.f, 0.f, 0.f, 0.f);
+      p01[u] = mul2(f2(e4.x, e4.y), inv2[u]);
+      p23[u] = mul2(f2(e4.z, e4.w), inv2[u]);
+    }
 #pragma unroll
     for (int d = 0; d < DPG; ++d) {
       const float4 vv = *reinterpret_cast<const float4*>(vd + dm_index(dg + d, t));
-      acc[d] = fma2(f2(vv.x, vv.y), p01, acc[d]);
-      acc[d] = fma2(f2(vv.z, vv.w), p23, acc[d]);
+#pragma unroll
+      for (int u = 0; u < QPT; ++u) {
+        acc[u][d] = fma2(f2(vv.x, vv.y), p01[u], acc[u][d]);
+        acc[u][d] = fma2(f2(vv.z, vv.w), p23[u], acc[u][d]);
+      }
     }
   }
   for (; t + 1 < L3; t += 2) {
-    const float2 p = mul2(f2(er[t], er[t + 1]), inv2);
 #pragma unroll
-    for (int d = 0; d < DPG; ++d)
-      acc[d] = fma2(f2(vd[dm_index(dg + d, t)], vd[dm_index(dg + d, t + 1)]), p, acc[d]);
+    for (int u = 0; u < QPT; ++u) {
+      const float2 p = mul2(f2(er[u][t], er[u][t + 1]), inv2[u]);
+#pragma unroll
+      for (int d = 0; d < DPG; ++d)
+        acc[u][d] = fma2(f2(vd[dm_index(dg + d, t)], vd[dm_index(dg + d, t + 1)]), p, acc[u][d]);
+    }
   }
   if (t < L3) {  // odd L: the last key goes to the even accumulator
-    const float pa = er[t] * inv;
 #pragma unroll
-    for (int d = 0; d < DPG; ++d) acc[d].x = fmaf(vd[dm_index(dg + d, t)], pa, acc[d].x);
+    for (int u = 0; u < QPT; ++u) {
+      const float pa = er[u][t] * inv2[u].x;
+#pragma unroll
+      for (int d = 0; d < DPG; ++d) acc[u][d].x = fmaf(vd[dm_index(dg + d, t)], pa, acc[u][d].x);
+    }
   }
-  if (active) {
-    float* o = a.out + size_t(s0 + qi) * kHidden + h * 32 + dg;
-    if constexpr (DPG == 4)
-      *reinterpret_cast<float4*>(o) =
-          make_float4(acc[0].x + acc[0].y, acc[1].x + acc[1].y, acc[2].x + acc[2].y, acc[3].x + acc[3].y);
-    else
-      *reinterpret_cast<float2*>(o) = make_float2(acc[0].x + acc[0].y, acc[1].x + acc[1].y);
+#pragma unroll
+  for (int u = 0; u < QPT; ++u) {
+    if (active[u]) {
+      float* o = a.out + size_t(s0 + qi[u]) * kHidden + h * 32 + dg;
+      if constexpr (DPG == 4)
+        *reinterpret_cast<float4*>(o) = make_float4(acc[u][0].x + acc[u][0].y, acc[u][1].x + acc[u][1].y,
+                                                    acc[u][2].x + acc[u][2].y, acc[u][3].x + acc[u][3].y);
+      else
+        *reinterpret_cast<float2*>(o) = make_float2(acc[u][0].x + acc[u][0].y, acc[u][1].x + acc[u][1].y);
+    }
   }
 }
 
@@ -1995,7 +2097,7 @@ static int launch_narrow_dm(const AttnArgs& a, int n_seqs, cudaStream_t st) {
   if (qt > 64) qt = 64;
   while (qt > 32 && narrow_dm_smem_bytes(a.max_len, qt) + g_static_narrow_dm2 > 227 * 1024) --qt;
   const dim3 grid(n_seqs, kHeads, (a.max_len + qt - 1) / qt);
-  return launch_pdl(k_attention_narrow_dm<8, 2>, grid, dim3(512), narrow_dm_smem_bytes(a.max_len, qt), st, a, qt) ==
+  return launch_pdl(k_attention_narrow_dm<8, 1, 2>, grid, dim3(256), narrow_dm_smem_bytes(a.max_len, qt), st, a, qt) ==
                  cudaSuccess
              ? 0
              : -3;
@@ -2021,11 +2123,11 @@ int attention_prime() {
   r |= static_smem((const void*)k_attention_lat8, &g_static_lat8);
   r |= static_smem((const void*)k_attention_narrow<kNarrowWarps>, &g_static_narrow);
   r |= static_smem((const void*)k_attention_narrow_dm<kNarrowWarps, 1>, &g_static_narrow_dm);
-  r |= static_smem((const void*)k_attention_narrow_dm<8, 2>, &g_static_narrow_dm2);
+  r |= static_smem((const void*)k_attention_narrow_dm<8, 1, 2>, &g_static_narrow_dm2);
   if (r) return r;
   r |= smem_attr((const void*)k_attention_narrow<kNarrowWarps>, 227 * 1024 - g_static_narrow);
   r |= smem_attr((const void*)k_attention_narrow_dm<kNarrowWarps, 1>, 227 * 1024 - g_static_narrow_dm);
-  r |= smem_attr((const void*)k_attention_narrow_dm<8, 2>, 227 * 1024 - g_static_narrow_dm2);
+  r |= smem_attr((const void*)k_attention_narrow_dm<8, 1, 2>, 227 * 1024 - g_static_narrow_dm2);
   r |= smem_attr((const void*)k_attention_lat8, 227 * 1024 - g_static_lat8);
   r |= smem_attr((const void*)k_attention_rows2, rows_smem_cap(g_static_rows2));
   r |= smem_attr((const void*)k_attention_rows<128>, rows_smem_cap(g_static_rows));
