@@ -134,7 +134,10 @@ int ae_plan_shards(const uint32_t* cu_seqlens, uint32_t n_seqs, int n_shards, in
  *   epi 2: GELU(epi 0) * inv_smooth, row-quantized -> out_q [M, 1536], out_scale [M]    (N = 1536)
  *   epi 3: epi 0 with res, then layernorm_inplace_row + l2_normalize_inplace -> out     (N = 384)
  * A [M, K] int8, W [N, K] int8 row-major; K a multiple of 128. acc (nullable) receives the raw
- * int32 accumulators [M, N]. Every pointer must be 16-byte aligned (AE_ERR_INVALID_ARG otherwise). */
+ * int32 accumulators [M, N]. Every pointer must be 16-byte aligned (AE_ERR_INVALID_ARG otherwise).
+ * Epilogues 1 and 3 run fused into the GEMM from 74 row tiles of 128 (M >= 9,345); below, as a
+ * GEMM into a context-owned scratch buffer (grown on demand) followed by a row kernel, with the
+ * same results. out may alias res, and out_q / out_scale may alias A / a_scale. */
 int ae_gemm_i8(ae_ctx* ctx, int epi, uint32_t M, uint32_t N, uint32_t K, const int8_t* d_a, const float* d_a_scale,
                const int8_t* d_w, const float* d_w_scale, const float* d_bias, const float* d_res,
                const float* d_gamma, const float* d_beta, const float* d_inv_smooth, float* d_out, int8_t* d_out_q,

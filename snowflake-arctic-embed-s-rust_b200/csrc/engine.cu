@@ -120,6 +120,8 @@ struct ae_ctx {
   float* h_lat = nullptr;  // pinned
   int* h_err = nullptr;    // pinned copy of d_err, taken on the stream before a synchronisation
   uint32_t* d_cu_single = nullptr;  // [513][2]: {0, L} at 2L, the cu_seqlens of one sequence of L ids
+  float* d_gemm_scratch = nullptr;  // ae_gemm_i8's split LayerNorm path: h of up to gemm_scratch_rows rows
+  uint32_t gemm_scratch_rows = 0;
   bool has_model = false;
   DevModel model;
   void* h_model = nullptr;  // pinned host image of the model arena (reused across loads)
@@ -1148,6 +1150,7 @@ int ae_ctx_destroy(ae_ctx* c) {
   if (c->h_lat) cudaFreeHost(c->h_lat);
   if (c->h_err) cudaFreeHost(c->h_err);
   if (c->d_cu_single) cudaFree(c->d_cu_single);
+  if (c->d_gemm_scratch) cudaFree(c->d_gemm_scratch);
   if (c->own_stream) cudaStreamDestroy(c->own_stream);
   delete c;
   return 0;
@@ -1570,6 +1573,34 @@ int ae_gemm_i8(ae_ctx* c, int epi, uint32_t M, uint32_t N, uint32_t K, const int
       break;
     default:
       return fail(c, AE_ERR_INVALID_ARG, "unknown epilogue %d", epi);
+  }
+  if ((epi == EPI_LN_QUANT || epi == EPI_LN_FINAL) && (M + 127) / 128 < 74) {
+    // few row tiles (fewer than half the SMs): as the forward does, a plain-epilogue GEMM over
+    // narrow column slices writes h = fma(acc, as*ws, bias + res) into scratch and a row kernel
+    // applies the same LayerNorm (and quantization) -- the same bits as the fused epilogue
+    if (c->gemm_scratch_rows < M) {
+      if (c->d_gemm_scratch) {
+        CUDA_TRY(c, cudaStreamSynchronize(c->stream));
+        cudaFree(c->d_gemm_scratch);
+        c->d_gemm_scratch = nullptr;
+        c->gemm_scratch_rows = 0;
+      }
+      CUDA_TRY(c, cudaMalloc(&c->d_gemm_scratch, size_t(M) * kHidden * sizeof(float)));
+      c->gemm_scratch_rows = M;
+    }
+    GemmArgs h = a;
+    h.out_f32 = c->d_gemm_scratch;
+    h.ldo = kHidden;
+    h.out_q = nullptr;
+    h.out_scale = nullptr;
+    const int r = gemm_i8_launch(EPI_F32, ta, tb, h, c->stream);
+    if (r) return fail(c, AE_ERR_CUDA, "GEMM launch failed (split LayerNorm path): code %d", r);
+    const int q = epi == EPI_LN_QUANT
+                      ? launch_ln_quant_rows(c->d_gemm_scratch, int(M), d_gamma, d_beta, d_inv_smooth, d_out, 0,
+                                             d_out_q, d_out_scale, c->stream)
+                      : launch_ln_final_rows(c->d_gemm_scratch, int(M), d_gamma, d_beta, d_out, c->stream);
+    if (q) return fail(c, AE_ERR_CUDA, "LayerNorm row kernel launch failed");
+    return 0;
   }
   const int r = gemm_i8_launch(epi, ta, tb, a, c->stream);
   if (r) return fail(c, AE_ERR_CUDA, "GEMM launch failed: code %d", r);

@@ -40,8 +40,10 @@ def test_f32_epilogue_bit_exact(engine, M, K, N):
     np.testing.assert_array_equal(out.cpu().numpy(), ref_out)
 
 
+# ae_gemm_i8 takes the LayerNorm epilogues fused into the GEMM from 74 row tiles (9,345+ rows) and
+# as a plain GEMM + row kernel below: both sides of the switch are checked
 @pytest.mark.parametrize("K", [384, 1536])
-@pytest.mark.parametrize("M", [1, 100, 256, 333])
+@pytest.mark.parametrize("M", [1, 100, 256, 333, 9473])
 def test_ln_quant_epilogue_bit_exact(engine, M, K):
     N = 384
     a, w, a_s, w_s, b = make_case(M, K, N, 11 * M + K)
@@ -64,9 +66,10 @@ def test_ln_quant_epilogue_bit_exact(engine, M, K):
     np.testing.assert_array_equal(sc.cpu().numpy(), s_ref)
 
 
-def test_ln_quant_in_place(engine):
+@pytest.mark.parametrize("M", [200, 9600])
+def test_ln_quant_in_place(engine, M):
     """The forward pass writes the LayerNorm output over the residual it reads."""
-    M, K, N = 200, 384, 384
+    K, N = 384, 384
     a, w, a_s, w_s, b = make_case(M, K, N, 5)
     r = rng(9)
     res = r.normal(0, 1, (M, N)).astype(np.float32)
@@ -110,7 +113,7 @@ def test_gelu_quant_epilogue(engine, M):
     assert (dq > 0).mean() < 1e-4
 
 
-@pytest.mark.parametrize("M", [1, 64, 129])
+@pytest.mark.parametrize("M", [1, 64, 129, 9473])
 def test_final_ln_l2_epilogue_bit_exact(engine, M):
     K, N = 1536, 384
     a, w, a_s, w_s, b = make_case(M, K, N, 13 + M)
