@@ -97,7 +97,9 @@ def make_batches(n_batches: int, seed: int, seqs: int = BATCH_SEQS, L: int = SEQ
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+    """nvidia-smi clocks and throttle reasons sampled every 50 ms from before the warm-up on, each
+    sample stamped on arrival; summary() keeps the samples inside the timed window (mark_start /
+    mark_end), or the first one after its start when the window is shorter than the interval."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -106,13 +108,14 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
-        self.lines: list[str] = []
+        self.lines: list[tuple[float, str]] = []
+        self.t0 = self.t1 = None
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
         except OSError:
@@ -121,7 +124,17 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.perf_counter(), line.strip()))
+
+    def mark_start(self):
+        self.t0 = time.perf_counter()
+
+    def mark_end(self):
+        self.t1 = time.perf_counter()
+        if self.proc:  # the sample that closes the window
+            deadline = self.t1 + 0.5
+            while time.perf_counter() < deadline and not any(t >= self.t1 for t, _ in self.lines):
+                time.sleep(0.01)
 
     def __exit__(self, *a):
         if self.proc:
@@ -132,9 +145,15 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
+        t0 = self.t0 if self.t0 is not None else float("-inf")
+        t1 = self.t1 if self.t1 is not None else float("inf")
+        inside = [ln for t, ln in self.lines if t0 <= t <= t1]
+        if not inside:
+            after = [ln for t, ln in self.lines if t >= t0]
+            inside = after[:1]
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in inside:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -148,7 +167,8 @@ class ClockSampler:
                     reasons.add(n)
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
-        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm),
+                "interval_ms": 50}
 
 
 def cpu_baseline(seconds: float = 10.0, L: int = SEQ_LEN, threads: int | None = None):
@@ -539,25 +559,26 @@ def main() -> int:
 
     # ---- value: device-resident inputs
     launches0 = eng.kernel_launches()
-    with torch.cuda.stream(stream):
+    with torch.cuda.stream(stream), ClockSampler(local) as clk:
         for i in range(args.warmup):
             eng.forward_device(d_in[i][0], d_in[i][1], BATCH_SEQS, T, SEQ_LEN, d_out)
         eng.sync()
         barrier()
         launches0 = eng.kernel_launches()
         evs = []
-        with ClockSampler(local) as clk:
-            for i in range(args.steps):
-                flush.fill_(float(i))
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-                b = d_in[args.warmup + i]
-                eng.forward_device(b[0], b[1], BATCH_SEQS, T, SEQ_LEN, d_out)
-                e1.record(stream)
-                evs.append((e0, e1))
-            stream.synchronize()
-            eng.sync()
-            barrier()
+        clk.mark_start()
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            b = d_in[args.warmup + i]
+            eng.forward_device(b[0], b[1], BATCH_SEQS, T, SEQ_LEN, d_out)
+            e1.record(stream)
+            evs.append((e0, e1))
+        stream.synchronize()
+        eng.sync()
+        clk.mark_end()
+        barrier()
         launches = eng.kernel_launches() - launches0
     step_ms = [a.elapsed_time(b) for a, b in evs]
     total_s = max_over_ranks(sum(step_ms) / 1e3)
