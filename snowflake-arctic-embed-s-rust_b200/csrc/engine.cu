@@ -1810,7 +1810,7 @@ int ae_embed_batch_multi(ae_ctx* const* ctxs, int n_ctx, const uint16_t* ids, co
 namespace {
 
 constexpr size_t kNoAllocBytes = size_t(8) << 20;  // 8 MiB: holds the workspace of one 512-token sequence
-__device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
 
 // Per-device view of g_noalloc_scratch: its device address (from cudaGetSymbolAddress, not the
 // host-side name) carved into a Workspace, with tensor maps for the GEMM A operands. The address
