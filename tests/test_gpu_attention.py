@@ -59,15 +59,13 @@ def test_attention_two_queries_per_thread_matches_oracle(engine):
     assert (got == ref).mean() > 0.99
 
 
-@pytest.mark.parametrize("lens", [[128] * 25, [128], [512], [144] * 3])
+@pytest.mark.parametrize("lens", [[128] * 25, [128], [512], [64] * 30, [144] * 3])
 def test_attention_bit_exact_without_scalar_tail(engine, lens):
     """Lengths that are multiples of 16 have no softmax tail element (every exponential is the
     reference's 8-wide Cody-Waite polynomial, computed on the packed f32x2 pipe): the attention then
-    equals the oracle bit for bit for the kernels that take these batches (two queries per thread
-    for 25 x 128, the single-sequence dim-major kernels at 128 and 512, the multi-warpgroup TMEM
-    kernel for 144). The key-pair kernel of wide batches of <= 64 keys is not in this list: on
-    30 x 64 keys about 3 outputs in 100,000 differ from the oracle by a few ulp (within the
-    tolerance of test_attention_matches_oracle)."""
+    equals the oracle bit for bit, whichever kernel takes the batch (two queries per thread for
+    25 x 128, the single-sequence dim-major kernels at 128 and 512, the key-pair kernel for 30 x 64,
+    the few-sequence kernel for 3 x 144)."""
     r = rng(sum(lens) + 1)
     T = sum(lens)
     qkv = r.normal(0, 1, (T, 1152)).astype(np.float32)
