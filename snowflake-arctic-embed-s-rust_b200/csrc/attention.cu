@@ -99,6 +99,18 @@ __device__ __forceinline__ float2 cw_exp2(float2 x) {
   return mul2(p, pw);
 }
 
+// (sequence, head, z) of a block of a (sequences, heads, z) grid, numbered so that z varies fastest
+// in launch order: the query-tile CTAs of one (sequence, head), which all stage the same K / V, are
+// dispatched together, and all but the first find K / V in L2 (launched with the sequence fastest,
+// the tiles of a pair were thousands of CTAs apart and re-read K / V from DRAM).
+__device__ __forceinline__ void tile_major_block(int& s, int& h, int& z) {
+  const unsigned lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  z = int(lin % gridDim.z);
+  const unsigned rest = lin / gridDim.z;
+  h = int(rest % gridDim.y);
+  s = int(rest / gridDim.y);
+}
+
 constexpr int KPS = 34;  // float2 per staged key pair (32 dims + 2 pad: 16-byte aligned, fewer bank conflicts)
 
 __device__ __forceinline__ float ld_act(const float* p, int C, int tt, int t, int c) {
@@ -196,7 +208,7 @@ __host__ __device__ constexpr uint32_t tmem_cols_for_len(int L) {
 // memory holds only the head's K / V pairs. Threads whose query lies past the sequence still take
 // part in the warp-collective TMEM loads and stores and write nothing.
 //
-// DSPLIT > 1 (few tiles: single sequences): blockIdx.z = tile * DSPLIT + part, and CTA `part`
+// DSPLIT > 1 (few tiles: single sequences): z = tile * DSPLIT + part, and CTA `part`
 // repeats the scores and exponentials of its tile but runs the weighted sum only for dims
 // part * 32 / DSPLIT .. + 32 / DSPLIT - 1.
 template <int QT, int DSPLIT = 1>
@@ -206,10 +218,10 @@ __global__ void __launch_bounds__(QT, 512 / QT) k_attention_rows(AttnArgs a) {
   constexpr int DN = 32 / DSPLIT;  // dims of this CTA's weighted sum
   extern __shared__ float4 smem4[];
   __shared__ uint32_t tmem_slot;
-  const int s = blockIdx.x;
-  const int h = blockIdx.y;
-  const int tile = blockIdx.z / DSPLIT;
-  const int dbase = (blockIdx.z % DSPLIT) * DN;
+  int s, h, bz;
+  tile_major_block(s, h, bz);
+  const int tile = bz / DSPLIT;
+  const int dbase = (bz % DSPLIT) * DN;
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int s0 = int(a.cu[s]);
@@ -1238,7 +1250,7 @@ __global__ void __launch_bounds__(512) k_attention_lat8(AttnArgs a, int qt) {
 // every 16-key chunk (KPG = 16 / NWG), so each of the reference's 16 sum slots is summed in order
 // by one group; P.V: group g accumulates dims g DPG .. (g + 1) DPG - 1 (DPG = 32 / NWG) over all
 // keys in order.
-// DSPLIT > 1 (few (sequence, head) pairs: single sequences): blockIdx.z = tile * DSPLIT + part,
+// DSPLIT > 1 (few (sequence, head) pairs: single sequences): z = tile * DSPLIT + part,
 // and CTA `part` runs the scores and exponentials of its tile (the same work in every part) but the
 // weighted sum only for dims part * 32 / DSPLIT .. + 32 / DSPLIT - 1, so a tile's attention spreads
 // over DSPLIT SMs.
@@ -1253,10 +1265,10 @@ __global__ void __launch_bounds__(128 * NWG, MINB) k_attention_wide(AttnArgs a) 
   __shared__ uint32_t tmem_slot;
   __shared__ float xmx[NWG][128];
   __shared__ float xsl[16][128];  // the 16 slot sums of every query
-  const int s = blockIdx.x;
-  const int h = blockIdx.y;
-  const int tile = blockIdx.z / DSPLIT;
-  const int dbase = (blockIdx.z % DSPLIT) * (32 / DSPLIT);  // first dim of this CTA's weighted sum
+  int s, h, bz;
+  tile_major_block(s, h, bz);
+  const int tile = bz / DSPLIT;
+  const int dbase = (bz % DSPLIT) * (32 / DSPLIT);  // first dim of this CTA's weighted sum
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int grp = warp >> 2;
