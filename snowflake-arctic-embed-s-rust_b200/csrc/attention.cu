@@ -2274,14 +2274,15 @@ __global__ void __launch_bounds__(kI8Queries, 4) k_attention_i8(AttnArgs a, int 
   pdl_wait();
   __shared__ I8Smem sm;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int s = blockIdx.x, h = blockIdx.y;
+  int s, h, z;
+  tile_major_block(s, h, z);  // the query tiles of a (sequence, head) together: K / V from L2
   const int s0 = int(a.cu[s]);
   const int L = int(a.cu[s + 1]) - s0;
   if (L <= 0 || L > a.max_len) {
     if (tid == 0) record_err(a.err, DEV_ERR_BAD_SHAPE);
     return;
   }
-  const int i0 = blockIdx.z * kI8Queries;
+  const int i0 = z * kI8Queries;
   if (L < min_len || i0 >= L) return;
   const int L8 = L & ~7, pairs = (L + 1) >> 1;
   const int qc = a.q_col + 32 * h, kc = a.k_col + 32 * h, vc = a.v_col + 32 * h;
